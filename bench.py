@@ -1,0 +1,387 @@
+"""Benchmark of the training step (BASELINE.json metric) on synthetic C1.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (N=1): BASELINE.json config 1 -- 1,000,000 seeded synthetic
+Gaussians rendered at 1297x840 from 16 cameras on a radius-4 sphere, the
+target of each camera a render of an independent seed-1 scene (mip-NeRF 360
+garden at 4x downscale is not available; see msplat_b200/synthetic.py).
+A step is one full training iteration of one view: projection + SH,
+binning, sort, forward raster, L1 + SSIM loss, backward, Adam on all six
+groups and the densification statistics.  `value` is training views/s over
+the whole job with every input resident in HBM; the per-step footprint
+(~2 GB of parameters, moments and buffers) exceeds the 126 MB L2.
+`e2e` is the same loop through the public API with the step's target image
+copied from pinned host memory and the loss read back every step.
+
+Under torchrun (N > 1) every rank trains its own view of the same scene
+each step and the ranks exchange the 59-float-per-Gaussian gradient with an
+NCCL all-reduce before Adam (msplat_b200.multigpu); per-GPU work is fixed,
+so scaling is weak.
+
+--impl reference times the reference's CPU implementation of the path (the
+oracle port, or oracle/_ref when the reference was compiled) on the host
+cores, rank 0 only, on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "train steps/s + render FPS @1M Gaussians 1297×840; 1/2/4/8-GPU views/s"
+UNIT = "views/s"
+CONFIG = "C1"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true",
+                    help="skip the timed CPU oracle sample (profiling runs)")
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self._t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self._t = threading.Thread(target=self._read, daemon=True)
+        self._t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+
+def build_workload(device_gt: bool = True):
+    import torch
+    from msplat_b200 import camera, engine, synthetic
+    g, cams = synthetic.scene(CONFIG)
+    setups = [camera.prepare_camera(c, step=10**9, sh_degree=3, sh_degree_interval=1000,
+                                    rest_bases=15) for c in cams]
+    # targets: renders of an independent seed-1 scene, one per camera
+    tgt, _ = synthetic.scene(CONFIG, seed=1)
+    tmodel = engine.GaussianModel(tgt.groups())
+    gts = []
+    h, w = setups[0].height, setups[0].width
+    for cs in setups:
+        ptr = engine.render(tmodel, cs)
+        buf = torch.empty((h, w, 3), dtype=torch.float32, device="cuda")
+        from msplat_b200 import _lib
+        _lib.check(_lib.load().msplat_copy(buf.data_ptr(), ptr, buf.numel() * 4, 2, 0), "copy")
+        gts.append(buf)
+    torch.cuda.synchronize()
+    del tmodel
+    model = engine.GaussianModel(g.groups())
+    return g, setups, gts, model
+
+
+def algorithmic_bytes_proj_bwd(n_total: int, n_vis: int, rest_floats: int) -> float:
+    """Algorithmic HBM bytes of the fused projection-backward + Adam + stats
+    kernel for one step: every Gaussian reads its radius and runs Adam on
+    11 floats of means/scales/quats/opacity (read p, m, v; write p, m, v);
+    a visible one also reads its 9 raster gradients and its conic/opacity
+    record, runs Adam on 3 dc and `rest_floats` SH-rest floats, and updates
+    3 statistics (read + write)."""
+    per_all = 4 + 11 * 24
+    per_vis = 9 * 4 + 16 + 3 * 24 + rest_floats * 24 + 3 * 8
+    return float(n_total * per_all + n_vis * per_vis)
+
+
+def run_ours(args, rank: int, world: int):
+    import torch
+    from msplat_b200 import _lib, engine
+    lib = _lib.load()
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    engine.bind_stream()
+    g, setups, gts, model = build_workload()
+    dist = None
+    if world > 1:
+        from msplat_b200 import multigpu
+        dist = multigpu.DataParallel(model, rank, world)
+    ncam = len(setups)
+
+    def view_of(step):
+        return (step * world + rank) % ncam
+
+    def one_step(step):
+        cs = setups[view_of(step)]
+        if dist is None:
+            engine.train_step(model, cs, gts[view_of(step)])
+        else:
+            dist.train_step(cs, gts[view_of(step)])
+
+    for s in range(args.warmup):
+        one_step(s)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    # --- timed: device-resident training ---------------------------------
+    lib.msplat_enable_gpu_timing(1)
+    lib.msplat_drain_gpu_times(None, 0)
+    nstage = 6
+    buf = (C_double * (nstage * 4096))()
+    lib.msplat_drain_stage_times(buf, nstage, 4096, None, None)
+    lib.msplat_kernel_launches(1)
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for s in range(args.steps):
+        one_step(args.warmup + s)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    launches = int(lib.msplat_kernel_launches(1))
+    lib.msplat_enable_gpu_timing(0)
+    ms = e0.elapsed_time(e1)
+    nsamp = C_int()
+    names = (C_char_p * nstage)()
+    ns = lib.msplat_drain_stage_times(buf, nstage, 4096, C_byref(nsamp), names)
+    stage_ms = {}
+    for si in range(ns):
+        vals = [buf[si * 4096 + j] for j in range(nsamp.value)]
+        stage_ms[names[si].decode()] = float(np.mean(vals)) if vals else 0.0
+    ms_max = ms
+    if dist is not None:
+        ms_max = dist.max_over_ranks(ms)
+    views = args.steps * world
+    value = views / (ms_max / 1000.0)
+
+    # --- render FPS (forward only) ------------------------------------------
+    torch.cuda.synchronize()
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for s in range(3):
+        engine.render(model, setups[s % ncam])
+    r0.record(stream)
+    for s in range(args.steps):
+        engine.render(model, setups[s % ncam])
+    r1.record(stream)
+    torch.cuda.synchronize()
+    render_ms = r0.elapsed_time(r1) / args.steps
+    n_isect = int(lib.msplat_num_intersections())
+    radii = engine.debug_buffer("radii", model.n, np.int32)
+    n_vis = int((radii > 0).sum())
+
+    # --- end to end through the public API with host buffers ----------------
+    h, w = setups[0].height, setups[0].width
+    host_gts = [t.cpu().pin_memory() for t in gts[:4]]
+    dev_gt = torch.empty_like(gts[0])
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    losses = []
+    for s in range(args.steps):
+        dev_gt.copy_(host_gts[s % len(host_gts)], non_blocking=True)
+        if dist is None:
+            engine.train_step(model, setups[view_of(s)], dev_gt)
+        else:
+            dist.train_step(setups[view_of(s)], dev_gt)
+        losses.append(lib.msplat_last_loss(0))
+    lib.msplat_last_loss(1)
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    if dist is not None:
+        e2e_s = dist.max_over_ranks(e2e_s * 1000.0) / 1000.0
+    e2e_value = views / e2e_s
+
+    # --- roofline of the dominant HBM-bound kernel ---------------------------
+    pk = peaks()
+    dom = "proj_bwd_adam"
+    algo = algorithmic_bytes_proj_bwd(model.n, n_vis, 45)
+    dom_ms = stage_ms.get(dom, 0.0)
+    achieved = algo / (dom_ms / 1000.0) / 1e9 if dom_ms > 0 else 0.0
+    roofline = {"bound": "hbm", "kernel": "project_backward_adam_kernel", "achieved": round(achieved, 1),
+                "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+                "peak_source": pk["source"], "algorithmic_bytes": algo, "launch_ms": round(dom_ms, 4),
+                "traffic": None}
+
+    result = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded C1 scene; targets are renders of a seed-1 scene)",
+        "config": {"workload": "C1: 1,000,000 Gaussians, SH degree 3, 1297x840, 16 cameras, "
+                               "one view per GPU per step",
+                   "gaussians": model.n, "width": w, "height": h, "cameras": ncam,
+                   "l2": "inputs larger than L2 (per-step footprint ~2 GB)",
+                   "parallelism": f"dp{world} (replicated Gaussians, gradient all-reduce)"
+                   if world > 1 else "single GPU"},
+        "train_steps_per_s": round(args.steps / (ms_max / 1000.0), 2),
+        "render_fps": round(1000.0 / render_ms, 1),
+        "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()},
+        "intersections": n_isect, "visible_gaussians": n_vis,
+        "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
+                "h2d_bytes_per_step": int(h * w * 3 * 4 + 512),
+                "d2h_bytes_per_step": 12},
+        "roofline": roofline,
+        "gpu_launches": launches,
+        "clocks": clk,
+        "loss": float(lib.msplat_last_loss(1)),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        result["cpu_baseline"] = cpu_baseline(g, setups, gts)
+    if dist is not None:
+        dist.shutdown()
+    return result
+
+
+def _oracle_kind():
+    ref = os.path.join(ROOT, "oracle", "_ref", "libmsplat_ref.so")
+    return ("reference", ref) if os.path.exists(ref) else ("port", None)
+
+
+def cpu_baseline(g, setups, gts, steps: int = 1, warmup: int = 0) -> dict:
+    """One C1 training step of the CPU implementation on all host threads."""
+    from oracle import oracle
+    kind, _ = _oracle_kind()
+    kind = "port"  # the reference shim is timed by --impl reference
+    threads = os.cpu_count() or 1
+    oracle.set_threads(threads)
+    cs = setups[0]
+    gt = gts[0].cpu().numpy() if hasattr(gts[0], "cpu") else gts[0]
+    params = [x.copy() for x in g.groups()]
+    m = [np.zeros_like(x) for x in params]
+    v = [np.zeros_like(x) for x in params]
+    st = [np.zeros(g.n, np.float32) for _ in range(3)]
+    run = oracle.Run(cs, g.n, adam_steps=[1e-3] * 6, adam_bc2=[0.0316] * 6)
+    for _ in range(warmup):
+        run.train_step(params, m, v, gt, *st)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        run.train_step(params, m, v, gt, *st)
+    dt = time.perf_counter() - t0
+    return {"value": round(steps / dt, 4), "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"{steps} full C1 training step(s) of one 1297x840 view, 1M Gaussians "
+                      f"(CPU oracle, OpenMP over {threads} threads)"}
+
+
+def run_reference(args, rank: int, world: int):
+    if rank != 0:
+        return None
+    from msplat_b200 import camera, synthetic
+    from oracle import oracle
+    g, cams = synthetic.scene(CONFIG)
+    setups = [camera.prepare_camera(c, step=10**9, sh_degree=3, sh_degree_interval=1000,
+                                    rest_bases=15) for c in cams]
+    gts = [synthetic.target_image(setups[0].width, setups[0].height, 1 + i) for i in range(2)]
+    threads = os.cpu_count() or 1
+    oracle.set_threads(threads)
+    params = [x.copy() for x in g.groups()]
+    m = [np.zeros_like(x) for x in params]
+    v = [np.zeros_like(x) for x in params]
+    st = [np.zeros(g.n, np.float32) for _ in range(3)]
+    steps = max(1, min(args.steps, 8))
+    warm = max(0, min(args.warmup, 1))
+    times = []
+    for s in range(warm + steps):
+        cs = setups[s % len(setups)]
+        run = oracle.Run(cs, g.n, adam_steps=[1e-3] * 6, adam_bc2=[0.0316] * 6)
+        t0 = time.perf_counter()
+        run.train_step(params, m, v, gts[s % 2], *st)
+        if s >= warm:
+            times.append(time.perf_counter() - t0)
+    value = len(times) / sum(times)
+    kind, _ = _oracle_kind()
+    return {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
+            "n_gpus": world, "steps": len(times), "warmup": warm,
+            "ms_per_step": round(1000 * sum(times) / len(times), 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "C1: 1,000,000 Gaussians, SH degree 3, 1297x840, one view "
+                                   "per step (CPU)"},
+            "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads,
+                             "kind": "port" if kind == "port" else "reference",
+                             "sample": f"{len(times)} full C1 training steps (capped at 8 of "
+                                       f"--steps {args.steps})"},
+            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+    else:
+        res = run_ours(args, rank, world)
+    if rank == 0 and res is not None:
+        print(json.dumps(res), flush=True)
+
+
+from ctypes import byref as C_byref, c_char_p as C_char_p, c_double as C_double, c_int as C_int  # noqa: E402
+
+if __name__ == "__main__":
+    main()

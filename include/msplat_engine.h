@@ -1,0 +1,153 @@
+/*
+ * msplat_engine.h -- C-ABI of the B200 engine: the backend seam that
+ * msplat's Metal engine exposes in core/metal/bindings.h, re-expressed with
+ * plain pointers and sizes (no C++ or torch types), plus the few calls a
+ * host needs that Metal's unified memory made implicit (stream, copies,
+ * last error).
+ *
+ * Memory: every "device" pointer below is CUDA device memory on the current
+ * device (cudaMalloc, msplat_gpu_alloc, or a torch CUDA tensor's data_ptr).
+ * Small per-step values the reference kept in GPU tensors (view/projection
+ * matrices, background colour) are passed as host arrays; the engine copies
+ * them into a per-step parameter block on its stream.
+ *
+ * Errors: functions that can fail return 0 on success and a negative code
+ * otherwise; msplat_last_error() describes the last failure.  Nothing here
+ * falls back to the CPU: without a usable CUDA device every compute entry
+ * point fails with MSPLAT_ERR_CUDA.
+ *
+ * Threading: one engine per process and device, used from one host thread
+ * at a time (the reference's single global context and serial dispatch
+ * queue, msplat_metal.mm:179, have the same rule).
+ */
+#ifndef MSPLAT_ENGINE_H
+#define MSPLAT_ENGINE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MSPLAT_OK 0
+#define MSPLAT_ERR_ARG (-1)      /* invalid argument */
+#define MSPLAT_ERR_CUDA (-2)     /* CUDA runtime error / no device */
+#define MSPLAT_ERR_OVERFLOW (-3) /* intersection buffer overflow */
+
+#define MSPLAT_N_ADAM_GROUPS 6   /* means, scales, quats, features_dc, features_rest, opacities */
+
+/* ---- lifecycle and memory (bindings.h:8-27) ---------------------------- */
+
+/* Last error message of this thread ("" when none). */
+const char *msplat_last_error(void);
+
+/* Use `cuda_stream` (a cudaStream_t) for all engine work; NULL selects the
+ * engine's own stream.  No reference counterpart (Metal used one queue). */
+int msplat_set_stream(void *cuda_stream);
+void *msplat_get_stream(void);
+
+/* Replaces msplat_device() (bindings.h:11-15): returns a pointer to the
+ * CUDA device ordinal the engine runs on, or NULL if there is no device. */
+void *msplat_device(void);
+
+/* Replaces gpu_zeros / gpu_empty (bindings.h:17-18): device allocation of
+ * `bytes`, zero-filled when `zero` != 0.  Free with msplat_gpu_free. */
+void *msplat_gpu_alloc(size_t bytes, int zero);
+void msplat_gpu_free(void *ptr);
+/* Host<->device copies on the engine stream (Metal's shared storage made
+ * these implicit); `kind` 0 = host to device, 1 = device to host,
+ * 2 = device to device.  Synchronous when `sync` != 0. */
+int msplat_copy(void *dst, const void *src, size_t bytes, int kind, int sync);
+
+/* msplat_commit (bindings.h:21): work is already queued on the stream;
+ * this records a commit point (for GPU timing) and returns immediately. */
+void msplat_commit(void);
+/* msplat_gpu_sync (bindings.h:24): block until all queued work is done. */
+void msplat_gpu_sync(void);
+/* cleanup_msplat_metal (bindings.h:8): free every cached buffer. */
+void cleanup_msplat_metal(void);
+void cleanup_msplat_cuda(void);
+/* msplat_set_metallib_path (msplat_metal.mm:168): accepted and ignored. */
+void msplat_set_metallib_path(const char *path);
+
+/* GPU timing (bindings.h:27-33).  Times are ms per committed step measured
+ * with CUDA events on the engine stream. */
+void msplat_enable_gpu_timing(int enable);
+int msplat_drain_gpu_times(double *out, int max_out);
+/* Per-stage times: fills stage_times[max_stages*max_samples] row-major by
+ * stage and stage_names; returns the number of stages. */
+int msplat_drain_stage_times(double *stage_times, int max_stages, int max_samples,
+                             int *n_samples, const char **stage_names);
+
+/* ---- the hot path ------------------------------------------------------- */
+
+/*
+ * One full training iteration: projection + SH, tile binning and per-tile
+ * depth sort, forward raster, L1 + SSIM loss, backward raster, projection
+ * backward, Adam for all six groups (SH groups only for visible Gaussians)
+ * and the densification statistics.
+ * Replaces std::tuple<MTensor,float> msplat_train_step(...) (bindings.h:50-67;
+ * implementation msplat_metal.mm:771-1330) argument for argument:
+ *   means3d (N,3), scales (N,3, log), quats (N,4, w x y z), features_dc (N,3),
+ *   features_rest (N,features_rest_bases,3), opacities (N, logit),
+ *   gt (H,W,3), vis_counts/xys_grad_norm/max_2d_size (N): device pointers;
+ *   viewmat, projmat (16, row-major), cam_pos (3), background (3),
+ *   tile_bounds (3), adam_step_sizes/adam_bc2_sqrts (num_adam_groups): host;
+ *   adam_params/adam_exp_avg/adam_exp_avg_sq: host arrays of device pointers
+ *   in group order means, scales, quats, features_dc, features_rest,
+ *   opacities (params alias the tensors above, as in Model::fullIteration).
+ *   window2d is accepted and unused (the loss uses the separable window).
+ * On return *radii_out (if non-NULL) aliases the engine's radii buffer (N,
+ * int32, device), valid until the next call, and *loss_out (if non-NULL) is
+ * the loss of the most recent step whose value has reached the host
+ * without a wait (the reference likewise reads its loss without syncing).
+ */
+int msplat_train_step(
+    int num_points, float *means3d, float *scales, float glob_scale, float *quats,
+    const float *viewmat, const float *projmat, float fx, float fy, float cx, float cy,
+    unsigned img_height, unsigned img_width, const int *tile_bounds, float clip_thresh,
+    unsigned degree, unsigned degrees_to_use, const float *cam_pos,
+    float *features_dc, float *features_rest, float *opacities, const float *background,
+    const float *gt, const float *window2d, float ssim_weight, float loss_inv_n,
+    int features_rest_bases, int num_adam_groups, float *const *adam_params,
+    float *const *adam_exp_avg, float *const *adam_exp_avg_sq,
+    const float *adam_step_sizes, const float *adam_bc2_sqrts, float adam_beta1,
+    float adam_beta2, float adam_eps, float *vis_counts, float *xys_grad_norm,
+    float *max_2d_size, float inv_max_dim, const int32_t **radii_out, float *loss_out);
+
+/*
+ * Forward-only render.  Replaces MTensor msplat_render(...) (bindings.h:37-46;
+ * implementation msplat_metal.mm:752-769).  *out_img receives a device
+ * pointer to the engine's (H,W,3) float image, valid until the next call
+ * (the reference returns an alias of its cached out_img the same way).
+ */
+int msplat_render(
+    int num_points, const float *means3d, const float *scales, float glob_scale,
+    const float *quats, const float *viewmat, const float *projmat, float fx, float fy,
+    float cx, float cy, unsigned img_height, unsigned img_width, const int *tile_bounds,
+    float clip_thresh, unsigned degree, unsigned degrees_to_use, const float *cam_pos,
+    const float *features_dc, const float *features_rest, const float *opacities,
+    const float *background, float **out_img);
+
+/* ---- introspection (tests and benchmarks) ------------------------------- */
+
+/* Loss of the last step; waits for it when `sync` != 0, else returns the
+ * latest value already on the host. */
+float msplat_last_loss(int sync);
+/* Intersections of the last step (waits for the step). */
+long long msplat_num_intersections(void);
+/* Device error word of the last step (waits); bit 1 = intersection overflow. */
+int msplat_device_errors(void);
+/* Device pointer and element count of a named engine buffer: "xy", "depth",
+ * "radii", "conic_op", "rgb", "tile_offset", "sorted_ids", "out_img",
+ * "final_T", "final_idx", "v_rendered", "grad_acc", "chunk_idx".  Returns 0
+ * or MSPLAT_ERR_ARG for an unknown name. */
+int msplat_debug_buffer(const char *name, void **dev_ptr, long long *count);
+/* Number of kernel launches the engine issued since the last reset. */
+long long msplat_kernel_launches(int reset);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,99 @@
+"""ctypes binding of libmsplat_b200.so (C-ABI in include/msplat_engine.h).
+
+The library is built in-tree by msplat_b200/build.py.  Loading fails loudly
+when it is missing: the engine has no CPU path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libmsplat_b200.so")
+
+_f = C.c_float
+_i = C.c_int
+_u = C.c_uint
+_p = C.c_void_p
+_fp = C.POINTER(C.c_float)
+_ip = C.POINTER(C.c_int)
+
+# name -> (restype, argtypes); mirrors include/msplat_engine.h
+SIGNATURES = {
+    "msplat_last_error": (C.c_char_p, []),
+    "msplat_set_stream": (_i, [_p]),
+    "msplat_get_stream": (_p, []),
+    "msplat_device": (_p, []),
+    "msplat_gpu_alloc": (_p, [C.c_size_t, _i]),
+    "msplat_gpu_free": (None, [_p]),
+    "msplat_copy": (_i, [_p, _p, C.c_size_t, _i, _i]),
+    "msplat_commit": (None, []),
+    "msplat_gpu_sync": (None, []),
+    "cleanup_msplat_metal": (None, []),
+    "cleanup_msplat_cuda": (None, []),
+    "msplat_set_metallib_path": (None, [C.c_char_p]),
+    "msplat_enable_gpu_timing": (None, [_i]),
+    "msplat_drain_gpu_times": (_i, [C.POINTER(C.c_double), _i]),
+    "msplat_drain_stage_times": (_i, [C.POINTER(C.c_double), _i, _i, _ip, C.POINTER(C.c_char_p)]),
+    "msplat_train_step": (_i, [
+        _i, _p, _p, _f, _p,            # num_points, means3d, scales, glob_scale, quats
+        _fp, _fp, _f, _f, _f, _f,      # viewmat, projmat, fx, fy, cx, cy
+        _u, _u, _ip, _f,               # img_height, img_width, tile_bounds, clip_thresh
+        _u, _u, _fp,                   # degree, degrees_to_use, cam_pos
+        _p, _p, _p, _fp,               # features_dc, features_rest, opacities, background
+        _p, _p, _f, _f,                # gt, window2d, ssim_weight, loss_inv_n
+        _i, _i, C.POINTER(_p), C.POINTER(_p), C.POINTER(_p),  # rest bases, groups, params, m, v
+        _fp, _fp, _f, _f, _f,          # step sizes, bc2 sqrts, beta1, beta2, eps
+        _p, _p, _p, _f,                # vis_counts, xys_grad_norm, max_2d_size, inv_max_dim
+        C.POINTER(_p), _fp,            # radii_out, loss_out
+    ]),
+    "msplat_render": (_i, [
+        _i, _p, _p, _f, _p, _fp, _fp, _f, _f, _f, _f, _u, _u, _ip, _f, _u, _u, _fp,
+        _p, _p, _p, _fp, C.POINTER(_p),
+    ]),
+    "msplat_last_loss": (_f, [_i]),
+    "msplat_num_intersections": (C.c_longlong, []),
+    "msplat_device_errors": (_i, []),
+    "msplat_debug_buffer": (_i, [C.c_char_p, C.POINTER(_p), C.POINTER(C.c_longlong)]),
+    "msplat_kernel_launches": (C.c_longlong, [_i]),
+}
+
+_lib = None
+
+
+def load() -> C.CDLL:
+    """Load the engine library (once) and attach argument types."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `python msplat_b200/build.py` "
+            "(the engine is CUDA-only and has no CPU fallback)")
+    lib = C.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+class EngineError(RuntimeError):
+    pass
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc != 0:
+        msg = load().msplat_last_error().decode(errors="replace")
+        raise EngineError(f"{what} failed ({rc}): {msg}")
+
+
+def farr(values) -> C.Array:
+    vals = [float(v) for v in values]
+    return (C.c_float * len(vals))(*vals)
+
+
+def iarr(values) -> C.Array:
+    vals = [int(v) for v in values]
+    return (C.c_int * len(vals))(*vals)

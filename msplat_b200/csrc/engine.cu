@@ -1,0 +1,675 @@
+// engine.cu -- host driver of the CUDA engine and the C-ABI seam
+// (include/msplat_engine.h).  Plays the role of msplat's Metal host driver
+// (core/metal/msplat_metal.mm): a process-wide buffer cache reused across
+// steps (FusedTensorCache, msplat_metal.mm:348-454), the dispatch order of
+// msplat_train_step (:771-1330) and forward_pipeline (:462-750), and the
+// depth-chunk rule (:873-889).  All work goes to one CUDA stream; per-step
+// scalars travel in a parameter block copied from a pinned ring.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/msplat_engine.h"
+#include "engine.h"
+
+namespace msp {
+
+static thread_local std::string t_last_error;
+
+static void set_error(const char* fmt, ...)
+{
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+}
+
+#define MSP_CUDA(expr)                                                                    \
+    do {                                                                                  \
+        cudaError_t e_ = (expr);                                                          \
+        if (e_ != cudaSuccess) {                                                          \
+            set_error("%s failed: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__,   \
+                      __LINE__);                                                          \
+            return MSPLAT_ERR_CUDA;                                                       \
+        }                                                                                 \
+    } while (0)
+
+constexpr int kRing = 8;
+constexpr unsigned kChunkHost = 512;  // depth chunk, as kChunk in msp_math.cuh
+constexpr int kStages = 6;
+static const char* kStageNames[kStages] = {"proj_sh_fwd", "bin_sort", "rast_fwd",
+                                           "loss_fwd_bwd", "rast_bwd", "proj_bwd_adam"};
+
+struct Engine {
+    bool ready = false;
+    int device = -1;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t user_stream = nullptr;
+    bool user_stream_set = false;
+    // allocated sizes
+    long long cap_N = 0, cap_grad_N = 0, cap_pix = 0, cap_T = 0, cap_isect = 0, cap_chunk = 0;
+    Buffers B{};
+    StepParams* d_params = nullptr;
+    StepParams* h_ring = nullptr;
+    cudaEvent_t ring_ev[kRing] = {};
+    int ring_pos = 0;
+    // readback
+    float* h_loss = nullptr;    // pinned [2]: loss_sum, isect total (as float bits unused)
+    int* h_misc = nullptr;      // pinned [2]: err, isect total
+    cudaEvent_t readback_ev = nullptr;
+    bool readback_pending = false;
+    float last_loss = 0.f;
+    double last_loss_scale = 1.0;
+    long long growth_isect = 0;  // requested capacity after an overflow
+    // timing
+    bool timing = false;
+    cudaEvent_t st_ev[kStages + 1][kRing] = {};
+    int st_pos = 0;
+    std::vector<double> step_times;
+    std::vector<double> stage_times[kStages];
+    std::vector<int> pending_timing;  // ring slots with recorded events
+    long long launches = 0;
+
+    cudaStream_t stream() const { return user_stream_set ? user_stream : own_stream; }
+};
+
+static Engine g;
+static std::mutex g_mu;
+
+static int init_engine()
+{
+    if (g.ready) return MSPLAT_OK;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n <= 0) {
+        set_error("no CUDA device available (%s); the engine has no CPU path",
+                  e == cudaSuccess ? "0 devices" : cudaGetErrorString(e));
+        return MSPLAT_ERR_CUDA;
+    }
+    MSP_CUDA(cudaGetDevice(&g.device));
+    MSP_CUDA(cudaStreamCreateWithFlags(&g.own_stream, cudaStreamNonBlocking));
+    MSP_CUDA(cudaMalloc(&g.d_params, sizeof(StepParams)));
+    MSP_CUDA(cudaMallocHost(&g.h_ring, sizeof(StepParams) * kRing));
+    for (int i = 0; i < kRing; i++) MSP_CUDA(cudaEventCreateWithFlags(&g.ring_ev[i], cudaEventDisableTiming));
+    MSP_CUDA(cudaMallocHost(&g.h_loss, sizeof(float) * 4));
+    MSP_CUDA(cudaMallocHost(&g.h_misc, sizeof(int) * 4));
+    memset(g.h_loss, 0, sizeof(float) * 4);
+    memset(g.h_misc, 0, sizeof(int) * 4);
+    MSP_CUDA(cudaEventCreateWithFlags(&g.readback_ev, cudaEventDisableTiming));
+    for (int s = 0; s <= kStages; s++)
+        for (int r = 0; r < kRing; r++) MSP_CUDA(cudaEventCreate(&g.st_ev[s][r]));
+    MSP_CUDA(cudaMalloc(&g.B.loss_sum, sizeof(float) * 4));
+    MSP_CUDA(cudaMalloc(&g.B.err, sizeof(int) * 4));
+    MSP_CUDA(cudaMemset(g.B.err, 0, sizeof(int) * 4));
+    MSP_CUDA(cudaDeviceSynchronize());
+    g.ready = true;
+    return MSPLAT_OK;
+}
+
+template <typename T>
+static int realloc_dev(T*& p, size_t count)
+{
+    if (p) cudaFree(p);
+    p = nullptr;
+    if (count == 0) count = 1;
+    MSP_CUDA(cudaMalloc(&p, count * sizeof(T)));
+    return MSPLAT_OK;
+}
+
+static void free_buffers()
+{
+    Buffers& B = g.B;
+    void* ptrs[] = {B.proj.xy, B.proj.depth, B.proj.radii, B.proj.conic_op, B.proj.rgb, B.proj.rect,
+                    B.tile_count, B.tile_offset, B.keys, B.keys_alt, B.sorted_ids, B.out_img,
+                    B.final_T, B.final_idx, B.v_rendered, B.ssim_h, B.ssim_d, B.grad_acc,
+                    B.chunk_T, B.chunk_C, B.chunk_idx, B.prefix_T, B.after_C};
+    for (void* p : ptrs)
+        if (p) cudaFree(p);
+    float* ls = B.loss_sum;
+    int* er = B.err;
+    B = Buffers{};
+    B.loss_sum = ls;
+    B.err = er;
+    g.cap_N = g.cap_grad_N = g.cap_pix = g.cap_T = g.cap_isect = g.cap_chunk = 0;
+}
+
+// Buffer cache: grow-only, like FusedTensorCache::ensure_* (msplat_metal.mm:383-452).
+static int ensure(long long N, long long W, long long H, long long T, int K, bool train)
+{
+    Buffers& B = g.B;
+    int rc;
+    if (N > g.cap_N) {
+        long long n = std::max(N, g.cap_N + g.cap_N / 4);
+        if ((rc = realloc_dev(B.proj.xy, n))) return rc;
+        if ((rc = realloc_dev(B.proj.depth, n))) return rc;
+        if ((rc = realloc_dev(B.proj.radii, n))) return rc;
+        if ((rc = realloc_dev(B.proj.conic_op, n))) return rc;
+        if ((rc = realloc_dev(B.proj.rgb, n))) return rc;
+        if ((rc = realloc_dev(B.proj.rect, n))) return rc;
+        g.cap_N = n;
+    }
+    if (train && N > g.cap_grad_N) {
+        long long n = std::max(N, g.cap_N);
+        if ((rc = realloc_dev(B.grad_acc, (size_t)n * kGradStride))) return rc;
+        g.cap_grad_N = n;
+    }
+    long long want_isect = std::max(16 * N, g.growth_isect);
+    if (want_isect > g.cap_isect) {
+        if ((rc = realloc_dev(B.keys, want_isect))) return rc;
+        if ((rc = realloc_dev(B.keys_alt, want_isect))) return rc;
+        if ((rc = realloc_dev(B.sorted_ids, want_isect))) return rc;
+        g.cap_isect = want_isect;
+    }
+    const long long P = W * H;
+    if (P > g.cap_pix) {
+        if ((rc = realloc_dev(B.out_img, P * 3))) return rc;
+        if ((rc = realloc_dev(B.final_T, P))) return rc;
+        if ((rc = realloc_dev(B.final_idx, P))) return rc;
+        if ((rc = realloc_dev(B.v_rendered, P * 3))) return rc;
+        if ((rc = realloc_dev(B.ssim_h, P * 15))) return rc;
+        if ((rc = realloc_dev(B.ssim_d, P * 9))) return rc;
+        g.cap_pix = P;
+    }
+    if (T > g.cap_T) {
+        if ((rc = realloc_dev(B.tile_count, T))) return rc;
+        if ((rc = realloc_dev(B.tile_offset, T + 1))) return rc;
+        MSP_CUDA(cudaMemsetAsync(B.tile_count, 0, sizeof(int) * T, g.stream()));
+        g.cap_T = T;
+    }
+    if (K > 1 && (long long)K * P > g.cap_chunk) {
+        const long long n = (long long)K * P;
+        if ((rc = realloc_dev(B.chunk_T, n))) return rc;
+        if ((rc = realloc_dev(B.chunk_C, n * 3))) return rc;
+        if ((rc = realloc_dev(B.chunk_idx, n))) return rc;
+        if ((rc = realloc_dev(B.prefix_T, n))) return rc;
+        if ((rc = realloc_dev(B.after_C, n * 3))) return rc;
+        g.cap_chunk = n;
+    }
+    return MSPLAT_OK;
+}
+
+// Depth-chunk rule of msplat_metal.mm:873-889 (capacity = 16 * N, :809).
+static int chunk_k_max(long long N, int num_tiles)
+{
+    if (num_tiles >= 400) return 1;
+    const long long capacity = N * 16;
+    const unsigned avg = (unsigned)(capacity / std::max(1, num_tiles));
+    const unsigned cons = avg * 6;
+    unsigned k = (cons + kChunkHost - 1) / kChunkHost;
+    if (k < 2) k = 2;
+    const unsigned abs_max = (unsigned)((capacity + kChunkHost - 1) / kChunkHost);
+    if (k > abs_max) k = abs_max;
+    return (int)k;
+}
+
+// Consume the previous step's readback if it is already complete.
+static void poll_readback(bool wait)
+{
+    if (!g.readback_pending) return;
+    if (wait) {
+        cudaEventSynchronize(g.readback_ev);
+    } else if (cudaEventQuery(g.readback_ev) != cudaSuccess) {
+        return;
+    }
+    g.readback_pending = false;
+    g.last_loss = (float)((double)g.h_loss[0] * g.last_loss_scale);
+    if (g.h_misc[0] & kErrIsectOverflow) {
+        const long long need = (long long)g.h_misc[1];
+        if (need > g.growth_isect) {
+            g.growth_isect = need + need / 4;
+            fprintf(stderr, "msplat: intersection buffer overflow (%lld > %lld); growing\n", need,
+                    g.cap_isect);
+        }
+    }
+}
+
+static void drain_timing_slot(int slot)
+{
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, g.st_ev[0][slot], g.st_ev[kStages][slot]) == cudaSuccess)
+        g.step_times.push_back(ms);
+    for (int s = 0; s < kStages; s++) {
+        if (cudaEventElapsedTime(&ms, g.st_ev[s][slot], g.st_ev[s + 1][slot]) == cudaSuccess)
+            g.stage_times[s].push_back(ms);
+    }
+}
+
+struct StageMarks {
+    bool on;
+    int slot;
+    void mark(int s, cudaStream_t st)
+    {
+        if (on) cudaEventRecord(g.st_ev[s][slot], st);
+    }
+};
+
+static StageMarks begin_timing()
+{
+    StageMarks m{g.timing, 0};
+    if (!m.on) return m;
+    m.slot = g.st_pos;
+    g.st_pos = (g.st_pos + 1) % kRing;
+    // the slot's previous events must be complete before reuse
+    for (size_t i = 0; i < g.pending_timing.size(); i++) {
+        if (g.pending_timing[i] == m.slot) {
+            cudaEventSynchronize(g.st_ev[kStages][m.slot]);
+            drain_timing_slot(m.slot);
+            g.pending_timing.erase(g.pending_timing.begin() + i);
+            break;
+        }
+    }
+    g.pending_timing.push_back(m.slot);
+    return m;
+}
+
+// Fill the next pinned ring slot and queue its copy into the device block.
+static int upload_params(const StepParams& p, cudaStream_t st)
+{
+    const int slot = g.ring_pos;
+    g.ring_pos = (g.ring_pos + 1) % kRing;
+    MSP_CUDA(cudaEventSynchronize(g.ring_ev[slot]));
+    g.h_ring[slot] = p;
+    MSP_CUDA(cudaMemcpyAsync(g.d_params, &g.h_ring[slot], sizeof(StepParams), cudaMemcpyHostToDevice, st));
+    MSP_CUDA(cudaEventRecord(g.ring_ev[slot], st));
+    return MSPLAT_OK;
+}
+
+struct CamArgs {
+    int N;
+    const float* viewmat;
+    const float* projmat;
+    float fx, fy, cx, cy, glob_scale, clip_thresh;
+    unsigned H, W;
+    const int* tile_bounds;
+    unsigned degree, degrees_to_use;
+    const float* cam_pos;
+    const float* background;
+    int rest_stride;
+};
+
+static int fill_params(StepParams& p, const CamArgs& a)
+{
+    if (a.N < 0 || a.W == 0 || a.H == 0 || !a.viewmat || !a.projmat || !a.cam_pos || !a.background) {
+        set_error("invalid arguments (num_points=%d, %ux%u)", a.N, a.W, a.H);
+        return MSPLAT_ERR_ARG;
+    }
+    memset(&p, 0, sizeof(p));
+    memcpy(p.viewmat, a.viewmat, sizeof(p.viewmat));
+    memcpy(p.projmat, a.projmat, sizeof(p.projmat));
+    p.fx = a.fx; p.fy = a.fy; p.cx = a.cx; p.cy = a.cy;
+    // msplat_metal.metal:1746-1747 (same float operations on the host)
+    p.tan_fovx = 0.5f * (float)a.W / a.fx;
+    p.tan_fovy = 0.5f * (float)a.H / a.fy;
+    p.glob_scale = a.glob_scale;
+    p.clip_thresh = a.clip_thresh;
+    memcpy(p.cam_pos, a.cam_pos, sizeof(p.cam_pos));
+    memcpy(p.bg, a.background, sizeof(p.bg));
+    p.num_points = a.N;
+    p.img_w = (int)a.W;
+    p.img_h = (int)a.H;
+    p.tiles_x = a.tile_bounds ? a.tile_bounds[0] : (int)((a.W + 15) / 16);
+    p.tiles_y = a.tile_bounds ? a.tile_bounds[1] : (int)((a.H + 15) / 16);
+    if (p.tiles_x != (int)((a.W + 15) / 16) || p.tiles_y != (int)((a.H + 15) / 16)) {
+        set_error("tile_bounds (%d,%d) do not cover %ux%u with 16x16 tiles", p.tiles_x, p.tiles_y,
+                  a.W, a.H);
+        return MSPLAT_ERR_ARG;
+    }
+    if (p.tiles_x > 65535 || p.tiles_y > 65535) {
+        set_error("image too large");
+        return MSPLAT_ERR_ARG;
+    }
+    p.num_tiles = p.tiles_x * p.tiles_y;
+    p.degree = (int)a.degree;
+    p.degrees_to_use = (int)std::min(a.degrees_to_use, a.degree);
+    p.rest_stride = a.rest_stride;
+    p.k_max = chunk_k_max(a.N, p.num_tiles);
+    return MSPLAT_OK;
+}
+
+// Forward half shared by render and train (forward_pipeline, msplat_metal.mm:462-750).
+static int run_forward(const StepParams& p, const float* means, const float* scales,
+                       const float* quats, const float* dc, const float* rest, const float* opac,
+                       bool train, StageMarks& tm, cudaStream_t st)
+{
+    const Buffers& B = g.B;
+    tm.mark(0, st);
+    launch_project_forward(g.d_params, p.num_points, means, scales, quats, dc, rest, opac, B, train,
+                           p.degrees_to_use, p.rest_stride, st);
+    tm.mark(1, st);
+    launch_scan_tiles(g.d_params, p.num_tiles, B, st);
+    launch_scatter(g.d_params, p.num_points, B, st);
+    launch_sort_tiles(g.d_params, p.num_tiles, B, st);
+    tm.mark(2, st);
+    launch_raster_forward(g.d_params, p.num_tiles, p.k_max, p.img_w, p.img_h, B, st);
+    g.launches += 4 + (p.k_max > 1 ? 2 : 1);
+    MSP_CUDA(cudaGetLastError());
+    return MSPLAT_OK;
+}
+
+static int queue_readback(cudaStream_t st, const StepParams& p)
+{
+    MSP_CUDA(cudaMemcpyAsync(g.h_loss, g.B.loss_sum, sizeof(float), cudaMemcpyDeviceToHost, st));
+    MSP_CUDA(cudaMemcpyAsync(g.h_misc, g.B.err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    MSP_CUDA(cudaMemcpyAsync(g.h_misc + 1, g.B.tile_offset + p.num_tiles, sizeof(int),
+                             cudaMemcpyDeviceToHost, st));
+    MSP_CUDA(cudaEventRecord(g.readback_ev, st));
+    g.readback_pending = true;
+    g.last_loss_scale = 1.0 / (3.0 * (double)p.img_w * (double)p.img_h);
+    return MSPLAT_OK;
+}
+
+}  // namespace msp
+
+using namespace msp;
+
+extern "C" {
+
+const char* msplat_last_error(void) { return t_last_error.c_str(); }
+
+int msplat_set_stream(void* cuda_stream)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = init_engine();
+    if (rc) return rc;
+    g.user_stream = (cudaStream_t)cuda_stream;
+    g.user_stream_set = cuda_stream != nullptr;
+    return MSPLAT_OK;
+}
+
+void* msplat_get_stream(void)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (init_engine()) return nullptr;
+    return (void*)g.stream();
+}
+
+void* msplat_device(void)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (init_engine()) return nullptr;
+    return (void*)&g.device;
+}
+
+void* msplat_gpu_alloc(size_t bytes, int zero)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (init_engine()) return nullptr;
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes ? bytes : 4) != cudaSuccess) {
+        set_error("cudaMalloc(%zu) failed", bytes);
+        return nullptr;
+    }
+    if (zero) cudaMemsetAsync(p, 0, bytes ? bytes : 4, g.stream());
+    return p;
+}
+
+void msplat_gpu_free(void* ptr)
+{
+    if (!ptr) return;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g.ready) cudaStreamSynchronize(g.stream());
+    cudaFree(ptr);
+}
+
+int msplat_copy(void* dst, const void* src, size_t bytes, int kind, int sync)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = init_engine();
+    if (rc) return rc;
+    cudaMemcpyKind k = kind == 0 ? cudaMemcpyHostToDevice
+                     : kind == 1 ? cudaMemcpyDeviceToHost : cudaMemcpyDeviceToDevice;
+    MSP_CUDA(cudaMemcpyAsync(dst, src, bytes, k, g.stream()));
+    if (sync) MSP_CUDA(cudaStreamSynchronize(g.stream()));
+    return MSPLAT_OK;
+}
+
+void msplat_commit(void) {}
+
+void msplat_gpu_sync(void)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.ready) return;
+    cudaStreamSynchronize(g.stream());
+    poll_readback(true);
+}
+
+void cleanup_msplat_cuda(void)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.ready) return;
+    cudaStreamSynchronize(g.stream());
+    free_buffers();
+    g.growth_isect = 0;
+}
+
+void cleanup_msplat_metal(void) { cleanup_msplat_cuda(); }
+
+void msplat_set_metallib_path(const char* path) { (void)path; }
+
+void msplat_enable_gpu_timing(int enable)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    g.timing = enable != 0;
+}
+
+static void drain_all_timing()
+{
+    for (int slot : g.pending_timing) {
+        cudaEventSynchronize(g.st_ev[kStages][slot]);
+        drain_timing_slot(slot);
+    }
+    g.pending_timing.clear();
+}
+
+int msplat_drain_gpu_times(double* out, int max_out)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    drain_all_timing();
+    int n = (int)std::min<size_t>(g.step_times.size(), (size_t)std::max(0, max_out));
+    for (int i = 0; i < n; i++) out[i] = g.step_times[i];
+    g.step_times.clear();
+    return n;
+}
+
+int msplat_drain_stage_times(double* stage_times, int max_stages, int max_samples, int* n_samples,
+                             const char** stage_names)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    drain_all_timing();
+    const int ns = std::min(max_stages, kStages);
+    int m = 0;
+    for (int s = 0; s < ns; s++) {
+        const int cnt = (int)std::min<size_t>(g.stage_times[s].size(), (size_t)max_samples);
+        for (int i = 0; i < cnt; i++) stage_times[s * max_samples + i] = g.stage_times[s][i];
+        m = std::max(m, cnt);
+        if (stage_names) stage_names[s] = kStageNames[s];
+        g.stage_times[s].clear();
+    }
+    if (n_samples) *n_samples = m;
+    return ns;
+}
+
+int msplat_train_step(
+    int num_points, float* means3d, float* scales, float glob_scale, float* quats,
+    const float* viewmat, const float* projmat, float fx, float fy, float cx, float cy,
+    unsigned img_height, unsigned img_width, const int* tile_bounds, float clip_thresh,
+    unsigned degree, unsigned degrees_to_use, const float* cam_pos, float* features_dc,
+    float* features_rest, float* opacities, const float* background, const float* gt,
+    const float* window2d, float ssim_weight, float loss_inv_n, int features_rest_bases,
+    int num_adam_groups, float* const* adam_params, float* const* adam_exp_avg,
+    float* const* adam_exp_avg_sq, const float* adam_step_sizes, const float* adam_bc2_sqrts,
+    float adam_beta1, float adam_beta2, float adam_eps, float* vis_counts, float* xys_grad_norm,
+    float* max_2d_size, float inv_max_dim, const int32_t** radii_out, float* loss_out)
+{
+    (void)window2d;
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = init_engine();
+    if (rc) return rc;
+    if (!gt || !vis_counts || !xys_grad_norm || !max_2d_size || num_adam_groups < 0 ||
+        num_adam_groups > kGroups || (num_adam_groups > 0 && (!adam_params || !adam_exp_avg ||
+                                                              !adam_exp_avg_sq || !adam_step_sizes ||
+                                                              !adam_bc2_sqrts))) {
+        set_error("msplat_train_step: missing gt, statistics or optimiser arguments");
+        return MSPLAT_ERR_ARG;
+    }
+    poll_readback(false);
+    CamArgs a{num_points, viewmat, projmat, fx, fy, cx, cy, glob_scale, clip_thresh, img_height,
+              img_width, tile_bounds, degree, degrees_to_use, cam_pos, background,
+              features_rest_bases * 3};
+    StepParams p;
+    if ((rc = fill_params(p, a))) return rc;
+    p.ssim_weight = ssim_weight;
+    p.loss_inv_n = loss_inv_n;
+    p.inv_max_dim = inv_max_dim;
+    p.beta1 = adam_beta1;
+    p.beta2 = adam_beta2;
+    p.eps = adam_eps;
+    p.num_adam_groups = num_adam_groups;
+    AdamPtrs A{};
+    for (int gi = 0; gi < num_adam_groups; gi++) {
+        p.adam_step[gi] = adam_step_sizes[gi];
+        p.adam_bc2[gi] = adam_bc2_sqrts[gi];
+        A.param[gi] = adam_params[gi];
+        A.exp_avg[gi] = adam_exp_avg[gi];
+        A.exp_avg_sq[gi] = adam_exp_avg_sq[gi];
+        A.numel[gi] = (A.param[gi] && A.exp_avg[gi] && A.exp_avg_sq[gi]) ? 1 : 0;
+    }
+    // The SH groups are only updated through the fused path when all of
+    // them are present (msplat_metal.mm:1079-1087).
+    if (num_adam_groups < 5) A.numel[3] = A.numel[4] = 0;
+    p.capacity = 0;
+    const cudaStream_t st = g.stream();
+    if ((rc = ensure(num_points, img_width, img_height, p.num_tiles, p.k_max, true))) return rc;
+    p.capacity = g.cap_isect;
+    StageMarks tm = begin_timing();
+    if ((rc = upload_params(p, st))) return rc;
+    MSP_CUDA(cudaMemsetAsync(g.B.err, 0, sizeof(int), st));
+    MSP_CUDA(cudaMemsetAsync(g.B.loss_sum, 0, sizeof(float), st));
+    if ((rc = run_forward(p, means3d, scales, quats, features_dc, features_rest, opacities, true,
+                          tm, st)))
+        return rc;
+    tm.mark(3, st);
+    launch_ssim(g.d_params, p.img_w, p.img_h, gt, g.B, st);
+    tm.mark(4, st);
+    launch_raster_backward(g.d_params, p.num_tiles, p.k_max, p.img_w, p.img_h, g.B, st);
+    tm.mark(5, st);
+    StatPtrs S{vis_counts, xys_grad_norm, max_2d_size};
+    launch_project_backward_adam(g.d_params, num_points, p.degrees_to_use, p.rest_stride, g.B, A, S,
+                                 st);
+    tm.mark(6, st);
+    g.launches += 3 + (p.k_max > 1 ? 2 : 1) + 1;
+    MSP_CUDA(cudaGetLastError());
+    if ((rc = queue_readback(st, p))) return rc;
+    if (radii_out) *radii_out = g.B.proj.radii;
+    if (loss_out) *loss_out = g.last_loss;
+    return MSPLAT_OK;
+}
+
+int msplat_render(int num_points, const float* means3d, const float* scales, float glob_scale,
+                  const float* quats, const float* viewmat, const float* projmat, float fx,
+                  float fy, float cx, float cy, unsigned img_height, unsigned img_width,
+                  const int* tile_bounds, float clip_thresh, unsigned degree,
+                  unsigned degrees_to_use, const float* cam_pos, const float* features_dc,
+                  const float* features_rest, const float* opacities, const float* background,
+                  float** out_img)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = init_engine();
+    if (rc) return rc;
+    poll_readback(false);
+    const int rest_stride = (num_sh_bases_host((int)degree) - 1) * 3;
+    CamArgs a{num_points, viewmat, projmat, fx, fy, cx, cy, glob_scale, clip_thresh, img_height,
+              img_width, tile_bounds, degree, degrees_to_use, cam_pos, background, rest_stride};
+    StepParams p;
+    if ((rc = fill_params(p, a))) return rc;
+    const cudaStream_t st = g.stream();
+    if ((rc = ensure(num_points, img_width, img_height, p.num_tiles, p.k_max, false))) return rc;
+    p.capacity = g.cap_isect;
+    StageMarks tm = begin_timing();
+    if ((rc = upload_params(p, st))) return rc;
+    MSP_CUDA(cudaMemsetAsync(g.B.err, 0, sizeof(int), st));
+    if ((rc = run_forward(p, means3d, scales, quats, features_dc, features_rest, opacities, false,
+                          tm, st)))
+        return rc;
+    for (int s = 3; s <= 6; s++) tm.mark(s, st);
+    MSP_CUDA(cudaMemcpyAsync(g.h_misc, g.B.err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    MSP_CUDA(cudaMemcpyAsync(g.h_misc + 1, g.B.tile_offset + p.num_tiles, sizeof(int),
+                             cudaMemcpyDeviceToHost, st));
+    MSP_CUDA(cudaEventRecord(g.readback_ev, st));
+    g.readback_pending = true;
+    if (out_img) *out_img = g.B.out_img;
+    return MSPLAT_OK;
+}
+
+float msplat_last_loss(int sync)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.ready) return 0.f;
+    poll_readback(sync != 0);
+    return g.last_loss;
+}
+
+long long msplat_num_intersections(void)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.ready) return 0;
+    cudaStreamSynchronize(g.stream());
+    poll_readback(true);
+    return (long long)g.h_misc[1];
+}
+
+int msplat_device_errors(void)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.ready) return 0;
+    cudaStreamSynchronize(g.stream());
+    poll_readback(true);
+    return g.h_misc[0];
+}
+
+int msplat_debug_buffer(const char* name, void** dev_ptr, long long* count)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.ready || !name || !dev_ptr) {
+        set_error("engine not initialised or bad arguments");
+        return MSPLAT_ERR_ARG;
+    }
+    const Buffers& B = g.B;
+    struct Ent { const char* n; void* p; long long c; };
+    const Ent ents[] = {
+        {"xy", B.proj.xy, g.cap_N}, {"depth", B.proj.depth, g.cap_N},
+        {"radii", B.proj.radii, g.cap_N}, {"conic_op", B.proj.conic_op, g.cap_N},
+        {"rgb", B.proj.rgb, g.cap_N}, {"tile_offset", B.tile_offset, g.cap_T + 1},
+        {"sorted_ids", B.sorted_ids, g.cap_isect}, {"out_img", B.out_img, g.cap_pix * 3},
+        {"final_T", B.final_T, g.cap_pix}, {"final_idx", B.final_idx, g.cap_pix},
+        {"v_rendered", B.v_rendered, g.cap_pix * 3},
+        {"grad_acc", B.grad_acc, g.cap_grad_N * kGradStride},
+        {"chunk_idx", B.chunk_idx, g.cap_chunk}};
+    for (const Ent& e : ents) {
+        if (strcmp(e.n, name) == 0) {
+            *dev_ptr = e.p;
+            if (count) *count = e.c;
+            return MSPLAT_OK;
+        }
+    }
+    set_error("unknown buffer '%s'", name);
+    return MSPLAT_ERR_ARG;
+}
+
+long long msplat_kernel_launches(int reset)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    long long n = g.launches;
+    if (reset) g.launches = 0;
+    return n;
+}
+
+}  // extern "C"

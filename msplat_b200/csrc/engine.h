@@ -1,0 +1,113 @@
+// engine.h -- internal types of the CUDA engine (not part of the C-ABI).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace msp {
+
+constexpr int kGroups = 6;        // means, scales, quats, features_dc, features_rest, opacities
+constexpr int kGradStride = 9;    // per-Gaussian raster gradient: v_rgb[3], v_conic[3], v_xy[2], v_opacity
+constexpr int kSortCap = 4096;    // keys sorted in shared memory in one pass
+
+// Per-step scalars.  Written by the host into a pinned ring slot and copied
+// into device memory on the step's stream, so every kernel reads the same
+// block and a captured graph can be replayed with new cameras.
+struct StepParams {
+    float viewmat[16];
+    float projmat[16];
+    float fx, fy, cx, cy;
+    float tan_fovx, tan_fovy;
+    float glob_scale, clip_thresh;
+    float cam_pos[3];
+    float bg[3];
+    float ssim_weight, loss_inv_n, inv_max_dim;
+    float adam_step[kGroups];
+    float adam_bc2[kGroups];
+    float beta1, beta2, eps;
+    int num_points;
+    int img_w, img_h;
+    int tiles_x, tiles_y, num_tiles;
+    int degree, degrees_to_use, rest_stride;
+    int k_max;
+    int num_adam_groups;
+    int pad0;
+    long long capacity;
+};
+
+// Device error word bits (read back by the host after a step).
+enum ErrorBits : int {
+    kErrIsectOverflow = 1,   // intersections exceeded the key buffer
+};
+
+// Per-Gaussian geometry written by the projection and read by binning and
+// both rasterizers.
+struct ProjOut {
+    float2* xy;          // pixel centre
+    float* depth;        // view-space z
+    int* radii;          // 3-sigma radius, 0 = culled
+    float4* conic_op;    // conic a, b, c and sigmoid(opacity)
+    float4* rgb;         // raw SH colour (w unused)
+    uint2* rect;         // tile rect: x0 | y0<<16, x1 | y1<<16 (exclusive max)
+};
+
+struct Buffers {
+    ProjOut proj;
+    int* tile_count;       // [T]   zero between steps
+    int* tile_offset;      // [T+1] exclusive scan
+    unsigned long long* keys;      // [capacity]
+    unsigned long long* keys_alt;  // [capacity] merge scratch for tiles > kSortCap
+    int* sorted_ids;       // [capacity]
+    float* out_img;        // [H*W*3]
+    float* final_T;        // [H*W]
+    int* final_idx;        // [H*W]
+    float* v_rendered;     // [H*W*3]
+    float* ssim_h;         // [H*W*15]
+    float* ssim_d;         // [H*W*9]
+    float* grad_acc;       // [N*9]
+    float* chunk_T;        // [K*H*W]
+    float* chunk_C;        // [K*H*W*3]
+    int* chunk_idx;        // [K*H*W]
+    float* prefix_T;       // [K*H*W]
+    float* after_C;        // [K*H*W*3]
+    float* loss_sum;       // [1]
+    int* err;              // [1]
+};
+
+// Device pointers of the optimiser, one entry per group.
+struct AdamPtrs {
+    float* param[kGroups];
+    float* exp_avg[kGroups];
+    float* exp_avg_sq[kGroups];
+    long long numel[kGroups];
+};
+
+struct StatPtrs {
+    float* vis_counts;
+    float* grad_norm;
+    float* max_2d;
+};
+
+inline int num_sh_bases_host(int degree)
+{
+    return degree <= 0 ? 1 : degree == 1 ? 4 : degree == 2 ? 9 : degree == 3 ? 16 : 25;
+}
+
+// Kernel launchers (kernels_*.cu).
+void launch_project_forward(const StepParams* P, int N, const float* means, const float* scales,
+                            const float* quats, const float* dc, const float* rest,
+                            const float* opac, const Buffers& B, bool zero_grads,
+                            int degrees_to_use_host, int rest_stride_host, cudaStream_t s);
+void launch_scan_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s);
+void launch_scatter(const StepParams* P, int N, const Buffers& B, cudaStream_t s);
+void launch_sort_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s);
+void launch_raster_forward(const StepParams* P, int num_tiles, int k_max, int W, int H,
+                           const Buffers& B, cudaStream_t s);
+void launch_ssim(const StepParams* P, int W, int H, const float* gt, const Buffers& B,
+                 cudaStream_t s);
+void launch_raster_backward(const StepParams* P, int num_tiles, int k_max, int W, int H,
+                            const Buffers& B, cudaStream_t s);
+void launch_project_backward_adam(const StepParams* P, int N, int degrees_to_use_host,
+                                  int rest_stride_host, const Buffers& B, const AdamPtrs& A,
+                                  const StatPtrs& St, cudaStream_t s);
+
+}  // namespace msp

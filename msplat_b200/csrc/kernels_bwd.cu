@@ -1,0 +1,536 @@
+// kernels_bwd.cu -- backward half of the step: rasterizer VJP, projection
+// VJP, and every Adam update, in two kernels.  Compiled with --fmad=false so
+// the alpha/T decisions replayed here are exactly the forward's.
+#include "engine.h"
+#include "msp_math.cuh"
+
+namespace msp {
+
+// ---------------------------------------------------------------------------
+// Rasterizer backward.  Reference: rasterize_backward_kernel
+// (msplat_metal.metal:898-1099) and, for depth chunks,
+// compute_chunk_prefix_suffix_kernel (:2804-2840) plus
+// rasterize_backward_chunked_kernel (:2844-3031).
+// One CTA per 16x16 tile (per (tile, chunk)), one thread per pixel, replay
+// back to front.  Each warp sums its 32 pixels' contributions to a Gaussian
+// with a transposed butterfly (8 values in 9 shuffles, the opacity term in
+// 5), then 9 lanes issue one RED each into the Gaussian's 9 contiguous
+// accumulators: v_rgb[3] (gated by the clamp mask), v_conic[3], v_xy[2],
+// v_opacity (w.r.t. the logit).
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ float sel(bool c, float a, float b) { return c ? a : b; }
+
+template <bool CHUNKED>
+__global__ void __launch_bounds__(kTileThreads)
+raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
+                       const int* __restrict__ ids, const float2* __restrict__ g_xy,
+                       const float4* __restrict__ g_co, const float4* __restrict__ g_rgb,
+                       const float* __restrict__ final_T, const int* __restrict__ final_idx,
+                       const float* __restrict__ v_rendered, const int* __restrict__ chunk_idx,
+                       const float* __restrict__ prefix_T, const float* __restrict__ chunk_T,
+                       const float* __restrict__ after_C, float* __restrict__ grad_acc)
+{
+    __shared__ int s_id[kTileThreads];
+    __shared__ float2 s_xy[kTileThreads];
+    __shared__ float4 s_co[kTileThreads];
+    __shared__ float4 s_rgb[kTileThreads];
+    __shared__ int s_wmax[kTileThreads / 32];
+    const int tile = blockIdx.x;
+    const int tx_n = P->tiles_x;
+    const int W = P->img_w, H = P->img_h;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int px = (tile % tx_n) * kBlockX + (tid & 15);
+    const int py = (tile / tx_n) * kBlockY + (tid >> 4);
+    const bool inside = px < W && py < H;
+    const long long cap = P->capacity;
+    const int fbeg = (int)min((long long)offset[tile], cap);
+    const int fend = (int)min((long long)offset[tile + 1], cap);
+    int beg = fbeg, end = fend;
+    int k = 0;
+    if (CHUNKED) {
+        k = blockIdx.y;
+        beg = fbeg + k * kChunk;
+        end = min(fbeg + (k + 1) * kChunk, fend);
+        if (beg >= end) return;
+    }
+    const size_t NP = (size_t)W * H;
+    const size_t pix = inside ? (size_t)py * W + px : 0;
+    float Tf = 0.f, T = 0.f, b0 = 0.f, b1 = 0.f, b2 = 0.f;
+    float vo0 = 0.f, vo1 = 0.f, vo2 = 0.f;
+    int bin_final = beg - 1;
+    if (inside) {
+        Tf = final_T[pix];
+        vo0 = v_rendered[3 * pix];
+        vo1 = v_rendered[3 * pix + 1];
+        vo2 = v_rendered[3 * pix + 2];
+        if (CHUNKED) {
+            const size_t o = (size_t)k * NP + pix;
+            const int bf = chunk_idx[o];
+            if (bf >= beg) {
+                bin_final = bf;
+                T = prefix_T[o] * chunk_T[o];
+                b0 = after_C[3 * o];
+                b1 = after_C[3 * o + 1];
+                b2 = after_C[3 * o + 2];
+            }
+        } else {
+            bin_final = final_idx[pix];
+            T = Tf;
+        }
+    }
+    const float tfb0 = Tf * P->bg[0], tfb1 = Tf * P->bg[1], tfb2 = Tf * P->bg[2];
+    const float fpx = (float)px, fpy = (float)py;
+    const int warp_max = __reduce_max_sync(0xffffffffu, bin_final);
+    if (lane == 0) s_wmax[warp] = warp_max;
+    __syncthreads();
+    int tile_max = s_wmax[0];
+#pragma unroll
+    for (int w = 1; w < kTileThreads / 32; w++) tile_max = max(tile_max, s_wmax[w]);
+    const int last = min(end - 1, tile_max);
+    float* __restrict__ acc = grad_acc;
+
+    for (int bend = last; bend >= beg; bend -= kTileThreads) {
+        const int n = min(kTileThreads, bend - beg + 1);
+        __syncthreads();
+        if (tid < n) {
+            const int g = ids[bend - tid];
+            s_id[tid] = g;
+            s_xy[tid] = g_xy[g];
+            s_co[tid] = g_co[g];
+            s_rgb[tid] = g_rgb[g];
+        }
+        __syncthreads();
+        const int t0 = max(0, bend - warp_max);
+        for (int t = t0; t < n; t++) {
+            const int idx = bend - t;
+            const float4 co = s_co[t];
+            const float2 xy = s_xy[t];
+            const float dx = xy.x - fpx, dy = xy.y - fpy;
+            bool contrib = false;
+            float alpha = 0.f;
+            if (idx <= bin_final) {
+                const float sigma = fmaf(0.5f, fmaf(co.x, dx * dx, co.z * dy * dy), co.y * dx * dy);
+                if (!(sigma < 0.f || sigma >= 5.55f)) {
+                    alpha = fminf(0.999f, co.w * msp_expf_normal(-sigma));
+                    contrib = !(alpha < 1.f / 255.f) && alpha < 0.999f;
+                }
+            }
+            if (!__any_sync(0xffffffffu, contrib)) continue;
+            const float4 raw = s_rgb[t];
+            float v[8];
+            float vop = 0.f;
+#pragma unroll
+            for (int q = 0; q < 8; q++) v[q] = 0.f;
+            if (contrib) {
+                const float ra = 1.f / (1.f - alpha);
+                T *= ra;
+                const float fac = alpha * T;
+                const float r0 = fmaxf(raw.x + 0.5f, 0.f), r1 = fmaxf(raw.y + 0.5f, 0.f),
+                            r2 = fmaxf(raw.z + 0.5f, 0.f);
+                const float nra = -ra;
+                const float e0 = fmaf(r0, T, fmaf(-b0, ra, nra * tfb0));
+                const float e1 = fmaf(r1, T, fmaf(-b1, ra, nra * tfb1));
+                const float e2 = fmaf(r2, T, fmaf(-b2, ra, nra * tfb2));
+                const float v_alpha = (e0 * vo0 + e1 * vo1) + e2 * vo2;
+                b0 = fmaf(r0, fac, b0);
+                b1 = fmaf(r1, fac, b1);
+                b2 = fmaf(r2, fac, b2);
+                const float v_sigma = -alpha * v_alpha;
+                v[0] = fac * vo0;
+                v[1] = fac * vo1;
+                v[2] = fac * vo2;
+                const float hv = 0.5f * v_sigma;
+                v[3] = hv * (dx * dx);
+                v[4] = hv * (dx * dy);
+                v[5] = hv * (dy * dy);
+                v[6] = v_sigma * fmaf(co.x, dx, co.y * dy);
+                v[7] = v_sigma * fmaf(co.y, dx, co.z * dy);
+                vop = -v_sigma * (1.f - co.w);
+            }
+            // Transposed butterfly: after it, lane L holds the warp sum of
+            // value (L >> 2).
+            const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4;
+            float u[4];
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const float send = sel(h16, v[q], v[q + 4]);
+                const float keep = sel(h16, v[q + 4], v[q]);
+                u[q] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+            }
+            float w2[2];
+#pragma unroll
+            for (int q = 0; q < 2; q++) {
+                const float send = sel(h8, u[q], u[q + 2]);
+                const float keep = sel(h8, u[q + 2], u[q]);
+                w2[q] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+            }
+            float x;
+            {
+                const float send = sel(h4, w2[0], w2[1]);
+                const float keep = sel(h4, w2[1], w2[0]);
+                x = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+            }
+            x += __shfl_xor_sync(0xffffffffu, x, 2);
+            x += __shfl_xor_sync(0xffffffffu, x, 1);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) vop += __shfl_xor_sync(0xffffffffu, vop, o);
+            const int g = s_id[t];
+            const int j = lane >> 2;
+            if ((lane & 3) == 0) {
+                bool ok = x != 0.f;
+                if (j < 3) ok = ok && ((j == 0 ? raw.x : (j == 1 ? raw.y : raw.z)) + 0.5f >= 0.f);
+                if (ok) atomicAdd(acc + (size_t)g * kGradStride + j, x);
+            } else if (lane == 1) {
+                if (vop != 0.f) atomicAdd(acc + (size_t)g * kGradStride + 8, vop);
+            }
+        }
+    }
+}
+
+// compute_chunk_prefix_suffix_kernel (msplat_metal.metal:2804-2840), over
+// the chunks that hold Gaussians (empty chunks have T = 1, C = 0 and change
+// neither product nor sum).
+__global__ void __launch_bounds__(256)
+chunk_prefix_suffix_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
+                           const float* __restrict__ chunk_T, const float* __restrict__ chunk_C,
+                           float* __restrict__ prefix_T, float* __restrict__ after_C)
+{
+    const int W = P->img_w, H = P->img_h;
+    const int px = blockIdx.x * 16 + (threadIdx.x & 15);
+    const int py = blockIdx.y * 16 + (threadIdx.x >> 4);
+    if (px >= W || py >= H) return;
+    const size_t NP = (size_t)W * H;
+    const size_t pix = (size_t)py * W + px;
+    const int tile = (py / kBlockY) * P->tiles_x + (px / kBlockX);
+    const long long cap = P->capacity;
+    const int fbeg = (int)min((long long)offset[tile], cap);
+    const int fend = (int)min((long long)offset[tile + 1], cap);
+    const int kt = min(P->k_max, (fend - fbeg + kChunk - 1) / kChunk);
+    float pT = 1.f;
+    for (int k = 0; k < kt; k++) {
+        const size_t o = (size_t)k * NP + pix;
+        prefix_T[o] = pT;
+        pT *= chunk_T[o];
+    }
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+    for (int k = kt - 1; k >= 0; k--) {
+        const size_t o = (size_t)k * NP + pix;
+        after_C[3 * o] = a0;
+        after_C[3 * o + 1] = a1;
+        after_C[3 * o + 2] = a2;
+        const float pk = prefix_T[o];
+        a0 += pk * chunk_C[3 * o];
+        a1 += pk * chunk_C[3 * o + 1];
+        a2 += pk * chunk_C[3 * o + 2];
+    }
+}
+
+void launch_raster_backward(const StepParams* P, int num_tiles, int k_max, int W, int H,
+                            const Buffers& B, cudaStream_t s)
+{
+    if (num_tiles <= 0) return;
+    if (k_max <= 1) {
+        raster_backward_kernel<false><<<num_tiles, kTileThreads, 0, s>>>(
+            P, B.tile_offset, B.sorted_ids, B.proj.xy, B.proj.conic_op, B.proj.rgb, B.final_T,
+            B.final_idx, B.v_rendered, nullptr, nullptr, nullptr, nullptr, B.grad_acc);
+    } else {
+        dim3 pgrid((W + 15) / 16, (H + 15) / 16);
+        chunk_prefix_suffix_kernel<<<pgrid, 256, 0, s>>>(P, B.tile_offset, B.chunk_T, B.chunk_C,
+                                                         B.prefix_T, B.after_C);
+        dim3 grid(num_tiles, k_max);
+        raster_backward_kernel<true><<<grid, kTileThreads, 0, s>>>(
+            P, B.tile_offset, B.sorted_ids, B.proj.xy, B.proj.conic_op, B.proj.rgb, B.final_T,
+            nullptr, B.v_rendered, B.chunk_idx, B.prefix_T, B.chunk_T, B.after_C, B.grad_acc);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Projection backward + every Adam update + densification statistics.
+// Reference: project_and_sh_backward_kernel (msplat_metal.metal:1813-1986,
+// VJPs :1216-1531), fused_adam_kernel (:1666-1689) launched for groups
+// 0,1,2,5 over every element (msplat_metal.mm:1117-1139), and
+// accumulate_grad_stats_kernel (:1643-1664).  One thread per Gaussian does
+// the geometry VJP and the Adam steps of means/scales/quats/opacity/dc;
+// each warp then updates its 32 Gaussians' SH-rest coefficients with
+// coalesced loads (the element order of the update does not matter).
+// ---------------------------------------------------------------------------
+constexpr int kBwdThreads = 128;
+
+struct M3 { float m[3][3]; };  // column-major m[col][row], as Metal's float3x3
+
+__device__ __forceinline__ M3 mul3(const M3& A, const M3& B)
+{
+    M3 C;
+#pragma unroll
+    for (int c = 0; c < 3; c++)
+#pragma unroll
+        for (int r = 0; r < 3; r++)
+            C.m[c][r] = (A.m[0][r] * B.m[c][0] + A.m[1][r] * B.m[c][1]) + A.m[2][r] * B.m[c][2];
+    return C;
+}
+__device__ __forceinline__ M3 tr3(const M3& A)
+{
+    M3 T;
+#pragma unroll
+    for (int c = 0; c < 3; c++)
+#pragma unroll
+        for (int r = 0; r < 3; r++) T.m[c][r] = A.m[r][c];
+    return T;
+}
+__device__ __forceinline__ M3 cols3(float a0, float a1, float a2, float b0, float b1, float b2,
+                                   float c0, float c1, float c2)
+{
+    M3 M;
+    M.m[0][0] = a0; M.m[0][1] = a1; M.m[0][2] = a2;
+    M.m[1][0] = b0; M.m[1][1] = b1; M.m[1][2] = b2;
+    M.m[2][0] = c0; M.m[2][1] = c1; M.m[2][2] = c2;
+    return M;
+}
+
+__device__ __forceinline__ void adam_elem(float* __restrict__ p, float* __restrict__ ea,
+                                          float* __restrict__ eas, float g, float step, float b1,
+                                          float b2, float bc2, float eps)
+{
+    const float m = fmaf(b1, *ea, (1.0f - b1) * g);
+    const float v = fmaf(b2, *eas, (1.0f - b2) * g * g);
+    *p -= step * m / (sqrtf(v) / bc2 + eps);
+    *ea = m;
+    *eas = v;
+}
+
+__global__ void __launch_bounds__(kBwdThreads)
+project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
+                             const int* __restrict__ radii, const float4* __restrict__ g_co,
+                             const float* __restrict__ grad_acc, AdamPtrs A, StatPtrs St,
+                             int nb_rest)
+{
+    __shared__ float s_basis[kBwdThreads][16];
+    __shared__ float s_vrgb[kBwdThreads][4];
+    __shared__ int s_vis[kBwdThreads];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int base = blockIdx.x * kBwdThreads;
+    const int i = base + tid;
+    const float b1 = P->beta1, b2 = P->beta2, eps = P->eps;
+    bool vis = false;
+    if (i < N) {
+        const int rad = radii[i];
+        vis = rad > 0;
+        float* means = A.param[0];
+        float* scales = A.param[1];
+        float* quats = A.param[2];
+        float vmean[3] = {0.f, 0.f, 0.f}, vscale[3] = {0.f, 0.f, 0.f};
+        float vq[4] = {0.f, 0.f, 0.f, 0.f};
+        float vop = 0.f;
+        if (vis) {
+            const float* ga = grad_acc + (size_t)i * kGradStride;
+            const float vr0 = ga[0], vr1 = ga[1], vr2 = ga[2];
+            const float vc0 = ga[3], vc1 = ga[4], vc2 = ga[5];
+            const float vx = ga[6], vy = ga[7];
+            vop = ga[8];
+            const float p[3] = {means[3 * (size_t)i], means[3 * (size_t)i + 1], means[3 * (size_t)i + 2]};
+            const float fx = P->fx, fy = P->fy;
+            const float* vm = P->viewmat;
+            const float* pm = P->projmat;
+            // project_pix_vjp (:1216-1234); v_depth is always 0 (:1860-1864)
+            const float h3 = ((pm[12] * p[0] + pm[13] * p[1]) + pm[14] * p[2]) + pm[15];
+            const float rw = 1.f / (h3 + 1e-6f);
+            const float vnx = (0.5f * (float)P->img_w) * vx, vny = (0.5f * (float)P->img_h) * vy;
+            const float vp0 = vnx * rw, vp1 = vny * rw, vp2 = 0.f;
+            vmean[0] = ((pm[0] * vp0 + pm[4] * vp1) + pm[8] * vp2) + vm[8] * 0.f;
+            vmean[1] = ((pm[1] * vp0 + pm[5] * vp1) + pm[9] * vp2) + vm[9] * 0.f;
+            vmean[2] = ((pm[2] * vp0 + pm[6] * vp1) + pm[10] * vp2) + vm[10] * 0.f;
+            // cov2d_to_conic_vjp (:1253-1264): ((-X) G) X
+            const float4 co = g_co[i];
+            const float X00 = -co.x, X01 = -co.y, X10 = -co.y, X11 = -co.z;
+            const float XG00 = X00 * vc0 + X10 * vc1, XG01 = X01 * vc0 + X11 * vc1;
+            const float XG10 = X00 * vc1 + X10 * vc2, XG11 = X01 * vc1 + X11 * vc2;
+            const float VS00 = XG00 * co.x + XG10 * co.y, VS01 = XG01 * co.x + XG11 * co.y;
+            const float VS10 = XG00 * co.y + XG10 * co.z, VS11 = XG01 * co.y + XG11 * co.z;
+            const float vcv0 = VS00, vcv1 = VS10 + VS01, vcv2 = VS11;
+            // recompute cov3d (:1875-1878)
+            const float es[3] = {msp_expf(scales[3 * (size_t)i]), msp_expf(scales[3 * (size_t)i + 1]),
+                                 msp_expf(scales[3 * (size_t)i + 2])};
+            const float q0 = quats[4 * (size_t)i], q1 = quats[4 * (size_t)i + 1],
+                        q2 = quats[4 * (size_t)i + 2], q3 = quats[4 * (size_t)i + 3];
+            const float qs = rsqrt_ieee(((q3 * q3 + q0 * q0) + q1 * q1) + q2 * q2);
+            const float w = q0 * qs, x = q1 * qs, y = q2 * qs, z = q3 * qs;
+            const M3 R = cols3(1.f - 2.f * (y * y + z * z), 2.f * (x * y + w * z), 2.f * (x * z - w * y),
+                               2.f * (x * y - w * z), 1.f - 2.f * (x * x + z * z), 2.f * (y * z + w * x),
+                               2.f * (x * z + w * y), 2.f * (y * z - w * x), 1.f - 2.f * (x * x + y * y));
+            const float gs = P->glob_scale;
+            const float sc[3] = {gs * es[0], gs * es[1], gs * es[2]};
+            M3 Mm;
+#pragma unroll
+            for (int c = 0; c < 3; c++)
+#pragma unroll
+                for (int r = 0; r < 3; r++) Mm.m[c][r] = R.m[c][r] * sc[c];
+            const M3 tmp = mul3(Mm, tr3(Mm));
+            const float cv[6] = {tmp.m[0][0], tmp.m[0][1], tmp.m[0][2], tmp.m[1][1], tmp.m[1][2], tmp.m[2][2]};
+            // project_cov3d_ewa_vjp (:1339-1407)
+            float pv0 = ((vm[0] * p[0] + vm[1] * p[1]) + vm[2] * p[2]) + vm[3];
+            float pv1 = ((vm[4] * p[0] + vm[5] * p[1]) + vm[6] * p[2]) + vm[7];
+            const float pv2 = ((vm[8] * p[0] + vm[9] * p[1]) + vm[10] * p[2]) + vm[11];
+            const float lim_x = 1.3f * P->tan_fovx, lim_y = 1.3f * P->tan_fovy;
+            pv0 = pv2 * fminf(lim_x, fmaxf(-lim_x, pv0 / pv2));
+            pv1 = pv2 * fminf(lim_y, fmaxf(-lim_y, pv1 / pv2));
+            const float rz = 1.f / pv2, rz2 = rz * rz;
+            const M3 Wm = cols3(vm[0], vm[4], vm[8], vm[1], vm[5], vm[9], vm[2], vm[6], vm[10]);
+            const M3 J = cols3(fx * rz, 0.f, 0.f, 0.f, fy * rz, 0.f, (-fx * pv0) * rz2,
+                               (-fy * pv1) * rz2, 0.f);
+            const M3 V = cols3(cv[0], cv[1], cv[2], cv[1], cv[3], cv[4], cv[2], cv[4], cv[5]);
+            const M3 vcov = cols3(vcv0, 0.5f * vcv1, 0.f, 0.5f * vcv1, vcv2, 0.f, 0.f, 0.f, 0.f);
+            const M3 T = mul3(J, Wm);
+            const M3 vV = mul3(mul3(tr3(T), vcov), T);
+            const M3 vT1 = mul3(mul3(vcov, T), tr3(V));
+            const M3 vT2 = mul3(mul3(tr3(vcov), T), V);
+            M3 vT;
+#pragma unroll
+            for (int c = 0; c < 3; c++)
+#pragma unroll
+                for (int r = 0; r < 3; r++) vT.m[c][r] = vT1.m[c][r] + vT2.m[c][r];
+            const float vcov3d[6] = {vV.m[0][0], vV.m[0][1] + vV.m[1][0], vV.m[0][2] + vV.m[2][0],
+                                     vV.m[1][1], vV.m[1][2] + vV.m[2][1], vV.m[2][2]};
+            const M3 vJ = mul3(vT, tr3(Wm));
+            const float fx_rz2 = fx * rz2, fy_rz2 = fy * rz2, rz3 = rz2 * rz;
+            const float vt0 = -fx_rz2 * vJ.m[2][0];
+            const float vt1 = -fy_rz2 * vJ.m[2][1];
+            const float vt2 = ((-fx_rz2 * vJ.m[0][0] + 2.f * fx * pv0 * rz3 * vJ.m[2][0]) -
+                               fy_rz2 * vJ.m[1][1]) + 2.f * fy * pv1 * rz3 * vJ.m[2][1];
+#pragma unroll
+            for (int c = 0; c < 3; c++)
+                vmean[c] += (vt0 * Wm.m[c][0] + vt1 * Wm.m[c][1]) + vt2 * Wm.m[c][2];
+            // scale_rot_to_cov3d_vjp (:1498-1531)
+            const M3 vVs = cols3(vcov3d[0], 0.5f * vcov3d[1], 0.5f * vcov3d[2], 0.5f * vcov3d[1],
+                                 vcov3d[3], 0.5f * vcov3d[4], 0.5f * vcov3d[2], 0.5f * vcov3d[4],
+                                 vcov3d[5]);
+            const M3 Sm = cols3(sc[0], 0.f, 0.f, 0.f, sc[1], 0.f, 0.f, 0.f, sc[2]);
+            const M3 M2 = mul3(R, Sm);
+            M3 vVs2;
+#pragma unroll
+            for (int c = 0; c < 3; c++)
+#pragma unroll
+                for (int r = 0; r < 3; r++) vVs2.m[c][r] = 2.f * vVs.m[c][r];
+            const M3 vM = mul3(vVs2, M2);
+#pragma unroll
+            for (int c = 0; c < 3; c++)
+                vscale[c] = ((R.m[c][0] * vM.m[c][0] + R.m[c][1] * vM.m[c][1]) + R.m[c][2] * vM.m[c][2]) * es[c];
+            const M3 vR = mul3(vM, Sm);
+            const float (*v)[3] = vR.m;
+            vq[0] = 2.f * ((x * (v[1][2] - v[2][1]) + y * (v[2][0] - v[0][2])) + z * (v[0][1] - v[1][0]));
+            vq[1] = 2.f * (((-2.f * x * (v[1][1] + v[2][2]) + y * (v[0][1] + v[1][0])) +
+                            z * (v[0][2] + v[2][0])) + w * (v[1][2] - v[2][1]));
+            vq[2] = 2.f * (((x * (v[0][1] + v[1][0]) - 2.f * y * (v[0][0] + v[2][2])) +
+                            z * (v[1][2] + v[2][1])) + w * (v[2][0] - v[0][2]));
+            vq[3] = 2.f * (((x * (v[0][2] + v[2][0]) + y * (v[1][2] + v[2][1])) -
+                            2.f * z * (v[0][0] + v[1][1])) + w * (v[0][1] - v[1][0]));
+            // SH basis of the view direction, for the dc/rest Adam (:1915-1985)
+            const float d0 = p[0] - P->cam_pos[0], d1 = p[1] - P->cam_pos[1], d2 = p[2] - P->cam_pos[2];
+            const float dn = rsqrt_ieee((d0 * d0 + d1 * d1) + d2 * d2);
+            const float ux = d0 * dn, uy = d1 * dn, uz = d2 * dn;
+            const float xx = ux * ux, xy = ux * uy, xz = ux * uz, yy = uy * uy, yz = uy * uz, zz = uz * uz;
+            float* bs = s_basis[tid];
+            bs[0] = -MSP_SH_C1 * uy;
+            bs[1] = MSP_SH_C1 * uz;
+            bs[2] = -MSP_SH_C1 * ux;
+            bs[3] = kSH_C2[0] * xy;
+            bs[4] = kSH_C2[1] * yz;
+            bs[5] = kSH_C2[2] * ((2.f * zz - xx) - yy);
+            bs[6] = kSH_C2[3] * xz;
+            bs[7] = kSH_C2[4] * (xx - yy);
+            bs[8] = kSH_C3[0] * uy * (3.f * xx - yy);
+            bs[9] = kSH_C3[1] * xy * uz;
+            bs[10] = kSH_C3[2] * uy * ((4.f * zz - xx) - yy);
+            bs[11] = kSH_C3[3] * uz * ((2.f * zz - 3.f * xx) - 3.f * yy);
+            bs[12] = kSH_C3[4] * ux * ((4.f * zz - xx) - yy);
+            bs[13] = kSH_C3[5] * uz * (xx - yy);
+            bs[14] = kSH_C3[6] * ux * (xx - 3.f * yy);
+            s_vrgb[tid][0] = vr0;
+            s_vrgb[tid][1] = vr1;
+            s_vrgb[tid][2] = vr2;
+            // dc Adam (group 3), visible only
+            if (A.numel[3] > 0) {
+                float* dcp = A.param[3] + 3 * (size_t)i;
+                float* dce = A.exp_avg[3] + 3 * (size_t)i;
+                float* dcs = A.exp_avg_sq[3] + 3 * (size_t)i;
+                const float step = P->adam_step[3], bc2 = P->adam_bc2[3];
+                adam_elem(dcp + 0, dce + 0, dcs + 0, MSP_SH_C0 * vr0, step, b1, b2, bc2, eps);
+                adam_elem(dcp + 1, dce + 1, dcs + 1, MSP_SH_C0 * vr1, step, b1, b2, bc2, eps);
+                adam_elem(dcp + 2, dce + 2, dcs + 2, MSP_SH_C0 * vr2, step, b1, b2, bc2, eps);
+            }
+            // densification statistics (accumulate_grad_stats_kernel)
+            St.vis_counts[i] += 1.0f;
+            St.grad_norm[i] += sqrtf(vx * vx + vy * vy);
+            St.max_2d[i] = fmaxf(St.max_2d[i], (float)rad * P->inv_max_dim);
+        }
+        // Adam over every element of groups 0, 1, 2, 5 (zero gradient when culled)
+        if (A.numel[0] > 0) {
+            const float step = P->adam_step[0], bc2 = P->adam_bc2[0];
+#pragma unroll
+            for (int c = 0; c < 3; c++)
+                adam_elem(means + 3 * (size_t)i + c, A.exp_avg[0] + 3 * (size_t)i + c,
+                          A.exp_avg_sq[0] + 3 * (size_t)i + c, vmean[c], step, b1, b2, bc2, eps);
+        }
+        if (A.numel[1] > 0) {
+            const float step = P->adam_step[1], bc2 = P->adam_bc2[1];
+#pragma unroll
+            for (int c = 0; c < 3; c++)
+                adam_elem(scales + 3 * (size_t)i + c, A.exp_avg[1] + 3 * (size_t)i + c,
+                          A.exp_avg_sq[1] + 3 * (size_t)i + c, vscale[c], step, b1, b2, bc2, eps);
+        }
+        if (A.numel[2] > 0) {
+            const float step = P->adam_step[2], bc2 = P->adam_bc2[2];
+#pragma unroll
+            for (int c = 0; c < 4; c++)
+                adam_elem(quats + 4 * (size_t)i + c, A.exp_avg[2] + 4 * (size_t)i + c,
+                          A.exp_avg_sq[2] + 4 * (size_t)i + c, vq[c], step, b1, b2, bc2, eps);
+        }
+        if (A.numel[5] > 0) {
+            adam_elem(A.param[5] + i, A.exp_avg[5] + i, A.exp_avg_sq[5] + i, vop, P->adam_step[5],
+                      b1, b2, P->adam_bc2[5], eps);
+        }
+    }
+    s_vis[tid] = vis;
+    __syncthreads();
+    // SH-rest Adam (group 4), warp-cooperative over 32 Gaussians.
+    if (nb_rest <= 0 || A.numel[4] <= 0) return;
+    const int stride = P->rest_stride;
+    const int used = nb_rest * 3;
+    const int wbase = warp * 32;
+    const int g0 = base + wbase;
+    if (g0 >= N) return;
+    const int cnt = min(32, N - g0);
+    float* rp = A.param[4] + (size_t)g0 * stride;
+    float* re = A.exp_avg[4] + (size_t)g0 * stride;
+    float* rs = A.exp_avg_sq[4] + (size_t)g0 * stride;
+    const float step = P->adam_step[4], bc2 = P->adam_bc2[4];
+    const int total = cnt * stride;
+    int gl = 0, kk = lane;
+    while (kk >= stride) { kk -= stride; gl++; }
+    for (int e = lane; e < total; e += 32) {
+        if (kk < used && s_vis[wbase + gl]) {
+            const int b = kk / 3, c = kk - 3 * (kk / 3);
+            const float grad = s_basis[wbase + gl][b] * s_vrgb[wbase + gl][c];
+            adam_elem(rp + e, re + e, rs + e, grad, step, b1, b2, bc2, eps);
+        }
+        kk += 32;
+        while (kk >= stride) { kk -= stride; gl++; }
+    }
+}
+
+void launch_project_backward_adam(const StepParams* P, int N, int degrees_to_use_host,
+                                  int rest_stride_host, const Buffers& B, const AdamPtrs& A,
+                                  const StatPtrs& St, cudaStream_t s)
+{
+    if (N <= 0) return;
+    // SH-rest bases updated: degrees_to_use 0 -> 0, 1 -> 3, 2 -> 8, >= 3 -> 15
+    // (the reference stops at degree 3 here, msplat_metal.metal:1931-1985).
+    int nb = degrees_to_use_host < 1 ? 0 : degrees_to_use_host == 1 ? 3
+             : degrees_to_use_host == 2 ? 8 : 15;
+    if (nb * 3 > rest_stride_host) nb = rest_stride_host / 3;
+    const int grid = (N + kBwdThreads - 1) / kBwdThreads;
+    project_backward_adam_kernel<<<grid, kBwdThreads, 0, s>>>(P, N, B.proj.radii, B.proj.conic_op,
+                                                              B.grad_acc, A, St, nb);
+}
+
+}  // namespace msp

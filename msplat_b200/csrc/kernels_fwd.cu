@@ -1,0 +1,593 @@
+// kernels_fwd.cu -- forward half of the step: projection + SH, tile binning,
+// per-tile depth sort and the forward rasterizer.  Compiled with
+// --fmad=false (see msp_math.cuh): every value here is bit-identical to the
+// CPU oracle.
+#include "engine.h"
+#include "msp_math.cuh"
+
+namespace msp {
+
+constexpr int kProjThreads = 128;
+constexpr int kSortThreads = 256;
+
+// ---------------------------------------------------------------------------
+// Projection + SH colour + tile counting.
+// Reference: project_and_sh_forward_kernel, msplat_metal.metal:1695-1787,
+// with helpers :53-317 and sh_coeffs_to_color :587-654.  The per-tile
+// counting of scatter_to_prealloc_bins_kernel (:2025-2059) is fused here:
+// each visible Gaussian adds one to every tile of its rect.
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ void sh_to_color(int degree, float x, float y, float z,
+                                            const float* dc, const float* r, float col[3])
+{
+    const float C1 = MSP_SH_C1;
+    float xx = x * x, xy = x * y, xz = x * z, yy = y * y, yz = y * z, zz = z * z;
+#pragma unroll
+    for (int c = 0; c < 3; c++) {
+        float v = MSP_SH_C0 * dc[c];
+        if (degree >= 1) {
+            v += C1 * ((-y * r[0 * 3 + c] + z * r[1 * 3 + c]) - x * r[2 * 3 + c]);
+            if (degree >= 2) {
+                v += ((((kSH_C2[0] * xy * r[3 * 3 + c] + kSH_C2[1] * yz * r[4 * 3 + c]) +
+                        kSH_C2[2] * ((2.f * zz - xx) - yy) * r[5 * 3 + c]) +
+                       kSH_C2[3] * xz * r[6 * 3 + c]) +
+                      kSH_C2[4] * (xx - yy) * r[7 * 3 + c]);
+                if (degree >= 3) {
+                    v += ((((((kSH_C3[0] * y * (3.f * xx - yy) * r[8 * 3 + c] +
+                               kSH_C3[1] * xy * z * r[9 * 3 + c]) +
+                              kSH_C3[2] * y * ((4.f * zz - xx) - yy) * r[10 * 3 + c]) +
+                             kSH_C3[3] * z * ((2.f * zz - 3.f * xx) - 3.f * yy) * r[11 * 3 + c]) +
+                            kSH_C3[4] * x * ((4.f * zz - xx) - yy) * r[12 * 3 + c]) +
+                           kSH_C3[5] * z * (xx - yy) * r[13 * 3 + c]) +
+                          kSH_C3[6] * x * (xx - 3.f * yy) * r[14 * 3 + c]);
+                    if (degree >= 4) {
+                        v += ((((((((kSH_C4[0] * xy * (xx - yy) * r[15 * 3 + c] +
+                                     kSH_C4[1] * yz * (3.f * xx - yy) * r[16 * 3 + c]) +
+                                    kSH_C4[2] * xy * (7.f * zz - 1.f) * r[17 * 3 + c]) +
+                                   kSH_C4[3] * yz * (7.f * zz - 3.f) * r[18 * 3 + c]) +
+                                  kSH_C4[4] * (zz * (35.f * zz - 30.f) + 3.f) * r[19 * 3 + c]) +
+                                 kSH_C4[5] * xz * (7.f * zz - 3.f) * r[20 * 3 + c]) +
+                                kSH_C4[6] * (xx - yy) * (7.f * zz - 1.f) * r[21 * 3 + c]) +
+                               kSH_C4[7] * xz * (xx - 3.f * yy) * r[22 * 3 + c]) +
+                              kSH_C4[8] * (xx * (xx - 3.f * yy) - yy * (3.f * xx - yy)) *
+                                  r[23 * 3 + c]);
+                    }
+                }
+            }
+        }
+        col[c] = v;
+    }
+}
+
+template <bool ZERO_GRADS>
+__global__ void __launch_bounds__(kProjThreads)
+project_forward_kernel(const StepParams* __restrict__ P, int N, const float* __restrict__ means,
+                       const float* __restrict__ scales, const float* __restrict__ quats,
+                       const float* __restrict__ dc, const float* __restrict__ rest,
+                       const float* __restrict__ opac, ProjOut out, int* __restrict__ tile_count,
+                       float* __restrict__ grad_acc, int used, int sstride)
+{
+    extern __shared__ float s_rest[];  // kProjThreads * sstride
+    __shared__ int s_vis[kProjThreads];
+    const int tid = threadIdx.x;
+    const int base = blockIdx.x * kProjThreads;
+    const int i = base + tid;
+
+    bool vis = false;
+    float px_c = 0.f, py_c = 0.f;
+    int x0 = 0, y0 = 0, x1 = 0, y1 = 0;
+    float p[3] = {0.f, 0.f, 0.f};
+    if (i < N) {
+        out.radii[i] = 0;
+        p[0] = means[3 * (size_t)i];
+        p[1] = means[3 * (size_t)i + 1];
+        p[2] = means[3 * (size_t)i + 2];
+        const float* vm = P->viewmat;
+        // clip_near_plane / transform_4x3 (:90-97, :134-145)
+        float pv0 = ((vm[0] * p[0] + vm[1] * p[1]) + vm[2] * p[2]) + vm[3];
+        float pv1 = ((vm[4] * p[0] + vm[5] * p[1]) + vm[6] * p[2]) + vm[7];
+        float pv2 = ((vm[8] * p[0] + vm[9] * p[1]) + vm[10] * p[2]) + vm[11];
+        if (!(pv2 <= P->clip_thresh)) {
+            float s0 = msp_expf(scales[3 * (size_t)i]);
+            float s1 = msp_expf(scales[3 * (size_t)i + 1]);
+            float s2 = msp_expf(scales[3 * (size_t)i + 2]);
+            const float4 q4 = make_float4(quats[4 * (size_t)i], quats[4 * (size_t)i + 1],
+                                          quats[4 * (size_t)i + 2], quats[4 * (size_t)i + 3]);
+            // quat_to_rotmat (:111-131): memory order w, x, y, z
+            float qs = rsqrt_ieee(((q4.w * q4.w + q4.x * q4.x) + q4.y * q4.y) + q4.z * q4.z);
+            float w = q4.x * qs, x = q4.y * qs, y = q4.z * qs, z = q4.w * qs;
+            // R columns (Metal float3x3 is column-major)
+            float R[3][3] = {{1.f - 2.f * (y * y + z * z), 2.f * (x * y + w * z), 2.f * (x * z - w * y)},
+                             {2.f * (x * y - w * z), 1.f - 2.f * (x * x + z * z), 2.f * (y * z + w * x)},
+                             {2.f * (x * z + w * y), 2.f * (y * z - w * x), 1.f - 2.f * (x * x + y * y)}};
+            float gsc = P->glob_scale;
+            float sc[3] = {gsc * s0, gsc * s1, gsc * s2};
+            float M[3][3];
+#pragma unroll
+            for (int c = 0; c < 3; c++)
+#pragma unroll
+                for (int r = 0; r < 3; r++) M[c][r] = R[c][r] * sc[c];
+            // tmp = M * M^T, cov3d upper triangle (:157-172)
+            float cv[6];
+            {
+                float t00 = (M[0][0] * M[0][0] + M[1][0] * M[1][0]) + M[2][0] * M[2][0];
+                float t01 = (M[0][1] * M[0][0] + M[1][1] * M[1][0]) + M[2][1] * M[2][0];
+                float t02 = (M[0][2] * M[0][0] + M[1][2] * M[1][0]) + M[2][2] * M[2][0];
+                float t11 = (M[0][1] * M[0][1] + M[1][1] * M[1][1]) + M[2][1] * M[2][1];
+                float t12 = (M[0][2] * M[0][1] + M[1][2] * M[1][1]) + M[2][2] * M[2][1];
+                float t22 = (M[0][2] * M[0][2] + M[1][2] * M[1][2]) + M[2][2] * M[2][2];
+                cv[0] = t00; cv[1] = t01; cv[2] = t02; cv[3] = t11; cv[4] = t12; cv[5] = t22;
+            }
+            // project_cov3d_ewa (:241-281)
+            const float fx = P->fx, fy = P->fy;
+            float lim_x = 1.3f * P->tan_fovx, lim_y = 1.3f * P->tan_fovy;
+            float qx = pv2 * fminf(lim_x, fmaxf(-lim_x, pv0 / pv2));
+            float qy = pv2 * fminf(lim_y, fmaxf(-lim_y, pv1 / pv2));
+            float rz = 1.f / pv2;
+            float rz2 = rz * rz;
+            float j00 = fx * rz, j11 = fy * rz;
+            float j20 = (-fx * qx) * rz2, j21 = (-fy * qy) * rz2;
+            float t0[3], t1[3];
+#pragma unroll
+            for (int k = 0; k < 3; k++) {
+                t0[k] = j00 * vm[k] + j20 * vm[8 + k];
+                t1[k] = j11 * vm[4 + k] + j21 * vm[8 + k];
+            }
+            float tv0[3] = {(t0[0] * cv[0] + t0[1] * cv[1]) + t0[2] * cv[2],
+                            (t0[0] * cv[1] + t0[1] * cv[3]) + t0[2] * cv[4],
+                            (t0[0] * cv[2] + t0[1] * cv[4]) + t0[2] * cv[5]};
+            float tv1[3] = {(t1[0] * cv[0] + t1[1] * cv[1]) + t1[2] * cv[2],
+                            (t1[0] * cv[1] + t1[1] * cv[3]) + t1[2] * cv[4],
+                            (t1[0] * cv[2] + t1[1] * cv[4]) + t1[2] * cv[5]};
+            float c2x = ((tv0[0] * t0[0] + tv0[1] * t0[1]) + tv0[2] * t0[2]) + 0.3f;
+            float c2y = (tv0[0] * t1[0] + tv0[1] * t1[1]) + tv0[2] * t1[2];
+            float c2z = ((tv1[0] * t1[0] + tv1[1] * t1[1]) + tv1[2] * t1[2]) + 0.3f;
+            // compute_cov2d_bounds (:283-305)
+            float det = c2x * c2z - c2y * c2y;
+            if (det != 0.f) {
+                float inv_det = 1.f / det;
+                float ca = c2z * inv_det, cb = -c2y * inv_det, cc = c2x * inv_det;
+                float bb = 0.5f * (c2x + c2z);
+                float disc = sqrtf(fmaxf(0.1f, bb * bb - det));
+                float radius = ceilf(3.f * sqrtf(bb + disc));
+                // project_pix (:308-317)
+                const float* pm = P->projmat;
+                float h0 = ((pm[0] * p[0] + pm[1] * p[1]) + pm[2] * p[2]) + pm[3];
+                float h1 = ((pm[4] * p[0] + pm[5] * p[1]) + pm[6] * p[2]) + pm[7];
+                float h3 = ((pm[12] * p[0] + pm[13] * p[1]) + pm[14] * p[2]) + pm[15];
+                float rw = 1.f / (h3 + 1e-6f);
+                float ndx = h0 * rw, ndy = h1 * rw;
+                px_c = ((0.5f * (float)P->img_w) * ndx + P->cx) - 0.5f;
+                py_c = ((0.5f * (float)P->img_h) * ndy + P->cy) - 0.5f;
+                float ax = ceilf(3.0f * sqrtf(c2x));
+                float ay = ceilf(3.0f * sqrtf(c2z));
+                // get_tile_bbox (:57-87)
+                float tcx = px_c / 16.f, tcy = py_c / 16.f;
+                float trx = ax / 16.f, try_ = ay / 16.f;
+                x0 = min(max(0, f2i(tcx - trx)), P->tiles_x);
+                x1 = min(max(0, f2i((tcx + trx) + 1)), P->tiles_x);
+                y0 = min(max(0, f2i(tcy - try_)), P->tiles_y);
+                y1 = min(max(0, f2i((tcy + try_) + 1)), P->tiles_y);
+                int area = (x1 - x0) * (y1 - y0);
+                if (area > 0) {
+                    vis = true;
+                    out.radii[i] = f2i(radius);
+                    out.depth[i] = pv2;
+                    out.xy[i] = make_float2(px_c, py_c);
+                    out.conic_op[i] = make_float4(ca, cb, cc, sigmoid_ref(opac[i]));
+                    out.rect[i] = make_uint2((unsigned)x0 | ((unsigned)y0 << 16),
+                                             (unsigned)x1 | ((unsigned)y1 << 16));
+                }
+            }
+        }
+    }
+    s_vis[tid] = vis;
+    __syncthreads();
+    // Stage the used SH-rest coefficients of the block's visible Gaussians:
+    // one warp per Gaussian reads its contiguous row.
+    if (used > 0) {
+        const int lane = tid & 31, warp = tid >> 5;
+        for (int gl = warp; gl < kProjThreads; gl += kProjThreads / 32) {
+            if (!s_vis[gl]) continue;
+            const float* src = rest + (size_t)(base + gl) * P->rest_stride;
+            for (int k = lane; k < used; k += 32) s_rest[gl * sstride + k] = src[k];
+        }
+        __syncthreads();
+    }
+    if (!vis) return;
+    // SH colour (:1780-1786): viewdir = normalize(p - cam_pos)
+    float d0 = p[0] - P->cam_pos[0], d1 = p[1] - P->cam_pos[1], d2 = p[2] - P->cam_pos[2];
+    float dn = rsqrt_ieee((d0 * d0 + d1 * d1) + d2 * d2);
+    float col[3];
+    float dcv[3] = {dc[3 * (size_t)i], dc[3 * (size_t)i + 1], dc[3 * (size_t)i + 2]};
+    sh_to_color(P->degrees_to_use, d0 * dn, d1 * dn, d2 * dn, dcv, s_rest + tid * sstride, col);
+    out.rgb[i] = make_float4(col[0], col[1], col[2], 0.f);
+    const int tx_n = P->tiles_x;
+    for (int ty = y0; ty < y1; ty++)
+        for (int tx = x0; tx < x1; tx++) atomicAdd(&tile_count[ty * tx_n + tx], 1);
+    if (ZERO_GRADS) {
+        float* g = grad_acc + (size_t)i * kGradStride;
+#pragma unroll
+        for (int k = 0; k < kGradStride; k++) g[k] = 0.f;
+    }
+}
+
+void launch_project_forward(const StepParams* P, int N, const float* means, const float* scales,
+                            const float* quats, const float* dc, const float* rest,
+                            const float* opac, const Buffers& B, bool zero_grads,
+                            int degrees_to_use_host, int rest_stride_host, cudaStream_t s)
+{
+    if (N <= 0) return;
+    int used = (num_sh_bases_host(degrees_to_use_host) - 1) * 3;
+    if (used > rest_stride_host) used = rest_stride_host;
+    int sstride = used | 1;
+    size_t smem = (size_t)kProjThreads * sstride * sizeof(float);
+    int grid = (N + kProjThreads - 1) / kProjThreads;
+    if (zero_grads)
+        project_forward_kernel<true><<<grid, kProjThreads, smem, s>>>(
+            P, N, means, scales, quats, dc, rest, opac, B.proj, B.tile_count, B.grad_acc, used,
+            sstride);
+    else
+        project_forward_kernel<false><<<grid, kProjThreads, smem, s>>>(
+            P, N, means, scales, quats, dc, rest, opac, B.proj, B.tile_count, nullptr, used,
+            sstride);
+}
+
+// ---------------------------------------------------------------------------
+// Exclusive scan of per-tile counts (one CTA, warp-shuffle scans).  Plays the
+// role of prefix_sum_kernel (msplat_metal.metal:2312-2364); ranges here are
+// [offset[t], offset[t+1]) with no per-tile cap.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024)
+scan_tiles_kernel(const StepParams* __restrict__ P, int T, const int* __restrict__ count,
+                  int* __restrict__ offset, int* __restrict__ err)
+{
+    __shared__ int s_warp[32];
+    const int tid = threadIdx.x;
+    const int per = (T + 1023) / 1024;
+    const int beg = min(tid * per, T), end = min(beg + per, T);
+    int local = 0;
+    for (int i = beg; i < end; i++) local += count[i];
+    const int lane = tid & 31, warp = tid >> 5;
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    if (lane == 31) s_warp[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        int v = s_warp[lane];
+        int wi = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            int u = __shfl_up_sync(0xffffffffu, wi, o);
+            if (lane >= o) wi += u;
+        }
+        s_warp[lane] = wi - v;  // exclusive
+    }
+    __syncthreads();
+    int run = s_warp[warp] + incl - local;
+    for (int i = beg; i < end; i++) {
+        offset[i] = run;
+        run += count[i];
+    }
+    if (tid == 1023) {
+        offset[T] = run;
+        if ((long long)run > P->capacity) atomicOr(err, kErrIsectOverflow);
+    }
+}
+
+void launch_scan_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s)
+{
+    scan_tiles_kernel<<<1, 1024, 0, s>>>(P, num_tiles, B.tile_count, B.tile_offset, B.err);
+}
+
+// ---------------------------------------------------------------------------
+// Key scatter: every visible Gaussian writes (depth bits << 32 | id) into
+// each tile of its rect.  The slot comes from counting the tile's counter
+// back down, which also leaves the counters at zero for the next step.
+// Reference key: scatter_to_prealloc_bins_kernel, msplat_metal.metal:2044-2056.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+scatter_kernel(const StepParams* __restrict__ P, int N, const int* __restrict__ radii,
+               const float* __restrict__ depth, const uint2* __restrict__ rect,
+               int* __restrict__ count, const int* __restrict__ offset,
+               unsigned long long* __restrict__ keys)
+{
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= N || radii[i] <= 0) return;
+    const uint2 r = rect[i];
+    const int x0 = r.x & 0xffff, y0 = r.x >> 16, x1 = r.y & 0xffff, y1 = r.y >> 16;
+    const unsigned long long key =
+        ((unsigned long long)__float_as_uint(depth[i]) << 32) | (unsigned)i;
+    const long long cap = P->capacity;
+    const int tx_n = P->tiles_x;
+    for (int ty = y0; ty < y1; ty++)
+        for (int tx = x0; tx < x1; tx++) {
+            const int t = ty * tx_n + tx;
+            const int pos = atomicSub(&count[t], 1) - 1;
+            const long long idx = (long long)offset[t] + pos;
+            if (idx < cap) keys[idx] = key;
+        }
+}
+
+void launch_scatter(const StepParams* P, int N, const Buffers& B, cudaStream_t s)
+{
+    if (N <= 0) return;
+    scatter_kernel<<<(N + 255) / 256, 256, 0, s>>>(P, N, B.proj.radii, B.proj.depth, B.proj.rect,
+                                                   B.tile_count, B.tile_offset, B.keys);
+}
+
+// ---------------------------------------------------------------------------
+// Per-tile ascending sort of the 64-bit keys, then the Gaussian ids in that
+// order.  Reference: bitonic_sort_per_tile_kernel, msplat_metal.metal:2064-2138
+// (the fused pack is replaced by id gathers in the rasterizers).  Tiles of
+// up to kSortCap keys sort in shared memory in one pass; larger tiles sort
+// kSortCap runs and merge them pairwise along merge paths.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void bitonic_smem(unsigned long long* s, int npow)
+{
+    for (int k = 2; k <= npow; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < (npow >> 1); i += kSortThreads) {
+                int pos = 2 * i - (i & (j - 1));
+                int partner = pos ^ j;
+                bool ascending = ((pos & k) == 0);
+                unsigned long long a = s[pos], b = s[partner];
+                if ((a > b) == ascending) {
+                    s[pos] = b;
+                    s[partner] = a;
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+__device__ __forceinline__ int merge_path(const unsigned long long* a, int la,
+                                          const unsigned long long* b, int lb, int d)
+{
+    int lo = max(0, d - lb), hi = min(d, la);
+    while (lo < hi) {
+        int mid = (lo + hi) >> 1;
+        if (a[mid] > b[d - 1 - mid]) hi = mid;
+        else lo = mid + 1;
+    }
+    return lo;
+}
+
+__global__ void __launch_bounds__(kSortThreads)
+sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
+                  unsigned long long* __restrict__ keys, unsigned long long* __restrict__ keys_alt,
+                  int* __restrict__ ids)
+{
+    __shared__ unsigned long long s[kSortCap];
+    const int t = blockIdx.x;
+    const long long cap = P->capacity;
+    const long long start = min((long long)offset[t], cap);
+    const long long end = min((long long)offset[t + 1], cap);
+    const int n = (int)(end - start);
+    if (n <= 0) return;
+    if (n <= kSortCap) {
+        int npow = 1;
+        while (npow < n) npow <<= 1;
+        for (int i = threadIdx.x; i < npow; i += kSortThreads)
+            s[i] = i < n ? keys[start + i] : ~0ull;
+        __syncthreads();
+        bitonic_smem(s, npow);
+        for (int i = threadIdx.x; i < n; i += kSortThreads)
+            ids[start + i] = (int)(unsigned)(s[i] & 0xffffffffull);
+        return;
+    }
+    // Large tile: sorted runs of kSortCap, then pairwise merges.
+    unsigned long long* src = keys + start;
+    unsigned long long* dst = keys_alt + start;
+    for (int r0 = 0; r0 < n; r0 += kSortCap) {
+        const int m = min(kSortCap, n - r0);
+        int npow = 1;
+        while (npow < m) npow <<= 1;
+        __syncthreads();
+        for (int i = threadIdx.x; i < npow; i += kSortThreads) s[i] = i < m ? src[r0 + i] : ~0ull;
+        __syncthreads();
+        bitonic_smem(s, npow);
+        for (int i = threadIdx.x; i < m; i += kSortThreads) src[r0 + i] = s[i];
+    }
+    __syncthreads();
+    for (long long L = kSortCap; L < n; L <<= 1) {
+        for (long long s0 = 0; s0 < n; s0 += 2 * L) {
+            const unsigned long long* a = src + s0;
+            const int la = (int)min(L, (long long)n - s0);
+            const unsigned long long* b = a + la;
+            const int lb = (int)max(0LL, min(L, (long long)n - s0 - la));
+            const int total = la + lb;
+            const int d0 = (int)((long long)total * threadIdx.x / kSortThreads);
+            const int d1 = (int)((long long)total * (threadIdx.x + 1) / kSortThreads);
+            int ia = merge_path(a, la, b, lb, d0);
+            int ib = d0 - ia;
+            unsigned long long* o = dst + s0 + d0;
+            for (int q = d0; q < d1; q++) {
+                bool take_a = ib >= lb || (ia < la && a[ia] < b[ib]);
+                *o++ = take_a ? a[ia++] : b[ib++];
+            }
+        }
+        __syncthreads();
+        unsigned long long* tmp = src;
+        src = dst;
+        dst = tmp;
+    }
+    for (int i = threadIdx.x; i < n; i += kSortThreads)
+        ids[start + i] = (int)(unsigned)(src[i] & 0xffffffffull);
+}
+
+void launch_sort_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s)
+{
+    if (num_tiles <= 0) return;
+    sort_tiles_kernel<<<num_tiles, kSortThreads, 0, s>>>(P, B.tile_offset, B.keys, B.keys_alt,
+                                                        B.sorted_ids);
+}
+
+// ---------------------------------------------------------------------------
+// Forward rasterizer: one CTA per 16x16 tile (or per (tile, depth chunk)),
+// one thread per pixel, batches of 256 Gaussians staged in shared memory.
+// Reference: nd_rasterize_forward_kernel (msplat_metal.metal:472-585) and
+// rasterize_forward_chunked_kernel (:2633-2741).  The per-pixel loop is the
+// reference's; the CTA leaves as soon as every pixel has terminated.
+// ---------------------------------------------------------------------------
+template <bool CHUNKED>
+__global__ void __launch_bounds__(kTileThreads)
+raster_forward_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
+                      const int* __restrict__ ids, const float2* __restrict__ g_xy,
+                      const float4* __restrict__ g_co, const float4* __restrict__ g_rgb,
+                      float* __restrict__ out_img, float* __restrict__ final_T,
+                      int* __restrict__ final_idx, float* __restrict__ chunk_T,
+                      float* __restrict__ chunk_C, int* __restrict__ chunk_idx)
+{
+    __shared__ float2 s_xy[kTileThreads];
+    __shared__ float4 s_co[kTileThreads];
+    __shared__ float4 s_rgb[kTileThreads];
+    const int tile = blockIdx.x;
+    const int tx_n = P->tiles_x;
+    const int W = P->img_w, H = P->img_h;
+    const int tid = threadIdx.x;
+    const int px = (tile % tx_n) * kBlockX + (tid & 15);
+    const int py = (tile / tx_n) * kBlockY + (tid >> 4);
+    const bool inside = px < W && py < H;
+    const long long cap = P->capacity;
+    const int fbeg = (int)min((long long)offset[tile], cap);
+    const int fend = (int)min((long long)offset[tile + 1], cap);
+    int beg = fbeg, end = fend;
+    int k = 0;
+    if (CHUNKED) {
+        k = blockIdx.y;
+        beg = fbeg + k * kChunk;
+        end = min(fbeg + (k + 1) * kChunk, fend);
+        if (beg >= end) return;
+    }
+    const float fpx = (float)px, fpy = (float)py;
+    float T = 1.f, c0 = 0.f, c1 = 0.f, c2 = 0.f;
+    int last = beg - 1;
+    bool done = !inside;
+    for (int b0 = beg; b0 < end; b0 += kTileThreads) {
+        if (__syncthreads_count(done) == kTileThreads) break;
+        const int idx = b0 + tid;
+        if (idx < end) {
+            const int g = ids[idx];
+            s_xy[tid] = g_xy[g];
+            s_co[tid] = g_co[g];
+            const float4 rc = g_rgb[g];
+            s_rgb[tid] = make_float4(fmaxf(rc.x + 0.5f, 0.f), fmaxf(rc.y + 0.5f, 0.f),
+                                     fmaxf(rc.z + 0.5f, 0.f), 0.f);
+        }
+        __syncthreads();
+        if (done) continue;
+        const int n = min(kTileThreads, end - b0);
+        for (int t = 0; t < n; t++) {
+            const float4 co = s_co[t];
+            const float2 xy = s_xy[t];
+            const float dx = xy.x - fpx, dy = xy.y - fpy;
+            const float sigma = fmaf(0.5f, fmaf(co.x, dx * dx, co.z * dy * dy), co.y * dx * dy);
+            if (sigma < 0.f || sigma >= 5.55f) continue;
+            const float alpha = fminf(0.999f, co.w * msp_expf_normal(-sigma));
+            if (alpha < 1.f / 255.f) continue;
+            const float next_T = T * (1.f - alpha);
+            if (next_T <= 1e-4f) {
+                last = b0 + t - 1;
+                done = true;
+                break;
+            }
+            const float vis = alpha * T;
+            const float4 rgb = s_rgb[t];
+            c0 = fmaf(rgb.x, vis, c0);
+            c1 = fmaf(rgb.y, vis, c1);
+            c2 = fmaf(rgb.z, vis, c2);
+            T = next_T;
+            last = b0 + t;
+        }
+    }
+    if (!inside) return;
+    const size_t pix = (size_t)py * W + px;
+    if (CHUNKED) {
+        const size_t o = (size_t)k * ((size_t)W * H) + pix;
+        chunk_T[o] = T;
+        chunk_C[3 * o] = c0;
+        chunk_C[3 * o + 1] = c1;
+        chunk_C[3 * o + 2] = c2;
+        chunk_idx[o] = last;
+    } else {
+        final_T[pix] = T;
+        final_idx[pix] = last;
+        out_img[3 * pix] = saturatef_ref(fmaf(P->bg[0], T, c0));
+        out_img[3 * pix + 1] = saturatef_ref(fmaf(P->bg[1], T, c1));
+        out_img[3 * pix + 2] = saturatef_ref(fmaf(P->bg[2], T, c2));
+    }
+}
+
+// Merge of the depth chunks, rasterize_forward_merge_kernel
+// (msplat_metal.metal:2746-2799).  Only chunks that hold Gaussians were
+// written; the reference's loop stops at the first empty chunk, so those are
+// the only ones it reads.
+__global__ void __launch_bounds__(256)
+merge_chunks_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
+                    const float* __restrict__ chunk_T, const float* __restrict__ chunk_C,
+                    int* __restrict__ chunk_idx, float* __restrict__ out_img,
+                    float* __restrict__ final_T, int* __restrict__ final_idx)
+{
+    const int W = P->img_w, H = P->img_h;
+    const int px = blockIdx.x * 16 + (threadIdx.x & 15);
+    const int py = blockIdx.y * 16 + (threadIdx.x >> 4);
+    if (px >= W || py >= H) return;
+    const size_t NP = (size_t)W * H;
+    const size_t pix = (size_t)py * W + px;
+    const int tile = (py / kBlockY) * P->tiles_x + (px / kBlockX);
+    const long long cap = P->capacity;
+    const int fbeg = (int)min((long long)offset[tile], cap);
+    const int fend = (int)min((long long)offset[tile + 1], cap);
+    const int K = P->k_max;
+    const int kt = min(K, (fend - fbeg + kChunk - 1) / kChunk);
+    float Tr = 1.f, r0 = 0.f, r1 = 0.f, r2 = 0.f;
+    int last_idx = -1;
+    int cutoff = kt;
+    for (int k = 0; k < kt; k++) {
+        const size_t o = (size_t)k * NP + pix;
+        const int cf = chunk_idx[o];
+        if (cf < 0 && k > 0) { cutoff = kt; break; }
+        const float cT = chunk_T[o];
+        r0 = fmaf(chunk_C[3 * o], Tr, r0);
+        r1 = fmaf(chunk_C[3 * o + 1], Tr, r1);
+        r2 = fmaf(chunk_C[3 * o + 2], Tr, r2);
+        Tr *= cT;
+        if (cf >= 0) last_idx = cf;
+        if (Tr <= 1e-4f) { cutoff = k + 1; break; }
+    }
+    for (int k = cutoff; k < kt; k++) chunk_idx[(size_t)k * NP + pix] = -1;
+    final_T[pix] = Tr;
+    final_idx[pix] = last_idx;
+    out_img[3 * pix] = saturatef_ref(fmaf(P->bg[0], Tr, r0));
+    out_img[3 * pix + 1] = saturatef_ref(fmaf(P->bg[1], Tr, r1));
+    out_img[3 * pix + 2] = saturatef_ref(fmaf(P->bg[2], Tr, r2));
+}
+
+void launch_raster_forward(const StepParams* P, int num_tiles, int k_max, int W, int H,
+                           const Buffers& B, cudaStream_t s)
+{
+    if (num_tiles <= 0) return;
+    if (k_max <= 1) {
+        raster_forward_kernel<false><<<num_tiles, kTileThreads, 0, s>>>(
+            P, B.tile_offset, B.sorted_ids, B.proj.xy, B.proj.conic_op, B.proj.rgb, B.out_img,
+            B.final_T, B.final_idx, nullptr, nullptr, nullptr);
+    } else {
+        dim3 grid(num_tiles, k_max);
+        raster_forward_kernel<true><<<grid, kTileThreads, 0, s>>>(
+            P, B.tile_offset, B.sorted_ids, B.proj.xy, B.proj.conic_op, B.proj.rgb, nullptr,
+            nullptr, nullptr, B.chunk_T, B.chunk_C, B.chunk_idx);
+        dim3 mgrid((W + 15) / 16, (H + 15) / 16);
+        merge_chunks_kernel<<<mgrid, 256, 0, s>>>(P, B.tile_offset, B.chunk_T, B.chunk_C,
+                                                  B.chunk_idx, B.out_img, B.final_T,
+                                                  B.final_idx);
+    }
+}
+
+}  // namespace msp

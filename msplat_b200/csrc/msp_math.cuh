@@ -1,0 +1,107 @@
+// msp_math.cuh -- scalar maths shared by the engine's kernels.
+//
+// The deterministic part of the step (projection, binning keys, the forward
+// raster, the loss) is compiled with --fmad=false so that a*b+c is never
+// contracted; explicit fmaf() is used exactly where the reference kernels
+// call fma() (core/metal/msplat_metal.metal).  exp() is msp_expf(), the
+// method below; sqrt and division are IEEE round-to-nearest (no fast math),
+// and rsqrt(x) is 1.0f/sqrtf(x).  The CPU oracle evaluates the same
+// sequences, which makes tile membership, per-tile order and the forward
+// image bit-identical between the two.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace msp {
+
+constexpr int kBlockX = 16;
+constexpr int kBlockY = 16;
+constexpr int kTileThreads = kBlockX * kBlockY;  // one thread per pixel of a tile
+constexpr int kChunk = 512;                      // depth chunk of the chunked raster
+
+__device__ __forceinline__ float pow2i(int e) { return __int_as_float((e + 127) << 23); }
+
+// exp(x): Cody & Waite (1980) argument reduction x = k*ln2 + r with ln2
+// split into a 12-bit-exact high part and a low part, then the degree-7
+// Taylor polynomial of e^r (|r| <= ln2/2, truncation error < 1e-8 relative)
+// in Horner form, and an exact two-step scale by 2^k.
+__device__ __forceinline__ float expf_poly(float x, float* kout)
+{
+    const float log2e = 1.44269502162933349609375f;
+    const float ln2_hi = 0.693145751953125f;
+    const float ln2_lo = 1.428606765330187045e-06f;
+    float k = rintf(__fmul_rn(x, log2e));
+    float r = fmaf(-k, ln2_hi, x);
+    r = fmaf(-k, ln2_lo, r);
+    float p = 1.98412698412698413e-04f;
+    p = fmaf(p, r, 1.38888888888888889e-03f);
+    p = fmaf(p, r, 8.33333333333333333e-03f);
+    p = fmaf(p, r, 4.16666666666666667e-02f);
+    p = fmaf(p, r, 1.66666666666666667e-01f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    *kout = k;
+    return p;
+}
+
+__device__ __forceinline__ float msp_expf(float x)
+{
+    if (x != x) return x + x;
+    if (x > 88.72283935546875f) return __int_as_float(0x7f800000);
+    if (x < -103.97208404541015625f) return 0.0f;
+    float k;
+    float p = expf_poly(x, &k);
+    int ki = (int)k;
+    int e1 = ki / 2;
+    int e2 = ki - e1;
+    return __fmul_rn(__fmul_rn(p, pow2i(e1)), pow2i(e2));
+}
+
+// Same value as msp_expf for x in [-87, 88] (normal results): the single
+// scale p*2^k is exact there, as is the two-step one.
+__device__ __forceinline__ float msp_expf_normal(float x)
+{
+    float k;
+    float p = expf_poly(x, &k);
+    return __fmul_rn(p, pow2i((int)k));
+}
+
+__device__ __forceinline__ float rsqrt_ieee(float x) { return __fdiv_rn(1.0f, __fsqrt_rn(x)); }
+
+// Truncating float->int; saturates and maps NaN to 0.
+__device__ __forceinline__ int f2i(float x) { return __float2int_rz(x); }
+
+__device__ __forceinline__ float sigmoid_ref(float x) { return __fdiv_rn(1.f, 1.f + msp_expf(-x)); }
+
+__device__ __forceinline__ float saturatef_ref(float x) { return fminf(fmaxf(x, 0.f), 1.f); }
+
+__device__ __forceinline__ int num_sh_bases(int degree)
+{
+    return degree == 0 ? 1 : degree == 1 ? 4 : degree == 2 ? 9 : degree == 3 ? 16 : 25;
+}
+
+// Reference SH constants (msplat_metal.metal:14-39).
+#define MSP_SH_C0 0.28209479177387814f
+#define MSP_SH_C1 0.4886025119029199f
+__device__ __constant__ static const float kSH_C2[5] = {
+    1.0925484305920792f, -1.0925484305920792f, 0.31539156525252005f,
+    -1.0925484305920792f, 0.5462742152960396f};
+__device__ __constant__ static const float kSH_C3[7] = {
+    -0.5900435899266435f, 2.890611442640554f, -0.4570457994644658f,
+    0.3731763325901154f, -0.4570457994644658f, 1.445305721320277f,
+    -0.5900435899266435f};
+__device__ __constant__ static const float kSH_C4[9] = {
+    2.5033429417967046f, (float)-1.7701307697799304, 0.9461746957575601f,
+    -0.6690465435572892f, 0.10578554691520431f, -0.6690465435572892f,
+    0.47308734787878004f, -1.7701307697799304f, 0.6258357354491761f};
+
+// 1D SSIM window (msplat_metal.metal:3041-3045).
+__device__ __constant__ static const float kGauss1D[11] = {
+    0.0010283801f, 0.0075987581f, 0.0360007721f, 0.1093606895f, 0.2130055377f,
+    0.2660117249f,
+    0.2130055377f, 0.1093606895f, 0.0360007721f, 0.0075987581f, 0.0010283801f};
+constexpr float kSsimC1 = 0.0001f;
+constexpr float kSsimC2 = 0.0009f;
+
+}  // namespace msp

@@ -1,0 +1,71 @@
+"""Shared set-up for parity tests: one scene, one camera, the engine (through
+the C-ABI) and the CPU oracle on identical float32 inputs."""
+from __future__ import annotations
+
+import numpy as np
+
+from msplat_b200 import camera, engine, synthetic
+from oracle import oracle
+
+BG = engine.DEFAULT_BG
+
+
+def setup_cam(cam, step=10**9, sh_degree=3, interval=1000, rest_bases=15):
+    return camera.prepare_camera(cam, step=step, sh_degree=sh_degree, sh_degree_interval=interval,
+                                 rest_bases=rest_bases)
+
+
+def tile_ids_engine(cs, n_isect):
+    T = cs.tile_bounds[0] * cs.tile_bounds[1]
+    off = engine.debug_buffer("tile_offset", T + 1, np.int32)
+    ids = engine.debug_buffer("sorted_ids", int(off[-1]), np.int32)
+    return off, ids
+
+
+def oracle_ranges(run, cs):
+    T = cs.tile_bounds[0] * cs.tile_bounds[1]
+    tb = run.tile_bins.reshape(T, 2)
+    return tb, run.gaussian_ids[: run.num_isects]
+
+
+def engine_forward_dump(n, cs):
+    xy = engine.debug_buffer("xy", 2 * n, np.float32)
+    depth = engine.debug_buffer("depth", n, np.float32)
+    radii = engine.debug_buffer("radii", n, np.int32)
+    co = engine.debug_buffer("conic_op", 4 * n, np.float32).reshape(n, 4)
+    rgb = engine.debug_buffer("rgb", 4 * n, np.float32).reshape(n, 4)
+    P = cs.width * cs.height
+    img = engine.debug_buffer("out_img", 3 * P, np.float32)
+    fT = engine.debug_buffer("final_T", P, np.float32)
+    fi = engine.debug_buffer("final_idx", P, np.int32)
+    return dict(xy=xy, depth=depth, radii=radii, conic=co[:, :3], opac=co[:, 3], rgb=rgb[:, :3],
+                img=img, final_T=fT, final_idx=fi)
+
+
+def assert_forward_bitexact(run, eng, cs):
+    n = eng["radii"].shape[0]
+    np.testing.assert_array_equal(eng["radii"], run.radii)
+    vis = run.radii > 0
+    np.testing.assert_array_equal(eng["xy"].reshape(n, 2)[vis], run.xys.reshape(n, 2)[vis])
+    np.testing.assert_array_equal(eng["depth"][vis], run.depths[vis])
+    np.testing.assert_array_equal(eng["conic"][vis], run.conics.reshape(n, 3)[vis])
+    np.testing.assert_array_equal(eng["rgb"][vis], run.colors.reshape(n, 3)[vis])
+    off, ids = tile_ids_engine(cs, run.num_isects)
+    tb, oids = oracle_ranges(run, cs)
+    np.testing.assert_array_equal(off[:-1], tb[:, 0])
+    np.testing.assert_array_equal(off[1:], tb[:, 1])
+    np.testing.assert_array_equal(ids, oids)
+    np.testing.assert_array_equal(eng["final_idx"], run.final_idx)
+    np.testing.assert_array_equal(eng["final_T"], run.final_T)
+    np.testing.assert_array_equal(eng["img"], run.out_img)
+
+
+def close(a, b, rtol, atol_frac):
+    """|a-b| <= rtol*max(|a|,|b|) + atol_frac*max|b| (the combined tolerance
+    for float-atomic reductions)."""
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    scale = max(float(np.abs(b).max()) if b.size else 0.0, 1e-30)
+    tol = rtol * np.maximum(np.abs(a), np.abs(b)) + atol_frac * scale
+    bad = np.abs(a - b) > tol
+    return int(bad.sum()), float((np.abs(a - b) / scale).max()) if a.size else 0.0

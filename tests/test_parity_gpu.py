@@ -1,0 +1,208 @@
+"""Parity of the CUDA engine (called through its C-ABI) against the CPU
+oracle on identical seeded inputs.
+
+Bars (north star): per-tile intersection counts and per-tile sorted id lists
+bit-exact; the forward (image, final T, last index) bit-exact, which is
+stricter than the 1e-5 absolute image bar; v_rendered bit-exact; raster
+gradients and Adam-updated parameters within 1e-4 relative plus a small
+absolute floor (the backward sums with float atomics in a different order
+than the oracle's double-precision sums).
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+from msplat_b200 import _lib, camera, engine, synthetic
+from oracle import oracle
+from tests import harness
+
+pytestmark = pytest.mark.gpu
+
+GRAD_RTOL = 1e-4
+GRAD_ATOL_FRAC = 2e-6     # absolute floor, as a fraction of the tensor's max |value|
+PARAM_RTOL = 1e-4
+
+
+@pytest.fixture(scope="module", autouse=True)
+def gpu():
+    import torch
+    assert torch.cuda.is_available(), "GPU parity tests need a CUDA device"
+    engine.bind_stream()
+    yield
+    from msplat_b200 import _lib
+    _lib.load().cleanup_msplat_cuda()
+
+
+def _render_pair(g, cam_setup):
+    model = engine.GaussianModel(g.groups())
+    engine.render(model, cam_setup)
+    eng = harness.engine_forward_dump(g.n, cam_setup)
+    run = oracle.Run(cam_setup, g.n)
+    run.render(g.groups())
+    return run, eng
+
+
+def _scene(n, w, h, seed=0, mean_range=1.0, log_mu=math.log(0.02), log_sigma=0.3, distance=3.0,
+           clusters=0):
+    g = synthetic.gaussians(n, seed, mean_range=mean_range, log_scale_mu=log_mu,
+                            log_scale_sigma=log_sigma, clusters=clusters)
+    cam = synthetic.front_camera(w, h, distance)
+    return g, harness.setup_cam(cam)
+
+
+def test_render_c0_chunked_bitexact():
+    g, cams = synthetic.scene("C0")
+    cs = harness.setup_cam(cams[0])
+    run, eng = _render_pair(g, cs)
+    assert run.P.k_max > 1  # 256 tiles < 400: the chunked path
+    assert run.S.max_tile_count > 2048  # C0 exceeds the reference's per-tile cap
+    harness.assert_forward_bitexact(run, eng, cs)
+
+
+def test_render_monolithic_bitexact():
+    g, cs = _scene(40_000, 640, 480, seed=3)
+    run, eng = _render_pair(g, cs)
+    assert run.P.k_max == 1
+    harness.assert_forward_bitexact(run, eng, cs)
+
+
+def test_render_ragged_image_bitexact():
+    g, cs = _scene(6_000, 100, 75, seed=4)
+    run, eng = _render_pair(g, cs)
+    harness.assert_forward_bitexact(run, eng, cs)
+
+
+def test_render_sphere_camera_bitexact():
+    g = synthetic.gaussians(60_000, 5, mean_range=2.0, log_scale_mu=math.log(0.01),
+                            log_scale_sigma=0.4)
+    cams = synthetic.fibonacci_cameras(16, 4.0, 648, 420)
+    for cam in cams[:3]:
+        cs = harness.setup_cam(cam)
+        run, eng = _render_pair(g, cs)
+        harness.assert_forward_bitexact(run, eng, cs)
+
+
+def test_big_tiles_merge_sort_bitexact():
+    # Everything piles into a few tiles: lists longer than the 4096-key
+    # shared-memory sort take the merge path.
+    g, cs = _scene(30_000, 320, 240, seed=6, clusters=2, log_mu=math.log(0.03), log_sigma=0.5)
+    run, eng = _render_pair(g, cs)
+    assert run.S.max_tile_count > 4096
+    harness.assert_forward_bitexact(run, eng, cs)
+
+
+def test_render_all_culled():
+    g, cs = _scene(1_000, 64, 64, seed=7, distance=-3.0)  # everything behind the camera
+    run, eng = _render_pair(g, cs)
+    assert (run.radii == 0).all()
+    harness.assert_forward_bitexact(run, eng, cs)
+    img = eng["img"].reshape(64, 64, 3)
+    np.testing.assert_allclose(img, np.broadcast_to(np.float32(engine.DEFAULT_BG), img.shape))
+
+
+def test_render_single_gaussian():
+    g, cs = _scene(1, 48, 48, seed=8, mean_range=0.01)
+    run, eng = _render_pair(g, cs)
+    harness.assert_forward_bitexact(run, eng, cs)
+
+
+# ---------------------------------------------------------------------------
+# Training steps
+# ---------------------------------------------------------------------------
+
+def _train_pair(g, cs, gt, steps=1, dtu=None, ssim_weight=0.2):
+    import torch
+    if dtu is not None:
+        cs.degrees_to_use = dtu
+    model = engine.GaussianModel(g.groups())
+    gt_dev = torch.as_tensor(gt).cuda().contiguous()
+    params = [x.copy() for x in g.groups()]
+    m = [np.zeros_like(x) for x in params]
+    v = [np.zeros_like(x) for x in params]
+    st = [np.zeros(g.n, np.float32) for _ in range(3)]
+    for _ in range(steps):
+        engine.train_step(model, cs, gt_dev, ssim_weight=ssim_weight)
+        steps_sz, bc2 = model.adam_scalars()
+        run = oracle.Run(cs, g.n, ssim_weight=ssim_weight, adam_steps=steps_sz, adam_bc2=bc2)
+        run.train_step(params, m, v, gt, *st)
+    torch.cuda.synchronize()
+    return model, run, params, m, v, st
+
+
+def _report(label, bad, worst):
+    print(f"  {label}: out-of-tolerance={bad} worst|diff|/max={worst:.3g}")
+
+
+def _check_train(model, run, params, m, v, st, cs, check_grads=True, exact_forward=True):
+    n = model.n
+    P = cs.width * cs.height
+    v_rend = engine.debug_buffer("v_rendered", 3 * P, np.float32)
+    if exact_forward:
+        # one step from identical inputs: the loss gradient is bit-exact
+        np.testing.assert_array_equal(v_rend, run.v_rendered)
+    else:
+        bad, worst = harness.close(v_rend, run.v_rendered, 1e-3, 1e-4)
+        _report("v_rendered", bad, worst)
+        assert bad <= max(1, P // 2000)
+    vis = run.radii > 0
+    if check_grads:
+        ga = engine.debug_buffer("grad_acc", 9 * n, np.float32).reshape(n, 9)
+        for name, eng_cols, ref in (("v_rgb", ga[:, 0:3], run.v_rgb.reshape(n, 3)),
+                                    ("v_conic", ga[:, 3:6], run.v_conic.reshape(n, 3)),
+                                    ("v_xy", ga[:, 6:8], run.v_xy.reshape(n, 2)),
+                                    ("v_opacity", ga[:, 8:9], run.v_opacity.reshape(n, 1))):
+            bad, worst = harness.close(eng_cols[vis], ref[vis], GRAD_RTOL, GRAD_ATOL_FRAC)
+            _report(name, bad, worst)
+            assert bad == 0, f"{name}: {bad} entries out of tolerance (worst {worst:.3g} of max)"
+    names = ("means", "scales", "quats", "features_dc", "features_rest", "opacities")
+    for gi, name in enumerate(names):
+        e_p = model.params[gi].cpu().numpy()
+        e_m = model.exp_avg[gi].cpu().numpy()
+        e_v = model.exp_avg_sq[gi].cpu().numpy()
+        for label, a, b in (("param", e_p, params[gi]), ("exp_avg", e_m, m[gi]),
+                            ("exp_avg_sq", e_v, v[gi])):
+            bad, worst = harness.close(a, b, PARAM_RTOL, 1e-6)
+            _report(f"{name}.{label}", bad, worst)
+            assert bad == 0, f"{name}.{label}: {bad} out of tolerance (worst {worst:.3g})"
+    for label, a, b in (("vis_counts", model.vis_counts, st[0]), ("grad_norm", model.xys_grad_norm, st[1]),
+                        ("max_2d", model.max_2d_size, st[2])):
+        bad, worst = harness.close(a.cpu().numpy(), b, GRAD_RTOL, GRAD_ATOL_FRAC)
+        assert bad == 0, f"{label}: {bad} out of tolerance (worst {worst:.3g})"
+
+
+def test_train_step_c0():
+    g, cams = synthetic.scene("C0")
+    cs = harness.setup_cam(cams[0])
+    gt = synthetic.target_image(cs.width, cs.height, 1)
+    out = _train_pair(g, cs, gt)
+    _check_train(*out, cs)
+    run = out[1]
+    assert abs(_lib.load().msplat_last_loss(1) - run.loss) <= 1e-4 * abs(run.loss)
+
+
+def test_train_step_monolithic():
+    g, cs = _scene(40_000, 640, 480, seed=9)
+    gt = synthetic.target_image(cs.width, cs.height, 2)
+    _check_train(*_train_pair(g, cs, gt), cs)
+
+
+@pytest.mark.parametrize("dtu", [0, 1, 2])
+def test_train_step_partial_sh(dtu):
+    g, cs = _scene(8_000, 160, 120, seed=10 + dtu)
+    gt = synthetic.target_image(cs.width, cs.height, 3)
+    _check_train(*_train_pair(g, cs, gt, dtu=dtu), cs)
+
+
+def test_train_three_steps():
+    g, cs = _scene(20_000, 480, 320, seed=12)
+    gt = synthetic.target_image(cs.width, cs.height, 4)
+    _check_train(*_train_pair(g, cs, gt, steps=3), cs, check_grads=False, exact_forward=False)
+
+
+def test_train_step_l1_only():
+    g, cs = _scene(8_000, 128, 96, seed=13)
+    gt = synthetic.target_image(cs.width, cs.height, 5)
+    _check_train(*_train_pair(g, cs, gt, ssim_weight=0.0), cs)
