@@ -95,7 +95,9 @@ static int init_engine()
         return MSPLAT_ERR_CUDA;
     }
     MSP_CUDA(cudaGetDevice(&g.device));
-    MSP_CUDA(cudaStreamCreateWithFlags(&g.own_stream, cudaStreamNonBlocking));
+    // A blocking stream: ordered with the legacy default stream, so callers
+    // that never pick a stream still see their own prior work completed.
+    MSP_CUDA(cudaStreamCreateWithFlags(&g.own_stream, cudaStreamDefault));
     MSP_CUDA(cudaMalloc(&g.d_params, sizeof(StepParams)));
     MSP_CUDA(cudaMallocHost(&g.h_ring, sizeof(StepParams) * kRing));
     for (int i = 0; i < kRing; i++) MSP_CUDA(cudaEventCreateWithFlags(&g.ring_ev[i], cudaEventDisableTiming));

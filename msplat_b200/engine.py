@@ -32,11 +32,30 @@ def _torch():
 
 
 def bind_stream() -> None:
-    """Run engine work on torch's current CUDA stream."""
+    """Run engine work on torch's current CUDA stream.  When that is the
+    legacy default stream (handle 0, which the C-ABI reads as "the engine's
+    own stream"), torch is first moved to a dedicated stream so torch ops,
+    CUDA events and engine kernels share one stream."""
     torch = _torch()
     lib = _lib.load()
-    _lib.check(lib.msplat_set_stream(C.c_void_p(torch.cuda.current_stream().cuda_stream)),
-               "msplat_set_stream")
+    cur = torch.cuda.current_stream()
+    if cur.cuda_stream == 0:
+        cur = torch.cuda.Stream()
+        torch.cuda.set_stream(cur)
+    _lib.check(lib.msplat_set_stream(C.c_void_p(cur.cuda_stream)), "msplat_set_stream")
+
+
+def adam_scalars(step_count: int, lr, beta1: float = 0.9, beta2: float = 0.999):
+    """Per-group lr/bc1 and sqrt(bc2) as Model::fullIteration forms them
+    (model.cpp:558-571): bc = 1 - std::pow(float beta, int t), where the
+    power is taken in double, then every value is a float."""
+    b1 = float(f32(beta1))
+    b2 = float(f32(beta2))
+    bc1 = f32(1.0 - b1 ** step_count)
+    bc2 = f32(1.0 - b2 ** step_count)
+    steps = [f32(f32(x) / bc1) for x in lr]
+    bc2s = [f32(math.sqrt(float(bc2)))] * len(lr)
+    return steps, bc2s
 
 
 class GaussianModel:
@@ -65,16 +84,7 @@ class GaussianModel:
         return int(self.params[4].shape[1])
 
     def adam_scalars(self):
-        """bc1/bc2 and per-group lr/bc1 exactly as Model::fullIteration
-        (model.cpp:558-571): std::pow(float, int) promotes to double."""
-        t = self.step_count
-        b1 = float(f32(self.beta1))
-        b2 = float(f32(self.beta2))
-        bc1 = f32(1.0 - b1 ** t)
-        bc2 = f32(1.0 - b2 ** t)
-        steps = [f32(f32(lr) / bc1) for lr in self.lr]
-        bc2s = [f32(math.sqrt(float(bc2)))] * 6
-        return steps, bc2s
+        return adam_scalars(self.step_count, self.lr, self.beta1, self.beta2)
 
     def schedule_means_lr(self, step: int, max_steps: int) -> None:
         """Model::schedulersStep (model.cpp:179-182)."""

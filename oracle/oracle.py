@@ -47,6 +47,21 @@ class State(C.Structure):
 
 
 _lib = None
+_ref = None
+REF_PATH = os.path.join(HERE, "_ref", "libmsplat_ref.so")
+
+
+def load_ref():
+    """The reference's own kernels built through the MSL shim
+    (oracle/ref_shim/build_ref.py); None when it was not built."""
+    global _ref
+    if _ref is None and os.path.exists(REF_PATH):
+        lib = C.CDLL(REF_PATH)
+        for name in ("ref_train_step", "ref_render", "ref_tile_cap"):
+            getattr(lib, name).restype = C.c_int
+        lib.ref_set_threads.argtypes = [C.c_int]
+        _ref = lib
+    return _ref
 
 
 def build() -> str:
@@ -140,24 +155,32 @@ class Run:
     def loss(self) -> float:
         return float(self.S.loss)
 
-    def render(self, groups) -> None:
-        lib = load()
+    def render(self, groups, impl: str = "oracle") -> int:
+        """impl "oracle" runs the C restatement, "reference" the reference's
+        kernels through the shim (returns 1 when a tile overflowed its cap)."""
         arrs = [np.ascontiguousarray(g, dtype=np.float32) for g in groups]
         ptrs = (_FP * 6)(*[_fp(a) for a in arrs])
-        rc = lib.orc_render(C.byref(self.P), C.byref(self.S), ptrs)
+        if impl == "reference":
+            return int(load_ref().ref_render(C.byref(self.P), C.byref(self.S), ptrs))
+        rc = load().orc_render(C.byref(self.P), C.byref(self.S), ptrs)
         if rc != 0:
             raise RuntimeError("oracle: intersection capacity too small")
+        return 0
 
-    def train_step(self, params, exp_avg, exp_avg_sq, gt, vis_counts, grad_norm, max_2d) -> None:
+    def train_step(self, params, exp_avg, exp_avg_sq, gt, vis_counts, grad_norm, max_2d,
+                   impl: str = "oracle") -> int:
         """Updates params / moments / statistics in place (float32 arrays)."""
-        lib = load()
         pp = (_FP * 6)(*[_fp(a) for a in params])
         mm = (_FP * 6)(*[_fp(a) for a in exp_avg])
         vv = (_FP * 6)(*[_fp(a) for a in exp_avg_sq])
-        rc = lib.orc_train_step(C.byref(self.P), C.byref(self.S), pp, mm, vv, _fp(gt),
-                                _fp(vis_counts), _fp(grad_norm), _fp(max_2d))
+        args = (C.byref(self.P), C.byref(self.S), pp, mm, vv, _fp(gt), _fp(vis_counts),
+                _fp(grad_norm), _fp(max_2d))
+        if impl == "reference":
+            return int(load_ref().ref_train_step(*args))
+        rc = load().orc_train_step(*args)
         if rc != 0:
             raise RuntimeError("oracle: intersection capacity too small")
+        return 0
 
 
 def expf(x: float) -> float:

@@ -1,0 +1,227 @@
+"""Build the reference's own kernels (msplat core/metal/msplat_metal.metal) as
+a CPU library, oracle/_ref/libmsplat_ref.so, through the MSL shim.
+
+TEST INFRASTRUCTURE ONLY.  Reads the reference where it lies (read-only);
+writes only under oracle/_ref/ (git-ignored; it travels to the GPU box).
+Nothing of the reference is copied into the repository.
+
+Mechanical transforms applied to the kernel source before compiling it as
+C++ (each keeps the reference's arithmetic; see DESIGN.md for why):
+  1. the Metal header include and `using namespace metal` are dropped;
+     address-space qualifiers become C++ (constant -> const, device/thread ->
+     nothing, kernel -> nothing) and [[attributes]] are removed;
+  2. overloads that differ only in address space (identical bodies) are kept
+     once;
+  3. only the kernels msplat_train_step / msplat_render dispatch are kept;
+  4. each `threadgroup T name[...]` becomes a reference to per-threadgroup
+     storage of the shim (filled with 0x7F bytes per threadgroup);
+  5. MAX_TILE_ELEMS (the per-tile cap, 2048) becomes overridable; the default
+     build raises it (REF_TILE_CAP) so no tile overflows;
+  6. in rasterize_backward*_kernel every lane reads the batch entry that the
+     reference reads on lane 0 and then broadcasts (the `if (wr == 0)` guard
+     of that load only, not of the atomics), which gives the broadcast a
+     defined value when lane 0 has returned;
+  7. in rasterize_backward_chunked_kernel a thread whose pixel has no
+     contributor in the chunk no longer returns early (only empty chunks
+     return): the reference's early return leaves that thread's share of the
+     cooperative batch load unwritten (other lanes then read stale
+     threadgroup memory as Gaussian data) and, when the thread is lane 0,
+     drops its SIMD-group's atomics.  Kept in the loop, the thread adds
+     nothing, since every index exceeds its bin_final.
+"""
+from __future__ import annotations
+
+import os
+import re
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE = os.path.dirname(HERE)
+OUT = os.path.join(ORACLE, "_ref")
+REFERENCE = os.environ.get("MSPLAT_REFERENCE", "/root/reference")
+METAL = os.path.join(REFERENCE, "core", "metal", "msplat_metal.metal")
+REF_TILE_CAP = int(os.environ.get("REF_TILE_CAP", "16384"))
+
+KERNELS = {
+    "project_and_sh_forward_kernel", "scatter_to_prealloc_bins_kernel", "prefix_sum_kernel",
+    "bitonic_sort_per_tile_kernel", "nd_rasterize_forward_kernel",
+    "rasterize_forward_chunked_kernel", "rasterize_forward_merge_kernel", "ssim_h_fwd_kernel",
+    "ssim_fused_v_fwd_h_bwd_kernel", "ssim_v_bwd_kernel", "rasterize_backward_kernel",
+    "compute_chunk_prefix_suffix_kernel", "rasterize_backward_chunked_kernel",
+    "project_and_sh_backward_kernel", "fused_adam_kernel", "accumulate_grad_stats_kernel",
+}
+BWD_KERNELS = {"rasterize_backward_kernel", "rasterize_backward_chunked_kernel"}
+
+
+def strip_comments(s: str) -> str:
+    s = re.sub(r"/\*.*?\*/", "", s, flags=re.S)
+    return re.sub(r"//[^\n]*", "", s)
+
+
+def split_top_level(src: str):
+    """Yield ('pp', line) / ('item', text) top-level units."""
+    i, n = 0, len(src)
+    buf = []
+    while i < n:
+        if src[i] == "#" and (i == 0 or src[i - 1] == "\n"):
+            j = src.find("\n", i)
+            j = n if j < 0 else j
+            if "".join(buf).strip():
+                yield ("item", "".join(buf))
+                buf = []
+            yield ("pp", src[i:j])
+            i = j + 1
+            continue
+        c = src[i]
+        buf.append(c)
+        if c == ";" and not any(ch == "{" for ch in "".join(buf)):
+            yield ("item", "".join(buf))
+            buf = []
+        elif c == "{":
+            depth = 1
+            i += 1
+            while i < n and depth:
+                buf.append(src[i])
+                depth += {"{": 1, "}": -1}.get(src[i], 0)
+                i += 1
+            # struct definitions end with ';'
+            k = i
+            while k < n and src[k] in " \t\n":
+                k += 1
+            if k < n and src[k] == ";":
+                buf.append(";")
+                i = k + 1
+            yield ("item", "".join(buf))
+            buf = []
+            continue
+        i += 1
+    if "".join(buf).strip():
+        yield ("item", "".join(buf))
+
+
+ADDR = re.compile(r"\b(device|thread|constant|threadgroup)\b")
+
+
+def signature_key(head: str) -> str:
+    h = re.sub(r"\[\[[^\]]*\]\]", "", head)
+    h = re.sub(r"\bconstant\b", "const", h)
+    h = re.sub(r"\b(device|thread|inline)\b", "", h)
+    h = re.sub(r"\b[A-Za-z_]\w*\s*(?=[,)])", "", h)  # drop parameter names
+    return re.sub(r"\s+", "", h)
+
+
+TG_DECL = re.compile(r"threadgroup\s+([\w:]+)\s+([^;]+);")
+
+
+def rewrite_tg(body: str, counter: list) -> str:
+    def repl(m):
+        typ, decls = m.group(1), m.group(2)
+        out = []
+        for d in re.split(r",\s*(?![^\[]*\])", decls):
+            dm = re.match(r"\s*(\w+)\s*((?:\[[^\]]+\])+)\s*$", d)
+            if not dm:
+                raise ValueError(f"unhandled threadgroup declaration: {d!r}")
+            name, dims = dm.group(1), dm.group(2)
+            counter[0] += 1
+            out.append(f"{typ} (&{name}){dims} = msl::tg_array<{typ}{dims}, {counter[0]}>();")
+        return " ".join(out)
+    return TG_DECL.sub(repl, body)
+
+
+def transform(src: str) -> str:
+    src = strip_comments(src)
+    src = src.replace("#include <metal_stdlib>", "")
+    src = re.sub(r"using\s+namespace\s+metal\s*;", "", src)
+    out, seen = [], set()
+    counter = [0]
+    for kind, text in split_top_level(src):
+        if kind == "pp":
+            m = re.match(r"#define\s+MAX_TILE_ELEMS\s+(\d+)", text)
+            if m:
+                out.append(f"#ifndef MAX_TILE_ELEMS\n#define MAX_TILE_ELEMS {m.group(1)}\n#endif")
+            else:
+                out.append(text)
+            continue
+        t = text.strip()
+        if "{" in t and "(" in t.split("{", 1)[0] and not t.startswith("struct"):
+            head, body = t.split("{", 1)
+            name = re.search(r"(\w+)\s*\(", head).group(1)
+            is_kernel = re.search(r"\bkernel\b", head) is not None
+            if is_kernel and name not in KERNELS:
+                continue
+            if not is_kernel:
+                key = signature_key(head)
+                if key in seen:
+                    continue
+                seen.add(key)
+            body = rewrite_tg(body, counter)
+            if name in BWD_KERNELS:
+                # only the batch-entry load that feeds simd_broadcast, not the
+                # lane-0 atomics that follow the reductions
+                body, n_sub = re.subn(r"if\s*\(\s*wr\s*==\s*0\s*\)\s*\{(\s*b_conic\s*=)",
+                                      r"if (true) {\1", body)
+                if n_sub != 1:
+                    raise ValueError(f"{name}: expected one broadcast load block, found {n_sub}")
+            if name == "rasterize_backward_chunked_kernel":
+                # threads without a contributor in the chunk stay in the
+                # threadgroup (they still load their batch entries and add
+                # nothing: every index exceeds their bin_final)
+                body, n_sub = re.subn(
+                    r"if\s*\(\s*chunk_start\s*>=\s*chunk_end\s*\|\|\s*bin_final\s*<\s*chunk_start\s*\)",
+                    "if (chunk_start >= chunk_end)", body)
+                if n_sub != 1:
+                    raise ValueError("chunked backward: early-return test not found")
+            t = head + "{" + body
+        out.append(t)
+    code = "\n".join(out)
+    code = re.sub(r"\[\[[^\]]*\]\]", "", code)
+    return code
+
+
+PRELUDE = """// Generated by oracle/ref_shim/build_ref.py from the reference's
+// core/metal/msplat_metal.metal -- do not edit, do not commit.
+#include "msl_shim.hpp"
+namespace msl {
+#define kernel
+#define device
+#define thread
+#define constant const
+"""
+EPILOGUE = """
+#undef kernel
+#undef device
+#undef thread
+#undef constant
+}  // namespace msl
+"""
+
+
+def build(verbose: bool = False) -> str:
+    if not os.path.exists(METAL):
+        raise FileNotFoundError(f"reference kernels not found at {METAL}")
+    os.makedirs(OUT, exist_ok=True)
+    gen = os.path.join(OUT, "msplat_metal_ref.inc")
+    code = PRELUDE + transform(open(METAL).read()) + EPILOGUE
+    if not os.path.exists(gen) or open(gen).read() != code:
+        with open(gen, "w") as f:
+            f.write(code)
+    lib = os.path.join(OUT, "libmsplat_ref.so")
+    srcs = [os.path.join(HERE, "ref_driver.cpp"), os.path.join(HERE, "msl_runtime.cpp")]
+    deps = srcs + [gen, os.path.join(HERE, "msl_shim.hpp"), os.path.join(HERE, "msl_runtime.hpp"),
+                   os.path.join(ORACLE, "msplat_oracle.h")]
+    if os.path.exists(lib) and all(os.path.getmtime(d) <= os.path.getmtime(lib) for d in deps):
+        return lib
+    cmd = ["g++", "-std=c++20", "-O2", "-ffp-contract=off", "-fno-fast-math", "-fopenmp", "-fPIC",
+           "-shared", "-Wno-attributes", "-Wno-unknown-pragmas", f"-DMAX_TILE_ELEMS={REF_TILE_CAP}",
+           f"-I{HERE}", f"-I{OUT}", f"-I{ORACLE}", "-o", lib, *srcs]
+    if verbose:
+        print(" ".join(cmd))
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"reference shim build failed:\n{r.stderr[-6000:]}")
+    return lib
+
+
+if __name__ == "__main__":
+    print(build(verbose="-v" in sys.argv))
