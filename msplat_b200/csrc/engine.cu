@@ -131,7 +131,7 @@ static void free_buffers()
     Buffers& B = g.B;
     void* ptrs[] = {B.proj.xy, B.proj.depth, B.proj.radii, B.proj.conic_op, B.proj.rgb, B.proj.rect,
                     B.tile_count, B.tile_offset, B.keys, B.keys_alt, B.sorted_ids, B.out_img,
-                    B.final_T, B.final_idx, B.v_rendered, B.ssim_h, B.ssim_d, B.grad_acc,
+                    B.final_T, B.final_idx, B.v_rendered, B.grad_acc,
                     B.chunk_T, B.chunk_C, B.chunk_idx, B.prefix_T, B.after_C};
     for (void* p : ptrs)
         if (p) cudaFree(p);
@@ -176,14 +176,12 @@ static int ensure(long long N, long long W, long long H, long long T, int K, boo
         if ((rc = realloc_dev(B.final_T, P))) return rc;
         if ((rc = realloc_dev(B.final_idx, P))) return rc;
         if ((rc = realloc_dev(B.v_rendered, P * 3))) return rc;
-        if ((rc = realloc_dev(B.ssim_h, P * 15))) return rc;
-        if ((rc = realloc_dev(B.ssim_d, P * 9))) return rc;
         g.cap_pix = P;
     }
     if (T > g.cap_T) {
-        if ((rc = realloc_dev(B.tile_count, T))) return rc;
+        if ((rc = realloc_dev(B.tile_count, T * kCountPitch))) return rc;
         if ((rc = realloc_dev(B.tile_offset, T + 1))) return rc;
-        MSP_CUDA(cudaMemsetAsync(B.tile_count, 0, sizeof(int) * T, g.stream()));
+        MSP_CUDA(cudaMemsetAsync(B.tile_count, 0, sizeof(int) * T * kCountPitch, g.stream()));
         g.cap_T = T;
     }
     if (K > 1 && (long long)K * P > g.cap_chunk) {
@@ -567,7 +565,7 @@ int msplat_train_step(
     launch_project_backward_adam(g.d_params, num_points, p.degrees_to_use, p.rest_stride, g.B, A, S,
                                  st);
     tm.mark(6, st);
-    g.launches += 3 + (p.k_max > 1 ? 2 : 1) + 1;
+    g.launches += 1 + (p.k_max > 1 ? 2 : 1) + 1;
     MSP_CUDA(cudaGetLastError());
     if ((rc = queue_readback(st, p))) return rc;
     if (radii_out) *radii_out = g.B.proj.radii;

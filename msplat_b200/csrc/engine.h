@@ -7,7 +7,10 @@ namespace msp {
 
 constexpr int kGroups = 6;        // means, scales, quats, features_dc, features_rest, opacities
 constexpr int kGradStride = 9;    // per-Gaussian raster gradient: v_rgb[3], v_conic[3], v_xy[2], v_opacity
-constexpr int kSortCap = 4096;    // keys sorted in shared memory in one pass
+// Tile counters are spread one per 128-byte line: every visible Gaussian
+// adds (and later subtracts) one per tile it covers, and counters sharing a
+// line would serialise those atomics in a single L2 slice.
+constexpr int kCountPitch = 32;
 
 // Per-step scalars.  Written by the host into a pinned ring slot and copied
 // into device memory on the step's stream, so every kernel reads the same
@@ -52,17 +55,15 @@ struct ProjOut {
 
 struct Buffers {
     ProjOut proj;
-    int* tile_count;       // [T]   zero between steps
+    int* tile_count;       // [T * kCountPitch] zero between steps
     int* tile_offset;      // [T+1] exclusive scan
     unsigned long long* keys;      // [capacity]
-    unsigned long long* keys_alt;  // [capacity] merge scratch for tiles > kSortCap
+    unsigned long long* keys_alt;  // [capacity] merge scratch for tiles longer than one register-sorted run
     int* sorted_ids;       // [capacity]
     float* out_img;        // [H*W*3]
     float* final_T;        // [H*W]
     int* final_idx;        // [H*W]
     float* v_rendered;     // [H*W*3]
-    float* ssim_h;         // [H*W*15]
-    float* ssim_d;         // [H*W*9]
     float* grad_acc;       // [N*9]
     float* chunk_T;        // [K*H*W]
     float* chunk_C;        // [K*H*W*3]

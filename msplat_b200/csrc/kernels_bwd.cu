@@ -11,18 +11,75 @@ namespace msp {
 // (msplat_metal.metal:898-1099) and, for depth chunks,
 // compute_chunk_prefix_suffix_kernel (:2804-2840) plus
 // rasterize_backward_chunked_kernel (:2844-3031).
-// One CTA per 16x16 tile (per (tile, chunk)), one thread per pixel, replay
-// back to front.  Each warp sums its 32 pixels' contributions to a Gaussian
-// with a transposed butterfly (8 values in 9 shuffles, the opacity term in
-// 5), then 9 lanes issue one RED each into the Gaussian's 9 contiguous
+// One CTA per 16x16 tile (per (tile, chunk)); each thread replays PPT
+// pixels, (x, y + 2h), back to front, so a warp owns a 16 x 2*PPT block.
+// Each lane adds
+// its pixels' contributions, the warp sums its lanes with
+// a transposed butterfly (8 values in 9 shuffles, the opacity term in 5),
+// then 9 lanes issue one RED each into the Gaussian's 9 contiguous
 // accumulators: v_rgb[3] (gated by the clamp mask), v_conic[3], v_xy[2],
 // v_opacity (w.r.t. the logit).
 // ---------------------------------------------------------------------------
 
 __device__ __forceinline__ float sel(bool c, float a, float b) { return c ? a : b; }
 
-template <bool CHUNKED>
-__global__ void __launch_bounds__(kTileThreads)
+// Two pixels per thread halve the per-Gaussian overhead (shared-memory
+// broadcasts, vote, warp reduction) per pixel; the 64-register cap (8 CTAs
+// of 128 threads per SM) keeps enough warps resident.  Measured at C1: 0.99
+// ms against 1.13 ms for one pixel per thread.
+constexpr int kBwdPPT = 2;
+constexpr int kBwdMinBlocks = 8;
+constexpr int kRastBatch = 256;
+
+// Back-to-front state of one pixel.
+struct PixelBwd {
+    float T, b0, b1, b2;
+    float vo0, vo1, vo2;
+    float tfb0, tfb1, tfb2;
+    int bin_final;
+};
+
+// One pixel's contribution to Gaussian (xy, co, raw) at list index idx,
+// added into v[0..8] (v_rgb, v_conic, v_xy, v_opacity); the same decisions
+// as the forward (rasterize_backward_kernel :1023-1075).
+__device__ __forceinline__ bool backprop(PixelBwd& s, float fpx, float fpy, const float2 xy,
+                                         const float4 co, const float4 raw, int idx, float v[9])
+{
+    if (idx > s.bin_final) return false;
+    const float dx = xy.x - fpx, dy = xy.y - fpy;
+    const float sigma = fmaf(0.5f, fmaf(co.x, dx * dx, co.z * dy * dy), co.y * dx * dy);
+    if (sigma < 0.f || sigma >= 5.55f) return false;
+    const float alpha = fminf(0.999f, co.w * msp_expf_normal(-sigma));
+    if (alpha < 1.f / 255.f || !(alpha < 0.999f)) return false;
+    const float ra = 1.f / (1.f - alpha);
+    s.T *= ra;
+    const float fac = alpha * s.T;
+    const float r0 = fmaxf(raw.x + 0.5f, 0.f), r1 = fmaxf(raw.y + 0.5f, 0.f),
+                r2 = fmaxf(raw.z + 0.5f, 0.f);
+    const float nra = -ra;
+    const float e0 = fmaf(r0, s.T, fmaf(-s.b0, ra, nra * s.tfb0));
+    const float e1 = fmaf(r1, s.T, fmaf(-s.b1, ra, nra * s.tfb1));
+    const float e2 = fmaf(r2, s.T, fmaf(-s.b2, ra, nra * s.tfb2));
+    const float v_alpha = (e0 * s.vo0 + e1 * s.vo1) + e2 * s.vo2;
+    s.b0 = fmaf(r0, fac, s.b0);
+    s.b1 = fmaf(r1, fac, s.b1);
+    s.b2 = fmaf(r2, fac, s.b2);
+    const float v_sigma = -alpha * v_alpha;
+    v[0] += fac * s.vo0;
+    v[1] += fac * s.vo1;
+    v[2] += fac * s.vo2;
+    const float hv = 0.5f * v_sigma;
+    v[3] += hv * (dx * dx);
+    v[4] += hv * (dx * dy);
+    v[5] += hv * (dy * dy);
+    v[6] += v_sigma * fmaf(co.x, dx, co.y * dy);
+    v[7] += v_sigma * fmaf(co.y, dx, co.z * dy);
+    v[8] += -v_sigma * (1.f - co.w);
+    return true;
+}
+
+template <bool CHUNKED, int PPT>
+__global__ void __launch_bounds__(256 / PPT, kBwdMinBlocks)
 raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
                        const int* __restrict__ ids, const float2* __restrict__ g_xy,
                        const float4* __restrict__ g_co, const float4* __restrict__ g_rgb,
@@ -31,18 +88,19 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
                        const float* __restrict__ prefix_T, const float* __restrict__ chunk_T,
                        const float* __restrict__ after_C, float* __restrict__ grad_acc)
 {
-    __shared__ int s_id[kTileThreads];
-    __shared__ float2 s_xy[kTileThreads];
-    __shared__ float4 s_co[kTileThreads];
-    __shared__ float4 s_rgb[kTileThreads];
-    __shared__ int s_wmax[kTileThreads / 32];
+    constexpr int kThreads = 256 / PPT;
+    __shared__ int s_id[kRastBatch];
+    __shared__ float2 s_xy[kRastBatch];
+    __shared__ float4 s_co[kRastBatch];
+    __shared__ float4 s_rgb[kRastBatch];
+    __shared__ int s_wmax[kThreads / 32];
     const int tile = blockIdx.x;
     const int tx_n = P->tiles_x;
     const int W = P->img_w, H = P->img_h;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int px = (tile % tx_n) * kBlockX + (tid & 15);
-    const int py = (tile / tx_n) * kBlockY + (tid >> 4);
-    const bool inside = px < W && py < H;
+    const int tx0 = (tile % tx_n) * kBlockX, ty0 = (tile / tx_n) * kBlockY;
+    const int px = tx0 + (lane & 15);
+    const int by = ty0 + warp * 2 * PPT;
     const long long cap = P->capacity;
     const int fbeg = (int)min((long long)offset[tile], cap);
     const int fend = (int)min((long long)offset[tile + 1], cap);
@@ -55,101 +113,81 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
         if (beg >= end) return;
     }
     const size_t NP = (size_t)W * H;
-    const size_t pix = inside ? (size_t)py * W + px : 0;
-    float Tf = 0.f, T = 0.f, b0 = 0.f, b1 = 0.f, b2 = 0.f;
-    float vo0 = 0.f, vo1 = 0.f, vo2 = 0.f;
-    int bin_final = beg - 1;
-    if (inside) {
-        Tf = final_T[pix];
-        vo0 = v_rendered[3 * pix];
-        vo1 = v_rendered[3 * pix + 1];
-        vo2 = v_rendered[3 * pix + 2];
-        if (CHUNKED) {
-            const size_t o = (size_t)k * NP + pix;
-            const int bf = chunk_idx[o];
-            if (bf >= beg) {
-                bin_final = bf;
-                T = prefix_T[o] * chunk_T[o];
-                b0 = after_C[3 * o];
-                b1 = after_C[3 * o + 1];
-                b2 = after_C[3 * o + 2];
+    PixelBwd st[PPT];
+    int my_max = beg - 1;
+#pragma unroll
+    for (int h = 0; h < PPT; h++) {
+        PixelBwd& s = st[h];
+        const int py = by + (lane >> 4) + 2 * h;
+        s = PixelBwd{0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, beg - 1};
+        if (px < W && py < H) {
+            const size_t pix = (size_t)py * W + px;
+            const float Tf = final_T[pix];
+            s.vo0 = v_rendered[3 * pix];
+            s.vo1 = v_rendered[3 * pix + 1];
+            s.vo2 = v_rendered[3 * pix + 2];
+            s.tfb0 = Tf * P->bg[0];
+            s.tfb1 = Tf * P->bg[1];
+            s.tfb2 = Tf * P->bg[2];
+            if (CHUNKED) {
+                const size_t o = (size_t)k * NP + pix;
+                const int bf = chunk_idx[o];
+                if (bf >= beg) {
+                    s.bin_final = bf;
+                    s.T = prefix_T[o] * chunk_T[o];
+                    s.b0 = after_C[3 * o];
+                    s.b1 = after_C[3 * o + 1];
+                    s.b2 = after_C[3 * o + 2];
+                }
+            } else {
+                s.bin_final = final_idx[pix];
+                s.T = Tf;
             }
-        } else {
-            bin_final = final_idx[pix];
-            T = Tf;
         }
+        my_max = max(my_max, s.bin_final);
     }
-    const float tfb0 = Tf * P->bg[0], tfb1 = Tf * P->bg[1], tfb2 = Tf * P->bg[2];
-    const float fpx = (float)px, fpy = (float)py;
-    const int warp_max = __reduce_max_sync(0xffffffffu, bin_final);
+    const float fpx = (float)px;
+    const int warp_max = __reduce_max_sync(0xffffffffu, my_max);
     if (lane == 0) s_wmax[warp] = warp_max;
     __syncthreads();
     int tile_max = s_wmax[0];
 #pragma unroll
-    for (int w = 1; w < kTileThreads / 32; w++) tile_max = max(tile_max, s_wmax[w]);
+    for (int w = 1; w < kThreads / 32; w++) tile_max = max(tile_max, s_wmax[w]);
     const int last = min(end - 1, tile_max);
-    float* __restrict__ acc = grad_acc;
 
-    for (int bend = last; bend >= beg; bend -= kTileThreads) {
-        const int n = min(kTileThreads, bend - beg + 1);
+    for (int bend = last; bend >= beg; bend -= kRastBatch) {
+        const int n = min(kRastBatch, bend - beg + 1);
         __syncthreads();
-        if (tid < n) {
-            const int g = ids[bend - tid];
-            s_id[tid] = g;
-            s_xy[tid] = g_xy[g];
-            s_co[tid] = g_co[g];
-            s_rgb[tid] = g_rgb[g];
+#pragma unroll
+        for (int h = 0; h < kRastBatch / kThreads; h++) {
+            const int slot = tid + h * kThreads;
+            if (slot < n) {
+                const int g = ids[bend - slot];
+                const float2 xy = g_xy[g];
+                const float4 co = g_co[g];
+                s_id[slot] = g;
+                s_xy[slot] = xy;
+                s_co[slot] = co;
+                s_rgb[slot] = g_rgb[g];
+            }
         }
         __syncthreads();
         const int t0 = max(0, bend - warp_max);
         for (int t = t0; t < n; t++) {
             const int idx = bend - t;
-            const float4 co = s_co[t];
             const float2 xy = s_xy[t];
-            const float dx = xy.x - fpx, dy = xy.y - fpy;
-            bool contrib = false;
-            float alpha = 0.f;
-            if (idx <= bin_final) {
-                const float sigma = fmaf(0.5f, fmaf(co.x, dx * dx, co.z * dy * dy), co.y * dx * dy);
-                if (!(sigma < 0.f || sigma >= 5.55f)) {
-                    alpha = fminf(0.999f, co.w * msp_expf_normal(-sigma));
-                    contrib = !(alpha < 1.f / 255.f) && alpha < 0.999f;
-                }
-            }
-            if (!__any_sync(0xffffffffu, contrib)) continue;
+            const float4 co = s_co[t];
             const float4 raw = s_rgb[t];
-            float v[8];
-            float vop = 0.f;
+            float v[9];
 #pragma unroll
-            for (int q = 0; q < 8; q++) v[q] = 0.f;
-            if (contrib) {
-                const float ra = 1.f / (1.f - alpha);
-                T *= ra;
-                const float fac = alpha * T;
-                const float r0 = fmaxf(raw.x + 0.5f, 0.f), r1 = fmaxf(raw.y + 0.5f, 0.f),
-                            r2 = fmaxf(raw.z + 0.5f, 0.f);
-                const float nra = -ra;
-                const float e0 = fmaf(r0, T, fmaf(-b0, ra, nra * tfb0));
-                const float e1 = fmaf(r1, T, fmaf(-b1, ra, nra * tfb1));
-                const float e2 = fmaf(r2, T, fmaf(-b2, ra, nra * tfb2));
-                const float v_alpha = (e0 * vo0 + e1 * vo1) + e2 * vo2;
-                b0 = fmaf(r0, fac, b0);
-                b1 = fmaf(r1, fac, b1);
-                b2 = fmaf(r2, fac, b2);
-                const float v_sigma = -alpha * v_alpha;
-                v[0] = fac * vo0;
-                v[1] = fac * vo1;
-                v[2] = fac * vo2;
-                const float hv = 0.5f * v_sigma;
-                v[3] = hv * (dx * dx);
-                v[4] = hv * (dx * dy);
-                v[5] = hv * (dy * dy);
-                v[6] = v_sigma * fmaf(co.x, dx, co.y * dy);
-                v[7] = v_sigma * fmaf(co.y, dx, co.z * dy);
-                vop = -v_sigma * (1.f - co.w);
-            }
-            // Transposed butterfly: after it, lane L holds the warp sum of
-            // value (L >> 2).
+            for (int q = 0; q < 9; q++) v[q] = 0.f;
+            bool on = false;
+#pragma unroll
+            for (int h = 0; h < PPT; h++)
+                on |= backprop(st[h], fpx, (float)(by + (lane >> 4) + 2 * h), xy, co, raw, idx, v);
+            if (!__any_sync(0xffffffffu, on)) continue;
+            // Transposed butterfly: afterwards lane L holds the warp sum of
+            // value (L >> 2); the opacity term takes a plain butterfly.
             const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4;
             float u[4];
 #pragma unroll
@@ -173,6 +211,7 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
             }
             x += __shfl_xor_sync(0xffffffffu, x, 2);
             x += __shfl_xor_sync(0xffffffffu, x, 1);
+            float vop = v[8];
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) vop += __shfl_xor_sync(0xffffffffu, vop, o);
             const int g = s_id[t];
@@ -180,9 +219,9 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
             if ((lane & 3) == 0) {
                 bool ok = x != 0.f;
                 if (j < 3) ok = ok && ((j == 0 ? raw.x : (j == 1 ? raw.y : raw.z)) + 0.5f >= 0.f);
-                if (ok) atomicAdd(acc + (size_t)g * kGradStride + j, x);
+                if (ok) atomicAdd(grad_acc + (size_t)g * kGradStride + j, x);
             } else if (lane == 1) {
-                if (vop != 0.f) atomicAdd(acc + (size_t)g * kGradStride + 8, vop);
+                if (vop != 0.f) atomicAdd(grad_acc + (size_t)g * kGradStride + 8, vop);
             }
         }
     }
@@ -231,7 +270,7 @@ void launch_raster_backward(const StepParams* P, int num_tiles, int k_max, int W
 {
     if (num_tiles <= 0) return;
     if (k_max <= 1) {
-        raster_backward_kernel<false><<<num_tiles, kTileThreads, 0, s>>>(
+        raster_backward_kernel<false, kBwdPPT><<<num_tiles, 256 / kBwdPPT, 0, s>>>(
             P, B.tile_offset, B.sorted_ids, B.proj.xy, B.proj.conic_op, B.proj.rgb, B.final_T,
             B.final_idx, B.v_rendered, nullptr, nullptr, nullptr, nullptr, B.grad_acc);
     } else {
@@ -239,7 +278,7 @@ void launch_raster_backward(const StepParams* P, int num_tiles, int k_max, int W
         chunk_prefix_suffix_kernel<<<pgrid, 256, 0, s>>>(P, B.tile_offset, B.chunk_T, B.chunk_C,
                                                          B.prefix_T, B.after_C);
         dim3 grid(num_tiles, k_max);
-        raster_backward_kernel<true><<<grid, kTileThreads, 0, s>>>(
+        raster_backward_kernel<true, kBwdPPT><<<grid, 256 / kBwdPPT, 0, s>>>(
             P, B.tile_offset, B.sorted_ids, B.proj.xy, B.proj.conic_op, B.proj.rgb, B.final_T,
             nullptr, B.v_rendered, B.chunk_idx, B.prefix_T, B.chunk_T, B.after_C, B.grad_acc);
     }
@@ -299,39 +338,87 @@ __device__ __forceinline__ void adam_elem(float* __restrict__ p, float* __restri
     *eas = v;
 }
 
-__global__ void __launch_bounds__(kBwdThreads)
+// Adam over one warp's contiguous slab of a parameter group: `total`
+// floats starting at element `e0`, `stride` floats per Gaussian.  grad_of
+// returns the element's gradient, or false when the element is not updated
+// (culled Gaussians for the SH groups).  Loads of kUnroll elements are issued
+// before any update so the warp keeps several coalesced requests in flight.
+template <int STRIDE, class G>
+__device__ __forceinline__ void adam_slab(float* __restrict__ P, float* __restrict__ M,
+                                          float* __restrict__ V, size_t e0, int total, int lane,
+                                          float step, float b1, float b2, float bc2, float eps,
+                                          G grad_of)
+{
+    constexpr int kUnroll = 4;
+    for (int base = lane; base < total; base += 32 * kUnroll) {
+        float p[kUnroll], m[kUnroll], v[kUnroll], g[kUnroll];
+        bool on[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; u++) {
+            const int e = base + 32 * u;
+            on[u] = e < total && grad_of(e / STRIDE, e % STRIDE, g[u]);
+            if (on[u]) {
+                p[u] = P[e0 + e];
+                m[u] = M[e0 + e];
+                v[u] = V[e0 + e];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; u++) {
+            if (!on[u]) continue;
+            const float mm = fmaf(b1, m[u], (1.0f - b1) * g[u]);
+            const float vv = fmaf(b2, v[u], (1.0f - b2) * g[u] * g[u]);
+            const size_t e = e0 + base + 32 * u;
+            P[e] = p[u] - step * mm / (sqrtf(vv) / bc2 + eps);
+            M[e] = mm;
+            V[e] = vv;
+        }
+    }
+}
+
+// Per-Gaussian gradient slots in shared memory (phase 1 -> phase 2).
+constexpr int kGradSlots = 12;  // v_mean[3], v_scale[3], v_quat[4], v_opacity, pad
+constexpr int kBasisSlots = 19; // 15 SH-rest basis values + v_rgb[3] (odd stride: no bank conflicts)
+
+__global__ void __launch_bounds__(kBwdThreads, 5)
 project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
                              const int* __restrict__ radii, const float4* __restrict__ g_co,
                              const float* __restrict__ grad_acc, AdamPtrs A, StatPtrs St,
                              int nb_rest)
 {
-    __shared__ float s_basis[kBwdThreads][16];
-    __shared__ float s_vrgb[kBwdThreads][4];
+    __shared__ float s_grad[kBwdThreads][kGradSlots];
+    __shared__ float s_basis[kBwdThreads][kBasisSlots];
     __shared__ int s_vis[kBwdThreads];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int base = blockIdx.x * kBwdThreads;
     const int i = base + tid;
     const float b1 = P->beta1, b2 = P->beta2, eps = P->eps;
     bool vis = false;
+    float gr[kGradSlots];
+#pragma unroll
+    for (int k = 0; k < kGradSlots; k++) gr[k] = 0.f;
     if (i < N) {
         const int rad = radii[i];
         vis = rad > 0;
-        float* means = A.param[0];
-        float* scales = A.param[1];
-        float* quats = A.param[2];
-        float vmean[3] = {0.f, 0.f, 0.f}, vscale[3] = {0.f, 0.f, 0.f};
-        float vq[4] = {0.f, 0.f, 0.f, 0.f};
-        float vop = 0.f;
         if (vis) {
+            const float* __restrict__ means = A.param[0];
+            const float* __restrict__ scales = A.param[1];
+            const float* __restrict__ quats = A.param[2];
             const float* ga = grad_acc + (size_t)i * kGradStride;
             const float vr0 = ga[0], vr1 = ga[1], vr2 = ga[2];
             const float vc0 = ga[3], vc1 = ga[4], vc2 = ga[5];
             const float vx = ga[6], vy = ga[7];
-            vop = ga[8];
+            const float vop = ga[8];
             const float p[3] = {means[3 * (size_t)i], means[3 * (size_t)i + 1], means[3 * (size_t)i + 2]};
+            const float ls0 = scales[3 * (size_t)i], ls1 = scales[3 * (size_t)i + 1],
+                        ls2 = scales[3 * (size_t)i + 2];
+            const float q0 = quats[4 * (size_t)i], q1 = quats[4 * (size_t)i + 1],
+                        q2 = quats[4 * (size_t)i + 2], q3 = quats[4 * (size_t)i + 3];
+            const float4 co = g_co[i];
             const float fx = P->fx, fy = P->fy;
             const float* vm = P->viewmat;
             const float* pm = P->projmat;
+            float vmean[3];
             // project_pix_vjp (:1216-1234); v_depth is always 0 (:1860-1864)
             const float h3 = ((pm[12] * p[0] + pm[13] * p[1]) + pm[14] * p[2]) + pm[15];
             const float rw = 1.f / (h3 + 1e-6f);
@@ -341,7 +428,6 @@ project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
             vmean[1] = ((pm[1] * vp0 + pm[5] * vp1) + pm[9] * vp2) + vm[9] * 0.f;
             vmean[2] = ((pm[2] * vp0 + pm[6] * vp1) + pm[10] * vp2) + vm[10] * 0.f;
             // cov2d_to_conic_vjp (:1253-1264): ((-X) G) X
-            const float4 co = g_co[i];
             const float X00 = -co.x, X01 = -co.y, X10 = -co.y, X11 = -co.z;
             const float XG00 = X00 * vc0 + X10 * vc1, XG01 = X01 * vc0 + X11 * vc1;
             const float XG10 = X00 * vc1 + X10 * vc2, XG11 = X01 * vc1 + X11 * vc2;
@@ -349,10 +435,7 @@ project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
             const float VS10 = XG00 * co.y + XG10 * co.z, VS11 = XG01 * co.y + XG11 * co.z;
             const float vcv0 = VS00, vcv1 = VS10 + VS01, vcv2 = VS11;
             // recompute cov3d (:1875-1878)
-            const float es[3] = {msp_expf(scales[3 * (size_t)i]), msp_expf(scales[3 * (size_t)i + 1]),
-                                 msp_expf(scales[3 * (size_t)i + 2])};
-            const float q0 = quats[4 * (size_t)i], q1 = quats[4 * (size_t)i + 1],
-                        q2 = quats[4 * (size_t)i + 2], q3 = quats[4 * (size_t)i + 3];
+            const float es[3] = {msp_expf(ls0), msp_expf(ls1), msp_expf(ls2)};
             const float qs = rsqrt_ieee(((q3 * q3 + q0 * q0) + q1 * q1) + q2 * q2);
             const float w = q0 * qs, x = q1 * qs, y = q2 * qs, z = q3 * qs;
             const M3 R = cols3(1.f - 2.f * (y * y + z * z), 2.f * (x * y + w * z), 2.f * (x * z - w * y),
@@ -414,17 +497,21 @@ project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
             const M3 vM = mul3(vVs2, M2);
 #pragma unroll
             for (int c = 0; c < 3; c++)
-                vscale[c] = ((R.m[c][0] * vM.m[c][0] + R.m[c][1] * vM.m[c][1]) + R.m[c][2] * vM.m[c][2]) * es[c];
+                gr[3 + c] = ((R.m[c][0] * vM.m[c][0] + R.m[c][1] * vM.m[c][1]) + R.m[c][2] * vM.m[c][2]) * es[c];
             const M3 vR = mul3(vM, Sm);
             const float (*v)[3] = vR.m;
-            vq[0] = 2.f * ((x * (v[1][2] - v[2][1]) + y * (v[2][0] - v[0][2])) + z * (v[0][1] - v[1][0]));
-            vq[1] = 2.f * (((-2.f * x * (v[1][1] + v[2][2]) + y * (v[0][1] + v[1][0])) +
+            gr[6] = 2.f * ((x * (v[1][2] - v[2][1]) + y * (v[2][0] - v[0][2])) + z * (v[0][1] - v[1][0]));
+            gr[7] = 2.f * (((-2.f * x * (v[1][1] + v[2][2]) + y * (v[0][1] + v[1][0])) +
                             z * (v[0][2] + v[2][0])) + w * (v[1][2] - v[2][1]));
-            vq[2] = 2.f * (((x * (v[0][1] + v[1][0]) - 2.f * y * (v[0][0] + v[2][2])) +
+            gr[8] = 2.f * (((x * (v[0][1] + v[1][0]) - 2.f * y * (v[0][0] + v[2][2])) +
                             z * (v[1][2] + v[2][1])) + w * (v[2][0] - v[0][2]));
-            vq[3] = 2.f * (((x * (v[0][2] + v[2][0]) + y * (v[1][2] + v[2][1])) -
+            gr[9] = 2.f * (((x * (v[0][2] + v[2][0]) + y * (v[1][2] + v[2][1])) -
                             2.f * z * (v[0][0] + v[1][1])) + w * (v[0][1] - v[1][0]));
-            // SH basis of the view direction, for the dc/rest Adam (:1915-1985)
+            gr[0] = vmean[0];
+            gr[1] = vmean[1];
+            gr[2] = vmean[2];
+            gr[10] = vop;
+            // SH basis of the view direction for the dc/rest Adam (:1915-1985)
             const float d0 = p[0] - P->cam_pos[0], d1 = p[1] - P->cam_pos[1], d2 = p[2] - P->cam_pos[2];
             const float dn = rsqrt_ieee((d0 * d0 + d1 * d1) + d2 * d2);
             const float ux = d0 * dn, uy = d1 * dn, uz = d2 * dn;
@@ -445,76 +532,71 @@ project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
             bs[12] = kSH_C3[4] * ux * ((4.f * zz - xx) - yy);
             bs[13] = kSH_C3[5] * uz * (xx - yy);
             bs[14] = kSH_C3[6] * ux * (xx - 3.f * yy);
-            s_vrgb[tid][0] = vr0;
-            s_vrgb[tid][1] = vr1;
-            s_vrgb[tid][2] = vr2;
-            // dc Adam (group 3), visible only
-            if (A.numel[3] > 0) {
-                float* dcp = A.param[3] + 3 * (size_t)i;
-                float* dce = A.exp_avg[3] + 3 * (size_t)i;
-                float* dcs = A.exp_avg_sq[3] + 3 * (size_t)i;
-                const float step = P->adam_step[3], bc2 = P->adam_bc2[3];
-                adam_elem(dcp + 0, dce + 0, dcs + 0, MSP_SH_C0 * vr0, step, b1, b2, bc2, eps);
-                adam_elem(dcp + 1, dce + 1, dcs + 1, MSP_SH_C0 * vr1, step, b1, b2, bc2, eps);
-                adam_elem(dcp + 2, dce + 2, dcs + 2, MSP_SH_C0 * vr2, step, b1, b2, bc2, eps);
-            }
+            bs[15] = vr0;
+            bs[16] = vr1;
+            bs[17] = vr2;
             // densification statistics (accumulate_grad_stats_kernel)
             St.vis_counts[i] += 1.0f;
             St.grad_norm[i] += sqrtf(vx * vx + vy * vy);
             St.max_2d[i] = fmaxf(St.max_2d[i], (float)rad * P->inv_max_dim);
         }
-        // Adam over every element of groups 0, 1, 2, 5 (zero gradient when culled)
-        if (A.numel[0] > 0) {
-            const float step = P->adam_step[0], bc2 = P->adam_bc2[0];
-#pragma unroll
-            for (int c = 0; c < 3; c++)
-                adam_elem(means + 3 * (size_t)i + c, A.exp_avg[0] + 3 * (size_t)i + c,
-                          A.exp_avg_sq[0] + 3 * (size_t)i + c, vmean[c], step, b1, b2, bc2, eps);
-        }
-        if (A.numel[1] > 0) {
-            const float step = P->adam_step[1], bc2 = P->adam_bc2[1];
-#pragma unroll
-            for (int c = 0; c < 3; c++)
-                adam_elem(scales + 3 * (size_t)i + c, A.exp_avg[1] + 3 * (size_t)i + c,
-                          A.exp_avg_sq[1] + 3 * (size_t)i + c, vscale[c], step, b1, b2, bc2, eps);
-        }
-        if (A.numel[2] > 0) {
-            const float step = P->adam_step[2], bc2 = P->adam_bc2[2];
-#pragma unroll
-            for (int c = 0; c < 4; c++)
-                adam_elem(quats + 4 * (size_t)i + c, A.exp_avg[2] + 4 * (size_t)i + c,
-                          A.exp_avg_sq[2] + 4 * (size_t)i + c, vq[c], step, b1, b2, bc2, eps);
-        }
-        if (A.numel[5] > 0) {
-            adam_elem(A.param[5] + i, A.exp_avg[5] + i, A.exp_avg_sq[5] + i, vop, P->adam_step[5],
-                      b1, b2, P->adam_bc2[5], eps);
-        }
     }
+#pragma unroll
+    for (int k = 0; k < kGradSlots; k++) s_grad[tid][k] = gr[k];
     s_vis[tid] = vis;
     __syncthreads();
-    // SH-rest Adam (group 4), warp-cooperative over 32 Gaussians.
-    if (nb_rest <= 0 || A.numel[4] <= 0) return;
-    const int stride = P->rest_stride;
-    const int used = nb_rest * 3;
+    // Phase 2: Adam over this warp's 32 Gaussians, group by group.
     const int wbase = warp * 32;
     const int g0 = base + wbase;
     if (g0 >= N) return;
     const int cnt = min(32, N - g0);
-    float* rp = A.param[4] + (size_t)g0 * stride;
-    float* re = A.exp_avg[4] + (size_t)g0 * stride;
-    float* rs = A.exp_avg_sq[4] + (size_t)g0 * stride;
-    const float step = P->adam_step[4], bc2 = P->adam_bc2[4];
-    const int total = cnt * stride;
-    int gl = 0, kk = lane;
-    while (kk >= stride) { kk -= stride; gl++; }
-    for (int e = lane; e < total; e += 32) {
-        if (kk < used && s_vis[wbase + gl]) {
-            const int b = kk / 3, c = kk - 3 * (kk / 3);
-            const float grad = s_basis[wbase + gl][b] * s_vrgb[wbase + gl][c];
-            adam_elem(rp + e, re + e, rs + e, grad, step, b1, b2, bc2, eps);
-        }
-        kk += 32;
-        while (kk >= stride) { kk -= stride; gl++; }
+    const float(*sg)[kGradSlots] = s_grad + wbase;
+    const float(*sb)[kBasisSlots] = s_basis + wbase;
+    const int* sv = s_vis + wbase;
+    if (A.numel[0] > 0)  // means, every Gaussian (zero gradient when culled)
+        adam_slab<3>(A.param[0], A.exp_avg[0], A.exp_avg_sq[0], (size_t)g0 * 3, cnt * 3, lane,
+                     P->adam_step[0], b1, b2, P->adam_bc2[0], eps,
+                     [&](int gl, int k, float& g) { g = sg[gl][k]; return true; });
+    if (A.numel[1] > 0)  // scales (log)
+        adam_slab<3>(A.param[1], A.exp_avg[1], A.exp_avg_sq[1], (size_t)g0 * 3, cnt * 3, lane,
+                     P->adam_step[1], b1, b2, P->adam_bc2[1], eps,
+                     [&](int gl, int k, float& g) { g = sg[gl][3 + k]; return true; });
+    if (A.numel[2] > 0)  // quats
+        adam_slab<4>(A.param[2], A.exp_avg[2], A.exp_avg_sq[2], (size_t)g0 * 4, cnt * 4, lane,
+                     P->adam_step[2], b1, b2, P->adam_bc2[2], eps,
+                     [&](int gl, int k, float& g) { g = sg[gl][6 + k]; return true; });
+    if (A.numel[5] > 0)  // opacity logits
+        adam_slab<1>(A.param[5], A.exp_avg[5], A.exp_avg_sq[5], (size_t)g0, cnt, lane,
+                     P->adam_step[5], b1, b2, P->adam_bc2[5], eps,
+                     [&](int gl, int, float& g) { g = sg[gl][10]; return true; });
+    if (A.numel[3] > 0)  // features_dc, visible only
+        adam_slab<3>(A.param[3], A.exp_avg[3], A.exp_avg_sq[3], (size_t)g0 * 3, cnt * 3, lane,
+                     P->adam_step[3], b1, b2, P->adam_bc2[3], eps,
+                     [&](int gl, int k, float& g) {
+                         g = MSP_SH_C0 * sb[gl][15 + k];
+                         return sv[gl] != 0;
+                     });
+    if (A.numel[4] > 0 && nb_rest > 0) {  // features_rest, visible only, degrees in use
+        const int stride = P->rest_stride;
+        const int used = nb_rest * 3;
+        auto rest_grad = [&](int gl, int kk, float& g) {
+            if (kk >= used || !sv[gl]) return false;
+            const int b = kk / 3, c = kk - 3 * b;
+            g = sb[gl][b] * sb[gl][15 + c];
+            return true;
+        };
+        if (stride == 45)
+            adam_slab<45>(A.param[4], A.exp_avg[4], A.exp_avg_sq[4], (size_t)g0 * 45, cnt * 45,
+                          lane, P->adam_step[4], b1, b2, P->adam_bc2[4], eps, rest_grad);
+        else if (stride == 24)
+            adam_slab<24>(A.param[4], A.exp_avg[4], A.exp_avg_sq[4], (size_t)g0 * 24, cnt * 24,
+                          lane, P->adam_step[4], b1, b2, P->adam_bc2[4], eps, rest_grad);
+        else if (stride == 9)
+            adam_slab<9>(A.param[4], A.exp_avg[4], A.exp_avg_sq[4], (size_t)g0 * 9, cnt * 9,
+                         lane, P->adam_step[4], b1, b2, P->adam_bc2[4], eps, rest_grad);
+        else if (stride == 72)
+            adam_slab<72>(A.param[4], A.exp_avg[4], A.exp_avg_sq[4], (size_t)g0 * 72, cnt * 72,
+                          lane, P->adam_step[4], b1, b2, P->adam_bc2[4], eps, rest_grad);
     }
 }
 

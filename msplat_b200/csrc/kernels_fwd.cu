@@ -9,6 +9,7 @@ namespace msp {
 
 constexpr int kProjThreads = 128;
 constexpr int kSortThreads = 256;
+constexpr int kSortRun = 8 * kSortThreads;  // keys sorted in registers in one pass
 
 // ---------------------------------------------------------------------------
 // Projection + SH colour + tile counting.
@@ -188,10 +189,27 @@ project_forward_kernel(const StepParams* __restrict__ P, int N, const float* __r
     // one warp per Gaussian reads its contiguous row.
     if (used > 0) {
         const int lane = tid & 31, warp = tid >> 5;
-        for (int gl = warp; gl < kProjThreads; gl += kProjThreads / 32) {
-            if (!s_vis[gl]) continue;
-            const float* src = rest + (size_t)(base + gl) * P->rest_stride;
-            for (int k = lane; k < used; k += 32) s_rest[gl * sstride + k] = src[k];
+        const int stride = P->rest_stride;
+        constexpr int kRows = 4;  // rows loaded before any is stored
+        for (int g0 = warp * kRows; g0 < kProjThreads; g0 += (kProjThreads / 32) * kRows) {
+            float v[kRows][3];
+#pragma unroll
+            for (int r = 0; r < kRows; r++) {
+                const int gl = g0 + r;
+                const float* src = rest + (size_t)(base + gl) * stride;
+#pragma unroll
+                for (int q = 0; q < 3; q++) {
+                    const int k = lane + 32 * q;
+                    v[r][q] = (s_vis[gl] && k < used) ? src[k] : 0.f;
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < kRows; r++)
+#pragma unroll
+                for (int q = 0; q < 3; q++) {
+                    const int k = lane + 32 * q;
+                    if (k < used) s_rest[(g0 + r) * sstride + k] = v[r][q];
+                }
         }
         __syncthreads();
     }
@@ -205,7 +223,7 @@ project_forward_kernel(const StepParams* __restrict__ P, int N, const float* __r
     out.rgb[i] = make_float4(col[0], col[1], col[2], 0.f);
     const int tx_n = P->tiles_x;
     for (int ty = y0; ty < y1; ty++)
-        for (int tx = x0; tx < x1; tx++) atomicAdd(&tile_count[ty * tx_n + tx], 1);
+        for (int tx = x0; tx < x1; tx++) atomicAdd(&tile_count[(ty * tx_n + tx) * kCountPitch], 1);
     if (ZERO_GRADS) {
         float* g = grad_acc + (size_t)i * kGradStride;
 #pragma unroll
@@ -248,7 +266,7 @@ scan_tiles_kernel(const StepParams* __restrict__ P, int T, const int* __restrict
     const int per = (T + 1023) / 1024;
     const int beg = min(tid * per, T), end = min(beg + per, T);
     int local = 0;
-    for (int i = beg; i < end; i++) local += count[i];
+    for (int i = beg; i < end; i++) local += count[i * kCountPitch];
     const int lane = tid & 31, warp = tid >> 5;
     int incl = local;
 #pragma unroll
@@ -272,7 +290,7 @@ scan_tiles_kernel(const StepParams* __restrict__ P, int T, const int* __restrict
     int run = s_warp[warp] + incl - local;
     for (int i = beg; i < end; i++) {
         offset[i] = run;
-        run += count[i];
+        run += count[i * kCountPitch];
     }
     if (tid == 1023) {
         offset[T] = run;
@@ -308,7 +326,7 @@ scatter_kernel(const StepParams* __restrict__ P, int N, const int* __restrict__ 
     for (int ty = y0; ty < y1; ty++)
         for (int tx = x0; tx < x1; tx++) {
             const int t = ty * tx_n + tx;
-            const int pos = atomicSub(&count[t], 1) - 1;
+            const int pos = atomicSub(&count[t * kCountPitch], 1) - 1;
             const long long idx = (long long)offset[t] + pos;
             if (idx < cap) keys[idx] = key;
         }
@@ -324,27 +342,103 @@ void launch_scatter(const StepParams* P, int N, const Buffers& B, cudaStream_t s
 // ---------------------------------------------------------------------------
 // Per-tile ascending sort of the 64-bit keys, then the Gaussian ids in that
 // order.  Reference: bitonic_sort_per_tile_kernel, msplat_metal.metal:2064-2138
-// (the fused pack is replaced by id gathers in the rasterizers).  Tiles of
-// up to kSortCap keys sort in shared memory in one pass; larger tiles sort
-// kSortCap runs and merge them pairwise along merge paths.
+// (the fused pack is replaced by id gathers in the rasterizers).
+// A tile of n <= kSortRun keys is padded with ~0 to npow = max(256, 2^ceil(log2 n))
+// and sorted by a bitonic network whose element e = thread*K + r lives in
+// register r of `thread` (K = npow / 256): compare-exchange distances below K
+// stay in registers, distances below 32K use warp shuffles, larger ones go
+// through shared memory.  Larger tiles sort kSortRun runs that way and merge
+// them pairwise along merge paths.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void bitonic_smem(unsigned long long* s, int npow)
+__device__ __forceinline__ void cmpx(unsigned long long& lo, unsigned long long& hi, bool up)
 {
+    const unsigned long long a = lo, b = hi;
+    const bool swap = (a > b) == up;
+    lo = swap ? b : a;
+    hi = swap ? a : b;
+}
+
+template <int K>
+__device__ __forceinline__ void bitonic_regs(unsigned long long (&v)[K], unsigned long long* s,
+                                             int npow)
+{
+    const int t = threadIdx.x, lane = t & 31;
     for (int k = 2; k <= npow; k <<= 1) {
         for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int i = threadIdx.x; i < (npow >> 1); i += kSortThreads) {
-                int pos = 2 * i - (i & (j - 1));
-                int partner = pos ^ j;
-                bool ascending = ((pos & k) == 0);
-                unsigned long long a = s[pos], b = s[partner];
-                if ((a > b) == ascending) {
-                    s[pos] = b;
-                    s[partner] = a;
+            if (j < K) {
+                // compile-time distance jj == j keeps v[] in registers
+#pragma unroll
+                for (int jj = K >> 1; jj >= 1; jj >>= 1) {
+                    if (jj != j) continue;
+#pragma unroll
+                    for (int r = 0; r < K; r++) {
+                        if (r & jj) continue;
+                        const int e = t * K + r;
+                        cmpx(v[r], v[r | jj], (e & k) == 0);
+                    }
+                }
+            } else if (j < 32 * K) {
+                const int lm = j / K;                   // partner lane offset
+                const bool lower = (lane & lm) == 0;
+#pragma unroll
+                for (int r = 0; r < K; r++) {
+                    const int e = t * K + r;
+                    const bool up = (e & k) == 0;
+                    const unsigned long long o = __shfl_xor_sync(0xffffffffu, v[r], lm);
+                    const bool take_min = lower == up;
+                    v[r] = take_min ? (o < v[r] ? o : v[r]) : (o > v[r] ? o : v[r]);
+                }
+            } else {
+                __syncthreads();
+#pragma unroll
+                for (int r = 0; r < K; r++) s[t * K + r] = v[r];
+                __syncthreads();
+#pragma unroll
+                for (int r = 0; r < K; r++) {
+                    const int e = t * K + r;
+                    const bool up = (e & k) == 0;
+                    const unsigned long long o = s[e ^ j];
+                    const bool take_min = ((e & j) == 0) == up;
+                    v[r] = take_min ? (o < v[r] ? o : v[r]) : (o > v[r] ? o : v[r]);
                 }
             }
-            __syncthreads();
         }
     }
+}
+
+// Sort keys[0, n) (n <= kSortRun) in registers; write the sorted keys back to
+// `out_keys` and/or their ids to `out_ids` (either may be null).
+template <int K>
+__device__ __forceinline__ void sort_run(const unsigned long long* keys, int n,
+                                         unsigned long long* s, unsigned long long* out_keys,
+                                         int* out_ids)
+{
+    const int npow = K * kSortThreads;
+    unsigned long long v[K];
+#pragma unroll
+    for (int r = 0; r < K; r++) {
+        const int e = threadIdx.x * K + r;
+        v[r] = e < n ? keys[e] : ~0ull;
+    }
+    bitonic_regs<K>(v, s, npow);
+#pragma unroll
+    for (int r = 0; r < K; r++) {
+        const int e = threadIdx.x * K + r;
+        if (e < n) {
+            if (out_keys) out_keys[e] = v[r];
+            if (out_ids) out_ids[e] = (int)(unsigned)(v[r] & 0xffffffffull);
+        }
+    }
+}
+
+__device__ __forceinline__ void sort_small(const unsigned long long* keys, int n,
+                                           unsigned long long* s, unsigned long long* out_keys,
+                                           int* out_ids)
+{
+    if (n <= kSortThreads) sort_run<1>(keys, n, s, out_keys, out_ids);
+    else if (n <= 2 * kSortThreads) sort_run<2>(keys, n, s, out_keys, out_ids);
+    else if (n <= 4 * kSortThreads) sort_run<4>(keys, n, s, out_keys, out_ids);
+    else sort_run<8>(keys, n, s, out_keys, out_ids);
 }
 
 __device__ __forceinline__ int merge_path(const unsigned long long* a, int la,
@@ -364,39 +458,26 @@ sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offs
                   unsigned long long* __restrict__ keys, unsigned long long* __restrict__ keys_alt,
                   int* __restrict__ ids)
 {
-    __shared__ unsigned long long s[kSortCap];
+    __shared__ unsigned long long s[kSortRun];
     const int t = blockIdx.x;
     const long long cap = P->capacity;
     const long long start = min((long long)offset[t], cap);
     const long long end = min((long long)offset[t + 1], cap);
     const int n = (int)(end - start);
     if (n <= 0) return;
-    if (n <= kSortCap) {
-        int npow = 1;
-        while (npow < n) npow <<= 1;
-        for (int i = threadIdx.x; i < npow; i += kSortThreads)
-            s[i] = i < n ? keys[start + i] : ~0ull;
-        __syncthreads();
-        bitonic_smem(s, npow);
-        for (int i = threadIdx.x; i < n; i += kSortThreads)
-            ids[start + i] = (int)(unsigned)(s[i] & 0xffffffffull);
+    if (n <= kSortRun) {
+        sort_small(keys + start, n, s, nullptr, ids + start);
         return;
     }
-    // Large tile: sorted runs of kSortCap, then pairwise merges.
+    // Large tile: sorted runs of kSortRun, then pairwise merges.
     unsigned long long* src = keys + start;
     unsigned long long* dst = keys_alt + start;
-    for (int r0 = 0; r0 < n; r0 += kSortCap) {
-        const int m = min(kSortCap, n - r0);
-        int npow = 1;
-        while (npow < m) npow <<= 1;
+    for (int r0 = 0; r0 < n; r0 += kSortRun) {
         __syncthreads();
-        for (int i = threadIdx.x; i < npow; i += kSortThreads) s[i] = i < m ? src[r0 + i] : ~0ull;
-        __syncthreads();
-        bitonic_smem(s, npow);
-        for (int i = threadIdx.x; i < m; i += kSortThreads) src[r0 + i] = s[i];
+        sort_small(src + r0, min(kSortRun, n - r0), s, src + r0, nullptr);
     }
     __syncthreads();
-    for (long long L = kSortCap; L < n; L <<= 1) {
+    for (long long L = kSortRun; L < n; L <<= 1) {
         for (long long s0 = 0; s0 < n; s0 += 2 * L) {
             const unsigned long long* a = src + s0;
             const int la = (int)min(L, (long long)n - s0);
