@@ -130,6 +130,35 @@ int msplat_render(
     const float *features_dc, const float *features_rest, const float *opacities,
     const float *background, float **out_img);
 
+/*
+ * Forward-only render that allocates nothing.  No counterpart in the
+ * reference: it exists for callers that must not allocate device memory
+ * while rendering (a frame loop that cannot take the device-wide stall of
+ * cudaMalloc/cudaFree, or a host that budgets all device memory up front).
+ * Same arguments and the same image as msplat_render, but the image goes
+ * into the caller's device buffer out_img (H*W*3 floats) and every
+ * intermediate lives in one static device array of
+ * MSPLAT_NOALLOC_SCRATCH_BYTES per device.
+ *
+ * Limit: the call is rejected with MSPLAT_ERR_ARG, before any CUDA call,
+ * when 56 bytes per Gaussian + 8 per pixel + 20 per depth-chunk pixel
+ * (chunked path only) + 132 per tile + 16 intersections of 20 bytes per
+ * Gaussian do not fit the array (about 160k Gaussians at 1280x720).  Spare
+ * bytes become extra intersection slots; more intersections than slots
+ * return MSPLAT_ERR_OVERFLOW.  The first call on a device (with it current)
+ * does the set-up and should precede any stream capture.  Calls on one
+ * device share the array: overlapping calls race and must be serialised.
+ * Synchronous on cuda_stream (NULL = the legacy default stream).
+ */
+#define MSPLAT_NOALLOC_SCRATCH_BYTES (64ull << 20)
+int msplat_render_noalloc(
+    int num_points, const float *means3d, const float *scales, float glob_scale,
+    const float *quats, const float *viewmat, const float *projmat, float fx, float fy,
+    float cx, float cy, unsigned img_height, unsigned img_width, const int *tile_bounds,
+    float clip_thresh, unsigned degree, unsigned degrees_to_use, const float *cam_pos,
+    const float *features_dc, const float *features_rest, const float *opacities,
+    const float *background, float *out_img, void *cuda_stream);
+
 /* ---- introspection (tests and benchmarks) ------------------------------- */
 
 /* Loss of the last step; waits for it when `sync` != 0, else returns the

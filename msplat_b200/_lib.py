@@ -51,6 +51,10 @@ SIGNATURES = {
         _i, _p, _p, _f, _p, _fp, _fp, _f, _f, _f, _f, _u, _u, _ip, _f, _u, _u, _fp,
         _p, _p, _p, _fp, C.POINTER(_p),
     ]),
+    "msplat_render_noalloc": (_i, [
+        _i, _p, _p, _f, _p, _fp, _fp, _f, _f, _f, _f, _u, _u, _ip, _f, _u, _u, _fp,
+        _p, _p, _p, _fp, _p, _p,
+    ]),
     "msplat_last_loss": (_f, [_i]),
     "msplat_num_intersections": (C.c_longlong, []),
     "msplat_device_errors": (_i, []),

@@ -22,7 +22,7 @@ namespace msp {
 
 static thread_local std::string t_last_error;
 
-static void set_error(const char* fmt, ...)
+void set_error(const char* fmt, ...)
 {
     char buf[512];
     va_list ap;
@@ -197,7 +197,7 @@ static int ensure(long long N, long long W, long long H, long long T, int K, boo
 }
 
 // Depth-chunk rule of msplat_metal.mm:873-889 (capacity = 16 * N, :809).
-static int chunk_k_max(long long N, int num_tiles)
+int chunk_k_max(long long N, int num_tiles)
 {
     if (num_tiles >= 400) return 1;
     const long long capacity = N * 16;
@@ -282,20 +282,7 @@ static int upload_params(const StepParams& p, cudaStream_t st)
     return MSPLAT_OK;
 }
 
-struct CamArgs {
-    int N;
-    const float* viewmat;
-    const float* projmat;
-    float fx, fy, cx, cy, glob_scale, clip_thresh;
-    unsigned H, W;
-    const int* tile_bounds;
-    unsigned degree, degrees_to_use;
-    const float* cam_pos;
-    const float* background;
-    int rest_stride;
-};
-
-static int fill_params(StepParams& p, const CamArgs& a)
+int fill_params(StepParams& p, const CamArgs& a)
 {
     if (a.N < 0 || a.W == 0 || a.H == 0 || !a.viewmat || !a.projmat || !a.cam_pos || !a.background) {
         set_error("invalid arguments (num_points=%d, %ux%u)", a.N, a.W, a.H);

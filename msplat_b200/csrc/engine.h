@@ -93,6 +93,25 @@ inline int num_sh_bases_host(int degree)
     return degree <= 0 ? 1 : degree == 1 ? 4 : degree == 2 ? 9 : degree == 3 ? 16 : 25;
 }
 
+// Camera arguments of one call, as passed through the C-ABI.
+struct CamArgs {
+    int N;
+    const float* viewmat;
+    const float* projmat;
+    float fx, fy, cx, cy, glob_scale, clip_thresh;
+    unsigned H, W;
+    const int* tile_bounds;
+    unsigned degree, degrees_to_use;
+    const float* cam_pos;
+    const float* background;
+    int rest_stride;
+};
+
+// Host helpers shared by the entry points (engine.cu).
+void set_error(const char* fmt, ...);                  // text for msplat_last_error()
+int fill_params(StepParams& p, const CamArgs& a);      // validates, fills the block
+int chunk_k_max(long long N, int num_tiles);           // depth chunks of one tile
+
 // Kernel launchers (kernels_*.cu).
 void launch_project_forward(const StepParams* P, int N, const float* means, const float* scales,
                             const float* quats, const float* dc, const float* rest,

@@ -1,0 +1,89 @@
+"""msplat_render_noalloc: the render that takes all scratch from a static
+device array must give the same image as msplat_render.
+
+Tolerance: exact (atol = rtol = 0).  Both entry points run the same kernels
+on the same inputs in the same order, so every pixel must agree bit for bit.
+Each case calls the no-alloc entry point twice in a row into a NaN-filled
+buffer, so a second call that saw leftovers of the first (tile counters not
+cleared, stale keys) or a pixel left unwritten would show.
+
+This file is named to be collected last: it must pass both alone in a fresh
+process (the first call then does the per-device set-up) and after the rest
+of the suite.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import numpy as np
+import pytest
+
+from msplat_b200 import _lib, engine, synthetic
+from tests import harness
+
+ATOL = 0.0
+RTOL = 0.0
+SCRATCH_BYTES = 64 << 20   # MSPLAT_NOALLOC_SCRATCH_BYTES
+
+
+def _call_noalloc(model, cs, out_ptr, stream):
+    p = [C.c_void_p(t.data_ptr()) for t in model.params]
+    return _lib.load().msplat_render_noalloc(
+        model.n, p[0], p[1], 1.0, p[2], _lib.farr(cs.viewmat), _lib.farr(cs.projmat), cs.fx,
+        cs.fy, cs.cx, cs.cy, cs.height, cs.width, _lib.iarr(cs.tile_bounds), 0.01, cs.degree,
+        cs.degrees_to_use, _lib.farr(cs.cam_pos), p[3], p[4], p[5],
+        _lib.farr(engine.DEFAULT_BG), C.c_void_p(out_ptr), C.c_void_p(stream))
+
+
+def test_rejects_sizes_beyond_scratch_before_any_cuda_call():
+    """2M Gaussians at 1280x720 need ~750 MB of scratch: refused with
+    MSPLAT_ERR_ARG on the host (no GPU needed, no pointer is touched)."""
+    cam = synthetic.front_camera(1280, 720, 3.0)
+    cs = harness.setup_cam(cam)
+    lib = _lib.load()
+    ptr = C.c_void_p(16)
+    rc = lib.msplat_render_noalloc(
+        2_000_000, ptr, ptr, 1.0, ptr, _lib.farr(cs.viewmat), _lib.farr(cs.projmat), cs.fx,
+        cs.fy, cs.cx, cs.cy, cs.height, cs.width, _lib.iarr(cs.tile_bounds), 0.01, cs.degree,
+        cs.degrees_to_use, _lib.farr(cs.cam_pos), ptr, ptr, ptr, _lib.farr(engine.DEFAULT_BG),
+        ptr, None)
+    assert rc == -1
+    msg = lib.msplat_last_error().decode()
+    assert "static array holds" in msg and str(SCRATCH_BYTES) in msg, msg
+
+
+CASES = {
+    # 130 tiles (< 400): the depth-chunked raster path, 29 chunks
+    "chunked_200x160": dict(n=20_000, w=200, h=160, log_mu=math.log(0.02)),
+    # 1200 tiles: the single-pass raster path
+    "mono_640x480": dict(n=40_000, w=640, h=480, log_mu=math.log(0.012)),
+    # ragged edge tiles on both axes
+    "ragged_333x250": dict(n=30_000, w=333, h=250, log_mu=math.log(0.015)),
+}
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", sorted(CASES))
+def test_noalloc_matches_render_twice(case):
+    import torch
+    assert torch.cuda.is_available(), "no-alloc render test needs a CUDA device"
+    engine.bind_stream()
+    c = CASES[case]
+    g = synthetic.gaussians(c["n"], 7, mean_range=1.0, log_scale_mu=c["log_mu"],
+                            log_scale_sigma=0.3)
+    cs = harness.setup_cam(synthetic.front_camera(c["w"], c["h"], 3.0))
+    model = engine.GaussianModel(g.groups())
+    npx = cs.height * cs.width * 3
+    expect = engine.download(engine.render(model, cs), npx, np.float32)
+    assert np.isfinite(expect).all()
+    out = torch.empty(npx, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    lib = _lib.load()
+    for call in range(2):
+        out.fill_(float("nan"))
+        rc = _call_noalloc(model, cs, out.data_ptr(), stream)
+        assert rc == 0, f"call {call}: {lib.msplat_last_error().decode()}"
+        got = out.cpu().numpy()
+        np.testing.assert_allclose(got, expect, rtol=RTOL, atol=ATOL,
+                                   err_msg=f"{case}: call {call}")
