@@ -117,6 +117,47 @@ int msplat_train_step(
     float *max_2d_size, float inv_max_dim, const int32_t **radii_out, float *loss_out);
 
 /*
+ * Data-parallel training, gradient half.  No counterpart in the reference
+ * (which trains one view on one device); it is msplat_train_step with the
+ * fused optimiser replaced by a gradient output, so that ranks training
+ * different views of the same Gaussians can sum their gradients before
+ * Adam.  Same arguments as msplat_train_step up to features_rest_bases,
+ * then grad_out: a device buffer of (15 + 3*features_rest_bases) * N floats
+ * holding, one after another, the gradients of means [N,3], scales [N,3],
+ * quats [N,4], features_dc [N,3], features_rest [N,features_rest_bases*3]
+ * and opacities [N], then a visibility flag per Gaussian (1 = radius > 0 in
+ * this view).  Every element is written.  Parameters and moments are not
+ * touched; the densification statistics are accumulated as in
+ * msplat_train_step.
+ */
+int msplat_train_step_grads(
+    int num_points, float *means3d, float *scales, float glob_scale, float *quats,
+    const float *viewmat, const float *projmat, float fx, float fy, float cx, float cy,
+    unsigned img_height, unsigned img_width, const int *tile_bounds, float clip_thresh,
+    unsigned degree, unsigned degrees_to_use, const float *cam_pos,
+    float *features_dc, float *features_rest, float *opacities, const float *background,
+    const float *gt, float ssim_weight, float loss_inv_n, int features_rest_bases,
+    float *grad_out, float *vis_counts, float *xys_grad_norm, float *max_2d_size,
+    float inv_max_dim, const int32_t **radii_out, float *loss_out);
+
+/*
+ * Data-parallel training, optimiser half: Adam on Gaussians [begin, end)
+ * from a gradient buffer in the msplat_train_step_grads layout (typically
+ * summed over ranks), each gradient multiplied by grad_scale.  The update,
+ * the per-group step sizes and the rule that features_dc/features_rest
+ * only move for Gaussians whose visibility entry is > 0 (and features_rest
+ * only for the SH degrees in use) are those of msplat_train_step's fused
+ * Adam (msplat_metal.metal:1666-1689 and :1915-1985).  With one rank and
+ * grad_scale = 1 the two halves give msplat_train_step's result bit for bit.
+ */
+int msplat_adam_apply(
+    int num_points, int features_rest_bases, unsigned degree, unsigned degrees_to_use,
+    const float *grads, float grad_scale, int begin, int end, int num_adam_groups,
+    float *const *adam_params, float *const *adam_exp_avg, float *const *adam_exp_avg_sq,
+    const float *adam_step_sizes, const float *adam_bc2_sqrts, float adam_beta1,
+    float adam_beta2, float adam_eps);
+
+/*
  * Forward-only render.  Replaces MTensor msplat_render(...) (bindings.h:37-46;
  * implementation msplat_metal.mm:752-769).  *out_img receives a device
  * pointer to the engine's (H,W,3) float image, valid until the next call

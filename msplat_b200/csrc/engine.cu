@@ -484,55 +484,41 @@ int msplat_drain_stage_times(double* stage_times, int max_stages, int max_sample
     return ns;
 }
 
-int msplat_train_step(
-    int num_points, float* means3d, float* scales, float glob_scale, float* quats,
-    const float* viewmat, const float* projmat, float fx, float fy, float cx, float cy,
-    unsigned img_height, unsigned img_width, const int* tile_bounds, float clip_thresh,
-    unsigned degree, unsigned degrees_to_use, const float* cam_pos, float* features_dc,
-    float* features_rest, float* opacities, const float* background, const float* gt,
-    const float* window2d, float ssim_weight, float loss_inv_n, int features_rest_bases,
-    int num_adam_groups, float* const* adam_params, float* const* adam_exp_avg,
-    float* const* adam_exp_avg_sq, const float* adam_step_sizes, const float* adam_bc2_sqrts,
-    float adam_beta1, float adam_beta2, float adam_eps, float* vis_counts, float* xys_grad_norm,
-    float* max_2d_size, float inv_max_dim, const int32_t** radii_out, float* loss_out)
+// Shared body of msplat_train_step (A = the optimiser, G unused) and
+// msplat_train_step_grads (G = the gradient buffer, Adam left to the caller).
+static int train_common(const char* who, int num_points, float* means3d, float* scales,
+                        float glob_scale, float* quats, const float* viewmat,
+                        const float* projmat, float fx, float fy, float cx, float cy,
+                        unsigned img_height, unsigned img_width, const int* tile_bounds,
+                        float clip_thresh, unsigned degree, unsigned degrees_to_use,
+                        const float* cam_pos, float* features_dc, float* features_rest,
+                        float* opacities, const float* background, const float* gt,
+                        float ssim_weight, float loss_inv_n, int features_rest_bases,
+                        StepParams& p, AdamPtrs& A, const GradOut* G, float* vis_counts,
+                        float* xys_grad_norm, float* max_2d_size, float inv_max_dim,
+                        const int32_t** radii_out, float* loss_out)
 {
-    (void)window2d;
-    std::lock_guard<std::mutex> lk(g_mu);
     int rc = init_engine();
     if (rc) return rc;
-    if (!gt || !vis_counts || !xys_grad_norm || !max_2d_size || num_adam_groups < 0 ||
-        num_adam_groups > kGroups || (num_adam_groups > 0 && (!adam_params || !adam_exp_avg ||
-                                                              !adam_exp_avg_sq || !adam_step_sizes ||
-                                                              !adam_bc2_sqrts))) {
-        set_error("msplat_train_step: missing gt, statistics or optimiser arguments");
+    if (!gt || !vis_counts || !xys_grad_norm || !max_2d_size) {
+        set_error("%s: missing gt or statistics buffers", who);
         return MSPLAT_ERR_ARG;
     }
     poll_readback(false);
     CamArgs a{num_points, viewmat, projmat, fx, fy, cx, cy, glob_scale, clip_thresh, img_height,
               img_width, tile_bounds, degree, degrees_to_use, cam_pos, background,
               features_rest_bases * 3};
-    StepParams p;
+    const StepParams adam = p;
     if ((rc = fill_params(p, a))) return rc;
+    memcpy(p.adam_step, adam.adam_step, sizeof(p.adam_step));
+    memcpy(p.adam_bc2, adam.adam_bc2, sizeof(p.adam_bc2));
+    p.beta1 = adam.beta1;
+    p.beta2 = adam.beta2;
+    p.eps = adam.eps;
+    p.num_adam_groups = adam.num_adam_groups;
     p.ssim_weight = ssim_weight;
     p.loss_inv_n = loss_inv_n;
     p.inv_max_dim = inv_max_dim;
-    p.beta1 = adam_beta1;
-    p.beta2 = adam_beta2;
-    p.eps = adam_eps;
-    p.num_adam_groups = num_adam_groups;
-    AdamPtrs A{};
-    for (int gi = 0; gi < num_adam_groups; gi++) {
-        p.adam_step[gi] = adam_step_sizes[gi];
-        p.adam_bc2[gi] = adam_bc2_sqrts[gi];
-        A.param[gi] = adam_params[gi];
-        A.exp_avg[gi] = adam_exp_avg[gi];
-        A.exp_avg_sq[gi] = adam_exp_avg_sq[gi];
-        A.numel[gi] = (A.param[gi] && A.exp_avg[gi] && A.exp_avg_sq[gi]) ? 1 : 0;
-    }
-    // The SH groups are only updated through the fused path when all of
-    // them are present (msplat_metal.mm:1079-1087).
-    if (num_adam_groups < 5) A.numel[3] = A.numel[4] = 0;
-    p.capacity = 0;
     const cudaStream_t st = g.stream();
     if ((rc = ensure(num_points, img_width, img_height, p.num_tiles, p.k_max, true))) return rc;
     p.capacity = g.cap_isect;
@@ -549,14 +535,158 @@ int msplat_train_step(
     launch_raster_backward(g.d_params, p.num_tiles, p.k_max, p.img_w, p.img_h, g.B, st);
     tm.mark(5, st);
     StatPtrs S{vis_counts, xys_grad_norm, max_2d_size};
-    launch_project_backward_adam(g.d_params, num_points, p.degrees_to_use, p.rest_stride, g.B, A, S,
-                                 st);
+    if (G)
+        launch_project_backward_grads(g.d_params, num_points, p.degrees_to_use, p.rest_stride,
+                                      g.B, A, S, *G, st);
+    else
+        launch_project_backward_adam(g.d_params, num_points, p.degrees_to_use, p.rest_stride,
+                                     g.B, A, S, st);
     tm.mark(6, st);
     g.launches += 1 + (p.k_max > 1 ? 2 : 1) + 1;
     MSP_CUDA(cudaGetLastError());
     if ((rc = queue_readback(st, p))) return rc;
     if (radii_out) *radii_out = g.B.proj.radii;
     if (loss_out) *loss_out = g.last_loss;
+    return MSPLAT_OK;
+}
+
+int msplat_train_step(
+    int num_points, float* means3d, float* scales, float glob_scale, float* quats,
+    const float* viewmat, const float* projmat, float fx, float fy, float cx, float cy,
+    unsigned img_height, unsigned img_width, const int* tile_bounds, float clip_thresh,
+    unsigned degree, unsigned degrees_to_use, const float* cam_pos, float* features_dc,
+    float* features_rest, float* opacities, const float* background, const float* gt,
+    const float* window2d, float ssim_weight, float loss_inv_n, int features_rest_bases,
+    int num_adam_groups, float* const* adam_params, float* const* adam_exp_avg,
+    float* const* adam_exp_avg_sq, const float* adam_step_sizes, const float* adam_bc2_sqrts,
+    float adam_beta1, float adam_beta2, float adam_eps, float* vis_counts, float* xys_grad_norm,
+    float* max_2d_size, float inv_max_dim, const int32_t** radii_out, float* loss_out)
+{
+    (void)window2d;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (num_adam_groups < 0 || num_adam_groups > kGroups ||
+        (num_adam_groups > 0 && (!adam_params || !adam_exp_avg || !adam_exp_avg_sq ||
+                                 !adam_step_sizes || !adam_bc2_sqrts))) {
+        set_error("msplat_train_step: missing optimiser arguments");
+        return MSPLAT_ERR_ARG;
+    }
+    StepParams p;
+    memset(&p, 0, sizeof(p));
+    p.beta1 = adam_beta1;
+    p.beta2 = adam_beta2;
+    p.eps = adam_eps;
+    p.num_adam_groups = num_adam_groups;
+    AdamPtrs A{};
+    for (int gi = 0; gi < num_adam_groups; gi++) {
+        p.adam_step[gi] = adam_step_sizes[gi];
+        p.adam_bc2[gi] = adam_bc2_sqrts[gi];
+        A.param[gi] = adam_params[gi];
+        A.exp_avg[gi] = adam_exp_avg[gi];
+        A.exp_avg_sq[gi] = adam_exp_avg_sq[gi];
+        A.numel[gi] = (A.param[gi] && A.exp_avg[gi] && A.exp_avg_sq[gi]) ? 1 : 0;
+    }
+    // The SH groups are only updated through the fused path when all of
+    // them are present (msplat_metal.mm:1079-1087).
+    if (num_adam_groups < 5) A.numel[3] = A.numel[4] = 0;
+    return train_common("msplat_train_step", num_points, means3d, scales, glob_scale, quats,
+                        viewmat, projmat, fx, fy, cx, cy, img_height, img_width, tile_bounds,
+                        clip_thresh, degree, degrees_to_use, cam_pos, features_dc, features_rest,
+                        opacities, background, gt, ssim_weight, loss_inv_n, features_rest_bases,
+                        p, A, nullptr, vis_counts, xys_grad_norm, max_2d_size, inv_max_dim,
+                        radii_out, loss_out);
+}
+
+int msplat_train_step_grads(
+    int num_points, float* means3d, float* scales, float glob_scale, float* quats,
+    const float* viewmat, const float* projmat, float fx, float fy, float cx, float cy,
+    unsigned img_height, unsigned img_width, const int* tile_bounds, float clip_thresh,
+    unsigned degree, unsigned degrees_to_use, const float* cam_pos, float* features_dc,
+    float* features_rest, float* opacities, const float* background, const float* gt,
+    float ssim_weight, float loss_inv_n, int features_rest_bases, float* grad_out,
+    float* vis_counts, float* xys_grad_norm, float* max_2d_size, float inv_max_dim,
+    const int32_t** radii_out, float* loss_out)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!grad_out || features_rest_bases < 0) {
+        set_error("msplat_train_step_grads: missing gradient buffer");
+        return MSPLAT_ERR_ARG;
+    }
+    StepParams p;
+    memset(&p, 0, sizeof(p));
+    AdamPtrs A{};
+    A.param[0] = means3d;
+    A.param[1] = scales;
+    A.param[2] = quats;
+    const size_t n = (size_t)std::max(num_points, 0);
+    const size_t rs = (size_t)features_rest_bases * 3;
+    GradOut G{};
+    G.g[0] = grad_out;
+    G.g[1] = G.g[0] + 3 * n;
+    G.g[2] = G.g[1] + 3 * n;
+    G.g[3] = G.g[2] + 4 * n;
+    G.g[4] = G.g[3] + 3 * n;
+    G.g[5] = G.g[4] + rs * n;
+    G.vis = G.g[5] + n;
+    return train_common("msplat_train_step_grads", num_points, means3d, scales, glob_scale, quats,
+                        viewmat, projmat, fx, fy, cx, cy, img_height, img_width, tile_bounds,
+                        clip_thresh, degree, degrees_to_use, cam_pos, features_dc, features_rest,
+                        opacities, background, gt, ssim_weight, loss_inv_n, features_rest_bases,
+                        p, A, &G, vis_counts, xys_grad_norm, max_2d_size, inv_max_dim, radii_out,
+                        loss_out);
+}
+
+int msplat_adam_apply(int num_points, int features_rest_bases, unsigned degree,
+                      unsigned degrees_to_use, const float* grads, float grad_scale, int begin,
+                      int end, int num_adam_groups, float* const* adam_params,
+                      float* const* adam_exp_avg, float* const* adam_exp_avg_sq,
+                      const float* adam_step_sizes, const float* adam_bc2_sqrts, float adam_beta1,
+                      float adam_beta2, float adam_eps)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = init_engine();
+    if (rc) return rc;
+    const long long rs = (long long)features_rest_bases * 3;
+    if (!grads || num_points < 0 || features_rest_bases < 0 || begin < 0 || end > num_points ||
+        begin > end || num_adam_groups < 0 || num_adam_groups > kGroups ||
+        (num_adam_groups > 0 && (!adam_params || !adam_exp_avg || !adam_exp_avg_sq ||
+                                 !adam_step_sizes || !adam_bc2_sqrts)) ||
+        (long long)num_points * std::max(rs, 4LL) >= (1LL << 31) - (1LL << 21)) {
+        set_error("msplat_adam_apply: invalid arguments (N=%d, range [%d,%d), groups %d)",
+                  num_points, begin, end, num_adam_groups);
+        return MSPLAT_ERR_ARG;
+    }
+    const size_t n = (size_t)num_points;
+    ApplyArgs a{};
+    const int strides[kGroups] = {3, 3, 4, 3, (int)rs, 1};
+    const float* gp = grads;
+    for (int gi = 0; gi < kGroups; gi++) {
+        a.grad[gi] = gp;
+        a.stride[gi] = strides[gi];
+        gp += (size_t)strides[gi] * n;
+    }
+    a.vis = gp;
+    for (int gi = 0; gi < num_adam_groups; gi++) {
+        if (!adam_params[gi] || !adam_exp_avg[gi] || !adam_exp_avg_sq[gi] || strides[gi] == 0)
+            continue;
+        a.param[gi] = adam_params[gi];
+        a.exp_avg[gi] = adam_exp_avg[gi];
+        a.exp_avg_sq[gi] = adam_exp_avg_sq[gi];
+        a.step[gi] = adam_step_sizes[gi];
+        a.bc2[gi] = adam_bc2_sqrts[gi];
+    }
+    // The SH groups move together, as in the fused step.
+    if (num_adam_groups < 5) a.param[3] = a.param[4] = nullptr;
+    const int dtu = (int)std::min(degrees_to_use, degree);
+    a.used_rest = rest_bases_updated(dtu, (int)rs) * 3;
+    a.beta1 = adam_beta1;
+    a.beta2 = adam_beta2;
+    a.eps = adam_eps;
+    a.scale = grad_scale;
+    a.begin = begin;
+    a.end = end;
+    launch_adam_apply(a, g.stream());
+    g.launches += 1;
+    MSP_CUDA(cudaGetLastError());
     return MSPLAT_OK;
 }
 

@@ -88,6 +88,30 @@ struct StatPtrs {
     float* max_2d;
 };
 
+// Planar per-group gradient output of the data-parallel step: group g's
+// gradient has the layout of its parameter tensor ([N, per-Gaussian
+// floats]); vis[i] is 1 for a Gaussian with radius > 0 in this view, else 0.
+struct GradOut {
+    float* g[kGroups];
+    float* vis;
+};
+
+// Adam over a range of Gaussians [begin, end) from a gradient buffer laid
+// out as GradOut; every gradient is multiplied by `scale` first.
+struct ApplyArgs {
+    float* param[kGroups];
+    float* exp_avg[kGroups];
+    float* exp_avg_sq[kGroups];
+    const float* grad[kGroups];
+    const float* vis;
+    float step[kGroups];
+    float bc2[kGroups];
+    int stride[kGroups];       // floats per Gaussian of each group
+    float beta1, beta2, eps, scale;
+    int begin, end;
+    int used_rest;             // SH-rest floats updated (degrees in use)
+};
+
 inline int num_sh_bases_host(int degree)
 {
     return degree <= 0 ? 1 : degree == 1 ? 4 : degree == 2 ? 9 : degree == 3 ? 16 : 25;
@@ -129,5 +153,10 @@ void launch_raster_backward(const StepParams* P, int num_tiles, int k_max, int W
 void launch_project_backward_adam(const StepParams* P, int N, int degrees_to_use_host,
                                   int rest_stride_host, const Buffers& B, const AdamPtrs& A,
                                   const StatPtrs& St, cudaStream_t s);
+void launch_project_backward_grads(const StepParams* P, int N, int degrees_to_use_host,
+                                   int rest_stride_host, const Buffers& B, const AdamPtrs& A,
+                                   const StatPtrs& St, const GradOut& G, cudaStream_t s);
+int rest_bases_updated(int degrees_to_use, int rest_stride);
+void launch_adam_apply(const ApplyArgs& a, cudaStream_t s);
 
 }  // namespace msp

@@ -1,6 +1,8 @@
 // kernels_bwd.cu -- backward half of the step: rasterizer VJP, projection
 // VJP, and every Adam update, in two kernels.  Compiled with --fmad=false so
 // the alpha/T decisions replayed here are exactly the forward's.
+#include <algorithm>
+
 #include "engine.h"
 #include "msp_math.cuh"
 
@@ -376,15 +378,32 @@ __device__ __forceinline__ void adam_slab(float* __restrict__ P, float* __restri
     }
 }
 
+// Writes one warp's contiguous slab of a gradient group (same walk as
+// adam_slab); elements that grad_of declines are written as 0.
+template <int STRIDE, class G>
+__device__ __forceinline__ void grad_slab(float* __restrict__ out, size_t e0, int total, int lane,
+                                          G grad_of)
+{
+    for (int e = lane; e < total; e += 32) {
+        float g = 0.f;
+        if (!grad_of(e / STRIDE, e % STRIDE, g)) g = 0.f;
+        out[e0 + e] = g;
+    }
+}
+
 // Per-Gaussian gradient slots in shared memory (phase 1 -> phase 2).
 constexpr int kGradSlots = 12;  // v_mean[3], v_scale[3], v_quat[4], v_opacity, pad
 constexpr int kBasisSlots = 19; // 15 SH-rest basis values + v_rgb[3] (odd stride: no bank conflicts)
 
+// GRAD_OUT = false: the single-GPU step, Adam applied in place.
+// GRAD_OUT = true: the data-parallel step, gradients written to G (the
+// same values Adam would have consumed) and no parameter touched.
+template <bool GRAD_OUT>
 __global__ void __launch_bounds__(kBwdThreads, 5)
 project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
                              const int* __restrict__ radii, const float4* __restrict__ g_co,
                              const float* __restrict__ grad_acc, AdamPtrs A, StatPtrs St,
-                             int nb_rest)
+                             GradOut G, int nb_rest)
 {
     __shared__ float s_grad[kBwdThreads][kGradSlots];
     __shared__ float s_basis[kBwdThreads][kBasisSlots];
@@ -553,6 +572,35 @@ project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
     const float(*sg)[kGradSlots] = s_grad + wbase;
     const float(*sb)[kBasisSlots] = s_basis + wbase;
     const int* sv = s_vis + wbase;
+    if constexpr (GRAD_OUT) {
+        const size_t gb = (size_t)g0;
+        grad_slab<3>(G.g[0], gb * 3, cnt * 3, lane,
+                     [&](int gl, int k, float& g) { g = sg[gl][k]; return true; });
+        grad_slab<3>(G.g[1], gb * 3, cnt * 3, lane,
+                     [&](int gl, int k, float& g) { g = sg[gl][3 + k]; return true; });
+        grad_slab<4>(G.g[2], gb * 4, cnt * 4, lane,
+                     [&](int gl, int k, float& g) { g = sg[gl][6 + k]; return true; });
+        grad_slab<1>(G.g[5], gb, cnt, lane,
+                     [&](int gl, int, float& g) { g = sg[gl][10]; return true; });
+        grad_slab<3>(G.g[3], gb * 3, cnt * 3, lane, [&](int gl, int k, float& g) {
+            g = MSP_SH_C0 * sb[gl][15 + k];
+            return sv[gl] != 0;
+        });
+        const int stride = P->rest_stride;
+        const int used = nb_rest * 3;
+        auto rest_grad = [&](int gl, int kk, float& g) {
+            if (kk >= used || !sv[gl]) return false;
+            const int b = kk / 3, c = kk - 3 * b;
+            g = sb[gl][b] * sb[gl][15 + c];
+            return true;
+        };
+        if (stride == 45) grad_slab<45>(G.g[4], gb * 45, cnt * 45, lane, rest_grad);
+        else if (stride == 24) grad_slab<24>(G.g[4], gb * 24, cnt * 24, lane, rest_grad);
+        else if (stride == 9) grad_slab<9>(G.g[4], gb * 9, cnt * 9, lane, rest_grad);
+        else if (stride == 72) grad_slab<72>(G.g[4], gb * 72, cnt * 72, lane, rest_grad);
+        if (lane < cnt) G.vis[g0 + lane] = sv[lane] ? 1.f : 0.f;
+        return;
+    }
     if (A.numel[0] > 0)  // means, every Gaussian (zero gradient when culled)
         adam_slab<3>(A.param[0], A.exp_avg[0], A.exp_avg_sq[0], (size_t)g0 * 3, cnt * 3, lane,
                      P->adam_step[0], b1, b2, P->adam_bc2[0], eps,
@@ -600,19 +648,78 @@ project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
     }
 }
 
+// SH-rest bases updated: degrees_to_use 0 -> 0, 1 -> 3, 2 -> 8, >= 3 -> 15
+// (the reference stops at degree 3 here, msplat_metal.metal:1931-1985).
+int rest_bases_updated(int degrees_to_use, int rest_stride)
+{
+    int nb = degrees_to_use < 1 ? 0 : degrees_to_use == 1 ? 3 : degrees_to_use == 2 ? 8 : 15;
+    if (nb * 3 > rest_stride) nb = rest_stride / 3;
+    return nb;
+}
+
 void launch_project_backward_adam(const StepParams* P, int N, int degrees_to_use_host,
                                   int rest_stride_host, const Buffers& B, const AdamPtrs& A,
                                   const StatPtrs& St, cudaStream_t s)
 {
     if (N <= 0) return;
-    // SH-rest bases updated: degrees_to_use 0 -> 0, 1 -> 3, 2 -> 8, >= 3 -> 15
-    // (the reference stops at degree 3 here, msplat_metal.metal:1931-1985).
-    int nb = degrees_to_use_host < 1 ? 0 : degrees_to_use_host == 1 ? 3
-             : degrees_to_use_host == 2 ? 8 : 15;
-    if (nb * 3 > rest_stride_host) nb = rest_stride_host / 3;
+    const int nb = rest_bases_updated(degrees_to_use_host, rest_stride_host);
     const int grid = (N + kBwdThreads - 1) / kBwdThreads;
-    project_backward_adam_kernel<<<grid, kBwdThreads, 0, s>>>(P, N, B.proj.radii, B.proj.conic_op,
-                                                              B.grad_acc, A, St, nb);
+    project_backward_adam_kernel<false><<<grid, kBwdThreads, 0, s>>>(
+        P, N, B.proj.radii, B.proj.conic_op, B.grad_acc, A, St, GradOut{}, nb);
+}
+
+void launch_project_backward_grads(const StepParams* P, int N, int degrees_to_use_host,
+                                   int rest_stride_host, const Buffers& B, const AdamPtrs& A,
+                                   const StatPtrs& St, const GradOut& G, cudaStream_t s)
+{
+    if (N <= 0) return;
+    const int nb = rest_bases_updated(degrees_to_use_host, rest_stride_host);
+    const int grid = (N + kBwdThreads - 1) / kBwdThreads;
+    project_backward_adam_kernel<true><<<grid, kBwdThreads, 0, s>>>(
+        P, N, B.proj.radii, B.proj.conic_op, B.grad_acc, A, St, G, nb);
+}
+
+// ---------------------------------------------------------------------------
+// Adam from a gradient buffer (the data-parallel step, after the gradients of
+// all views were summed).  Same update and the same visible-only rule for
+// the SH groups as project_backward_adam_kernel: groups 3 and 4 skip
+// Gaussians no view saw, and group 4 only updates the degrees in use.
+// One block row per group (blockIdx.y); 32-bit element indices (the host
+// checks N * stride < 2^31).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+adam_apply_kernel(ApplyArgs a)
+{
+    const int gi = blockIdx.y;
+    float* __restrict__ P = a.param[gi];
+    if (!P) return;
+    float* __restrict__ M = a.exp_avg[gi];
+    float* __restrict__ V = a.exp_avg_sq[gi];
+    const float* __restrict__ Gd = a.grad[gi];
+    const int S = a.stride[gi];
+    const int e_end = a.end * S;
+    const float step = a.step[gi], bc2 = a.bc2[gi];
+    const bool sh = gi == 3 || gi == 4;
+    for (int e = a.begin * S + blockIdx.x * blockDim.x + threadIdx.x; e < e_end;
+         e += gridDim.x * blockDim.x) {
+        if (sh) {
+            const int i = e / S;
+            if (!(a.vis[i] > 0.f)) continue;
+            if (gi == 4 && e - i * S >= a.used_rest) continue;
+        }
+        adam_elem(P + e, M + e, V + e, Gd[e] * a.scale, step, a.beta1, a.beta2, bc2, a.eps);
+    }
+}
+
+void launch_adam_apply(const ApplyArgs& a, cudaStream_t s)
+{
+    if (a.end <= a.begin) return;
+    long long widest = 0;
+    for (int gi = 0; gi < kGroups; gi++)
+        if (a.param[gi]) widest = std::max(widest, (long long)(a.end - a.begin) * a.stride[gi]);
+    if (widest <= 0) return;
+    const long long blocks = std::min((widest + 255) / 256, 148LL * 16);
+    adam_apply_kernel<<<dim3((unsigned)blocks, kGroups), 256, 0, s>>>(a);
 }
 
 }  // namespace msp

@@ -1,0 +1,44 @@
+"""One rank of the two-GPU data-parallel test (launched by torchrun from
+tests/test_dp_gpu.py): three DataParallel steps over NCCL on a seeded
+scene, rank r training view (step * world + r) % 3; saves its parameters.
+
+  torchrun --nproc-per-node 2 tests/dp_worker.py OUT_DIR N WIDTH HEIGHT SEED
+"""
+from __future__ import annotations
+
+import math
+import os
+import sys
+
+import numpy as np
+import torch
+
+from msplat_b200 import engine, multigpu, synthetic
+from tests import harness
+
+
+def main():
+    out_dir, n, w, h, seed = sys.argv[1], *map(int, sys.argv[2:6])
+    rank, world = multigpu.rank_and_world()
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    engine.bind_stream()
+    g = synthetic.gaussians(n, seed, mean_range=1.0, log_scale_mu=math.log(0.02),
+                            log_scale_sigma=0.3)
+    cams = [synthetic.front_camera(w, h, 3.0 + 0.3 * k) for k in range(3)]
+    model = engine.GaussianModel(g.groups())
+    dp = multigpu.DataParallel(model, rank, world, timeout_s=60)
+    for step in range(3):
+        v = (step * world + rank) % 3
+        cs = harness.setup_cam(cams[v])
+        gen = torch.Generator(device="cuda").manual_seed(v)
+        gt = torch.rand(cs.height, cs.width, 3, device="cuda", generator=gen)
+        dp.train_step(cs, gt)
+    torch.cuda.synchronize()
+    dp.barrier()
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"),
+             **{f"p{i}": model.params[i].cpu().numpy() for i in range(6)})
+    dp.shutdown()
+
+
+if __name__ == "__main__":
+    main()

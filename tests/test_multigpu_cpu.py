@@ -1,0 +1,164 @@
+"""The data-parallel protocol of msplat_b200.multigpu on two gloo ranks (CPU).
+
+The engine's two halves are replaced by a stand-in (`FakeOps`) with the same
+buffer layout and the same optimiser rules, so the test checks the host
+logic: each rank fills its gradient buffer for its own view, the buffers are
+summed across ranks, every rank applies Adam with grad_scale = 1/world, and
+the replicas stay identical and equal to a single-process run that sums the
+two views' gradients itself.  Also covered: sync_stats, max_over_ranks,
+barrier and shutdown.
+"""
+from __future__ import annotations
+
+import os
+import socket
+import tempfile
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from msplat_b200 import engine, multigpu, synthetic
+
+N = 96
+REST_BASES = 15
+STEPS = 3
+
+
+class FakeCam:
+    def __init__(self, view: int, degree: int = 3, degrees_to_use: int = 2):
+        self.view, self.degree, self.degrees_to_use = view, degree, degrees_to_use
+
+
+def fake_grads(model, view: int, out) -> None:
+    """Deterministic per-view gradient in the engine's buffer layout: SH
+    groups zero where the Gaussian is not visible, SH-rest zero beyond the
+    degrees in use (2 -> 8 bases)."""
+    groups, vis = multigpu.grad_views(out, model.n, model.rest_bases)
+    seen = (torch.arange(model.n) % (view + 2) != 0).float()
+    vis.copy_(seen)
+    for gi, g in enumerate(groups):
+        g.copy_(torch.sin(model.params[gi].reshape(model.n, -1) * (view + 1) + gi))
+    groups[3].mul_(seen[:, None])
+    groups[4].mul_(seen[:, None])
+    groups[4][:, 8 * 3:] = 0.0
+
+
+def fake_adam(model, cam, grad, scale) -> None:
+    """The optimiser rules of msplat_adam_apply, in torch on the CPU."""
+    groups, vis = multigpu.grad_views(grad, model.n, model.rest_bases)
+    steps, bc2s = model.adam_scalars()
+    b1, b2, eps = model.beta1, model.beta2, model.eps
+    used = {0: 0, 1: 3, 2: 8}.get(min(cam.degrees_to_use, cam.degree), 15) * 3
+    for gi in range(6):
+        p = model.params[gi].view(model.n, -1)
+        m = model.exp_avg[gi].view(model.n, -1)
+        v = model.exp_avg_sq[gi].view(model.n, -1)
+        g = groups[gi] * scale
+        mask = torch.ones_like(p, dtype=torch.bool)
+        if gi in (3, 4):
+            mask &= (vis > 0)[:, None]
+        if gi == 4:
+            mask[:, used:] = False
+        mm = b1 * m + (1 - b1) * g
+        vv = b2 * v + (1 - b2) * g * g
+        pp = p - steps[gi] * mm / (torch.sqrt(vv) / bc2s[gi] + eps)
+        p.copy_(torch.where(mask, pp, p))
+        m.copy_(torch.where(mask, mm, m))
+        v.copy_(torch.where(mask, vv, v))
+
+
+class FakeOps:
+    def alloc(self, count):
+        return torch.empty(count, dtype=torch.float32)
+
+    def grads(self, model, cam, gt, out, *args):
+        fake_grads(model, cam.view, out)
+        model.vis_counts += 1.0
+        model.xys_grad_norm += float(cam.view)
+        model.max_2d_size.copy_(torch.maximum(model.max_2d_size,
+                                              torch.full_like(model.max_2d_size, cam.view * 0.1)))
+        return float(cam.view)
+
+    def adam_apply(self, model, cam, grad, scale):
+        fake_adam(model, cam, grad, scale)
+
+
+def _model():
+    g = synthetic.gaussians(N, 3, sh_degree=3)
+    return engine.GaussianModel(g.groups(), device="cpu")
+
+
+def _worker(rank, world, port, out_dir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    model = _model()
+    dp = multigpu.DataParallel(model, rank, world, ops=FakeOps(), backend="gloo", timeout_s=60)
+    losses = []
+    for s in range(STEPS):
+        losses.append(dp.train_step(FakeCam(s * world + rank), None))
+    dp.barrier()
+    mx = dp.max_over_ranks(float(rank) + 0.5)
+    dp.sync_stats()
+    dp.shutdown()
+    arrs = {f"p{i}": t.numpy() for i, t in enumerate(model.params)}
+    arrs.update({f"m{i}": t.numpy() for i, t in enumerate(model.exp_avg)})
+    arrs.update({f"v{i}": t.numpy() for i, t in enumerate(model.exp_avg_sq)})
+    arrs.update(vis=model.vis_counts.numpy(), gn=model.xys_grad_norm.numpy(),
+                m2d=model.max_2d_size.numpy(), losses=np.array(losses), mx=np.array([mx]))
+    np.savez(os.path.join(out_dir, f"rank{rank}.npz"), **arrs)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.fixture(scope="module")
+def two_ranks():
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_worker, args=(2, _free_port(), d), nprocs=2, join=True,
+                           start_method="spawn")
+        yield [dict(np.load(os.path.join(d, f"rank{r}.npz"))) for r in range(2)]
+
+
+def test_replicas_identical(two_ranks):
+    r0, r1 = two_ranks
+    for k in r0:
+        if k.startswith(("p", "m", "v")) and k[1:].isdigit():
+            np.testing.assert_array_equal(r0[k], r1[k], err_msg=k)
+
+
+def test_matches_single_process_sum_of_views(two_ranks):
+    world = 2
+    model = _model()
+    buf = torch.empty(multigpu.grad_floats(N, REST_BASES))
+    tmp = torch.empty_like(buf)
+    for s in range(STEPS):
+        model.step_count += 1
+        buf.zero_()
+        for r in range(world):
+            fake_grads(model, s * world + r, tmp)
+            buf += tmp
+        fake_adam(model, FakeCam(0), buf, 1.0 / world)
+    for i in range(6):
+        np.testing.assert_allclose(two_ranks[0][f"p{i}"], model.params[i].numpy(), rtol=1e-6,
+                                   atol=1e-7, err_msg=f"group {i}")
+
+
+def test_views_differ_per_rank_and_stats_combine(two_ranks):
+    r0, r1 = two_ranks
+    assert list(r0["losses"]) == [0.0, 2.0, 4.0] and list(r1["losses"]) == [1.0, 3.0, 5.0]
+    np.testing.assert_array_equal(r0["vis"], np.full(N, 2.0 * STEPS, np.float32))
+    np.testing.assert_array_equal(r0["gn"], np.full(N, 15.0, np.float32))
+    np.testing.assert_allclose(r0["m2d"], np.full(N, 0.5, np.float32), rtol=1e-6)
+    assert r0["mx"][0] == 1.5 and r1["mx"][0] == 1.5
+
+
+def test_grad_buffer_layout():
+    bufs, vis = multigpu.grad_views(torch.arange(multigpu.grad_floats(4, 15), dtype=torch.float32),
+                                    4, 15)
+    assert [tuple(b.shape) for b in bufs] == [(4, 3), (4, 3), (4, 4), (4, 3), (4, 45), (4, 1)]
+    assert vis.shape == (4,) and vis[0].item() == 59 * 4
