@@ -159,6 +159,17 @@ def algorithmic_bytes_proj_bwd(n_total: int, n_vis: int, rest_floats: int) -> fl
     return float(n_total * per_all + n_vis * per_vis)
 
 
+def algorithmic_bytes_proj_bwd_grads(n_total: int, n_vis: int, rest_floats: int) -> float:
+    """The same kernel in its data-parallel form (N > 1): every Gaussian
+    reads its radius and writes its (15 + rest_floats)-float gradient row
+    and visibility flag; a visible one also reads its 9 raster gradients,
+    its conic/opacity record and its 10 geometry floats, and updates 3
+    statistics."""
+    per_all = 4 + (15 + rest_floats) * 4
+    per_vis = 9 * 4 + 16 + 10 * 4 + 3 * 8
+    return float(n_total * per_all + n_vis * per_vis)
+
+
 def run_ours(args, rank: int, world: int):
     import torch
     from msplat_b200 import _lib, engine
@@ -260,10 +271,15 @@ def run_ours(args, rank: int, world: int):
     # --- roofline of the dominant HBM-bound kernel ---------------------------
     pk = peaks()
     dom = "proj_bwd_adam"
-    algo = algorithmic_bytes_proj_bwd(model.n, n_vis, 45)
+    if world == 1:
+        algo = algorithmic_bytes_proj_bwd(model.n, n_vis, 45)
+    else:
+        algo = algorithmic_bytes_proj_bwd_grads(model.n, n_vis, 45)
     dom_ms = stage_ms.get(dom, 0.0)
     achieved = algo / (dom_ms / 1000.0) / 1e9 if dom_ms > 0 else 0.0
-    roofline = {"bound": "hbm", "kernel": "project_backward_adam_kernel", "achieved": round(achieved, 1),
+    kname = ("rest_adam_kernel + project_backward_adam_kernel<false> (projection VJP + Adam)"
+             if world == 1 else "project_backward_adam_kernel<true> (gradient output)")
+    roofline = {"bound": "hbm", "kernel": kname, "achieved": round(achieved, 1),
                 "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
                 "peak_source": pk["source"], "algorithmic_bytes": algo, "launch_ms": round(dom_ms, 4),
                 "traffic": None}

@@ -535,14 +535,15 @@ static int train_common(const char* who, int num_points, float* means3d, float* 
     launch_raster_backward(g.d_params, p.num_tiles, p.k_max, p.img_w, p.img_h, g.B, st);
     tm.mark(5, st);
     StatPtrs S{vis_counts, xys_grad_norm, max_2d_size};
+    int bwd_launches = 1;
     if (G)
         launch_project_backward_grads(g.d_params, num_points, p.degrees_to_use, p.rest_stride,
                                       g.B, A, S, *G, st);
     else
-        launch_project_backward_adam(g.d_params, num_points, p.degrees_to_use, p.rest_stride,
-                                     g.B, A, S, st);
+        bwd_launches = launch_project_backward_adam(g.d_params, num_points, p.degrees_to_use,
+                                                    p.rest_stride, g.B, A, S, st);
     tm.mark(6, st);
-    g.launches += 1 + (p.k_max > 1 ? 2 : 1) + 1;
+    g.launches += 1 + (p.k_max > 1 ? 2 : 1) + bwd_launches;
     MSP_CUDA(cudaGetLastError());
     if ((rc = queue_readback(st, p))) return rc;
     if (radii_out) *radii_out = g.B.proj.radii;

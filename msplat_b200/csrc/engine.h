@@ -150,9 +150,10 @@ void launch_ssim(const StepParams* P, int W, int H, const float* gt, const Buffe
                  cudaStream_t s);
 void launch_raster_backward(const StepParams* P, int num_tiles, int k_max, int W, int H,
                             const Buffers& B, cudaStream_t s);
-void launch_project_backward_adam(const StepParams* P, int N, int degrees_to_use_host,
-                                  int rest_stride_host, const Buffers& B, const AdamPtrs& A,
-                                  const StatPtrs& St, cudaStream_t s);
+// Returns the number of kernels launched (the SH-rest Adam runs as its own kernel).
+int launch_project_backward_adam(const StepParams* P, int N, int degrees_to_use_host,
+                                 int rest_stride_host, const Buffers& B, const AdamPtrs& A,
+                                 const StatPtrs& St, cudaStream_t s);
 void launch_project_backward_grads(const StepParams* P, int N, int degrees_to_use_host,
                                    int rest_stride_host, const Buffers& B, const AdamPtrs& A,
                                    const StatPtrs& St, const GradOut& G, cudaStream_t s);

@@ -329,13 +329,34 @@ __device__ __forceinline__ M3 cols3(float a0, float a1, float a2, float b0, floa
     return M;
 }
 
+__device__ __forceinline__ float sqrt_approx(float x)
+{
+    float r;
+    asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+// One Adam update (fused_adam_kernel, msplat_metal.metal:1666-1689):
+//   m = b1 m + (1 - b1) g;  v = b2 v + (1 - b2) g^2;
+//   p -= step * m / (sqrt(v) / bc2 + eps)
+// with the square root and the division done by the hardware's approximate
+// instructions (a few ulp, as the reference's fast-math Metal build does;
+// the parameters' bar is 1e-4 relative).  inv_bc2 = 1 / bc2.
+__device__ __forceinline__ void adam_math(float& p, float& m, float& v, float g, float step,
+                                          float b1, float b2, float inv_bc2, float eps)
+{
+    m = fmaf(b1, m, (1.0f - b1) * g);
+    v = fmaf(b2, v, (1.0f - b2) * g * g);
+    p = p - __fdividef(step * m, fmaf(sqrt_approx(v), inv_bc2, eps));
+}
+
 __device__ __forceinline__ void adam_elem(float* __restrict__ p, float* __restrict__ ea,
                                           float* __restrict__ eas, float g, float step, float b1,
-                                          float b2, float bc2, float eps)
+                                          float b2, float inv_bc2, float eps)
 {
-    const float m = fmaf(b1, *ea, (1.0f - b1) * g);
-    const float v = fmaf(b2, *eas, (1.0f - b2) * g * g);
-    *p -= step * m / (sqrtf(v) / bc2 + eps);
+    float pp = *p, m = *ea, v = *eas;
+    adam_math(pp, m, v, g, step, b1, b2, inv_bc2, eps);
+    *p = pp;
     *ea = m;
     *eas = v;
 }
@@ -348,7 +369,7 @@ __device__ __forceinline__ void adam_elem(float* __restrict__ p, float* __restri
 template <int STRIDE, class G>
 __device__ __forceinline__ void adam_slab(float* __restrict__ P, float* __restrict__ M,
                                           float* __restrict__ V, size_t e0, int total, int lane,
-                                          float step, float b1, float b2, float bc2, float eps,
+                                          float step, float b1, float b2, float inv_bc2, float eps,
                                           G grad_of)
 {
     constexpr int kUnroll = 4;
@@ -368,12 +389,11 @@ __device__ __forceinline__ void adam_slab(float* __restrict__ P, float* __restri
 #pragma unroll
         for (int u = 0; u < kUnroll; u++) {
             if (!on[u]) continue;
-            const float mm = fmaf(b1, m[u], (1.0f - b1) * g[u]);
-            const float vv = fmaf(b2, v[u], (1.0f - b2) * g[u] * g[u]);
+            adam_math(p[u], m[u], v[u], g[u], step, b1, b2, inv_bc2, eps);
             const size_t e = e0 + base + 32 * u;
-            P[e] = p[u] - step * mm / (sqrtf(vv) / bc2 + eps);
-            M[e] = mm;
-            V[e] = vv;
+            P[e] = p[u];
+            M[e] = m[u];
+            V[e] = v[u];
         }
     }
 }
@@ -394,6 +414,150 @@ __device__ __forceinline__ void grad_slab(float* __restrict__ out, size_t e0, in
 // Per-Gaussian gradient slots in shared memory (phase 1 -> phase 2).
 constexpr int kGradSlots = 12;  // v_mean[3], v_scale[3], v_quat[4], v_opacity, pad
 constexpr int kBasisSlots = 19; // 15 SH-rest basis values + v_rgb[3] (odd stride: no bank conflicts)
+
+// SH-rest basis values (degrees 1-3, 15 of them) of the unit direction from
+// the camera to mean p: the factors of the rest gradient, g[b][c] =
+// basis[b] * v_rgb[c] (msplat_metal.metal:1915-1985).
+__device__ __forceinline__ void sh_rest_basis(const StepParams* __restrict__ P, const float p[3],
+                                              float* bs)
+{
+    const float d0 = p[0] - P->cam_pos[0], d1 = p[1] - P->cam_pos[1], d2 = p[2] - P->cam_pos[2];
+    const float dn = rsqrt_ieee((d0 * d0 + d1 * d1) + d2 * d2);
+    const float ux = d0 * dn, uy = d1 * dn, uz = d2 * dn;
+    const float xx = ux * ux, xy = ux * uy, xz = ux * uz, yy = uy * uy, yz = uy * uz, zz = uz * uz;
+    bs[0] = -MSP_SH_C1 * uy;
+    bs[1] = MSP_SH_C1 * uz;
+    bs[2] = -MSP_SH_C1 * ux;
+    bs[3] = kSH_C2[0] * xy;
+    bs[4] = kSH_C2[1] * yz;
+    bs[5] = kSH_C2[2] * ((2.f * zz - xx) - yy);
+    bs[6] = kSH_C2[3] * xz;
+    bs[7] = kSH_C2[4] * (xx - yy);
+    bs[8] = kSH_C3[0] * uy * (3.f * xx - yy);
+    bs[9] = kSH_C3[1] * xy * uz;
+    bs[10] = kSH_C3[2] * uy * ((4.f * zz - xx) - yy);
+    bs[11] = kSH_C3[3] * uz * ((2.f * zz - 3.f * xx) - 3.f * yy);
+    bs[12] = kSH_C3[4] * ux * ((4.f * zz - xx) - yy);
+    bs[13] = kSH_C3[5] * uz * (xx - yy);
+    bs[14] = kSH_C3[6] * ux * (xx - 3.f * yy);
+}
+
+// Geometry and colour VJP of one visible Gaussian (project_and_sh_backward_kernel,
+// msplat_metal.metal:1813-1986; VJPs :1216-1531): from its 9 raster
+// gradients `ga` fills gr[] (v_mean, v_scale, v_quat, v_opacity) and the
+// row bs[] (15 SH-rest basis values of the view direction, then v_rgb).
+__device__ __forceinline__ void gaussian_vjp(const StepParams* __restrict__ P,
+                                             const float* __restrict__ ga, const float4 co,
+                                             const float p[3], float ls0, float ls1, float ls2,
+                                             float q0, float q1, float q2, float q3,
+                                             float gr[kGradSlots], float* bs)
+{
+    const float vr0 = ga[0], vr1 = ga[1], vr2 = ga[2];
+    const float vc0 = ga[3], vc1 = ga[4], vc2 = ga[5];
+    const float vx = ga[6], vy = ga[7];
+    const float vop = ga[8];
+    const float fx = P->fx, fy = P->fy;
+    const float* vm = P->viewmat;
+    const float* pm = P->projmat;
+    float vmean[3];
+    // project_pix_vjp (:1216-1234); v_depth is always 0 (:1860-1864)
+    const float h3 = ((pm[12] * p[0] + pm[13] * p[1]) + pm[14] * p[2]) + pm[15];
+    const float rw = 1.f / (h3 + 1e-6f);
+    const float vnx = (0.5f * (float)P->img_w) * vx, vny = (0.5f * (float)P->img_h) * vy;
+    const float vp0 = vnx * rw, vp1 = vny * rw, vp2 = 0.f;
+    vmean[0] = ((pm[0] * vp0 + pm[4] * vp1) + pm[8] * vp2) + vm[8] * 0.f;
+    vmean[1] = ((pm[1] * vp0 + pm[5] * vp1) + pm[9] * vp2) + vm[9] * 0.f;
+    vmean[2] = ((pm[2] * vp0 + pm[6] * vp1) + pm[10] * vp2) + vm[10] * 0.f;
+    // cov2d_to_conic_vjp (:1253-1264): ((-X) G) X
+    const float X00 = -co.x, X01 = -co.y, X10 = -co.y, X11 = -co.z;
+    const float XG00 = X00 * vc0 + X10 * vc1, XG01 = X01 * vc0 + X11 * vc1;
+    const float XG10 = X00 * vc1 + X10 * vc2, XG11 = X01 * vc1 + X11 * vc2;
+    const float VS00 = XG00 * co.x + XG10 * co.y, VS01 = XG01 * co.x + XG11 * co.y;
+    const float VS10 = XG00 * co.y + XG10 * co.z, VS11 = XG01 * co.y + XG11 * co.z;
+    const float vcv0 = VS00, vcv1 = VS10 + VS01, vcv2 = VS11;
+    // recompute cov3d (:1875-1878)
+    const float es[3] = {msp_expf(ls0), msp_expf(ls1), msp_expf(ls2)};
+    const float qs = rsqrt_ieee(((q3 * q3 + q0 * q0) + q1 * q1) + q2 * q2);
+    const float w = q0 * qs, x = q1 * qs, y = q2 * qs, z = q3 * qs;
+    const M3 R = cols3(1.f - 2.f * (y * y + z * z), 2.f * (x * y + w * z), 2.f * (x * z - w * y),
+                       2.f * (x * y - w * z), 1.f - 2.f * (x * x + z * z), 2.f * (y * z + w * x),
+                       2.f * (x * z + w * y), 2.f * (y * z - w * x), 1.f - 2.f * (x * x + y * y));
+    const float gs = P->glob_scale;
+    const float sc[3] = {gs * es[0], gs * es[1], gs * es[2]};
+    M3 Mm;
+#pragma unroll
+    for (int c = 0; c < 3; c++)
+#pragma unroll
+        for (int r = 0; r < 3; r++) Mm.m[c][r] = R.m[c][r] * sc[c];
+    const M3 tmp = mul3(Mm, tr3(Mm));
+    const float cv[6] = {tmp.m[0][0], tmp.m[0][1], tmp.m[0][2], tmp.m[1][1], tmp.m[1][2], tmp.m[2][2]};
+    // project_cov3d_ewa_vjp (:1339-1407)
+    float pv0 = ((vm[0] * p[0] + vm[1] * p[1]) + vm[2] * p[2]) + vm[3];
+    float pv1 = ((vm[4] * p[0] + vm[5] * p[1]) + vm[6] * p[2]) + vm[7];
+    const float pv2 = ((vm[8] * p[0] + vm[9] * p[1]) + vm[10] * p[2]) + vm[11];
+    const float lim_x = 1.3f * P->tan_fovx, lim_y = 1.3f * P->tan_fovy;
+    pv0 = pv2 * fminf(lim_x, fmaxf(-lim_x, pv0 / pv2));
+    pv1 = pv2 * fminf(lim_y, fmaxf(-lim_y, pv1 / pv2));
+    const float rz = 1.f / pv2, rz2 = rz * rz;
+    const M3 Wm = cols3(vm[0], vm[4], vm[8], vm[1], vm[5], vm[9], vm[2], vm[6], vm[10]);
+    const M3 J = cols3(fx * rz, 0.f, 0.f, 0.f, fy * rz, 0.f, (-fx * pv0) * rz2,
+                       (-fy * pv1) * rz2, 0.f);
+    const M3 V = cols3(cv[0], cv[1], cv[2], cv[1], cv[3], cv[4], cv[2], cv[4], cv[5]);
+    const M3 vcov = cols3(vcv0, 0.5f * vcv1, 0.f, 0.5f * vcv1, vcv2, 0.f, 0.f, 0.f, 0.f);
+    const M3 T = mul3(J, Wm);
+    const M3 vV = mul3(mul3(tr3(T), vcov), T);
+    const M3 vT1 = mul3(mul3(vcov, T), tr3(V));
+    const M3 vT2 = mul3(mul3(tr3(vcov), T), V);
+    M3 vT;
+#pragma unroll
+    for (int c = 0; c < 3; c++)
+#pragma unroll
+        for (int r = 0; r < 3; r++) vT.m[c][r] = vT1.m[c][r] + vT2.m[c][r];
+    const float vcov3d[6] = {vV.m[0][0], vV.m[0][1] + vV.m[1][0], vV.m[0][2] + vV.m[2][0],
+                             vV.m[1][1], vV.m[1][2] + vV.m[2][1], vV.m[2][2]};
+    const M3 vJ = mul3(vT, tr3(Wm));
+    const float fx_rz2 = fx * rz2, fy_rz2 = fy * rz2, rz3 = rz2 * rz;
+    const float vt0 = -fx_rz2 * vJ.m[2][0];
+    const float vt1 = -fy_rz2 * vJ.m[2][1];
+    const float vt2 = ((-fx_rz2 * vJ.m[0][0] + 2.f * fx * pv0 * rz3 * vJ.m[2][0]) -
+                       fy_rz2 * vJ.m[1][1]) + 2.f * fy * pv1 * rz3 * vJ.m[2][1];
+#pragma unroll
+    for (int c = 0; c < 3; c++)
+        vmean[c] += (vt0 * Wm.m[c][0] + vt1 * Wm.m[c][1]) + vt2 * Wm.m[c][2];
+    // scale_rot_to_cov3d_vjp (:1498-1531)
+    const M3 vVs = cols3(vcov3d[0], 0.5f * vcov3d[1], 0.5f * vcov3d[2], 0.5f * vcov3d[1],
+                         vcov3d[3], 0.5f * vcov3d[4], 0.5f * vcov3d[2], 0.5f * vcov3d[4],
+                         vcov3d[5]);
+    const M3 Sm = cols3(sc[0], 0.f, 0.f, 0.f, sc[1], 0.f, 0.f, 0.f, sc[2]);
+    const M3 M2 = mul3(R, Sm);
+    M3 vVs2;
+#pragma unroll
+    for (int c = 0; c < 3; c++)
+#pragma unroll
+        for (int r = 0; r < 3; r++) vVs2.m[c][r] = 2.f * vVs.m[c][r];
+    const M3 vM = mul3(vVs2, M2);
+#pragma unroll
+    for (int c = 0; c < 3; c++)
+        gr[3 + c] = ((R.m[c][0] * vM.m[c][0] + R.m[c][1] * vM.m[c][1]) + R.m[c][2] * vM.m[c][2]) * es[c];
+    const M3 vR = mul3(vM, Sm);
+    const float (*v)[3] = vR.m;
+    gr[6] = 2.f * ((x * (v[1][2] - v[2][1]) + y * (v[2][0] - v[0][2])) + z * (v[0][1] - v[1][0]));
+    gr[7] = 2.f * (((-2.f * x * (v[1][1] + v[2][2]) + y * (v[0][1] + v[1][0])) +
+                    z * (v[0][2] + v[2][0])) + w * (v[1][2] - v[2][1]));
+    gr[8] = 2.f * (((x * (v[0][1] + v[1][0]) - 2.f * y * (v[0][0] + v[2][2])) +
+                    z * (v[1][2] + v[2][1])) + w * (v[2][0] - v[0][2]));
+    gr[9] = 2.f * (((x * (v[0][2] + v[2][0]) + y * (v[1][2] + v[2][1])) -
+                    2.f * z * (v[0][0] + v[1][1])) + w * (v[0][1] - v[1][0]));
+    gr[0] = vmean[0];
+    gr[1] = vmean[1];
+    gr[2] = vmean[2];
+    gr[10] = vop;
+    // SH basis of the view direction for the dc/rest Adam (:1915-1985)
+    sh_rest_basis(P, p, bs);
+    bs[15] = vr0;
+    bs[16] = vr1;
+    bs[17] = vr2;
+}
 
 // GRAD_OUT = false: the single-GPU step, Adam applied in place.
 // GRAD_OUT = true: the data-parallel step, gradients written to G (the
@@ -424,136 +588,13 @@ project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
             const float* __restrict__ scales = A.param[1];
             const float* __restrict__ quats = A.param[2];
             const float* ga = grad_acc + (size_t)i * kGradStride;
-            const float vr0 = ga[0], vr1 = ga[1], vr2 = ga[2];
-            const float vc0 = ga[3], vc1 = ga[4], vc2 = ga[5];
-            const float vx = ga[6], vy = ga[7];
-            const float vop = ga[8];
             const float p[3] = {means[3 * (size_t)i], means[3 * (size_t)i + 1], means[3 * (size_t)i + 2]};
             const float ls0 = scales[3 * (size_t)i], ls1 = scales[3 * (size_t)i + 1],
                         ls2 = scales[3 * (size_t)i + 2];
             const float q0 = quats[4 * (size_t)i], q1 = quats[4 * (size_t)i + 1],
                         q2 = quats[4 * (size_t)i + 2], q3 = quats[4 * (size_t)i + 3];
-            const float4 co = g_co[i];
-            const float fx = P->fx, fy = P->fy;
-            const float* vm = P->viewmat;
-            const float* pm = P->projmat;
-            float vmean[3];
-            // project_pix_vjp (:1216-1234); v_depth is always 0 (:1860-1864)
-            const float h3 = ((pm[12] * p[0] + pm[13] * p[1]) + pm[14] * p[2]) + pm[15];
-            const float rw = 1.f / (h3 + 1e-6f);
-            const float vnx = (0.5f * (float)P->img_w) * vx, vny = (0.5f * (float)P->img_h) * vy;
-            const float vp0 = vnx * rw, vp1 = vny * rw, vp2 = 0.f;
-            vmean[0] = ((pm[0] * vp0 + pm[4] * vp1) + pm[8] * vp2) + vm[8] * 0.f;
-            vmean[1] = ((pm[1] * vp0 + pm[5] * vp1) + pm[9] * vp2) + vm[9] * 0.f;
-            vmean[2] = ((pm[2] * vp0 + pm[6] * vp1) + pm[10] * vp2) + vm[10] * 0.f;
-            // cov2d_to_conic_vjp (:1253-1264): ((-X) G) X
-            const float X00 = -co.x, X01 = -co.y, X10 = -co.y, X11 = -co.z;
-            const float XG00 = X00 * vc0 + X10 * vc1, XG01 = X01 * vc0 + X11 * vc1;
-            const float XG10 = X00 * vc1 + X10 * vc2, XG11 = X01 * vc1 + X11 * vc2;
-            const float VS00 = XG00 * co.x + XG10 * co.y, VS01 = XG01 * co.x + XG11 * co.y;
-            const float VS10 = XG00 * co.y + XG10 * co.z, VS11 = XG01 * co.y + XG11 * co.z;
-            const float vcv0 = VS00, vcv1 = VS10 + VS01, vcv2 = VS11;
-            // recompute cov3d (:1875-1878)
-            const float es[3] = {msp_expf(ls0), msp_expf(ls1), msp_expf(ls2)};
-            const float qs = rsqrt_ieee(((q3 * q3 + q0 * q0) + q1 * q1) + q2 * q2);
-            const float w = q0 * qs, x = q1 * qs, y = q2 * qs, z = q3 * qs;
-            const M3 R = cols3(1.f - 2.f * (y * y + z * z), 2.f * (x * y + w * z), 2.f * (x * z - w * y),
-                               2.f * (x * y - w * z), 1.f - 2.f * (x * x + z * z), 2.f * (y * z + w * x),
-                               2.f * (x * z + w * y), 2.f * (y * z - w * x), 1.f - 2.f * (x * x + y * y));
-            const float gs = P->glob_scale;
-            const float sc[3] = {gs * es[0], gs * es[1], gs * es[2]};
-            M3 Mm;
-#pragma unroll
-            for (int c = 0; c < 3; c++)
-#pragma unroll
-                for (int r = 0; r < 3; r++) Mm.m[c][r] = R.m[c][r] * sc[c];
-            const M3 tmp = mul3(Mm, tr3(Mm));
-            const float cv[6] = {tmp.m[0][0], tmp.m[0][1], tmp.m[0][2], tmp.m[1][1], tmp.m[1][2], tmp.m[2][2]};
-            // project_cov3d_ewa_vjp (:1339-1407)
-            float pv0 = ((vm[0] * p[0] + vm[1] * p[1]) + vm[2] * p[2]) + vm[3];
-            float pv1 = ((vm[4] * p[0] + vm[5] * p[1]) + vm[6] * p[2]) + vm[7];
-            const float pv2 = ((vm[8] * p[0] + vm[9] * p[1]) + vm[10] * p[2]) + vm[11];
-            const float lim_x = 1.3f * P->tan_fovx, lim_y = 1.3f * P->tan_fovy;
-            pv0 = pv2 * fminf(lim_x, fmaxf(-lim_x, pv0 / pv2));
-            pv1 = pv2 * fminf(lim_y, fmaxf(-lim_y, pv1 / pv2));
-            const float rz = 1.f / pv2, rz2 = rz * rz;
-            const M3 Wm = cols3(vm[0], vm[4], vm[8], vm[1], vm[5], vm[9], vm[2], vm[6], vm[10]);
-            const M3 J = cols3(fx * rz, 0.f, 0.f, 0.f, fy * rz, 0.f, (-fx * pv0) * rz2,
-                               (-fy * pv1) * rz2, 0.f);
-            const M3 V = cols3(cv[0], cv[1], cv[2], cv[1], cv[3], cv[4], cv[2], cv[4], cv[5]);
-            const M3 vcov = cols3(vcv0, 0.5f * vcv1, 0.f, 0.5f * vcv1, vcv2, 0.f, 0.f, 0.f, 0.f);
-            const M3 T = mul3(J, Wm);
-            const M3 vV = mul3(mul3(tr3(T), vcov), T);
-            const M3 vT1 = mul3(mul3(vcov, T), tr3(V));
-            const M3 vT2 = mul3(mul3(tr3(vcov), T), V);
-            M3 vT;
-#pragma unroll
-            for (int c = 0; c < 3; c++)
-#pragma unroll
-                for (int r = 0; r < 3; r++) vT.m[c][r] = vT1.m[c][r] + vT2.m[c][r];
-            const float vcov3d[6] = {vV.m[0][0], vV.m[0][1] + vV.m[1][0], vV.m[0][2] + vV.m[2][0],
-                                     vV.m[1][1], vV.m[1][2] + vV.m[2][1], vV.m[2][2]};
-            const M3 vJ = mul3(vT, tr3(Wm));
-            const float fx_rz2 = fx * rz2, fy_rz2 = fy * rz2, rz3 = rz2 * rz;
-            const float vt0 = -fx_rz2 * vJ.m[2][0];
-            const float vt1 = -fy_rz2 * vJ.m[2][1];
-            const float vt2 = ((-fx_rz2 * vJ.m[0][0] + 2.f * fx * pv0 * rz3 * vJ.m[2][0]) -
-                               fy_rz2 * vJ.m[1][1]) + 2.f * fy * pv1 * rz3 * vJ.m[2][1];
-#pragma unroll
-            for (int c = 0; c < 3; c++)
-                vmean[c] += (vt0 * Wm.m[c][0] + vt1 * Wm.m[c][1]) + vt2 * Wm.m[c][2];
-            // scale_rot_to_cov3d_vjp (:1498-1531)
-            const M3 vVs = cols3(vcov3d[0], 0.5f * vcov3d[1], 0.5f * vcov3d[2], 0.5f * vcov3d[1],
-                                 vcov3d[3], 0.5f * vcov3d[4], 0.5f * vcov3d[2], 0.5f * vcov3d[4],
-                                 vcov3d[5]);
-            const M3 Sm = cols3(sc[0], 0.f, 0.f, 0.f, sc[1], 0.f, 0.f, 0.f, sc[2]);
-            const M3 M2 = mul3(R, Sm);
-            M3 vVs2;
-#pragma unroll
-            for (int c = 0; c < 3; c++)
-#pragma unroll
-                for (int r = 0; r < 3; r++) vVs2.m[c][r] = 2.f * vVs.m[c][r];
-            const M3 vM = mul3(vVs2, M2);
-#pragma unroll
-            for (int c = 0; c < 3; c++)
-                gr[3 + c] = ((R.m[c][0] * vM.m[c][0] + R.m[c][1] * vM.m[c][1]) + R.m[c][2] * vM.m[c][2]) * es[c];
-            const M3 vR = mul3(vM, Sm);
-            const float (*v)[3] = vR.m;
-            gr[6] = 2.f * ((x * (v[1][2] - v[2][1]) + y * (v[2][0] - v[0][2])) + z * (v[0][1] - v[1][0]));
-            gr[7] = 2.f * (((-2.f * x * (v[1][1] + v[2][2]) + y * (v[0][1] + v[1][0])) +
-                            z * (v[0][2] + v[2][0])) + w * (v[1][2] - v[2][1]));
-            gr[8] = 2.f * (((x * (v[0][1] + v[1][0]) - 2.f * y * (v[0][0] + v[2][2])) +
-                            z * (v[1][2] + v[2][1])) + w * (v[2][0] - v[0][2]));
-            gr[9] = 2.f * (((x * (v[0][2] + v[2][0]) + y * (v[1][2] + v[2][1])) -
-                            2.f * z * (v[0][0] + v[1][1])) + w * (v[0][1] - v[1][0]));
-            gr[0] = vmean[0];
-            gr[1] = vmean[1];
-            gr[2] = vmean[2];
-            gr[10] = vop;
-            // SH basis of the view direction for the dc/rest Adam (:1915-1985)
-            const float d0 = p[0] - P->cam_pos[0], d1 = p[1] - P->cam_pos[1], d2 = p[2] - P->cam_pos[2];
-            const float dn = rsqrt_ieee((d0 * d0 + d1 * d1) + d2 * d2);
-            const float ux = d0 * dn, uy = d1 * dn, uz = d2 * dn;
-            const float xx = ux * ux, xy = ux * uy, xz = ux * uz, yy = uy * uy, yz = uy * uz, zz = uz * uz;
-            float* bs = s_basis[tid];
-            bs[0] = -MSP_SH_C1 * uy;
-            bs[1] = MSP_SH_C1 * uz;
-            bs[2] = -MSP_SH_C1 * ux;
-            bs[3] = kSH_C2[0] * xy;
-            bs[4] = kSH_C2[1] * yz;
-            bs[5] = kSH_C2[2] * ((2.f * zz - xx) - yy);
-            bs[6] = kSH_C2[3] * xz;
-            bs[7] = kSH_C2[4] * (xx - yy);
-            bs[8] = kSH_C3[0] * uy * (3.f * xx - yy);
-            bs[9] = kSH_C3[1] * xy * uz;
-            bs[10] = kSH_C3[2] * uy * ((4.f * zz - xx) - yy);
-            bs[11] = kSH_C3[3] * uz * ((2.f * zz - 3.f * xx) - 3.f * yy);
-            bs[12] = kSH_C3[4] * ux * ((4.f * zz - xx) - yy);
-            bs[13] = kSH_C3[5] * uz * (xx - yy);
-            bs[14] = kSH_C3[6] * ux * (xx - 3.f * yy);
-            bs[15] = vr0;
-            bs[16] = vr1;
-            bs[17] = vr2;
+            gaussian_vjp(P, ga, g_co[i], p, ls0, ls1, ls2, q0, q1, q2, q3, gr, s_basis[tid]);
+            const float vx = ga[6], vy = ga[7];
             // densification statistics (accumulate_grad_stats_kernel)
             St.vis_counts[i] += 1.0f;
             St.grad_norm[i] += sqrtf(vx * vx + vy * vy);
@@ -603,23 +644,23 @@ project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
     }
     if (A.numel[0] > 0)  // means, every Gaussian (zero gradient when culled)
         adam_slab<3>(A.param[0], A.exp_avg[0], A.exp_avg_sq[0], (size_t)g0 * 3, cnt * 3, lane,
-                     P->adam_step[0], b1, b2, P->adam_bc2[0], eps,
+                     P->adam_step[0], b1, b2, 1.0f / P->adam_bc2[0], eps,
                      [&](int gl, int k, float& g) { g = sg[gl][k]; return true; });
     if (A.numel[1] > 0)  // scales (log)
         adam_slab<3>(A.param[1], A.exp_avg[1], A.exp_avg_sq[1], (size_t)g0 * 3, cnt * 3, lane,
-                     P->adam_step[1], b1, b2, P->adam_bc2[1], eps,
+                     P->adam_step[1], b1, b2, 1.0f / P->adam_bc2[1], eps,
                      [&](int gl, int k, float& g) { g = sg[gl][3 + k]; return true; });
     if (A.numel[2] > 0)  // quats
         adam_slab<4>(A.param[2], A.exp_avg[2], A.exp_avg_sq[2], (size_t)g0 * 4, cnt * 4, lane,
-                     P->adam_step[2], b1, b2, P->adam_bc2[2], eps,
+                     P->adam_step[2], b1, b2, 1.0f / P->adam_bc2[2], eps,
                      [&](int gl, int k, float& g) { g = sg[gl][6 + k]; return true; });
     if (A.numel[5] > 0)  // opacity logits
         adam_slab<1>(A.param[5], A.exp_avg[5], A.exp_avg_sq[5], (size_t)g0, cnt, lane,
-                     P->adam_step[5], b1, b2, P->adam_bc2[5], eps,
+                     P->adam_step[5], b1, b2, 1.0f / P->adam_bc2[5], eps,
                      [&](int gl, int, float& g) { g = sg[gl][10]; return true; });
     if (A.numel[3] > 0)  // features_dc, visible only
         adam_slab<3>(A.param[3], A.exp_avg[3], A.exp_avg_sq[3], (size_t)g0 * 3, cnt * 3, lane,
-                     P->adam_step[3], b1, b2, P->adam_bc2[3], eps,
+                     P->adam_step[3], b1, b2, 1.0f / P->adam_bc2[3], eps,
                      [&](int gl, int k, float& g) {
                          g = MSP_SH_C0 * sb[gl][15 + k];
                          return sv[gl] != 0;
@@ -635,16 +676,16 @@ project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
         };
         if (stride == 45)
             adam_slab<45>(A.param[4], A.exp_avg[4], A.exp_avg_sq[4], (size_t)g0 * 45, cnt * 45,
-                          lane, P->adam_step[4], b1, b2, P->adam_bc2[4], eps, rest_grad);
+                          lane, P->adam_step[4], b1, b2, 1.0f / P->adam_bc2[4], eps, rest_grad);
         else if (stride == 24)
             adam_slab<24>(A.param[4], A.exp_avg[4], A.exp_avg_sq[4], (size_t)g0 * 24, cnt * 24,
-                          lane, P->adam_step[4], b1, b2, P->adam_bc2[4], eps, rest_grad);
+                          lane, P->adam_step[4], b1, b2, 1.0f / P->adam_bc2[4], eps, rest_grad);
         else if (stride == 9)
             adam_slab<9>(A.param[4], A.exp_avg[4], A.exp_avg_sq[4], (size_t)g0 * 9, cnt * 9,
-                         lane, P->adam_step[4], b1, b2, P->adam_bc2[4], eps, rest_grad);
+                         lane, P->adam_step[4], b1, b2, 1.0f / P->adam_bc2[4], eps, rest_grad);
         else if (stride == 72)
             adam_slab<72>(A.param[4], A.exp_avg[4], A.exp_avg_sq[4], (size_t)g0 * 72, cnt * 72,
-                          lane, P->adam_step[4], b1, b2, P->adam_bc2[4], eps, rest_grad);
+                          lane, P->adam_step[4], b1, b2, 1.0f / P->adam_bc2[4], eps, rest_grad);
     }
 }
 
@@ -657,15 +698,115 @@ int rest_bases_updated(int degrees_to_use, int rest_stride)
     return nb;
 }
 
-void launch_project_backward_adam(const StepParams* P, int N, int degrees_to_use_host,
-                                  int rest_stride_host, const Buffers& B, const AdamPtrs& A,
-                                  const StatPtrs& St, cudaStream_t s)
+// ---------------------------------------------------------------------------
+// SH-rest Adam (the fused SH update of project_and_sh_backward_kernel,
+// msplat_metal.metal:1931-1985, for features_rest only), as its own
+// streaming kernel: 75% of the optimiser's bytes, and it needs nothing from
+// the geometry VJP -- only the view direction (from the mean, before the
+// means are updated, so this runs first), v_rgb and visibility.  Each lane
+// first builds its Gaussian's 15 basis values in shared memory; then each
+// warp streams its 32 Gaussians' contiguous rest slab, kU independent
+// elements per lane per round so every lane keeps 3*kU loads in flight.
+// Culled Gaussians are neither read nor written.
+// ---------------------------------------------------------------------------
+constexpr int kRestThreads = 256;
+
+template <int RS>
+__global__ void __launch_bounds__(kRestThreads)
+rest_adam_kernel(const StepParams* __restrict__ P, int N, const int* __restrict__ radii,
+                 const float* __restrict__ grad_acc, const float* __restrict__ means,
+                 float* __restrict__ rest, float* __restrict__ rest_m, float* __restrict__ rest_v,
+                 int used)
 {
-    if (N <= 0) return;
+    __shared__ float s_b[kRestThreads][17];  // 15 basis values + pad (odd stride)
+    __shared__ float s_c[kRestThreads][3];   // v_rgb
+    __shared__ int s_vis[kRestThreads];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int base = blockIdx.x * kRestThreads;
+    const int i = base + tid;
+    bool vis = false;
+    if (i < N && radii[i] > 0) {
+        vis = true;
+        const float p[3] = {means[3 * (size_t)i], means[3 * (size_t)i + 1], means[3 * (size_t)i + 2]};
+        sh_rest_basis(P, p, s_b[tid]);
+        const float* ga = grad_acc + (size_t)i * kGradStride;
+        s_c[tid][0] = ga[0];
+        s_c[tid][1] = ga[1];
+        s_c[tid][2] = ga[2];
+    }
+    s_vis[tid] = vis;
+    __syncthreads();
+    const int wbase = warp * 32;
+    const int g0 = base + wbase;
+    if (g0 >= N) return;
+    const int cnt = min(32, N - g0);
+    if (!__any_sync(0xffffffffu, s_vis[wbase + (lane < cnt ? lane : 0)])) return;
+    const float step = P->adam_step[4], inv_bc2 = 1.0f / P->adam_bc2[4];
+    const float b1 = P->beta1, b2 = P->beta2, eps = P->eps;
+    const size_t e0 = (size_t)g0 * RS;
+    const int total = cnt * RS;
+    constexpr int kU = 8;
+    for (int eb = lane; eb < total; eb += 32 * kU) {
+        float g[kU], pv[kU], mv[kU], vv[kU];
+        bool on[kU];
+#pragma unroll
+        for (int u = 0; u < kU; u++) {
+            const int e = eb + 32 * u;
+            const int gl = e / RS, kk = e - gl * RS;
+            on[u] = e < total && kk < used && s_vis[wbase + gl];
+            if (on[u]) {
+                const int b = kk / 3, c = kk - 3 * b;
+                g[u] = s_b[wbase + gl][b] * s_c[wbase + gl][c];
+                pv[u] = rest[e0 + e];
+                mv[u] = rest_m[e0 + e];
+                vv[u] = rest_v[e0 + e];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kU; u++) {
+            if (!on[u]) continue;
+            adam_math(pv[u], mv[u], vv[u], g[u], step, b1, b2, inv_bc2, eps);
+            const size_t e = e0 + eb + 32 * u;
+            rest[e] = pv[u];
+            rest_m[e] = mv[u];
+            rest_v[e] = vv[u];
+        }
+    }
+}
+
+int launch_project_backward_adam(const StepParams* P, int N, int degrees_to_use_host,
+                                 int rest_stride_host, const Buffers& B, const AdamPtrs& A,
+                                 const StatPtrs& St, cudaStream_t s)
+{
+    if (N <= 0) return 0;
     const int nb = rest_bases_updated(degrees_to_use_host, rest_stride_host);
+    AdamPtrs A2 = A;
+    int launches = 1;
+    if (A.numel[4] > 0 && nb > 0) {
+        const int grid = (N + kRestThreads - 1) / kRestThreads;
+        const int used = nb * 3;
+#define MSP_REST(RS)                                                                           \
+    rest_adam_kernel<RS><<<grid, kRestThreads, 0, s>>>(P, N, B.proj.radii, B.grad_acc,       \
+                                                       A.param[0], A.param[4], A.exp_avg[4],  \
+                                                       A.exp_avg_sq[4], used)
+        bool done = true;
+        switch (rest_stride_host) {
+            case 45: MSP_REST(45); break;
+            case 24: MSP_REST(24); break;
+            case 9: MSP_REST(9); break;
+            case 72: MSP_REST(72); break;
+            default: done = false; break;
+        }
+#undef MSP_REST
+        if (done) {
+            A2.numel[4] = 0;  // the rest group is done
+            launches++;
+        }
+    }
     const int grid = (N + kBwdThreads - 1) / kBwdThreads;
     project_backward_adam_kernel<false><<<grid, kBwdThreads, 0, s>>>(
-        P, N, B.proj.radii, B.proj.conic_op, B.grad_acc, A, St, GradOut{}, nb);
+        P, N, B.proj.radii, B.proj.conic_op, B.grad_acc, A2, St, GradOut{}, nb);
+    return launches;
 }
 
 void launch_project_backward_grads(const StepParams* P, int N, int degrees_to_use_host,
@@ -698,7 +839,7 @@ adam_apply_kernel(ApplyArgs a)
     const float* __restrict__ Gd = a.grad[gi];
     const int S = a.stride[gi];
     const int e_end = a.end * S;
-    const float step = a.step[gi], bc2 = a.bc2[gi];
+    const float step = a.step[gi], inv_bc2 = 1.0f / a.bc2[gi];
     const bool sh = gi == 3 || gi == 4;
     for (int e = a.begin * S + blockIdx.x * blockDim.x + threadIdx.x; e < e_end;
          e += gridDim.x * blockDim.x) {
@@ -707,7 +848,7 @@ adam_apply_kernel(ApplyArgs a)
             if (!(a.vis[i] > 0.f)) continue;
             if (gi == 4 && e - i * S >= a.used_rest) continue;
         }
-        adam_elem(P + e, M + e, V + e, Gd[e] * a.scale, step, a.beta1, a.beta2, bc2, a.eps);
+        adam_elem(P + e, M + e, V + e, Gd[e] * a.scale, step, a.beta1, a.beta2, inv_bc2, a.eps);
     }
 }
 
