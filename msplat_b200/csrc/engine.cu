@@ -221,6 +221,8 @@ static void poll_readback(bool wait)
     }
     g.readback_pending = false;
     g.last_loss = (float)((double)g.h_loss[0] * g.last_loss_scale);
+    if (g.h_misc[0] & kErrStageTimeout)
+        fprintf(stderr, "msplat: a shared-memory bulk copy timed out; the step is incomplete\n");
     if (g.h_misc[0] & kErrIsectOverflow) {
         const long long need = (long long)g.h_misc[1];
         if (need > g.growth_isect) {

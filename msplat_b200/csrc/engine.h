@@ -40,6 +40,7 @@ struct StepParams {
 // Device error word bits (read back by the host after a step).
 enum ErrorBits : int {
     kErrIsectOverflow = 1,   // intersections exceeded the key buffer
+    kErrStageTimeout = 2,    // a bulk copy into shared memory did not complete in time
 };
 
 // Per-Gaussian geometry written by the projection and read by binning and

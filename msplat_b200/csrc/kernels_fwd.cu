@@ -4,6 +4,7 @@
 // CPU oracle.
 #include "engine.h"
 #include "msp_math.cuh"
+#include "tma.cuh"
 
 namespace msp {
 
@@ -61,19 +62,81 @@ __device__ __forceinline__ void sh_to_color(int degree, float x, float y, float 
     }
 }
 
+// Block layout of the staged inputs in shared memory (floats).
+struct ProjStage {
+    static constexpr int kMeans = 0;
+    static constexpr int kScales = kMeans + 3 * kProjThreads;
+    static constexpr int kQuats = kScales + 3 * kProjThreads;
+    static constexpr int kOpac = kQuats + 4 * kProjThreads;
+    static constexpr int kDc = kOpac + kProjThreads;
+    static constexpr int kRest = kDc + 3 * kProjThreads;  // + kProjThreads * rest_stride
+};
+
+// All of a block's inputs (means, scales, quats, opacities, dc and the
+// SH-rest rows, ~30 KB for 128 Gaussians at SH degree 3) are staged in
+// shared memory first: by seven 1D bulk copies issued together when the
+// block is full and the arrays are 16-byte aligned, else by plain loads.
+// Every byte of the block is then in flight at once instead of in two
+// dependent rounds (geometry, then the SH rows of the visible Gaussians).
 template <bool ZERO_GRADS>
 __global__ void __launch_bounds__(kProjThreads)
 project_forward_kernel(const StepParams* __restrict__ P, int N, const float* __restrict__ means,
                        const float* __restrict__ scales, const float* __restrict__ quats,
                        const float* __restrict__ dc, const float* __restrict__ rest,
                        const float* __restrict__ opac, ProjOut out, int* __restrict__ tile_count,
-                       float* __restrict__ grad_acc, int used, int sstride)
+                       float* __restrict__ grad_acc, int rest_stride, int bulk,
+                       int* __restrict__ err)
 {
-    extern __shared__ float s_rest[];  // kProjThreads * sstride
-    __shared__ int s_vis[kProjThreads];
+    extern __shared__ __align__(16) float sm[];
+    __shared__ unsigned long long s_bar;
+    __shared__ int s_fail;
+    const float* s_means = sm + ProjStage::kMeans;
+    const float* s_scales = sm + ProjStage::kScales;
+    const float* s_quats = sm + ProjStage::kQuats;
+    const float* s_opac = sm + ProjStage::kOpac;
+    const float* s_dc = sm + ProjStage::kDc;
+    const float* s_rest = sm + ProjStage::kRest;
     const int tid = threadIdx.x;
     const int base = blockIdx.x * kProjThreads;
     const int i = base + tid;
+    const int cnt = min(kProjThreads, N - base);
+    const size_t gb = (size_t)base;
+
+    if (bulk && cnt == kProjThreads) {
+        if (tid == 0) mbar_init(&s_bar);
+        __syncthreads();
+        if (tid == 0) {
+            const unsigned rs_bytes = (unsigned)(kProjThreads * rest_stride * 4);
+            mbar_expect_tx(&s_bar, (unsigned)(ProjStage::kRest * 4) + rs_bytes);
+            bulk_load(sm + ProjStage::kMeans, means + gb * 3, kProjThreads * 12, &s_bar);
+            bulk_load(sm + ProjStage::kScales, scales + gb * 3, kProjThreads * 12, &s_bar);
+            bulk_load(sm + ProjStage::kQuats, quats + gb * 4, kProjThreads * 16, &s_bar);
+            bulk_load(sm + ProjStage::kOpac, opac + gb, kProjThreads * 4, &s_bar);
+            bulk_load(sm + ProjStage::kDc, dc + gb * 3, kProjThreads * 12, &s_bar);
+            if (rs_bytes) bulk_load(sm + ProjStage::kRest, rest + gb * rest_stride, rs_bytes, &s_bar);
+            s_fail = !mbar_wait_bounded(&s_bar, 0);
+            if (s_fail) {
+                atomicOr(err, kErrStageTimeout);
+                mbar_wait_bounded(&s_bar, 0);  // let copies still in flight land
+            }
+        }
+        __syncthreads();
+        if (s_fail) {  // leave the block's Gaussians culled
+            out.radii[i] = 0;
+            return;
+        }
+    } else {
+        for (int e = tid; e < cnt * 3; e += kProjThreads) {
+            sm[ProjStage::kMeans + e] = means[gb * 3 + e];
+            sm[ProjStage::kScales + e] = scales[gb * 3 + e];
+            sm[ProjStage::kDc + e] = dc[gb * 3 + e];
+        }
+        for (int e = tid; e < cnt * 4; e += kProjThreads) sm[ProjStage::kQuats + e] = quats[gb * 4 + e];
+        if (tid < cnt) sm[ProjStage::kOpac + tid] = opac[gb + tid];
+        for (int e = tid; e < cnt * rest_stride; e += kProjThreads)
+            sm[ProjStage::kRest + e] = rest[gb * rest_stride + e];
+        __syncthreads();
+    }
 
     bool vis = false;
     float px_c = 0.f, py_c = 0.f;
@@ -81,20 +144,20 @@ project_forward_kernel(const StepParams* __restrict__ P, int N, const float* __r
     float p[3] = {0.f, 0.f, 0.f};
     if (i < N) {
         out.radii[i] = 0;
-        p[0] = means[3 * (size_t)i];
-        p[1] = means[3 * (size_t)i + 1];
-        p[2] = means[3 * (size_t)i + 2];
+        p[0] = s_means[3 * tid];
+        p[1] = s_means[3 * tid + 1];
+        p[2] = s_means[3 * tid + 2];
         const float* vm = P->viewmat;
         // clip_near_plane / transform_4x3 (:90-97, :134-145)
         float pv0 = ((vm[0] * p[0] + vm[1] * p[1]) + vm[2] * p[2]) + vm[3];
         float pv1 = ((vm[4] * p[0] + vm[5] * p[1]) + vm[6] * p[2]) + vm[7];
         float pv2 = ((vm[8] * p[0] + vm[9] * p[1]) + vm[10] * p[2]) + vm[11];
         if (!(pv2 <= P->clip_thresh)) {
-            float s0 = msp_expf(scales[3 * (size_t)i]);
-            float s1 = msp_expf(scales[3 * (size_t)i + 1]);
-            float s2 = msp_expf(scales[3 * (size_t)i + 2]);
-            const float4 q4 = make_float4(quats[4 * (size_t)i], quats[4 * (size_t)i + 1],
-                                          quats[4 * (size_t)i + 2], quats[4 * (size_t)i + 3]);
+            float s0 = msp_expf(s_scales[3 * tid]);
+            float s1 = msp_expf(s_scales[3 * tid + 1]);
+            float s2 = msp_expf(s_scales[3 * tid + 2]);
+            const float4 q4 = make_float4(s_quats[4 * tid], s_quats[4 * tid + 1],
+                                          s_quats[4 * tid + 2], s_quats[4 * tid + 3]);
             // quat_to_rotmat (:111-131): memory order w, x, y, z
             float qs = rsqrt_ieee(((q4.w * q4.w + q4.x * q4.x) + q4.y * q4.y) + q4.z * q4.z);
             float w = q4.x * qs, x = q4.y * qs, y = q4.z * qs, z = q4.w * qs;
@@ -176,50 +239,20 @@ project_forward_kernel(const StepParams* __restrict__ P, int N, const float* __r
                     out.radii[i] = f2i(radius);
                     out.depth[i] = pv2;
                     out.xy[i] = make_float2(px_c, py_c);
-                    out.conic_op[i] = make_float4(ca, cb, cc, sigmoid_ref(opac[i]));
+                    out.conic_op[i] = make_float4(ca, cb, cc, sigmoid_ref(s_opac[tid]));
                     out.rect[i] = make_uint2((unsigned)x0 | ((unsigned)y0 << 16),
                                              (unsigned)x1 | ((unsigned)y1 << 16));
                 }
             }
         }
     }
-    s_vis[tid] = vis;
-    __syncthreads();
-    // Stage the used SH-rest coefficients of the block's visible Gaussians:
-    // one warp per Gaussian reads its contiguous row.
-    if (used > 0) {
-        const int lane = tid & 31, warp = tid >> 5;
-        const int stride = P->rest_stride;
-        constexpr int kRows = 4;  // rows loaded before any is stored
-        for (int g0 = warp * kRows; g0 < kProjThreads; g0 += (kProjThreads / 32) * kRows) {
-            float v[kRows][3];
-#pragma unroll
-            for (int r = 0; r < kRows; r++) {
-                const int gl = g0 + r;
-                const float* src = rest + (size_t)(base + gl) * stride;
-#pragma unroll
-                for (int q = 0; q < 3; q++) {
-                    const int k = lane + 32 * q;
-                    v[r][q] = (s_vis[gl] && k < used) ? src[k] : 0.f;
-                }
-            }
-#pragma unroll
-            for (int r = 0; r < kRows; r++)
-#pragma unroll
-                for (int q = 0; q < 3; q++) {
-                    const int k = lane + 32 * q;
-                    if (k < used) s_rest[(g0 + r) * sstride + k] = v[r][q];
-                }
-        }
-        __syncthreads();
-    }
     if (!vis) return;
     // SH colour (:1780-1786): viewdir = normalize(p - cam_pos)
     float d0 = p[0] - P->cam_pos[0], d1 = p[1] - P->cam_pos[1], d2 = p[2] - P->cam_pos[2];
     float dn = rsqrt_ieee((d0 * d0 + d1 * d1) + d2 * d2);
     float col[3];
-    float dcv[3] = {dc[3 * (size_t)i], dc[3 * (size_t)i + 1], dc[3 * (size_t)i + 2]};
-    sh_to_color(P->degrees_to_use, d0 * dn, d1 * dn, d2 * dn, dcv, s_rest + tid * sstride, col);
+    float dcv[3] = {s_dc[3 * tid], s_dc[3 * tid + 1], s_dc[3 * tid + 2]};
+    sh_to_color(P->degrees_to_use, d0 * dn, d1 * dn, d2 * dn, dcv, s_rest + tid * rest_stride, col);
     out.rgb[i] = make_float4(col[0], col[1], col[2], 0.f);
     const int tx_n = P->tiles_x;
     for (int ty = y0; ty < y1; ty++)
@@ -236,20 +269,21 @@ void launch_project_forward(const StepParams* P, int N, const float* means, cons
                             const float* opac, const Buffers& B, bool zero_grads,
                             int degrees_to_use_host, int rest_stride_host, cudaStream_t s)
 {
+    (void)degrees_to_use_host;
     if (N <= 0) return;
-    int used = (num_sh_bases_host(degrees_to_use_host) - 1) * 3;
-    if (used > rest_stride_host) used = rest_stride_host;
-    int sstride = used | 1;
-    size_t smem = (size_t)kProjThreads * sstride * sizeof(float);
-    int grid = (N + kProjThreads - 1) / kProjThreads;
+    const size_t smem = (size_t)(ProjStage::kRest + kProjThreads * rest_stride_host) * sizeof(float);
+    const uintptr_t mis = (uintptr_t)means | (uintptr_t)scales | (uintptr_t)quats |
+                          (uintptr_t)dc | (uintptr_t)opac | (rest_stride_host ? (uintptr_t)rest : 0);
+    const int bulk = (mis & 15) == 0 && smem <= 48 * 1024;
+    const int grid = (N + kProjThreads - 1) / kProjThreads;
     if (zero_grads)
         project_forward_kernel<true><<<grid, kProjThreads, smem, s>>>(
-            P, N, means, scales, quats, dc, rest, opac, B.proj, B.tile_count, B.grad_acc, used,
-            sstride);
+            P, N, means, scales, quats, dc, rest, opac, B.proj, B.tile_count, B.grad_acc,
+            rest_stride_host, bulk, B.err);
     else
         project_forward_kernel<false><<<grid, kProjThreads, smem, s>>>(
-            P, N, means, scales, quats, dc, rest, opac, B.proj, B.tile_count, nullptr, used,
-            sstride);
+            P, N, means, scales, quats, dc, rest, opac, B.proj, B.tile_count, nullptr,
+            rest_stride_host, bulk, B.err);
 }
 
 // ---------------------------------------------------------------------------
@@ -315,21 +349,55 @@ scatter_kernel(const StepParams* __restrict__ P, int N, const int* __restrict__ 
                int* __restrict__ count, const int* __restrict__ offset,
                unsigned long long* __restrict__ keys)
 {
+    // Warp-cooperative: the warp's 32 Gaussians' (Gaussian, tile) pairs are
+    // dealt out to all lanes, 32 at a time, so every lane has an atomic in
+    // flight each round however unevenly the rects are sized.
+    const int lane = threadIdx.x & 31;
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= N || radii[i] <= 0) return;
-    const uint2 r = rect[i];
-    const int x0 = r.x & 0xffff, y0 = r.x >> 16, x1 = r.y & 0xffff, y1 = r.y >> 16;
-    const unsigned long long key =
-        ((unsigned long long)__float_as_uint(depth[i]) << 32) | (unsigned)i;
+    int x0 = 0, y0 = 0, w = 0, area = 0;
+    unsigned long long key = 0;
+    if (i < N && radii[i] > 0) {
+        const uint2 r = rect[i];
+        x0 = r.x & 0xffff;
+        y0 = r.x >> 16;
+        w = (r.y & 0xffff) - x0;
+        area = w * ((r.y >> 16) - y0);
+        key = ((unsigned long long)__float_as_uint(depth[i]) << 32) | (unsigned)i;
+    }
+    // inclusive prefix of the areas over the warp
+    int incl = area;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += u;
+    }
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
     const long long cap = P->capacity;
     const int tx_n = P->tiles_x;
-    for (int ty = y0; ty < y1; ty++)
-        for (int tx = x0; tx < x1; tx++) {
+    for (int p0 = 0; p0 < total; p0 += 32) {
+        const int pidx = p0 + lane;
+        // owner = first lane whose inclusive prefix exceeds pidx
+        int owner = 0;
+#pragma unroll
+        for (int step = 16; step > 0; step >>= 1) {
+            const int probe = __shfl_sync(0xffffffffu, incl, owner + step - 1);
+            if (probe <= pidx) owner += step;
+        }
+        const int o_incl = __shfl_sync(0xffffffffu, incl, owner);
+        const int o_area = __shfl_sync(0xffffffffu, area, owner);
+        const int o_x0 = __shfl_sync(0xffffffffu, x0, owner);
+        const int o_y0 = __shfl_sync(0xffffffffu, y0, owner);
+        const int o_w = __shfl_sync(0xffffffffu, w, owner);
+        const unsigned long long o_key = __shfl_sync(0xffffffffu, key, owner);
+        if (pidx < total) {
+            const int k = pidx - (o_incl - o_area);
+            const int ty = o_y0 + k / o_w, tx = o_x0 + k % o_w;
             const int t = ty * tx_n + tx;
             const int pos = atomicSub(&count[t * kCountPitch], 1) - 1;
             const long long idx = (long long)offset[t] + pos;
-            if (idx < cap) keys[idx] = key;
+            if (idx < cap) keys[idx] = o_key;
         }
+    }
 }
 
 void launch_scatter(const StepParams* P, int N, const Buffers& B, cudaStream_t s)
