@@ -1,10 +1,12 @@
 """Build the engine's shared library, libmsplat_b200.so, in-tree.
 
-nvcc compiles every .cu under csrc/ for sm_100a (B200) only.  The kernels
-are compiled with --fmad=false: the engine's projection, binning, forward
-raster and loss must produce the same bits as the CPU oracle, and the
-backward must replay the forward's alpha decisions exactly; explicit fmaf()
-calls mark the fused multiply-adds the reference kernels ask for.
+nvcc compiles every .cu under csrc/ for sm_100a (B200) only.  The forward
+files are compiled with --fmad=false: the engine's projection, binning,
+forward raster and loss must produce the same bits as the CPU oracle, and
+explicit fmaf() calls mark the fused multiply-adds the reference kernels ask
+for.  The backward file (gradients and Adam, held to a tolerance) is
+compiled with FMA contraction; the forward decisions it replays are written
+with explicit non-fused operations.
 """
 from __future__ import annotations
 
@@ -20,8 +22,13 @@ LIB = os.path.join(HERE, "libmsplat_b200.so")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CFLAGS = ["-O3", "-lineinfo", "-std=c++17", "--fmad=false", "-Xcompiler", "-fPIC",
-          "-Xcompiler", "-Wall", f"-I{INCLUDE}"]
+CFLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
+          f"-I{INCLUDE}"]
+FMA_CONTRACTED = {"kernels_bwd.cu"}   # every other file: --fmad=false
+
+
+def fmad_flag(src: str) -> str:
+    return "--fmad=true" if os.path.basename(src) in FMA_CONTRACTED else "--fmad=false"
 
 
 def _nvcc() -> str:
@@ -58,7 +65,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
         obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
         objs.append(obj)
         if force or _stale(obj, [src] + deps):
-            jobs.append([nvcc, *ARCH, *CFLAGS, "-c", src, "-o", obj])
+            jobs.append([nvcc, *ARCH, *CFLAGS, fmad_flag(src), "-c", src, "-o", obj])
 
     def run(cmd):
         if verbose:

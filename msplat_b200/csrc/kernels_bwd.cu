@@ -1,6 +1,8 @@
 // kernels_bwd.cu -- backward half of the step: rasterizer VJP, projection
-// VJP, and every Adam update, in two kernels.  Compiled with --fmad=false so
-// the alpha/T decisions replayed here are exactly the forward's.
+// VJP, and every Adam update.  Unlike the forward files this one is compiled
+// with FMA contraction (its results are held to a tolerance, not to the
+// bit); the few expressions that replay forward decisions (sigma, alpha) are
+// written with explicit non-fused operations so they stay bit-identical.
 #include <algorithm>
 
 #include "engine.h"
@@ -33,50 +35,56 @@ constexpr int kBwdPPT = 2;
 constexpr int kBwdMinBlocks = 8;
 constexpr int kRastBatch = 256;
 
-// Back-to-front state of one pixel.
+// Back-to-front state of one pixel.  Bs = sum_c (buffer_c + T_final*bg_c) *
+// v_out_c, the colour "behind" the current Gaussian weighted by the pixel's
+// output gradient: the reference's per-channel v_alpha terms (rgb_c*T -
+// buffer_c*ra - T_final*bg_c*ra) * v_out_c summed over c need only this one
+// scalar, updated as buffer_c += rgb_c * fac.
 struct PixelBwd {
-    float T, b0, b1, b2;
+    float T, Bs;
     float vo0, vo1, vo2;
-    float tfb0, tfb1, tfb2;
     int bin_final;
 };
 
-// One pixel's contribution to Gaussian (xy, co, raw) at list index idx,
-// added into v[0..8] (v_rgb, v_conic, v_xy, v_opacity); the same decisions
-// as the forward (rasterize_backward_kernel :1023-1075).
+// One pixel's contribution to Gaussian (xy, co, rc) at list index idx,
+// added into v[0..8]; rc holds the clamped colour max(rgb + 0.5, 0).
+// sigma and alpha replay the forward bit for bit (its exact products, no
+// contraction; this file is otherwise compiled with FMA contraction), so the
+// skip decisions are the forward's (rasterize_backward_kernel :1023-1075).
+// v[3..5] are summed without the factor 0.5 and v[8] without the factor
+// -(1 - opacity); both are applied once after the warp reduction.
 __device__ __forceinline__ bool backprop(PixelBwd& s, float fpx, float fpy, const float2 xy,
-                                         const float4 co, const float4 raw, int idx, float v[9])
+                                         const float4 co, const float4 rc, int idx, float v[9])
 {
     if (idx > s.bin_final) return false;
     const float dx = xy.x - fpx, dy = xy.y - fpy;
-    const float sigma = fmaf(0.5f, fmaf(co.x, dx * dx, co.z * dy * dy), co.y * dx * dy);
+    const float dxx = __fmul_rn(dx, dx);
+    const float sigma = fmaf(0.5f, fmaf(co.x, dxx, __fmul_rn(__fmul_rn(co.z, dy), dy)),
+                             __fmul_rn(__fmul_rn(co.y, dx), dy));
     if (sigma < 0.f || sigma >= 5.55f) return false;
-    const float alpha = fminf(0.999f, co.w * msp_expf_normal(-sigma));
+    const float alpha = fminf(0.999f, __fmul_rn(co.w, msp_expf_normal(-sigma)));
     if (alpha < 1.f / 255.f || !(alpha < 0.999f)) return false;
-    const float ra = 1.f / (1.f - alpha);
+    // 1 / (1 - alpha): the hardware reciprocal refined by one Newton step
+    // (the product of these factors rebuilds T along the whole list, so a
+    // last-ulp bias would compound; d lies in (0.001, 1], no special cases)
+    const float d = 1.f - alpha;
+    const float r0 = __fdividef(1.f, d);
+    const float ra = fmaf(r0, fmaf(-d, r0, 1.f), r0);
     s.T *= ra;
     const float fac = alpha * s.T;
-    const float r0 = fmaxf(raw.x + 0.5f, 0.f), r1 = fmaxf(raw.y + 0.5f, 0.f),
-                r2 = fmaxf(raw.z + 0.5f, 0.f);
-    const float nra = -ra;
-    const float e0 = fmaf(r0, s.T, fmaf(-s.b0, ra, nra * s.tfb0));
-    const float e1 = fmaf(r1, s.T, fmaf(-s.b1, ra, nra * s.tfb1));
-    const float e2 = fmaf(r2, s.T, fmaf(-s.b2, ra, nra * s.tfb2));
-    const float v_alpha = (e0 * s.vo0 + e1 * s.vo1) + e2 * s.vo2;
-    s.b0 = fmaf(r0, fac, s.b0);
-    s.b1 = fmaf(r1, fac, s.b1);
-    s.b2 = fmaf(r2, fac, s.b2);
-    const float v_sigma = -alpha * v_alpha;
+    const float rv = rc.x * s.vo0 + rc.y * s.vo1 + rc.z * s.vo2;
+    const float v_alpha = s.T * rv - ra * s.Bs;
+    s.Bs += fac * rv;
     v[0] += fac * s.vo0;
     v[1] += fac * s.vo1;
     v[2] += fac * s.vo2;
-    const float hv = 0.5f * v_sigma;
-    v[3] += hv * (dx * dx);
-    v[4] += hv * (dx * dy);
-    v[5] += hv * (dy * dy);
-    v[6] += v_sigma * fmaf(co.x, dx, co.y * dy);
-    v[7] += v_sigma * fmaf(co.y, dx, co.z * dy);
-    v[8] += -v_sigma * (1.f - co.w);
+    const float v_sigma = -alpha * v_alpha;
+    v[3] += v_sigma * dxx;
+    v[4] += v_sigma * (dx * dy);
+    v[5] += v_sigma * (dy * dy);
+    v[6] += v_sigma * (co.x * dx + co.y * dy);
+    v[7] += v_sigma * (co.y * dx + co.z * dy);
+    v[8] += v_sigma;
     return true;
 }
 
@@ -121,30 +129,30 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
     for (int h = 0; h < PPT; h++) {
         PixelBwd& s = st[h];
         const int py = by + (lane >> 4) + 2 * h;
-        s = PixelBwd{0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, beg - 1};
+        s = PixelBwd{0.f, 0.f, 0.f, 0.f, 0.f, beg - 1};
         if (px < W && py < H) {
             const size_t pix = (size_t)py * W + px;
             const float Tf = final_T[pix];
             s.vo0 = v_rendered[3 * pix];
             s.vo1 = v_rendered[3 * pix + 1];
             s.vo2 = v_rendered[3 * pix + 2];
-            s.tfb0 = Tf * P->bg[0];
-            s.tfb1 = Tf * P->bg[1];
-            s.tfb2 = Tf * P->bg[2];
+            float b0 = 0.f, b1 = 0.f, b2 = 0.f;
             if (CHUNKED) {
                 const size_t o = (size_t)k * NP + pix;
                 const int bf = chunk_idx[o];
                 if (bf >= beg) {
                     s.bin_final = bf;
                     s.T = prefix_T[o] * chunk_T[o];
-                    s.b0 = after_C[3 * o];
-                    s.b1 = after_C[3 * o + 1];
-                    s.b2 = after_C[3 * o + 2];
+                    b0 = after_C[3 * o];
+                    b1 = after_C[3 * o + 1];
+                    b2 = after_C[3 * o + 2];
                 }
             } else {
                 s.bin_final = final_idx[pix];
                 s.T = Tf;
             }
+            s.Bs = (b0 + Tf * P->bg[0]) * s.vo0 + (b1 + Tf * P->bg[1]) * s.vo1 +
+                   (b2 + Tf * P->bg[2]) * s.vo2;
         }
         my_max = max(my_max, s.bin_final);
     }
@@ -170,7 +178,12 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
                 s_id[slot] = g;
                 s_xy[slot] = xy;
                 s_co[slot] = co;
-                s_rgb[slot] = g_rgb[g];
+                // clamped colour; .w holds the clamp mask (bit c: rgb_c + 0.5 >= 0)
+                const float4 raw = g_rgb[g];
+                const int mask = (raw.x + 0.5f >= 0.f ? 1 : 0) | (raw.y + 0.5f >= 0.f ? 2 : 0) |
+                                 (raw.z + 0.5f >= 0.f ? 4 : 0);
+                s_rgb[slot] = make_float4(fmaxf(raw.x + 0.5f, 0.f), fmaxf(raw.y + 0.5f, 0.f),
+                                          fmaxf(raw.z + 0.5f, 0.f), __int_as_float(mask));
             }
         }
         __syncthreads();
@@ -179,14 +192,14 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
             const int idx = bend - t;
             const float2 xy = s_xy[t];
             const float4 co = s_co[t];
-            const float4 raw = s_rgb[t];
+            const float4 rc = s_rgb[t];
             float v[9];
 #pragma unroll
             for (int q = 0; q < 9; q++) v[q] = 0.f;
             bool on = false;
 #pragma unroll
             for (int h = 0; h < PPT; h++)
-                on |= backprop(st[h], fpx, (float)(by + (lane >> 4) + 2 * h), xy, co, raw, idx, v);
+                on |= backprop(st[h], fpx, (float)(by + (lane >> 4) + 2 * h), xy, co, rc, idx, v);
             if (!__any_sync(0xffffffffu, on)) continue;
             // Transposed butterfly: afterwards lane L holds the warp sum of
             // value (L >> 2); the opacity term takes a plain butterfly.
@@ -220,10 +233,11 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
             const int j = lane >> 2;
             if ((lane & 3) == 0) {
                 bool ok = x != 0.f;
-                if (j < 3) ok = ok && ((j == 0 ? raw.x : (j == 1 ? raw.y : raw.z)) + 0.5f >= 0.f);
+                if (j < 3) ok = ok && ((__float_as_int(rc.w) >> j) & 1);
+                if (j >= 3 && j < 6) x *= 0.5f;
                 if (ok) atomicAdd(grad_acc + (size_t)g * kGradStride + j, x);
             } else if (lane == 1) {
-                if (vop != 0.f) atomicAdd(grad_acc + (size_t)g * kGradStride + 8, vop);
+                if (vop != 0.f) atomicAdd(grad_acc + (size_t)g * kGradStride + 8, -(1.f - co.w) * vop);
             }
         }
     }

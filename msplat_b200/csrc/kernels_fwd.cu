@@ -374,28 +374,43 @@ scatter_kernel(const StepParams* __restrict__ P, int N, const int* __restrict__ 
     const int total = __shfl_sync(0xffffffffu, incl, 31);
     const long long cap = P->capacity;
     const int tx_n = P->tiles_x;
-    for (int p0 = 0; p0 < total; p0 += 32) {
-        const int pidx = p0 + lane;
-        // owner = first lane whose inclusive prefix exceeds pidx
-        int owner = 0;
+    // kRounds rounds of 32 pairs per iteration: their atomics are issued
+    // together, so a lane waits for one atomic latency per kRounds pairs.
+    constexpr int kRounds = 4;
+    for (int p0 = 0; p0 < total; p0 += 32 * kRounds) {
+        int tile[kRounds];
+        unsigned long long kv[kRounds];
 #pragma unroll
-        for (int step = 16; step > 0; step >>= 1) {
-            const int probe = __shfl_sync(0xffffffffu, incl, owner + step - 1);
-            if (probe <= pidx) owner += step;
+        for (int u = 0; u < kRounds; u++) {
+            const int pidx = p0 + 32 * u + lane;
+            // owner = first lane whose inclusive prefix exceeds pidx
+            int owner = 0;
+#pragma unroll
+            for (int step = 16; step > 0; step >>= 1) {
+                const int probe = __shfl_sync(0xffffffffu, incl, owner + step - 1);
+                if (probe <= pidx) owner += step;
+            }
+            const int o_incl = __shfl_sync(0xffffffffu, incl, owner);
+            const int o_area = __shfl_sync(0xffffffffu, area, owner);
+            const int o_x0 = __shfl_sync(0xffffffffu, x0, owner);
+            const int o_y0 = __shfl_sync(0xffffffffu, y0, owner);
+            const int o_w = __shfl_sync(0xffffffffu, w, owner);
+            kv[u] = __shfl_sync(0xffffffffu, key, owner);
+            tile[u] = -1;
+            if (pidx < total) {
+                const int k = pidx - (o_incl - o_area);
+                tile[u] = (o_y0 + k / o_w) * tx_n + o_x0 + k % o_w;
+            }
         }
-        const int o_incl = __shfl_sync(0xffffffffu, incl, owner);
-        const int o_area = __shfl_sync(0xffffffffu, area, owner);
-        const int o_x0 = __shfl_sync(0xffffffffu, x0, owner);
-        const int o_y0 = __shfl_sync(0xffffffffu, y0, owner);
-        const int o_w = __shfl_sync(0xffffffffu, w, owner);
-        const unsigned long long o_key = __shfl_sync(0xffffffffu, key, owner);
-        if (pidx < total) {
-            const int k = pidx - (o_incl - o_area);
-            const int ty = o_y0 + k / o_w, tx = o_x0 + k % o_w;
-            const int t = ty * tx_n + tx;
-            const int pos = atomicSub(&count[t * kCountPitch], 1) - 1;
-            const long long idx = (long long)offset[t] + pos;
-            if (idx < cap) keys[idx] = o_key;
+        int pos[kRounds];
+#pragma unroll
+        for (int u = 0; u < kRounds; u++)
+            if (tile[u] >= 0) pos[u] = atomicSub(&count[tile[u] * kCountPitch], 1) - 1;
+#pragma unroll
+        for (int u = 0; u < kRounds; u++) {
+            if (tile[u] < 0) continue;
+            const long long idx = (long long)offset[tile[u]] + pos[u];
+            if (idx < cap) keys[idx] = kv[u];
         }
     }
 }
@@ -457,15 +472,21 @@ __device__ __forceinline__ void bitonic_regs(unsigned long long (&v)[K], unsigne
                     v[r] = take_min ? (o < v[r] ? o : v[r]) : (o > v[r] ? o : v[r]);
                 }
             } else {
+                // shared-memory exchange; index e is stored at e + e/16 so
+                // that a warp's 64-bit accesses hit distinct banks
                 __syncthreads();
 #pragma unroll
-                for (int r = 0; r < K; r++) s[t * K + r] = v[r];
+                for (int r = 0; r < K; r++) {
+                    const int e = t * K + r;
+                    s[e + (e >> 4)] = v[r];
+                }
                 __syncthreads();
 #pragma unroll
                 for (int r = 0; r < K; r++) {
                     const int e = t * K + r;
                     const bool up = (e & k) == 0;
-                    const unsigned long long o = s[e ^ j];
+                    const int f = e ^ j;
+                    const unsigned long long o = s[f + (f >> 4)];
                     const bool take_min = ((e & j) == 0) == up;
                     v[r] = take_min ? (o < v[r] ? o : v[r]) : (o > v[r] ? o : v[r]);
                 }
@@ -526,7 +547,7 @@ sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offs
                   unsigned long long* __restrict__ keys, unsigned long long* __restrict__ keys_alt,
                   int* __restrict__ ids)
 {
-    __shared__ unsigned long long s[kSortRun];
+    __shared__ unsigned long long s[kSortRun + kSortRun / 16];
     const int t = blockIdx.x;
     const long long cap = P->capacity;
     const long long start = min((long long)offset[t], cap);
