@@ -22,7 +22,8 @@ namespace msp {
 // a transposed butterfly (8 values in 9 shuffles, the opacity term in 5),
 // then 9 lanes issue one RED each into the Gaussian's 9 contiguous
 // accumulators: v_rgb[3] (gated by the clamp mask), v_conic[3], v_xy[2],
-// v_opacity (w.r.t. the logit).
+// v_opacity (w.r.t. the logit).  Staged batches drop the Gaussians that cannot
+// reach any pixel of the tile (tile_may_contribute), as the forward does.
 // ---------------------------------------------------------------------------
 
 __device__ __forceinline__ float sel(bool c, float a, float b) { return c ? a : b; }
@@ -104,6 +105,8 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
     __shared__ float4 s_co[kRastBatch];
     __shared__ float4 s_rgb[kRastBatch];
     __shared__ int s_wmax[kThreads / 32];
+    __shared__ int s_order[kRastBatch];
+    __shared__ int s_wcnt[kRastBatch / 32];
     const int tile = blockIdx.x;
     const int tx_n = P->tiles_x;
     const int W = P->img_w, H = P->img_h;
@@ -165,30 +168,65 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
     for (int w = 1; w < kThreads / 32; w++) tile_max = max(tile_max, s_wmax[w]);
     const int last = min(end - 1, tile_max);
 
+    const float tx0f = (float)tx0, ty0f = (float)ty0;
+    constexpr int kH = kRastBatch / kThreads;  // candidates staged per thread
     for (int bend = last; bend >= beg; bend -= kRastBatch) {
         const int n = min(kRastBatch, bend - beg + 1);
         __syncthreads();
+        // Stage the batch (list positions bend, bend-1, ...) and list, in that
+        // order, the slots of the Gaussians that can reach a pixel of this tile.
+        unsigned keepbits = 0;
 #pragma unroll
-        for (int h = 0; h < kRastBatch / kThreads; h++) {
+        for (int h = 0; h < kH; h++) {
             const int slot = tid + h * kThreads;
+            bool keep = false;
             if (slot < n) {
                 const int g = ids[bend - slot];
                 const float2 xy = g_xy[g];
                 const float4 co = g_co[g];
+                const float4 raw = g_rgb[g];
                 s_id[slot] = g;
                 s_xy[slot] = xy;
                 s_co[slot] = co;
                 // clamped colour; .w holds the clamp mask (bit c: rgb_c + 0.5 >= 0)
-                const float4 raw = g_rgb[g];
                 const int mask = (raw.x + 0.5f >= 0.f ? 1 : 0) | (raw.y + 0.5f >= 0.f ? 2 : 0) |
                                  (raw.z + 0.5f >= 0.f ? 4 : 0);
                 s_rgb[slot] = make_float4(fmaxf(raw.x + 0.5f, 0.f), fmaxf(raw.y + 0.5f, 0.f),
                                           fmaxf(raw.z + 0.5f, 0.f), __int_as_float(mask));
+                keep = tile_may_contribute(xy, co, tx0f, ty0f);
             }
+            const unsigned bal = __ballot_sync(0xffffffffu, keep);
+            if (lane == 0) s_wcnt[h * (kThreads / 32) + warp] = __popc(bal);
+            keepbits |= (keep ? 1u : 0u) << h;
         }
         __syncthreads();
-        const int t0 = max(0, bend - warp_max);
-        for (int t = t0; t < n; t++) {
+        int m = 0;
+        int woff[kH];
+#pragma unroll
+        for (int h = 0; h < kH; h++) woff[h] = 0;
+#pragma unroll
+        for (int c = 0; c < kRastBatch / 32; c++) {
+            const int cw = s_wcnt[c];
+#pragma unroll
+            for (int h = 0; h < kH; h++) woff[h] += c < h * (kThreads / 32) + warp ? cw : 0;
+            m += cw;
+        }
+#pragma unroll
+        for (int h = 0; h < kH; h++) {
+            const bool keep = (keepbits >> h) & 1u;
+            const unsigned bal = __ballot_sync(0xffffffffu, keep);
+            if (keep) s_order[woff[h] + __popc(bal & ((1u << lane) - 1u))] = tid + h * kThreads;
+        }
+        __syncthreads();
+        // first listed Gaussian at or below this warp's last contributing index
+        int t0 = 0, hi = m;
+        while (t0 < hi) {
+            const int mid = (t0 + hi) >> 1;
+            if (bend - s_order[mid] > warp_max) t0 = mid + 1;
+            else hi = mid;
+        }
+        for (int t0i = t0; t0i < m; t0i++) {
+            const int t = s_order[t0i];
             const int idx = bend - t;
             const float2 xy = s_xy[t];
             const float4 co = s_co[t];

@@ -604,7 +604,10 @@ void launch_sort_tiles(const StepParams* P, int num_tiles, const Buffers& B, cud
 // one thread per pixel, batches of 256 Gaussians staged in shared memory.
 // Reference: nd_rasterize_forward_kernel (msplat_metal.metal:472-585) and
 // rasterize_forward_chunked_kernel (:2633-2741).  The per-pixel loop is the
-// reference's; the CTA leaves as soon as every pixel has terminated.
+// reference's; the CTA leaves as soon as every pixel has terminated.  Each
+// staged batch drops the Gaussians that cannot reach any pixel of the tile
+// (tile_may_contribute), which changes no result: those never pass the
+// per-pixel tests.
 // ---------------------------------------------------------------------------
 template <bool CHUNKED>
 __global__ void __launch_bounds__(kTileThreads)
@@ -618,10 +621,13 @@ raster_forward_kernel(const StepParams* __restrict__ P, const int* __restrict__ 
     __shared__ float2 s_xy[kTileThreads];
     __shared__ float4 s_co[kTileThreads];
     __shared__ float4 s_rgb[kTileThreads];
+    __shared__ int s_idx[kTileThreads];
+    __shared__ int s_wcnt[kTileThreads / 32];
     const int tile = blockIdx.x;
     const int tx_n = P->tiles_x;
     const int W = P->img_w, H = P->img_h;
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float tx0 = (float)((tile % tx_n) * kBlockX), ty0 = (float)((tile / tx_n) * kBlockY);
     const int px = (tile % tx_n) * kBlockX + (tid & 15);
     const int py = (tile / tx_n) * kBlockY + (tid >> 4);
     const bool inside = px < W && py < H;
@@ -642,18 +648,39 @@ raster_forward_kernel(const StepParams* __restrict__ P, const int* __restrict__ 
     bool done = !inside;
     for (int b0 = beg; b0 < end; b0 += kTileThreads) {
         if (__syncthreads_count(done) == kTileThreads) break;
+        // Stage the batch, keeping (in list order) only the Gaussians that
+        // can reach a pixel of this tile; s_idx keeps their list positions.
         const int idx = b0 + tid;
+        bool keep = false;
+        float2 xy = make_float2(0.f, 0.f);
+        float4 co = make_float4(0.f, 0.f, 0.f, 0.f), rc = co;
         if (idx < end) {
             const int g = ids[idx];
-            s_xy[tid] = g_xy[g];
-            s_co[tid] = g_co[g];
-            const float4 rc = g_rgb[g];
-            s_rgb[tid] = make_float4(fmaxf(rc.x + 0.5f, 0.f), fmaxf(rc.y + 0.5f, 0.f),
-                                     fmaxf(rc.z + 0.5f, 0.f), 0.f);
+            xy = g_xy[g];
+            co = g_co[g];
+            rc = g_rgb[g];
+            keep = tile_may_contribute(xy, co, tx0, ty0);
+        }
+        const unsigned bal = __ballot_sync(0xffffffffu, keep);
+        if (lane == 0) s_wcnt[warp] = __popc(bal);
+        __syncthreads();
+        int n = 0, woff = 0;
+#pragma unroll
+        for (int w = 0; w < kTileThreads / 32; w++) {
+            const int cw = s_wcnt[w];
+            woff += w < warp ? cw : 0;
+            n += cw;
+        }
+        if (keep) {
+            const int slot = woff + __popc(bal & ((1u << lane) - 1u));
+            s_xy[slot] = xy;
+            s_co[slot] = co;
+            s_rgb[slot] = make_float4(fmaxf(rc.x + 0.5f, 0.f), fmaxf(rc.y + 0.5f, 0.f),
+                                      fmaxf(rc.z + 0.5f, 0.f), 0.f);
+            s_idx[slot] = idx;
         }
         __syncthreads();
         if (done) continue;
-        const int n = min(kTileThreads, end - b0);
         for (int t = 0; t < n; t++) {
             const float4 co = s_co[t];
             const float2 xy = s_xy[t];
@@ -664,7 +691,7 @@ raster_forward_kernel(const StepParams* __restrict__ P, const int* __restrict__ 
             if (alpha < 1.f / 255.f) continue;
             const float next_T = T * (1.f - alpha);
             if (next_T <= 1e-4f) {
-                last = b0 + t - 1;
+                last = s_idx[t] - 1;
                 done = true;
                 break;
             }
@@ -674,7 +701,7 @@ raster_forward_kernel(const StepParams* __restrict__ P, const int* __restrict__ 
             c1 = fmaf(rgb.y, vis, c1);
             c2 = fmaf(rgb.z, vis, c2);
             T = next_T;
-            last = b0 + t;
+            last = s_idx[t];
         }
     }
     if (!inside) return;

@@ -76,6 +76,39 @@ __device__ __forceinline__ float sigmoid_ref(float x) { return __fdiv_rn(1.f, 1.
 
 __device__ __forceinline__ float saturatef_ref(float x) { return fminf(fmaxf(x, 0.f), 1.f); }
 
+// Whether a Gaussian (centre xy; conic a = co.x, b = co.y, c = co.z;
+// opacity co.w) can pass the rasterizers' tests -- sigma in [0, 5.55) and
+// alpha = min(0.999, opacity * exp(-sigma)) >= 1/255 -- at any pixel centre
+// of the 16x16 tile whose first pixel centre is (x0, y0).  The least sigma
+// over the tile's rectangle of pixel centres (exact for a positive definite
+// conic: 0 if the centre lies inside, else the least of the four edge
+// minima) is compared with min(5.55, ln(255 opacity)) under margins far
+// above float rounding (1e-3 absolute and relative on the cut-off, 1e-5 of
+// the terms' magnitude on sigma), so only Gaussians that cannot touch any
+// pixel of the tile are dropped.  Other conics, and NaNs, are kept.
+__device__ __forceinline__ bool tile_may_contribute(float2 xy, float4 co, float x0, float y0)
+{
+    const float a = co.x, b = co.y, c = co.z;
+    if (!(a > 0.f && c > 0.f && a * c - b * b > 0.f)) return true;
+    const float cut = fminf(5.55f, __logf(255.f * co.w));
+    if (!(cut == cut)) return true;
+    const float lim = cut + fabsf(cut) * 1e-3f + 1e-3f;
+    const float dxl = xy.x - (x0 + 15.f), dxh = xy.x - x0;
+    const float dyl = xy.y - (y0 + 15.f), dyh = xy.y - y0;
+    if (dxl <= 0.f && dxh >= 0.f && dyl <= 0.f && dyh >= 0.f) return lim >= 0.f;
+    const float ia = 1.f / a, ic = 1.f / c;
+    float qmin = 3.0e38f;
+    auto edge = [&](float dx, float dy) {
+        const float t0 = 0.5f * a * dx * dx, t1 = 0.5f * c * dy * dy, t2 = b * dx * dy;
+        qmin = fminf(qmin, (t0 + t1 + t2) - 1e-5f * (t0 + t1 + fabsf(t2)));
+    };
+    edge(dxl, fminf(fmaxf(-b * dxl * ic, dyl), dyh));
+    edge(dxh, fminf(fmaxf(-b * dxh * ic, dyl), dyh));
+    edge(fminf(fmaxf(-b * dyl * ia, dxl), dxh), dyl);
+    edge(fminf(fmaxf(-b * dyh * ia, dxl), dxh), dyh);
+    return qmin <= lim;
+}
+
 __device__ __forceinline__ int num_sh_bases(int degree)
 {
     return degree == 0 ? 1 : degree == 1 ? 4 : degree == 2 ? 9 : degree == 3 ? 16 : 25;
