@@ -23,7 +23,8 @@ namespace msp {
 // then 9 lanes issue one RED each into the Gaussian's 9 contiguous
 // accumulators: v_rgb[3] (gated by the clamp mask), v_conic[3], v_xy[2],
 // v_opacity (w.r.t. the logit).  Staged batches drop the Gaussians that cannot
-// reach any pixel of the tile (tile_may_contribute), as the forward does.
+// reach any pixel of the tile (tile_may_contribute), as the forward does, and
+// each warp walks only those that can reach its rows (band_mask).
 // ---------------------------------------------------------------------------
 
 __device__ __forceinline__ float sel(bool c, float a, float b) { return c ? a : b; }
@@ -106,6 +107,7 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
     __shared__ float4 s_rgb[kRastBatch];
     __shared__ int s_wmax[kThreads / 32];
     __shared__ int s_order[kRastBatch];
+    __shared__ unsigned char s_band[kRastBatch];
     __shared__ int s_wcnt[kRastBatch / 32];
     const int tile = blockIdx.x;
     const int tx_n = P->tiles_x;
@@ -193,7 +195,10 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
                                  (raw.z + 0.5f >= 0.f ? 4 : 0);
                 s_rgb[slot] = make_float4(fmaxf(raw.x + 0.5f, 0.f), fmaxf(raw.y + 0.5f, 0.f),
                                           fmaxf(raw.z + 0.5f, 0.f), __int_as_float(mask));
-                keep = tile_may_contribute(xy, co, tx0f, ty0f);
+                const float lim = cull_limit(co);
+                keep = tile_may_contribute(xy, co, tx0f, ty0f, lim);
+                // warp w owns the 2*PPT rows from 2*PPT*w
+                s_band[slot] = (unsigned char)band_mask<2 * PPT>(xy, co, ty0f, lim);
             }
             const unsigned bal = __ballot_sync(0xffffffffu, keep);
             if (lane == 0) s_wcnt[h * (kThreads / 32) + warp] = __popc(bal);
@@ -225,57 +230,64 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
             if (bend - s_order[mid] > warp_max) t0 = mid + 1;
             else hi = mid;
         }
-        for (int t0i = t0; t0i < m; t0i++) {
-            const int t = s_order[t0i];
-            const int idx = bend - t;
-            const float2 xy = s_xy[t];
-            const float4 co = s_co[t];
-            const float4 rc = s_rgb[t];
-            float v[9];
+        // walk the listed Gaussians that can reach this warp's rows, in order
+        for (int b = t0; b < m; b += 32) {
+            const int oi = b + lane;
+            const int my_slot = oi < m ? s_order[oi] : 0;
+            unsigned bits = __ballot_sync(0xffffffffu, oi < m && ((s_band[my_slot] >> warp) & 1u));
+            while (bits) {
+                const int t = __shfl_sync(0xffffffffu, my_slot, __ffs(bits) - 1);
+                bits &= bits - 1u;
+                const int idx = bend - t;
+                const float2 xy = s_xy[t];
+                const float4 co = s_co[t];
+                const float4 rc = s_rgb[t];
+                float v[9];
 #pragma unroll
-            for (int q = 0; q < 9; q++) v[q] = 0.f;
-            bool on = false;
+                for (int q = 0; q < 9; q++) v[q] = 0.f;
+                bool on = false;
 #pragma unroll
-            for (int h = 0; h < PPT; h++)
-                on |= backprop(st[h], fpx, (float)(by + (lane >> 4) + 2 * h), xy, co, rc, idx, v);
-            if (!__any_sync(0xffffffffu, on)) continue;
-            // Transposed butterfly: afterwards lane L holds the warp sum of
-            // value (L >> 2); the opacity term takes a plain butterfly.
-            const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4;
-            float u[4];
+                for (int h = 0; h < PPT; h++)
+                    on |= backprop(st[h], fpx, (float)(by + (lane >> 4) + 2 * h), xy, co, rc, idx, v);
+                if (!__any_sync(0xffffffffu, on)) continue;
+                // Transposed butterfly: afterwards lane L holds the warp sum of
+                // value (L >> 2); the opacity term takes a plain butterfly.
+                const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4;
+                float u[4];
 #pragma unroll
-            for (int q = 0; q < 4; q++) {
-                const float send = sel(h16, v[q], v[q + 4]);
-                const float keep = sel(h16, v[q + 4], v[q]);
-                u[q] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-            }
-            float w2[2];
+                for (int q = 0; q < 4; q++) {
+                    const float send = sel(h16, v[q], v[q + 4]);
+                    const float keep = sel(h16, v[q + 4], v[q]);
+                    u[q] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+                }
+                float w2[2];
 #pragma unroll
-            for (int q = 0; q < 2; q++) {
-                const float send = sel(h8, u[q], u[q + 2]);
-                const float keep = sel(h8, u[q + 2], u[q]);
-                w2[q] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-            }
-            float x;
-            {
-                const float send = sel(h4, w2[0], w2[1]);
-                const float keep = sel(h4, w2[1], w2[0]);
-                x = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-            }
-            x += __shfl_xor_sync(0xffffffffu, x, 2);
-            x += __shfl_xor_sync(0xffffffffu, x, 1);
-            float vop = v[8];
+                for (int q = 0; q < 2; q++) {
+                    const float send = sel(h8, u[q], u[q + 2]);
+                    const float keep = sel(h8, u[q + 2], u[q]);
+                    w2[q] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+                }
+                float x;
+                {
+                    const float send = sel(h4, w2[0], w2[1]);
+                    const float keep = sel(h4, w2[1], w2[0]);
+                    x = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+                }
+                x += __shfl_xor_sync(0xffffffffu, x, 2);
+                x += __shfl_xor_sync(0xffffffffu, x, 1);
+                float vop = v[8];
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) vop += __shfl_xor_sync(0xffffffffu, vop, o);
-            const int g = s_id[t];
-            const int j = lane >> 2;
-            if ((lane & 3) == 0) {
-                bool ok = x != 0.f;
-                if (j < 3) ok = ok && ((__float_as_int(rc.w) >> j) & 1);
-                if (j >= 3 && j < 6) x *= 0.5f;
-                if (ok) atomicAdd(grad_acc + (size_t)g * kGradStride + j, x);
-            } else if (lane == 1) {
-                if (vop != 0.f) atomicAdd(grad_acc + (size_t)g * kGradStride + 8, -(1.f - co.w) * vop);
+                for (int o = 16; o > 0; o >>= 1) vop += __shfl_xor_sync(0xffffffffu, vop, o);
+                const int g = s_id[t];
+                const int j = lane >> 2;
+                if ((lane & 3) == 0) {
+                    bool ok = x != 0.f;
+                    if (j < 3) ok = ok && ((__float_as_int(rc.w) >> j) & 1);
+                    if (j >= 3 && j < 6) x *= 0.5f;
+                    if (ok) atomicAdd(grad_acc + (size_t)g * kGradStride + j, x);
+                } else if (lane == 1) {
+                    if (vop != 0.f) atomicAdd(grad_acc + (size_t)g * kGradStride + 8, -(1.f - co.w) * vop);
+                }
             }
         }
     }

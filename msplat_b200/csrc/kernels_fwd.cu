@@ -659,7 +659,7 @@ raster_forward_kernel(const StepParams* __restrict__ P, const int* __restrict__ 
             xy = g_xy[g];
             co = g_co[g];
             rc = g_rgb[g];
-            keep = tile_may_contribute(xy, co, tx0, ty0);
+            keep = tile_may_contribute(xy, co, tx0, ty0, cull_limit(co));
         }
         const unsigned bal = __ballot_sync(0xffffffffu, keep);
         if (lane == 0) s_wcnt[warp] = __popc(bal);

@@ -76,23 +76,33 @@ __device__ __forceinline__ float sigmoid_ref(float x) { return __fdiv_rn(1.f, 1.
 
 __device__ __forceinline__ float saturatef_ref(float x) { return fminf(fmaxf(x, 0.f), 1.f); }
 
-// Whether a Gaussian (centre xy; conic a = co.x, b = co.y, c = co.z;
-// opacity co.w) can pass the rasterizers' tests -- sigma in [0, 5.55) and
-// alpha = min(0.999, opacity * exp(-sigma)) >= 1/255 -- at any pixel centre
-// of the 16x16 tile whose first pixel centre is (x0, y0).  The least sigma
-// over the tile's rectangle of pixel centres (exact for a positive definite
-// conic: 0 if the centre lies inside, else the least of the four edge
-// minima) is compared with min(5.55, ln(255 opacity)) under margins far
-// above float rounding (1e-3 absolute and relative on the cut-off, 1e-5 of
-// the terms' magnitude on sigma), so only Gaussians that cannot touch any
-// pixel of the tile are dropped.  Other conics, and NaNs, are kept.
-__device__ __forceinline__ bool tile_may_contribute(float2 xy, float4 co, float x0, float y0)
+// Culling of staged Gaussians in the rasterizers.  A pixel only takes a
+// Gaussian when sigma lies in [0, 5.55) and alpha = min(0.999, opacity *
+// exp(-sigma)) >= 1/255, i.e. sigma <= min(5.55, ln(255 opacity)).  The
+// tests below only drop a Gaussian for pixels it provably cannot reach:
+// the cut-off gets margins far above float rounding (1e-3 absolute and
+// relative, and 1e-5 of the terms' magnitude on sigma), and conics that are
+// not positive definite, or NaNs, are always kept.
+
+// Cut-off with margins, or +inf when the Gaussian must be kept.
+__device__ __forceinline__ float cull_limit(float4 co)
 {
     const float a = co.x, b = co.y, c = co.z;
-    if (!(a > 0.f && c > 0.f && a * c - b * b > 0.f)) return true;
+    if (!(a > 0.f && c > 0.f && a * c - b * b > 0.f)) return 3.0e38f;
     const float cut = fminf(5.55f, __logf(255.f * co.w));
-    if (!(cut == cut)) return true;
-    const float lim = cut + fabsf(cut) * 1e-3f + 1e-3f;
+    if (!(cut == cut)) return 3.0e38f;
+    return cut + fabsf(cut) * 1e-3f + 1e-3f;
+}
+
+// Whether the Gaussian (centre xy, conic co) can reach any pixel centre of
+// the 16x16 tile whose first pixel centre is (x0, y0): the least sigma over
+// the rectangle of pixel centres (0 if the centre lies inside, else the
+// least of the four edge minima, exact for a convex quadratic) against lim.
+__device__ __forceinline__ bool tile_may_contribute(float2 xy, float4 co, float x0, float y0,
+                                                    float lim)
+{
+    if (lim >= 1.0e38f) return true;
+    const float a = co.x, b = co.y, c = co.z;
     const float dxl = xy.x - (x0 + 15.f), dxh = xy.x - x0;
     const float dyl = xy.y - (y0 + 15.f), dyh = xy.y - y0;
     if (dxl <= 0.f && dxh >= 0.f && dyl <= 0.f && dyh >= 0.f) return lim >= 0.f;
@@ -107,6 +117,26 @@ __device__ __forceinline__ bool tile_may_contribute(float2 xy, float4 co, float 
     edge(fminf(fmaxf(-b * dyl * ia, dxl), dxh), dyl);
     edge(fminf(fmaxf(-b * dyh * ia, dxl), dxh), dyh);
     return qmin <= lim;
+}
+
+// Bands of ROWS pixel rows of the tile (bit w: rows y0 + ROWS*w ...) that
+// the Gaussian can reach: over any row the least sigma is
+// 0.5 * dy^2 * det / a, so only rows with |dy| <= sqrt(2 lim a / det) can.
+template <int ROWS>
+__device__ __forceinline__ unsigned band_mask(float2 xy, float4 co, float y0, float lim)
+{
+    constexpr int kBands = 16 / ROWS;
+    constexpr unsigned kAll = (1u << kBands) - 1u;
+    if (lim >= 1.0e38f) return kAll;
+    if (lim < 0.f) return 0u;
+    const float a = co.x, b = co.y, c = co.z;
+    const float ry = sqrtf(2.f * lim * a / (a * c - b * b)) * 1.001f + 0.01f;
+    const float inv = 1.f / (float)ROWS;
+    const float flo = floorf((xy.y - ry - y0) * inv), fhi = floorf((xy.y + ry - y0) * inv);
+    if (!(fhi == fhi && flo == flo)) return kAll;
+    if (fhi < 0.f || flo > (float)(kBands - 1)) return 0u;
+    const int lo = (int)fmaxf(flo, 0.f), hi = (int)fminf(fhi, (float)(kBands - 1));
+    return kAll & ((2u << hi) - 1u) & ~((1u << lo) - 1u);
 }
 
 __device__ __forceinline__ int num_sh_bases(int degree)
