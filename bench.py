@@ -48,7 +48,7 @@ CONFIG = "C1"
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true",
@@ -73,7 +73,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -120,6 +120,35 @@ def peaks() -> dict:
             d = json.load(f)
         return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
     return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+# Per-step figures from one ncu capture of the first C1 training step
+# (profiles/kernels_c1_train_step.md): DRAM bytes of the optimiser stage
+# (rest_adam_kernel + project_backward_adam_kernel) and warp instructions of
+# the issue-bound kernels.  Instruction counts vary a little with the view;
+# the capture's view stands for all.
+C1_OPT_STAGE_TRAFFIC = 510081536 + 344526592 + 235912960 + 118926592
+C1_WARP_INSTR = {"rast_fwd": ("raster_forward_kernel<0>", 374211050),
+                 "rast_bwd": ("raster_backward_kernel<0,2>", 667931406),
+                 "loss_fwd_bwd": ("ssim_loss_fused_kernel", 105998350)}
+SM_COUNT, ISSUE_PER_SM_CLK = 148, 4
+
+
+def issue_rooflines(stage_ms: dict, sm_mhz: float) -> list:
+    """Achieved warp-instruction issue rate of the issue-bound kernels
+    against the SMs' issue slots (148 SMs x 4 schedulers x 1/clock at the SM
+    clock sampled during the timed region)."""
+    peak = SM_COUNT * ISSUE_PER_SM_CLK * sm_mhz * 1e6 / 1e9   # G warp-instr/s
+    out = []
+    for stage, (kernel, instr) in C1_WARP_INSTR.items():
+        ms = stage_ms.get(stage, 0.0)
+        if ms <= 0:
+            continue
+        ach = instr / (ms / 1000.0) / 1e9
+        out.append({"bound": "issue", "kernel": kernel, "achieved": round(ach, 1),
+                    "peak": round(peak, 1), "unit": "G warp-instr/s", "frac": round(ach / peak, 4),
+                    "launch_ms": round(ms, 4), "warp_instructions": instr})
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -282,7 +311,9 @@ def run_ours(args, rank: int, world: int):
     roofline = {"bound": "hbm", "kernel": kname, "achieved": round(achieved, 1),
                 "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
                 "peak_source": pk["source"], "algorithmic_bytes": algo, "launch_ms": round(dom_ms, 4),
-                "traffic": None}
+                "traffic": C1_OPT_STAGE_TRAFFIC if world == 1 else None,
+                "traffic_source": "ncu dram__bytes_read+write of the stage's kernels, first C1 step"
+                if world == 1 else None}
 
     result = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
@@ -303,6 +334,7 @@ def run_ours(args, rank: int, world: int):
                 "h2d_bytes_per_step": int(h * w * 3 * 4 + 512),
                 "d2h_bytes_per_step": 12},
         "roofline": roofline,
+        "issue_roofline": issue_rooflines(stage_ms, float(clk.get("sm_mhz") or 1965.0)),
         "gpu_launches": launches,
         "clocks": clk,
         "loss": float(lib.msplat_last_loss(1)),
