@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--dp-mode", choices=("peer", "nccl"), default="peer",
+                    help="N > 1: optimiser over NVLink peer memory, or NCCL all-reduce")
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the timed CPU oracle sample (profiling runs)")
     return ap.parse_args()
@@ -209,7 +211,7 @@ def run_ours(args, rank: int, world: int):
     dist = None
     if world > 1:
         from msplat_b200 import multigpu
-        dist = multigpu.DataParallel(model, rank, world)
+        dist = multigpu.DataParallel(model, rank, world, mode=args.dp_mode)
     ncam = len(setups)
 
     def view_of(step):
@@ -324,8 +326,11 @@ def run_ours(args, rank: int, world: int):
                                "one view per GPU per step",
                    "gaussians": model.n, "width": w, "height": h, "cameras": ncam,
                    "l2": "inputs larger than L2 (per-step footprint ~2 GB)",
-                   "parallelism": f"dp{world} (replicated Gaussians, gradient all-reduce)"
-                   if world > 1 else "single GPU"},
+                   "parallelism": (f"dp{world}: replicated Gaussians; " + (
+                       "each rank sums its 1/N gradient shard over NVLink peer memory, "
+                       "applies Adam and writes the shard into every replica"
+                       if args.dp_mode == "peer" else "NCCL all-reduce of the gradient, "
+                       "then Adam on every replica")) if world > 1 else "single GPU"},
         "train_steps_per_s": round(args.steps / (ms_max / 1000.0), 2),
         "render_fps": round(1000.0 / render_ms, 1),
         "stage_ms": {k: round(v, 4) for k, v in stage_ms.items()},
@@ -342,6 +347,11 @@ def run_ours(args, rank: int, world: int):
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         result["cpu_baseline"] = cpu_baseline(g, setups, gts)
     if dist is not None:
+        if dist.mode == "peer":
+            errs = dist.peer_errors()
+            if errs:
+                raise RuntimeError(f"peer-memory optimiser reported error bits {errs}: "
+                                   "a cross-GPU wait timed out, the run is invalid")
         dist.shutdown()
     return result
 

@@ -158,6 +158,40 @@ int msplat_adam_apply(
     float adam_beta2, float adam_eps);
 
 /*
+ * Data-parallel optimiser over peer memory.  No counterpart in the reference.
+ * Replaces the all-reduce + msplat_adam_apply pair of the data-parallel step
+ * when every rank's gradient buffer, parameter arrays and flag array are
+ * mapped into every process (msplat_ipc_*): rank `rank` of `world` (<= 8)
+ * sums the world gradient buffers (msplat_train_step_grads layout) for its
+ * 1/world of the Gaussians, applies Adam with grad_scale 1/world using its
+ * own moments (only its shard of them is ever used), and stores the updated
+ * parameters into every rank's arrays.  rank_grads[world] and
+ * rank_flags[world] (2*world unsigned each, zeroed once at allocation) and
+ * rank_params[world*6] (group order as in msplat_train_step) are this
+ * process's pointers to every rank's buffers.  `epoch` must grow by one per
+ * step (from 1).  Queued on the engine stream: returns before the work
+ * finishes; the step's cross-GPU waits give up after timeout_s seconds and
+ * set bits read by msplat_dp_errors (1: gradients of a peer missing,
+ * 2: updated shards of a peer missing).
+ */
+int msplat_dp_reduce_adam(
+    int rank, int world, int num_points, int features_rest_bases, unsigned degree,
+    unsigned degrees_to_use, const float *const *rank_grads, float *const *rank_params,
+    float *const *exp_avg, float *const *exp_avg_sq, unsigned *const *rank_flags,
+    unsigned epoch, const float *adam_step_sizes, const float *adam_bc2_sqrts,
+    float adam_beta1, float adam_beta2, float adam_eps, double timeout_s);
+/* Error bits of the peer-memory steps on this device (waits until the
+ * engine stream is idle); clears them when `reset` != 0.  -1 on failure. */
+int msplat_dp_errors(int reset);
+/* CUDA IPC: the 64-byte handle of an allocation made by msplat_gpu_alloc
+ * (pass the pointer it returned), the mapping of a peer's handle into this
+ * process (each handle is mapped once and cached), and the release of every
+ * mapping.  No counterpart in the reference (a single-device engine). */
+int msplat_ipc_get_handle(const void *dev_ptr, void *handle_out);
+int msplat_ipc_open_handle(const void *handle, void **dev_ptr_out);
+int msplat_ipc_close_all(void);
+
+/*
  * Forward-only render.  Replaces MTensor msplat_render(...) (bindings.h:37-46;
  * implementation msplat_metal.mm:752-769).  *out_img receives a device
  * pointer to the engine's (H,W,3) float image, valid until the next call

@@ -24,7 +24,7 @@ INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CFLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
           f"-I{INCLUDE}"]
-FMA_CONTRACTED = {"kernels_bwd.cu"}   # every other file: --fmad=false
+FMA_CONTRACTED = {"kernels_bwd.cu", "dp_peer.cu"}   # every other file: --fmad=false
 
 
 def fmad_flag(src: str) -> str:

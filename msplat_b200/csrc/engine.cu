@@ -116,6 +116,12 @@ static int init_engine()
     return MSPLAT_OK;
 }
 
+// Access for the other host files of the engine (dp_peer.cu).
+std::mutex& engine_mutex() { return g_mu; }
+int engine_init() { return init_engine(); }
+cudaStream_t engine_stream() { return g.stream(); }
+void engine_add_launches(int n) { g.launches += n; }
+
 template <typename T>
 static int realloc_dev(T*& p, size_t count)
 {

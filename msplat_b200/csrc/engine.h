@@ -3,6 +3,8 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include <mutex>
+
 namespace msp {
 
 constexpr int kGroups = 6;        // means, scales, quats, features_dc, features_rest, opacities
@@ -131,6 +133,12 @@ struct CamArgs {
     const float* background;
     int rest_stride;
 };
+
+// Engine state shared with the other host files (engine.cu).
+std::mutex& engine_mutex();          // the engine's lock (take it in every entry point)
+int engine_init();                   // idempotent; MSPLAT_OK or an error code
+cudaStream_t engine_stream();        // stream all engine work goes to
+void engine_add_launches(int n);     // for msplat_kernel_launches
 
 // Host helpers shared by the entry points (engine.cu).
 void set_error(const char* fmt, ...);                  // text for msplat_last_error()

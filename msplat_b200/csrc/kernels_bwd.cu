@@ -6,6 +6,7 @@
 #include <algorithm>
 
 #include "engine.h"
+#include "adam.cuh"
 #include "msp_math.cuh"
 
 namespace msp {
@@ -391,27 +392,6 @@ __device__ __forceinline__ M3 cols3(float a0, float a1, float a2, float b0, floa
     M.m[1][0] = b0; M.m[1][1] = b1; M.m[1][2] = b2;
     M.m[2][0] = c0; M.m[2][1] = c1; M.m[2][2] = c2;
     return M;
-}
-
-__device__ __forceinline__ float sqrt_approx(float x)
-{
-    float r;
-    asm("sqrt.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
-    return r;
-}
-
-// One Adam update (fused_adam_kernel, msplat_metal.metal:1666-1689):
-//   m = b1 m + (1 - b1) g;  v = b2 v + (1 - b2) g^2;
-//   p -= step * m / (sqrt(v) / bc2 + eps)
-// with the square root and the division done by the hardware's approximate
-// instructions (a few ulp, as the reference's fast-math Metal build does;
-// the parameters' bar is 1e-4 relative).  inv_bc2 = 1 / bc2.
-__device__ __forceinline__ void adam_math(float& p, float& m, float& v, float g, float step,
-                                          float b1, float b2, float inv_bc2, float eps)
-{
-    m = fmaf(b1, m, (1.0f - b1) * g);
-    v = fmaf(b2, v, (1.0f - b2) * g * g);
-    p = p - __fdividef(step * m, fmaf(sqrt_approx(v), inv_bc2, eps));
 }
 
 __device__ __forceinline__ void adam_elem(float* __restrict__ p, float* __restrict__ ea,

@@ -94,8 +94,53 @@ class EngineOps:
         _lib.check(rc, "msplat_adam_apply")
 
 
+class DeviceBuffer:
+    """A whole cudaMalloc allocation (msplat_gpu_alloc), so that its CUDA IPC
+    handle maps exactly this buffer in the peers; torch sees it through the
+    CUDA array interface without a copy.  Freed only by free()."""
+
+    def __init__(self, count: int, typestr: str = "<f4", zero: bool = True):
+        lib = _lib.load()
+        self.count = int(count)
+        self.ptr = lib.msplat_gpu_alloc(4 * max(self.count, 1), 1 if zero else 0)
+        if not self.ptr:
+            raise _lib.EngineError(f"msplat_gpu_alloc: {lib.msplat_last_error().decode()}")
+        self.__cuda_array_interface__ = {"shape": (self.count,), "typestr": typestr,
+                                         "data": (self.ptr, False), "version": 3}
+
+    def tensor(self, shape=None):
+        import torch
+        t = torch.as_tensor(self, device="cuda")
+        return t.view(shape) if shape is not None else t
+
+    def handle(self) -> bytes:
+        h = C.create_string_buffer(64)
+        _lib.check(_lib.load().msplat_ipc_get_handle(C.c_void_p(self.ptr), h),
+                   "msplat_ipc_get_handle")
+        return h.raw
+
+    def free(self) -> None:
+        if self.ptr:
+            _lib.load().msplat_gpu_free(C.c_void_p(self.ptr))
+            self.ptr = 0
+
+
+def _open_handle(h: bytes) -> int:
+    out = C.c_void_p()
+    _lib.check(_lib.load().msplat_ipc_open_handle(C.create_string_buffer(h, 64), C.byref(out)),
+               "msplat_ipc_open_handle")
+    return int(out.value)
+
+
 class DataParallel:
-    """Replicated Gaussians, one view per rank per step, gradient all-reduce.
+    """Replicated Gaussians, one view per rank per step.
+
+    mode "peer" (GPUs): the gradient buffers, parameter arrays and flag
+    arrays of all ranks are mapped into every process, and one kernel per
+    rank sums its 1/world shard of the gradients over NVLink, applies Adam to
+    it and writes it into every replica (msplat_dp_reduce_adam).
+    mode "nccl": one all-reduce of the gradient buffer, then Adam on every
+    replica (msplat_adam_apply).  The stand-in ops of the CPU tests use it.
 
     Creates the default process group from the torchrun environment when
     none exists (NCCL on GPUs; `backend` overrides, e.g. "gloo" on CPU) and
@@ -103,12 +148,18 @@ class DataParallel:
     """
 
     def __init__(self, model: GaussianModel, rank: int, world: int, ops=None,
-                 backend: str | None = None, timeout_s: float = 120.0):
+                 backend: str | None = None, timeout_s: float = 120.0, mode: str | None = None,
+                 peer_timeout_s: float = 10.0):
         import torch
         import torch.distributed as dist
         self.model, self.rank, self.world = model, rank, world
         self.ops = ops if ops is not None else EngineOps()
         self._owns_group = False
+        self.mode = mode or ("peer" if ops is None and torch.cuda.is_available() else "nccl")
+        if self.mode not in ("peer", "nccl"):
+            raise ValueError(f"unknown data-parallel mode {self.mode!r}")
+        self.peer_timeout_s = float(peer_timeout_s)
+        self._bufs = []
         if not dist.is_initialized():
             be = backend or ("nccl" if torch.cuda.is_available() else "gloo")
             kw = dict(backend=be, rank=rank, world_size=world,
@@ -118,20 +169,75 @@ class DataParallel:
             dist.init_process_group(**kw)
             self._owns_group = True
         self.backend = dist.get_backend()
-        self.grad = self.ops.alloc(grad_floats(model.n, model.rest_bases))
         self.last_loss = 0.0
+        if self.mode == "peer":
+            self._setup_peer()
+        else:
+            self.grad = self.ops.alloc(grad_floats(model.n, model.rest_bases))
+
+    def _setup_peer(self) -> None:
+        """Move the parameters into shareable allocations and map every
+        rank's buffers into this process."""
+        import torch
+        import torch.distributed as dist
+        m = self.model
+        gbuf = DeviceBuffer(grad_floats(m.n, m.rest_bases))
+        fbuf = DeviceBuffer(2 * self.world, typestr="<u4")
+        pbufs = [DeviceBuffer(p.numel()) for p in m.params]
+        self._bufs = [gbuf, fbuf] + pbufs
+        torch.cuda.synchronize()
+        for i, (buf, p) in enumerate(zip(pbufs, m.params)):
+            t = buf.tensor(p.shape)
+            t.copy_(p)
+            m.params[i] = t
+        self.grad = gbuf.tensor()
+        mine = [b.handle() for b in self._bufs]
+        every = [None] * self.world
+        dist.all_gather_object(every, mine)
+        ptrs = []
+        for q in range(self.world):
+            ptrs.append([b.ptr for b in self._bufs] if q == self.rank
+                        else [_open_handle(h) for h in every[q]])
+        self._grads_arr = (C.c_void_p * self.world)(*[ptrs[q][0] for q in range(self.world)])
+        self._flags_arr = (C.c_void_p * self.world)(*[ptrs[q][1] for q in range(self.world)])
+        self._params_arr = (C.c_void_p * (6 * self.world))(
+            *[ptrs[q][2 + g] for q in range(self.world) for g in range(6)])
+        self.epoch = 0
+        torch.cuda.synchronize()
+        self.barrier()
 
     def train_step(self, cam, gt, ssim_weight: float = 0.2, background=DEFAULT_BG,
                    glob_scale: float = 1.0, clip_thresh: float = 0.01) -> float:
         """One data-parallel step; every rank passes its own view."""
-        import torch.distributed as dist
         self.model.step_count += 1
         self.last_loss = self.ops.grads(self.model, cam, gt, self.grad, ssim_weight, background,
                                         glob_scale, clip_thresh)
+        self.apply(cam)
+        return self.last_loss
+
+    def apply(self, cam) -> None:
+        """The optimiser half of a step, from the gradients in self.grad
+        (this rank's view); model.step_count must already count the step."""
+        import torch.distributed as dist
+        if self.mode == "peer":
+            m = self.model
+            steps, bc2s = m.adam_scalars()
+            self.epoch += 1
+            rc = _lib.load().msplat_dp_reduce_adam(
+                self.rank, self.world, m.n, m.rest_bases, cam.degree, cam.degrees_to_use,
+                self._grads_arr, self._params_arr, _ptr_array(m.exp_avg), _ptr_array(m.exp_avg_sq),
+                self._flags_arr, self.epoch, _lib.farr(steps), _lib.farr(bc2s), m.beta1, m.beta2,
+                m.eps, self.peer_timeout_s)
+            _lib.check(rc, "msplat_dp_reduce_adam")
+            return
         if self.world > 1:
             dist.all_reduce(self.grad, op=dist.ReduceOp.SUM)
         self.ops.adam_apply(self.model, cam, self.grad, 1.0 / self.world)
-        return self.last_loss
+
+    def peer_errors(self, reset: bool = False) -> int:
+        """Error bits of the peer-memory steps so far (0 = none; waits for
+        the GPU): 1 a peer's gradients, 2 a peer's updated shard never came."""
+        return int(_lib.load().msplat_dp_errors(1 if reset else 0))
 
     def sync_stats(self) -> None:
         """Combine the ranks' densification statistics (before densifying)."""
@@ -159,7 +265,22 @@ class DataParallel:
         return float(t.item())
 
     def shutdown(self) -> None:
+        """Hands the parameters back to torch-owned memory, unmaps the peers'
+        buffers and frees this rank's (peer mode), then ends the group if this
+        object created it."""
+        import torch
         import torch.distributed as dist
+        if self._bufs:
+            torch.cuda.synchronize()
+            self.barrier()
+            self.model.params = [p.clone() for p in self.model.params]
+            self.grad = None
+            torch.cuda.synchronize()
+            _lib.load().msplat_ipc_close_all()
+            self.barrier()
+            for b in self._bufs:
+                b.free()
+            self._bufs = []
         if self._owns_group and dist.is_initialized():
             dist.destroy_process_group()
         self._owns_group = False

@@ -2,7 +2,9 @@
 tests/test_dp_gpu.py): three DataParallel steps over NCCL on a seeded
 scene, rank r training view (step * world + r) % 3; saves its parameters.
 
-  torchrun --nproc-per-node 2 tests/dp_worker.py OUT_DIR N WIDTH HEIGHT SEED
+  torchrun --nproc-per-node 2 tests/dp_worker.py OUT_DIR N WIDTH HEIGHT SEED MODE
+
+MODE is the DataParallel mode: "peer" (NVLink kernel) or "nccl".
 """
 from __future__ import annotations
 
@@ -19,6 +21,7 @@ from tests import harness
 
 def main():
     out_dir, n, w, h, seed = sys.argv[1], *map(int, sys.argv[2:6])
+    mode = sys.argv[6]
     rank, world = multigpu.rank_and_world()
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
     engine.bind_stream()
@@ -26,7 +29,7 @@ def main():
                             log_scale_sigma=0.3)
     cams = [synthetic.front_camera(w, h, 3.0 + 0.3 * k) for k in range(3)]
     model = engine.GaussianModel(g.groups())
-    dp = multigpu.DataParallel(model, rank, world, timeout_s=60)
+    dp = multigpu.DataParallel(model, rank, world, timeout_s=60, mode=mode)
     for step in range(3):
         v = (step * world + rank) % 3
         cs = harness.setup_cam(cams[v])
@@ -35,6 +38,8 @@ def main():
         dp.train_step(cs, gt)
     torch.cuda.synchronize()
     dp.barrier()
+    if mode == "peer":
+        assert dp.peer_errors() == 0, "peer step timed out"
     np.savez(os.path.join(out_dir, f"rank{rank}.npz"),
              **{f"p{i}": model.params[i].cpu().numpy() for i in range(6)})
     dp.shutdown()

@@ -9,10 +9,14 @@
    for parameters and moments: the parity suite's one-step gradient floor
    (2e-6) grown for three steps of moment accumulation, where near-zero
    entries carry the absolute error of the atomics-ordered sums.
-2. Two NCCL ranks (tests/dp_worker.py under torchrun, when the box has two
-   GPUs): the replicas must be bit-identical to each other (every rank
-   applies the same summed buffer), and within the same bar of a one-GPU
+2. Two ranks (tests/dp_worker.py under torchrun, when the box has two
+   GPUs), through NCCL and through the peer-memory kernel: the replicas must
+   be bit-identical to each other, and within the same bar of a one-GPU
    emulation that sums the two views' gradients and applies scale 1/2.
+3. The peer-memory optimiser: at world 1 bit-identical to msplat_adam_apply
+   on the same gradients; and its cross-GPU waits give up and report when a
+   peer never signals (a second rank that does not exist), leaving the GPU
+   usable.
 """
 from __future__ import annotations
 
@@ -114,6 +118,93 @@ def test_split_step_equals_fused_step(case):
     assert not b["m3"][never].any() and not b["m4"][never].any()
 
 
+def _single_rank_group():
+    import socket
+    import torch
+    import torch.distributed as dist
+    if dist.is_initialized():
+        return
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1,
+                            device_id=torch.device("cuda", torch.cuda.current_device()))
+
+
+def test_peer_apply_equals_adam_apply_one_rank():
+    """The peer-memory optimiser at world 1 and msplat_adam_apply, given the
+    same gradient buffer, produce the same bits (same sum, scale 1, same
+    update)."""
+    import torch
+    import torch.distributed as dist
+    n, w, h = 30_000, 640, 480
+    g, cams = _scene(n, w, h, seed=3)
+    ref = engine.GaussianModel(g.groups())
+    peer_model = engine.GaussianModel(g.groups())
+    ops = multigpu.EngineOps()
+    grad = ops.alloc(multigpu.grad_floats(n, ref.rest_bases))
+    _single_rank_group()
+    dp = multigpu.DataParallel(peer_model, 0, 1, mode="peer")
+    try:
+        for step in range(3):
+            cs = harness.setup_cam(cams[step % len(cams)], step=step, interval=1)
+            ref.step_count += 1
+            ops.grads(ref, cs, _gt(cs, step), grad, 0.2, engine.DEFAULT_BG, 1.0, 0.01)
+            ops.adam_apply(ref, cs, grad, 1.0)
+            peer_model.step_count += 1
+            dp.grad.copy_(grad)
+            dp.apply(cs)
+            # the next gradients are taken at the reference's parameters
+            for a, b in zip(peer_model.params, ref.params):
+                assert torch.equal(a, b), "parameters differ"
+        torch.cuda.synchronize()
+        assert dp.peer_errors() == 0
+        for i in range(6):
+            assert torch.equal(peer_model.exp_avg[i], ref.exp_avg[i]), f"exp_avg {i}"
+            assert torch.equal(peer_model.exp_avg_sq[i], ref.exp_avg_sq[i]), f"exp_avg_sq {i}"
+    finally:
+        dp.shutdown()
+        dist.destroy_process_group()
+
+
+def test_peer_wait_times_out_and_reports():
+    """A world-2 step whose second rank never signals: both cross-GPU waits
+    give up after their limit, the error bits are set, and the GPU stays
+    usable."""
+    import ctypes as C
+    import time
+    import torch
+    from msplat_b200 import _lib
+    lib = _lib.load()
+    n = 4096
+    g, cams = _scene(n, 320, 240, seed=4)
+    model = engine.GaussianModel(g.groups())
+    grad = torch.zeros(multigpu.grad_floats(n, model.rest_bases), device="cuda")
+    flags = [torch.zeros(4, dtype=torch.int32, device="cuda") for _ in range(2)]
+    lib.msplat_dp_errors(1)
+    P = C.c_void_p
+    grads_arr = (P * 2)(grad.data_ptr(), grad.data_ptr())
+    params_arr = (P * 12)(*([p.data_ptr() for p in model.params] * 2))
+    flags_arr = (P * 2)(flags[0].data_ptr(), flags[1].data_ptr())
+    steps, bc2s = engine.adam_scalars(1, engine.LR_INIT)
+    t0 = time.perf_counter()
+    rc = lib.msplat_dp_reduce_adam(0, 2, n, model.rest_bases, 3, 3, grads_arr, params_arr,
+                                   engine._ptr_array(model.exp_avg),
+                                   engine._ptr_array(model.exp_avg_sq), flags_arr, 1,
+                                   _lib.farr(steps), _lib.farr(bc2s), 0.9, 0.999, 1e-8, 0.2)
+    assert rc == 0
+    errs = lib.msplat_dp_errors(1)
+    elapsed = time.perf_counter() - t0
+    assert errs == 3, f"error bits {errs}"
+    assert elapsed < 5.0
+    assert flags[0][0].item() == 1 and flags[1][0].item() == 1   # rank 0 signalled phase 0
+    # the context still works
+    cs = harness.setup_cam(cams[0])
+    engine.render(model, cs)
+    torch.cuda.synchronize()
+    assert lib.msplat_dp_errors(0) == 0
+
+
 def test_two_rank_nccl_matches_summed_views():
     import torch
     if torch.cuda.device_count() < 2:
@@ -136,15 +227,17 @@ def test_two_rank_nccl_matches_summed_views():
         ops.adam_apply(model, harness.setup_cam(cams[0]), total, 0.5)
     torch.cuda.synchronize()
     want = {f"p{i}": model.params[i].cpu().numpy() for i in range(6)}
-    with tempfile.TemporaryDirectory() as d:
-        cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-               "--master-addr", "127.0.0.1", "--master-port", "29561",
-               os.path.join(ROOT, "tests", "dp_worker.py"), d, str(n), str(w), str(h), "5"]
-        env = dict(os.environ, PYTHONPATH=ROOT)
-        res = subprocess.run(["timeout", "-k", "30", "300"] + cmd, cwd=ROOT, env=env,
-                             capture_output=True, text=True)
-        assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
-        got = [dict(np.load(os.path.join(d, f"rank{r}.npz"))) for r in range(2)]
-    for k, v in want.items():
-        np.testing.assert_array_equal(got[0][k], got[1][k], err_msg=f"replicas differ: {k}")
-        _assert_close(got[0][k], v, PARAM_RTOL, PARAM_ATOL_FRAC, f"vs emulation: {k}")
+    for mode, port in (("nccl", 29561), ("peer", 29562)):
+        with tempfile.TemporaryDirectory() as d:
+            cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                   "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(port),
+                   os.path.join(ROOT, "tests", "dp_worker.py"), d, str(n), str(w), str(h), "5",
+                   mode]
+            env = dict(os.environ, PYTHONPATH=ROOT)
+            res = subprocess.run(["timeout", "-k", "30", "300"] + cmd, cwd=ROOT, env=env,
+                                 capture_output=True, text=True)
+            assert res.returncode == 0, mode + res.stdout[-3000:] + res.stderr[-3000:]
+            got = [dict(np.load(os.path.join(d, f"rank{r}.npz"))) for r in range(2)]
+        for k, v in want.items():
+            np.testing.assert_array_equal(got[0][k], got[1][k], err_msg=f"{mode}: replicas differ: {k}")
+            _assert_close(got[0][k], v, PARAM_RTOL, PARAM_ATOL_FRAC, f"{mode} vs emulation: {k}")
