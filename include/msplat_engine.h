@@ -141,6 +141,26 @@ int msplat_train_step_grads(
     float inv_max_dim, const int32_t **radii_out, float *loss_out);
 
 /*
+ * The gradient half in compact form, for msplat_dp_reduce_adam(compact=1).
+ * No counterpart in the reference.  Same arguments as
+ * msplat_train_step_grads; grad_out holds 15 * N + 4 floats: the gradients
+ * of means [N,3], scales [N,3], quats [N,4], then v_rgb [N,3] (the colour
+ * gradient of each visible Gaussian, 0 for the others), the gradient of
+ * opacities [N], the visibility flags [N] and the camera position (3 floats).
+ * Every SH coefficient's gradient is v_rgb times a basis value of the view
+ * direction, so the optimiser rebuilds them from v_rgb and the camera.
+ */
+int msplat_train_step_grads_compact(
+    int num_points, float *means3d, float *scales, float glob_scale, float *quats,
+    const float *viewmat, const float *projmat, float fx, float fy, float cx, float cy,
+    unsigned img_height, unsigned img_width, const int *tile_bounds, float clip_thresh,
+    unsigned degree, unsigned degrees_to_use, const float *cam_pos,
+    float *features_dc, float *features_rest, float *opacities, const float *background,
+    const float *gt, float ssim_weight, float loss_inv_n, int features_rest_bases,
+    float *grad_out, float *vis_counts, float *xys_grad_norm, float *max_2d_size,
+    float inv_max_dim, const int32_t **radii_out, float *loss_out);
+
+/*
  * Data-parallel training, optimiser half: Adam on Gaussians [begin, end)
  * from a gradient buffer in the msplat_train_step_grads layout (typically
  * summed over ranks), each gradient multiplied by grad_scale.  The update,
@@ -172,14 +192,15 @@ int msplat_adam_apply(
  * step (from 1).  Queued on the engine stream: returns before the work
  * finishes; the step's cross-GPU waits give up after timeout_s seconds and
  * set bits read by msplat_dp_errors (1: gradients of a peer missing,
- * 2: updated shards of a peer missing).
+ * 2: updated shards of a peer missing).  With `compact` != 0 the gradient
+ * buffers are in the msplat_train_step_grads_compact layout (4x smaller).
  */
 int msplat_dp_reduce_adam(
     int rank, int world, int num_points, int features_rest_bases, unsigned degree,
     unsigned degrees_to_use, const float *const *rank_grads, float *const *rank_params,
     float *const *exp_avg, float *const *exp_avg_sq, unsigned *const *rank_flags,
     unsigned epoch, const float *adam_step_sizes, const float *adam_bc2_sqrts,
-    float adam_beta1, float adam_beta2, float adam_eps, double timeout_s);
+    float adam_beta1, float adam_beta2, float adam_eps, int compact, double timeout_s);
 /* Error bits of the peer-memory steps on this device (waits until the
  * engine stream is idle); clears them when `reset` != 0.  -1 on failure. */
 int msplat_dp_errors(int reset);

@@ -34,6 +34,7 @@
 #include "../../include/msplat_engine.h"
 #include "adam.cuh"
 #include "engine.h"
+#include "msp_math.cuh"
 
 namespace msp {
 namespace {
@@ -56,6 +57,8 @@ struct DpArgs {
     int stride[kGroups];
     long long goff[kGroups];                 // group offsets in the gradient buffer
     long long vis_off;                       // visibility flags' offset
+    long long cam_off;                       // compact form: camera position's offset
+    int rest_stride;                         // floats per Gaussian of features_rest
     int rank, world, begin, end, used_rest;
     int vec;                                 // bit g: group g's arrays are 16-byte aligned
     float b1, b2, eps, scale;
@@ -247,6 +250,167 @@ dp_reduce_adam_kernel(DpArgs a, const unsigned char* __restrict__ vis)
     }
 }
 
+// Compact form.  Each rank's buffer holds, per Gaussian, the gradients of
+// means, scales, quats and opacity, v_rgb (the colour gradient) and a
+// visibility flag, plus the rank's camera position.  The gradient of every
+// SH coefficient of a view is v_rgb times a basis value of that view's
+// direction to the mean, so the owner of a Gaussian rebuilds each rank's
+// dc and features_rest gradients (C0 * v_rgb, basis[b] * v_rgb[c]) from its
+// pre-update mean and sums them in rank order, exactly as the full buffer
+// would have carried them -- while 4x fewer bytes cross NVLink.
+constexpr int kCompactG = 256;   // Gaussians per work chunk (one per thread)
+
+template <int W>
+__global__ void __launch_bounds__(kDpThreads, 2)
+dp_compact_kernel(DpArgs a)
+{
+    extern __shared__ float s_rest[];               // [kCompactG][rsp] rest gradients
+    __shared__ float s_dc[kCompactG][3];
+    __shared__ unsigned char s_vis[kCompactG];
+    __shared__ float s_cam[W][3];
+    const bool ok = (*(volatile int*)a.err & kDpWaitGrads) == 0;
+    const int rs = a.rest_stride, rsp = rs | 1;
+    if (ok) {
+        const int tid = threadIdx.x;
+        if (tid < 3 * W) s_cam[tid / 3][tid % 3] = a.grads[tid / 3][a.cam_off + tid % 3];
+        const int nchunks = (a.end - a.begin + kCompactG - 1) / kCompactG;
+        for (int ch = blockIdx.x; ch < nchunks; ch += gridDim.x) {
+            const int c0 = a.begin + ch * kCompactG;
+            const int cn = min(kCompactG, a.end - c0);
+            __syncthreads();
+            // phase A: this thread's Gaussian
+            if (tid < cn) {
+                const long long i = c0 + tid;
+                float vsum = a.grads[0][a.vis_off + i];
+#pragma unroll
+                for (int q = 1; q < W; q++) vsum += a.grads[q][a.vis_off + i];
+                const bool vis = vsum > 0.f;
+                s_vis[tid] = vis;
+                if (vis) {
+                    const float* mp = a.params[a.rank][0] + 3 * i;
+                    const float p[3] = {mp[0], mp[1], mp[2]};
+                    float* row = s_rest + tid * rsp;
+#pragma unroll 1
+                    for (int q = 0; q < W; q++) {
+                        const float* vr = a.grads[q] + a.goff[3] + 3 * i;
+                        const float v0 = vr[0], v1 = vr[1], v2 = vr[2];
+                        const float d0 = MSP_SH_C0 * v0, d1 = MSP_SH_C0 * v1, d2 = MSP_SH_C0 * v2;
+                        if (q == 0) {
+                            s_dc[tid][0] = d0;
+                            s_dc[tid][1] = d1;
+                            s_dc[tid][2] = d2;
+                        } else {
+                            s_dc[tid][0] += d0;
+                            s_dc[tid][1] += d1;
+                            s_dc[tid][2] += d2;
+                        }
+                        if (a.used_rest > 0) {
+                            float bs[15];
+                            sh_rest_basis(s_cam[q], p, bs);
+                            for (int kk = 0; kk < a.used_rest; kk++) {
+                                const int b = kk / 3, c = kk - 3 * b;
+                                const float g = bs[b] * (c == 0 ? v0 : c == 1 ? v1 : v2);
+                                row[kk] = q == 0 ? g : row[kk] + g;
+                            }
+                        }
+                    }
+                }
+            }
+            __syncthreads();
+            // phase B: the chunk's slice of every group
+            for (int gi = 0; gi < kGroups; gi++) {
+                if (!a.params[a.rank][gi]) continue;
+                const int S = a.stride[gi];
+                const long long e0s = (long long)c0 * S;
+                const int total = cn * S;
+                if (gi == 3 || gi == 4) {
+                    // gradients from shared memory; 16-byte parameter and
+                    // moment traffic, two vectors per thread per round
+                    auto sh_grad = [&](int rel, float& g) {
+                        const int il = rel / S, kk = rel - il * S;
+                        if (!s_vis[il] || (gi == 4 && kk >= a.used_rest)) return false;
+                        g = gi == 3 ? s_dc[il][kk] : s_rest[il * rsp + kk];
+                        return true;
+                    };
+                    int body = 0;
+                    if (a.vec & (1 << gi)) {
+                        body = total / 4 * 4;
+                        const int nvec = body / 4;
+                        for (int v0 = tid; v0 < nvec; v0 += 2 * kDpThreads) {
+                            float4 pv[2], mv[2], vv[2];
+                            bool on[2];
+#pragma unroll
+                            for (int u = 0; u < 2; u++) {
+                                const int vi = v0 + u * kDpThreads;
+                                on[u] = vi < nvec;
+                                if (!on[u]) continue;
+                                const long long e = e0s + 4 * vi;
+                                pv[u] = ld4(a.params[a.rank][gi] + e);
+                                mv[u] = ld4(a.exp_avg[gi] + e);
+                                vv[u] = ld4(a.exp_avg_sq[gi] + e);
+                            }
+#pragma unroll
+                            for (int u = 0; u < 2; u++) {
+                                if (!on[u]) continue;
+                                const int vi = v0 + u * kDpThreads;
+#pragma unroll
+                                for (int k = 0; k < 4; k++) {
+                                    float g;
+                                    if (sh_grad(4 * vi + k, g))
+                                        adam_math(comp(pv[u], k), comp(mv[u], k), comp(vv[u], k),
+                                                  g * a.scale, a.step[gi], a.b1, a.b2,
+                                                  a.inv_bc2[gi], a.eps);
+                                }
+                                const long long e = e0s + 4 * vi;
+                                st4(a.exp_avg[gi] + e, mv[u]);
+                                st4(a.exp_avg_sq[gi] + e, vv[u]);
+#pragma unroll
+                                for (int q = 0; q < W; q++) st4(a.params[q][gi] + e, pv[u]);
+                            }
+                        }
+                    }
+                    for (int rel = body + tid; rel < total; rel += kDpThreads) {
+                        float g;
+                        if (!sh_grad(rel, g)) continue;
+                        const long long e = e0s + rel;
+                        float p = a.params[a.rank][gi][e], m = a.exp_avg[gi][e],
+                              v = a.exp_avg_sq[gi][e];
+                        adam_math(p, m, v, g * a.scale, a.step[gi], a.b1, a.b2, a.inv_bc2[gi],
+                                  a.eps);
+                        a.exp_avg[gi][e] = m;
+                        a.exp_avg_sq[gi][e] = v;
+#pragma unroll
+                        for (int q = 0; q < W; q++) a.params[q][gi][e] = p;
+                    }
+                    continue;
+                }
+                // means, scales, quats, opacity: the ranks' gradients, summed here
+                long long body = 0;
+                if (a.vec & (1 << gi)) {
+                    body = total / 4 * 4;
+                    const int nvec = (int)(body / 4);
+                    for (int v = tid; v < nvec; v += 2 * kDpThreads) {
+                        update_vec4<W>(a, gi, S, nullptr, e0s, 4 * v);
+                        if (v + kDpThreads < nvec) update_vec4<W>(a, gi, S, nullptr, e0s, 4 * (v + kDpThreads));
+                    }
+                }
+                for (long long rel = body + tid; rel < total; rel += kDpThreads)
+                    update_scalar<W>(a, gi, S, nullptr, e0s, rel);
+            }
+        }
+    }
+    // the last CTA to finish publishes phase 1 for this rank
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned prev = atomicAdd(a.done_ctas, 1u);
+        if (prev == gridDim.x - 1) {
+            *a.done_ctas = 0;
+            if (ok) signal_all(a, 1);
+        }
+    }
+}
+
 // Per-device DP state: the error word and the CTA counter.
 struct DpState {
     int* err = nullptr;
@@ -343,7 +507,7 @@ int msplat_dp_reduce_adam(int rank, int world, int num_points, int features_rest
                           float* const* exp_avg, float* const* exp_avg_sq,
                           unsigned* const* rank_flags, unsigned epoch,
                           const float* step_sizes, const float* bc2_sqrts, float beta1,
-                          float beta2, float eps, double timeout_s)
+                          float beta2, float eps, int compact, double timeout_s)
 {
     std::lock_guard<std::mutex> lk(engine_mutex());
     int rc = engine_init();
@@ -371,6 +535,19 @@ int msplat_dp_reduce_adam(int rank, int world, int num_points, int features_rest
         a.exp_avg_sq[gi] = exp_avg_sq[gi];
     }
     a.vis_off = off;
+    a.rest_stride = (int)rs;
+    if (compact) {
+        // means, scales, quats, v_rgb, opacities, visibility, camera
+        const long long n = num_points;
+        a.goff[0] = 0;
+        a.goff[1] = 3 * n;
+        a.goff[2] = 6 * n;
+        a.goff[3] = 10 * n;
+        a.goff[4] = 0;
+        a.goff[5] = 13 * n;
+        a.vis_off = 14 * n;
+        a.cam_off = 15 * n;
+    }
     for (int q = 0; q < world; q++) {
         a.grads[q] = rank_grads[q];
         a.flags[q] = rank_flags[q];
@@ -400,8 +577,11 @@ int msplat_dp_reduce_adam(int rank, int world, int num_points, int features_rest
     for (int gi = 0; gi < kGroups; gi++) {
         if (!a.params[rank][gi]) continue;
         uintptr_t mis = (uintptr_t)a.exp_avg[gi] | (uintptr_t)a.exp_avg_sq[gi];
-        for (int q = 0; q < world; q++)
-            mis |= (uintptr_t)(a.grads[q] + a.goff[gi]) | (uintptr_t)a.params[q][gi];
+        for (int q = 0; q < world; q++) {
+            mis |= (uintptr_t)a.params[q][gi];
+            // compact form: the SH groups' gradients come from shared memory
+            if (!(compact && (gi == 3 || gi == 4))) mis |= (uintptr_t)(a.grads[q] + a.goff[gi]);
+        }
         if ((mis & 15) == 0) a.vec |= 1 << gi;
     }
     const int dtu = (int)std::min(degrees_to_use, degree);
@@ -418,6 +598,39 @@ int msplat_dp_reduce_adam(int rank, int world, int num_points, int features_rest
     a.done_ctas = st->done;
     const cudaStream_t s = engine_stream();
     dp_signal_kernel<<<1, 32, 0, s>>>(a, 0);
+    if (compact) {
+        const int rsp = (int)rs | 1;
+        const size_t smem = (size_t)kCompactG * rsp * sizeof(float);
+        const int nchunks = std::max(1, (a.end - a.begin + kCompactG - 1) / kCompactG);
+        const int grid = std::min(nchunks, 148 * 2);
+        dp_signal_kernel<<<1, 32, 0, s>>>(a, 0);
+        dp_wait_kernel<<<1, 32, 0, s>>>(a, 0, kDpWaitGrads);
+#define MSP_COMPACT(W)                                                                          \
+    do {                                                                                        \
+        static bool set = false;                                                                \
+        if (!set) {                                                                             \
+            DP_CUDA(cudaFuncSetAttribute(dp_compact_kernel<W>,                                   \
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024)); \
+            set = true;                                                                         \
+        }                                                                                       \
+        dp_compact_kernel<W><<<grid, kDpThreads, smem, s>>>(a);                                 \
+    } while (0)
+        switch (world) {
+            case 1: MSP_COMPACT(1); break;
+            case 2: MSP_COMPACT(2); break;
+            case 3: MSP_COMPACT(3); break;
+            case 4: MSP_COMPACT(4); break;
+            case 5: MSP_COMPACT(5); break;
+            case 6: MSP_COMPACT(6); break;
+            case 7: MSP_COMPACT(7); break;
+            default: MSP_COMPACT(8); break;
+        }
+#undef MSP_COMPACT
+        dp_wait_kernel<<<1, 32, 0, s>>>(a, 1, kDpWaitShards);
+        engine_add_launches(4);
+        DP_CUDA(cudaGetLastError());
+        return MSPLAT_OK;
+    }
     const long long shard = a.end - a.begin;
     if (shard > st->vis_cap) {
         if (st->vis) cudaFree(st->vis);

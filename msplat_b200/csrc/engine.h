@@ -94,9 +94,16 @@ struct StatPtrs {
 // Planar per-group gradient output of the data-parallel step: group g's
 // gradient has the layout of its parameter tensor ([N, per-Gaussian
 // floats]); vis[i] is 1 for a Gaussian with radius > 0 in this view, else 0.
+//
+// Compact form (peer-memory data parallelism): g[3] holds v_rgb (the colour
+// gradient, from which every SH coefficient's gradient follows with the view
+// direction), g[4] is unused, and cam (3 floats) receives the camera
+// position of the step.
 struct GradOut {
     float* g[kGroups];
     float* vis;
+    float* cam;
+    int compact;
 };
 
 // Adam over a range of Gaussians [begin, end) from a gradient buffer laid

@@ -459,32 +459,6 @@ __device__ __forceinline__ void grad_slab(float* __restrict__ out, size_t e0, in
 constexpr int kGradSlots = 12;  // v_mean[3], v_scale[3], v_quat[4], v_opacity, pad
 constexpr int kBasisSlots = 19; // 15 SH-rest basis values + v_rgb[3] (odd stride: no bank conflicts)
 
-// SH-rest basis values (degrees 1-3, 15 of them) of the unit direction from
-// the camera to mean p: the factors of the rest gradient, g[b][c] =
-// basis[b] * v_rgb[c] (msplat_metal.metal:1915-1985).
-__device__ __forceinline__ void sh_rest_basis(const StepParams* __restrict__ P, const float p[3],
-                                              float* bs)
-{
-    const float d0 = p[0] - P->cam_pos[0], d1 = p[1] - P->cam_pos[1], d2 = p[2] - P->cam_pos[2];
-    const float dn = rsqrt_ieee((d0 * d0 + d1 * d1) + d2 * d2);
-    const float ux = d0 * dn, uy = d1 * dn, uz = d2 * dn;
-    const float xx = ux * ux, xy = ux * uy, xz = ux * uz, yy = uy * uy, yz = uy * uz, zz = uz * uz;
-    bs[0] = -MSP_SH_C1 * uy;
-    bs[1] = MSP_SH_C1 * uz;
-    bs[2] = -MSP_SH_C1 * ux;
-    bs[3] = kSH_C2[0] * xy;
-    bs[4] = kSH_C2[1] * yz;
-    bs[5] = kSH_C2[2] * ((2.f * zz - xx) - yy);
-    bs[6] = kSH_C2[3] * xz;
-    bs[7] = kSH_C2[4] * (xx - yy);
-    bs[8] = kSH_C3[0] * uy * (3.f * xx - yy);
-    bs[9] = kSH_C3[1] * xy * uz;
-    bs[10] = kSH_C3[2] * uy * ((4.f * zz - xx) - yy);
-    bs[11] = kSH_C3[3] * uz * ((2.f * zz - 3.f * xx) - 3.f * yy);
-    bs[12] = kSH_C3[4] * ux * ((4.f * zz - xx) - yy);
-    bs[13] = kSH_C3[5] * uz * (xx - yy);
-    bs[14] = kSH_C3[6] * ux * (xx - 3.f * yy);
-}
 
 // Geometry and colour VJP of one visible Gaussian (project_and_sh_backward_kernel,
 // msplat_metal.metal:1813-1986; VJPs :1216-1531): from its 9 raster
@@ -494,7 +468,7 @@ __device__ __forceinline__ void gaussian_vjp(const StepParams* __restrict__ P,
                                              const float* __restrict__ ga, const float4 co,
                                              const float p[3], float ls0, float ls1, float ls2,
                                              float q0, float q1, float q2, float q3,
-                                             float gr[kGradSlots], float* bs)
+                                             float gr[kGradSlots], float* bs, bool with_basis)
 {
     const float vr0 = ga[0], vr1 = ga[1], vr2 = ga[2];
     const float vc0 = ga[3], vc1 = ga[4], vc2 = ga[5];
@@ -597,7 +571,7 @@ __device__ __forceinline__ void gaussian_vjp(const StepParams* __restrict__ P,
     gr[2] = vmean[2];
     gr[10] = vop;
     // SH basis of the view direction for the dc/rest Adam (:1915-1985)
-    sh_rest_basis(P, p, bs);
+    if (with_basis) sh_rest_basis(P->cam_pos, p, bs);
     bs[15] = vr0;
     bs[16] = vr1;
     bs[17] = vr2;
@@ -637,7 +611,11 @@ project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
                         ls2 = scales[3 * (size_t)i + 2];
             const float q0 = quats[4 * (size_t)i], q1 = quats[4 * (size_t)i + 1],
                         q2 = quats[4 * (size_t)i + 2], q3 = quats[4 * (size_t)i + 3];
-            gaussian_vjp(P, ga, g_co[i], p, ls0, ls1, ls2, q0, q1, q2, q3, gr, s_basis[tid]);
+            // the SH-rest basis only when this kernel forms the rest gradient
+            const bool with_basis =
+                GRAD_OUT ? !G.compact : (A.numel[4] > 0 && nb_rest > 0);
+            gaussian_vjp(P, ga, g_co[i], p, ls0, ls1, ls2, q0, q1, q2, q3, gr, s_basis[tid],
+                         with_basis);
             const float vx = ga[6], vy = ga[7];
             // densification statistics (accumulate_grad_stats_kernel)
             St.vis_counts[i] += 1.0f;
@@ -667,6 +645,16 @@ project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
                      [&](int gl, int k, float& g) { g = sg[gl][6 + k]; return true; });
         grad_slab<1>(G.g[5], gb, cnt, lane,
                      [&](int gl, int, float& g) { g = sg[gl][10]; return true; });
+        if (G.compact) {
+            // v_rgb of the visible Gaussians (0 for the others) and the camera
+            grad_slab<3>(G.g[3], gb * 3, cnt * 3, lane, [&](int gl, int k, float& g) {
+                g = sb[gl][15 + k];
+                return sv[gl] != 0;
+            });
+            if (lane < cnt) G.vis[g0 + lane] = sv[lane] ? 1.f : 0.f;
+            if (g0 == 0 && lane < 3) G.cam[lane] = P->cam_pos[lane];
+            return;
+        }
         grad_slab<3>(G.g[3], gb * 3, cnt * 3, lane, [&](int gl, int k, float& g) {
             g = MSP_SH_C0 * sb[gl][15 + k];
             return sv[gl] != 0;
@@ -772,7 +760,7 @@ rest_adam_kernel(const StepParams* __restrict__ P, int N, const int* __restrict_
     if (i < N && radii[i] > 0) {
         vis = true;
         const float p[3] = {means[3 * (size_t)i], means[3 * (size_t)i + 1], means[3 * (size_t)i + 2]};
-        sh_rest_basis(P, p, s_b[tid]);
+        sh_rest_basis(P->cam_pos, p, s_b[tid]);
         const float* ga = grad_acc + (size_t)i * kGradStride;
         s_c[tid][0] = ga[0];
         s_c[tid][1] = ga[1];

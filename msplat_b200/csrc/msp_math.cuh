@@ -159,6 +159,32 @@ __device__ __constant__ static const float kSH_C4[9] = {
     -0.6690465435572892f, 0.10578554691520431f, -0.6690465435572892f,
     0.47308734787878004f, -1.7701307697799304f, 0.6258357354491761f};
 
+// SH-rest basis values (degrees 1-3, 15 of them) of the unit direction from
+// the camera to mean p: the factors of the rest gradient, g[b][c] =
+// basis[b] * v_rgb[c] (msplat_metal.metal:1915-1985).
+__device__ __forceinline__ void sh_rest_basis(const float cam[3], const float p[3], float* bs)
+{
+    const float d0 = p[0] - cam[0], d1 = p[1] - cam[1], d2 = p[2] - cam[2];
+    const float dn = rsqrt_ieee((d0 * d0 + d1 * d1) + d2 * d2);
+    const float ux = d0 * dn, uy = d1 * dn, uz = d2 * dn;
+    const float xx = ux * ux, xy = ux * uy, xz = ux * uz, yy = uy * uy, yz = uy * uz, zz = uz * uz;
+    bs[0] = -MSP_SH_C1 * uy;
+    bs[1] = MSP_SH_C1 * uz;
+    bs[2] = -MSP_SH_C1 * ux;
+    bs[3] = kSH_C2[0] * xy;
+    bs[4] = kSH_C2[1] * yz;
+    bs[5] = kSH_C2[2] * ((2.f * zz - xx) - yy);
+    bs[6] = kSH_C2[3] * xz;
+    bs[7] = kSH_C2[4] * (xx - yy);
+    bs[8] = kSH_C3[0] * uy * (3.f * xx - yy);
+    bs[9] = kSH_C3[1] * xy * uz;
+    bs[10] = kSH_C3[2] * uy * ((4.f * zz - xx) - yy);
+    bs[11] = kSH_C3[3] * uz * ((2.f * zz - 3.f * xx) - 3.f * yy);
+    bs[12] = kSH_C3[4] * ux * ((4.f * zz - xx) - yy);
+    bs[13] = kSH_C3[5] * uz * (xx - yy);
+    bs[14] = kSH_C3[6] * ux * (xx - 3.f * yy);
+}
+
 // 1D SSIM window (msplat_metal.metal:3041-3045).
 __device__ __constant__ static const float kGauss1D[11] = {
     0.0010283801f, 0.0075987581f, 0.0360007721f, 0.1093606895f, 0.2130055377f,

@@ -46,6 +46,12 @@ def grad_floats(n: int, rest_bases: int) -> int:
     return (15 + 3 * rest_bases) * n
 
 
+def grad_floats_compact(n: int) -> int:
+    """Length of the compact gradient buffer (msplat_train_step_grads_compact):
+    means, scales, quats, v_rgb, opacities, visibility, camera position."""
+    return 15 * n + 4
+
+
 def grad_views(buf, n: int, rest_bases: int):
     """Views of the flat buffer: the six groups' gradients and `vis`."""
     widths = [w if w is not None else 3 * rest_bases for w in GROUP_WIDTHS]
@@ -81,6 +87,26 @@ class EngineOps:
             _ptr(model.vis_counts), _ptr(model.xys_grad_norm), _ptr(model.max_2d_size),
             inv_max_dim, C.byref(radii), C.byref(loss))
         _lib.check(rc, "msplat_train_step_grads")
+        return float(loss.value)
+
+    def grads_compact(self, model: GaussianModel, cam, gt, out, ssim_weight, background,
+                      glob_scale, clip_thresh) -> float:
+        lib = _lib.load()
+        h, w = cam.height, cam.width
+        loss_inv_n = float(f32(1.0) / f32(h * w * 3))
+        inv_max_dim = float(f32(1.0) / f32(max(h, w)))
+        p = model.params
+        radii = C.c_void_p()
+        loss = C.c_float()
+        rc = lib.msplat_train_step_grads_compact(
+            model.n, _ptr(p[0]), _ptr(p[1]), glob_scale, _ptr(p[2]),
+            _lib.farr(cam.viewmat), _lib.farr(cam.projmat), cam.fx, cam.fy, cam.cx, cam.cy,
+            h, w, _lib.iarr(cam.tile_bounds), clip_thresh, cam.degree, cam.degrees_to_use,
+            _lib.farr(cam.cam_pos), _ptr(p[3]), _ptr(p[4]), _ptr(p[5]), _lib.farr(background),
+            _ptr(gt), ssim_weight, loss_inv_n, model.rest_bases, _ptr(out),
+            _ptr(model.vis_counts), _ptr(model.xys_grad_norm), _ptr(model.max_2d_size),
+            inv_max_dim, C.byref(radii), C.byref(loss))
+        _lib.check(rc, "msplat_train_step_grads_compact")
         return float(loss.value)
 
     def adam_apply(self, model: GaussianModel, cam, grad, scale: float) -> None:
@@ -138,7 +164,10 @@ class DataParallel:
     mode "peer" (GPUs): the gradient buffers, parameter arrays and flag
     arrays of all ranks are mapped into every process, and one kernel per
     rank sums its 1/world shard of the gradients over NVLink, applies Adam to
-    it and writes it into every replica (msplat_dp_reduce_adam).
+    it and writes it into every replica (msplat_dp_reduce_adam).  With
+    `compact` (the default) the ranks exchange each Gaussian's colour
+    gradient v_rgb instead of its 48 SH gradients, which the owner rebuilds
+    from every rank's camera position (15 instead of 60 floats per Gaussian).
     mode "nccl": one all-reduce of the gradient buffer, then Adam on every
     replica (msplat_adam_apply).  The stand-in ops of the CPU tests use it.
 
@@ -149,7 +178,7 @@ class DataParallel:
 
     def __init__(self, model: GaussianModel, rank: int, world: int, ops=None,
                  backend: str | None = None, timeout_s: float = 120.0, mode: str | None = None,
-                 peer_timeout_s: float = 10.0):
+                 peer_timeout_s: float = 10.0, compact: bool = True):
         import torch
         import torch.distributed as dist
         self.model, self.rank, self.world = model, rank, world
@@ -159,6 +188,8 @@ class DataParallel:
         if self.mode not in ("peer", "nccl"):
             raise ValueError(f"unknown data-parallel mode {self.mode!r}")
         self.peer_timeout_s = float(peer_timeout_s)
+        # peer mode: exchange v_rgb instead of the 48 SH gradients per Gaussian
+        self.compact = bool(compact) and self.mode == "peer"
         self._bufs = []
         if not dist.is_initialized():
             be = backend or ("nccl" if torch.cuda.is_available() else "gloo")
@@ -181,7 +212,8 @@ class DataParallel:
         import torch
         import torch.distributed as dist
         m = self.model
-        gbuf = DeviceBuffer(grad_floats(m.n, m.rest_bases))
+        gbuf = DeviceBuffer(grad_floats_compact(m.n) if self.compact
+                            else grad_floats(m.n, m.rest_bases))
         fbuf = DeviceBuffer(2 * self.world, typestr="<u4")
         pbufs = [DeviceBuffer(p.numel()) for p in m.params]
         self._bufs = [gbuf, fbuf] + pbufs
@@ -210,8 +242,9 @@ class DataParallel:
                    glob_scale: float = 1.0, clip_thresh: float = 0.01) -> float:
         """One data-parallel step; every rank passes its own view."""
         self.model.step_count += 1
-        self.last_loss = self.ops.grads(self.model, cam, gt, self.grad, ssim_weight, background,
-                                        glob_scale, clip_thresh)
+        grads = self.ops.grads_compact if self.compact else self.ops.grads
+        self.last_loss = grads(self.model, cam, gt, self.grad, ssim_weight, background,
+                               glob_scale, clip_thresh)
         self.apply(cam)
         return self.last_loss
 
@@ -227,7 +260,7 @@ class DataParallel:
                 self.rank, self.world, m.n, m.rest_bases, cam.degree, cam.degrees_to_use,
                 self._grads_arr, self._params_arr, _ptr_array(m.exp_avg), _ptr_array(m.exp_avg_sq),
                 self._flags_arr, self.epoch, _lib.farr(steps), _lib.farr(bc2s), m.beta1, m.beta2,
-                m.eps, self.peer_timeout_s)
+                m.eps, 1 if self.compact else 0, self.peer_timeout_s)
             _lib.check(rc, "msplat_dp_reduce_adam")
             return
         if self.world > 1:

@@ -14,9 +14,10 @@
    be bit-identical to each other, and within the same bar of a one-GPU
    emulation that sums the two views' gradients and applies scale 1/2.
 3. The peer-memory optimiser: at world 1 bit-identical to msplat_adam_apply
-   on the same gradients; and its cross-GPU waits give up and report when a
-   peer never signals (a second rank that does not exist), leaving the GPU
-   usable.
+   on the same gradients; its compact exchange (v_rgb instead of the SH
+   gradients) within the bar of the full one; and its cross-GPU waits give
+   up and report when a peer never signals (a second rank that does not
+   exist), leaving the GPU usable.
 """
 from __future__ import annotations
 
@@ -144,7 +145,7 @@ def test_peer_apply_equals_adam_apply_one_rank():
     ops = multigpu.EngineOps()
     grad = ops.alloc(multigpu.grad_floats(n, ref.rest_bases))
     _single_rank_group()
-    dp = multigpu.DataParallel(peer_model, 0, 1, mode="peer")
+    dp = multigpu.DataParallel(peer_model, 0, 1, mode="peer", compact=False)
     try:
         for step in range(3):
             cs = harness.setup_cam(cams[step % len(cams)], step=step, interval=1)
@@ -164,6 +165,38 @@ def test_peer_apply_equals_adam_apply_one_rank():
             assert torch.equal(peer_model.exp_avg_sq[i], ref.exp_avg_sq[i]), f"exp_avg_sq {i}"
     finally:
         dp.shutdown()
+        dist.destroy_process_group()
+
+
+def test_peer_compact_equals_full_one_rank():
+    """Exchanging v_rgb and rebuilding the SH gradients from the camera gives
+    the parameters of the full gradient exchange (within the bar: the two
+    runs take their gradients with differently ordered float atomics)."""
+    import torch
+    import torch.distributed as dist
+    n, w, h = 30_000, 640, 480
+    g, cams = _scene(n, w, h, seed=6)
+    models = [engine.GaussianModel(g.groups()) for _ in range(2)]
+    _single_rank_group()
+    dps = [multigpu.DataParallel(m, 0, 1, mode="peer", compact=c)
+           for m, c in zip(models, (False, True))]
+    try:
+        for step in range(3):
+            cs = harness.setup_cam(cams[step % len(cams)], step=step + 1, interval=1)
+            gt = _gt(cs, step)
+            for dp in dps:
+                dp.train_step(cs, gt)
+        torch.cuda.synchronize()
+        assert all(dp.peer_errors() == 0 for dp in dps)
+        a, b = _state(models[0]), _state(models[1])
+        for k in a:
+            if k in ("vis", "gn", "m2d"):
+                _assert_close(b[k], a[k], STAT_RTOL, STAT_ATOL_FRAC, f"compact: {k}")
+            else:
+                _assert_close(b[k], a[k], PARAM_RTOL, PARAM_ATOL_FRAC, f"compact: {k}")
+    finally:
+        for dp in dps:
+            dp.shutdown()
         dist.destroy_process_group()
 
 
@@ -191,7 +224,7 @@ def test_peer_wait_times_out_and_reports():
     rc = lib.msplat_dp_reduce_adam(0, 2, n, model.rest_bases, 3, 3, grads_arr, params_arr,
                                    engine._ptr_array(model.exp_avg),
                                    engine._ptr_array(model.exp_avg_sq), flags_arr, 1,
-                                   _lib.farr(steps), _lib.farr(bc2s), 0.9, 0.999, 1e-8, 0.2)
+                                   _lib.farr(steps), _lib.farr(bc2s), 0.9, 0.999, 1e-8, 0, 0.2)
     assert rc == 0
     errs = lib.msplat_dp_errors(1)
     elapsed = time.perf_counter() - t0
