@@ -255,6 +255,41 @@ int msplat_render_noalloc(
     const float *features_dc, const float *features_rest, const float *opacities,
     const float *background, float *out_img, void *cuda_stream);
 
+/* ---- densification (follows the training step) ------------------------- */
+
+/*
+ * Densification.  Replaces int msplat_densify(...) (bindings.h:69-84;
+ * implementation msplat_metal.mm:1337-1592) argument for argument, MTensor
+ * replaced by device pointers: classify every Gaussian as split / duplicate
+ * (average screen-space gradient above grad_thresh, largest scale above or
+ * below size_thresh, screen size above screen_thresh when check_screen),
+ * append two children per split (offsets R(q) * (sample * exp(scale)),
+ * scale - ln 1.6, zero Adam state; random_samples [2N,3] standard normals)
+ * and one copy per duplicate, cull (opacity below cull_alpha_thresh, split
+ * parents, and with check_huge: largest scale above cull_scale_thresh or
+ * screen size above cull_screen_size), and compact all 18 buffers (the six
+ * parameter arrays and their two Adam moments, group order as in
+ * msplat_train_step, each with room for 3N rows: buf_capacity) in order.
+ * The scratch arrays may be NULL, in which case the engine provides them.
+ * Synchronous; returns the new number of Gaussians, or a negative code.
+ */
+int msplat_densify(
+    int N, int buf_capacity, float grad_thresh, float size_thresh, float screen_thresh,
+    int check_screen, float cull_alpha_thresh, float cull_scale_thresh, float cull_screen_size,
+    int check_huge, const float *xys_grad_norm, const float *vis_counts,
+    const float *max_2d_size, float half_max_dim, float *means_buf, float *scales_buf,
+    float *quats_buf, float *features_dc_buf, float *features_rest_buf, float *opacities_buf,
+    int fr_stride, float *const *adam_exp_avg_buf, float *const *adam_exp_avg_sq_buf,
+    int *split_flag, int *dup_flag, int *split_prefix, int *dup_prefix, int *keep_flag,
+    int *keep_prefix, int *block_totals, float *compact_scratch, const float *random_samples);
+
+/*
+ * The opacity reset of Model::afterTrain (model.cpp:280-290), on the GPU
+ * instead of the host: every opacity logit above logit(0.2) is lowered to
+ * it and the opacity group's Adam moments are zeroed (n Gaussians).
+ */
+int msplat_reset_opacity(float *opacities, float *exp_avg, float *exp_avg_sq, int n);
+
 /* ---- introspection (tests and benchmarks) ------------------------------- */
 
 /* Loss of the last step; waits for it when `sync` != 0, else returns the

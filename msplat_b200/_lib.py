@@ -71,6 +71,11 @@ SIGNATURES = {
     "msplat_ipc_get_handle": (_i, [_p, _p]),
     "msplat_ipc_open_handle": (_i, [_p, C.POINTER(_p)]),
     "msplat_ipc_close_all": (_i, []),
+    "msplat_densify": (_i, [
+        _i, _i, _f, _f, _f, _i, _f, _f, _f, _i, _p, _p, _p, _f, _p, _p, _p, _p, _p, _p, _i,
+        C.POINTER(_p), C.POINTER(_p), _p, _p, _p, _p, _p, _p, _p, _p, _p,
+    ]),
+    "msplat_reset_opacity": (_i, [_p, _p, _p, _i]),
     "msplat_render_noalloc": (_i, [
         _i, _p, _p, _f, _p, _fp, _fp, _f, _f, _f, _f, _u, _u, _ip, _f, _u, _u, _fp,
         _p, _p, _p, _fp, _p, _p,

@@ -59,25 +59,48 @@ def adam_scalars(step_count: int, lr, beta1: float = 0.9, beta2: float = 0.999):
 
 
 class GaussianModel:
-    """Device-resident Gaussians + Adam state + densification statistics."""
+    """Device-resident Gaussians + Adam state + densification statistics.
 
-    def __init__(self, groups, device: str = "cuda", lr=LR_INIT):
+    As Model does (core/src/model.cpp:128-195), every group lives in a
+    backing buffer with room for `capacity` rows (4N at first) and the
+    parameters, moments and statistics are views of the first num_active
+    rows; densification grows the buffers (ensure_capacity) and changes
+    num_active.
+    """
+
+    def __init__(self, groups, device: str = "cuda", lr=LR_INIT, capacity: int | None = None):
         torch = _torch()
-        self.params = [torch.as_tensor(np.ascontiguousarray(g)).to(device).contiguous()
-                       for g in groups]
-        self.exp_avg = [torch.zeros_like(p) for p in self.params]
-        self.exp_avg_sq = [torch.zeros_like(p) for p in self.params]
-        n = self.params[0].shape[0]
-        self.vis_counts = torch.zeros(n, dtype=torch.float32, device=device)
-        self.xys_grad_norm = torch.zeros(n, dtype=torch.float32, device=device)
-        self.max_2d_size = torch.zeros(n, dtype=torch.float32, device=device)
+        arrs = [np.ascontiguousarray(g, dtype=np.float32) for g in groups]
+        n = int(arrs[0].shape[0])
+        cap = max(int(capacity) if capacity is not None else 4 * n, n, 1)
+        self._device = device
+        self._bufs = [torch.zeros((cap,) + a.shape[1:], dtype=torch.float32, device=device)
+                      for a in arrs]
+        for buf, a in zip(self._bufs, arrs):
+            buf[:n].copy_(torch.as_tensor(a))
+        self._m = [torch.zeros_like(b) for b in self._bufs]
+        self._v = [torch.zeros_like(b) for b in self._bufs]
+        self._stats = [torch.zeros(cap, dtype=torch.float32, device=device) for _ in range(3)]
+        self.num_active = n
         self.lr = [float(x) for x in lr]
         self.beta1, self.beta2, self.eps = 0.9, 0.999, 1e-8
         self.step_count = 0
+        self._refresh()
+
+    def _refresh(self) -> None:
+        n = self.num_active
+        self.params = [b[:n] for b in self._bufs]
+        self.exp_avg = [m[:n] for m in self._m]
+        self.exp_avg_sq = [v[:n] for v in self._v]
+        self.vis_counts, self.xys_grad_norm, self.max_2d_size = [s[:n] for s in self._stats]
 
     @property
     def n(self) -> int:
         return int(self.params[0].shape[0])
+
+    @property
+    def capacity(self) -> int:
+        return int(self._bufs[0].shape[0])
 
     @property
     def rest_bases(self) -> int:
@@ -91,6 +114,107 @@ class GaussianModel:
         t = min(max(f32(step) / f32(max_steps), f32(0.0)), f32(1.0))
         self.lr[0] = float(f32(math.exp(float(f32(math.log(float(f32(LR_INIT[0])))) * (f32(1.0) - t)
                                                + f32(math.log(float(f32(MEANS_LR_FINAL)))) * t))))
+
+    def ensure_capacity(self, needed: int) -> None:
+        """Model::ensureCapacity (model.cpp:197-225): grow every backing
+        buffer to max(needed, 2 x capacity), keeping the active rows."""
+        if needed <= self.capacity:
+            return
+        torch = _torch()
+        cap = max(int(needed), 2 * self.capacity)
+        n = self.num_active
+
+        def grow(buf):
+            out = torch.zeros((cap,) + tuple(buf.shape[1:]), dtype=buf.dtype, device=buf.device)
+            out[:n].copy_(buf[:n])
+            return out
+        self._bufs = [grow(b) for b in self._bufs]
+        self._m = [grow(m) for m in self._m]
+        self._v = [grow(v) for v in self._v]
+        self._stats = [grow(st) for st in self._stats]
+        self._refresh()
+
+    def densify(self, step: int, grad_thresh: float, size_thresh: float, screen_thresh: float,
+                check_screen: bool, check_huge: bool, half_max_dim: float,
+                random_samples=None, cull_alpha_thresh: float = 0.1,
+                cull_scale_thresh: float = 0.5, cull_screen_size: float = 0.15) -> int:
+        """msplat_densify over this model (the densification branch of
+        Model::afterTrain, model.cpp:243-275).  random_samples: [2N, 3]
+        standard normals on the device; by default drawn from a generator
+        seeded with the step (the reference seeds std::mt19937 with it).
+        Returns the new number of Gaussians."""
+        torch = _torch()
+        n = self.num_active
+        self.ensure_capacity(3 * n)
+        if random_samples is None:
+            gen = torch.Generator(device=self._device).manual_seed(int(step))
+            random_samples = torch.randn(2 * n, 3, generator=gen, device=self._device)
+        samples = random_samples.contiguous()   # held until the call returns
+        b = self._bufs
+        fr_stride = int(np.prod(b[4].shape[1:]))
+        rc = _lib.load().msplat_densify(
+            n, self.capacity, grad_thresh, size_thresh, screen_thresh, int(check_screen),
+            cull_alpha_thresh, cull_scale_thresh, cull_screen_size, int(check_huge),
+            _ptr(self._stats[1]), _ptr(self._stats[0]), _ptr(self._stats[2]), half_max_dim,
+            _ptr(b[0]), _ptr(b[1]), _ptr(b[2]), _ptr(b[3]), _ptr(b[4]), _ptr(b[5]), fr_stride,
+            _ptr_array(self._m), _ptr_array(self._v), None, None, None, None, None, None, None,
+            None, _ptr(samples))
+        if rc < 0:
+            _lib.check(rc, "msplat_densify")
+        self.num_active = int(rc)
+        self._refresh()
+        return self.num_active
+
+    def reset_opacity(self) -> None:
+        """The opacity reset of Model::afterTrain (model.cpp:280-290)."""
+        _lib.check(_lib.load().msplat_reset_opacity(_ptr(self.params[5]), _ptr(self.exp_avg[5]),
+                                                    _ptr(self.exp_avg_sq[5]), self.n),
+                   "msplat_reset_opacity")
+
+    def reset_stats(self) -> None:
+        for st in self._stats:
+            st.zero_()
+
+
+class Schedule:
+    """The refinement schedule of Model::afterTrain (model.cpp:236-296),
+    with the reference's defaults (msplat_api.hpp:16-33)."""
+
+    def __init__(self, max_steps: int = 30000, num_cameras: int = 1, refine_every: int = 100,
+                 warmup_length: int = 500, reset_alpha_every: int = 30,
+                 densify_grad_thresh: float = 0.0002, densify_size_thresh: float = 0.01,
+                 stop_screen_size_at: int = 4000, split_screen_size: float = 0.05):
+        self.num_cameras = num_cameras
+        self.refine_every = refine_every
+        self.warmup_length = warmup_length
+        self.reset_alpha_every = reset_alpha_every
+        self.stop_split_at = max_steps // 2
+        self.densify_grad_thresh = densify_grad_thresh
+        self.densify_size_thresh = densify_size_thresh
+        self.stop_screen_size_at = stop_screen_size_at
+        self.split_screen_size = split_screen_size
+
+    def after_train(self, model: GaussianModel, step: int, width: int, height: int) -> dict:
+        """Runs the densification / opacity reset due at `step` (after the
+        step's training) and resets the statistics on refinement steps.
+        Returns what happened."""
+        done = {"densified": None, "opacity_reset": False}
+        if not (step % self.refine_every == 0 and step > self.warmup_length):
+            return done
+        reset_interval = self.reset_alpha_every * self.refine_every
+        if step < self.stop_split_at and step % reset_interval > self.num_cameras + self.refine_every:
+            before = model.n
+            after = model.densify(
+                step, self.densify_grad_thresh, self.densify_size_thresh, self.split_screen_size,
+                check_screen=step < self.stop_screen_size_at,
+                check_huge=step > self.refine_every * self.reset_alpha_every,
+                half_max_dim=float(f32(0.5) * f32(max(width, height))))
+            done["densified"] = (before, after)
+        if step < self.stop_split_at and step % reset_interval == self.refine_every:
+            model.reset_opacity()
+            done["opacity_reset"] = True
+        model.reset_stats()
+        return done
 
 
 def _ptr(t) -> C.c_void_p:

@@ -1085,3 +1085,160 @@ int orc_render(const orc_params *P, orc_state *S, const float *params[6])
     orc_rasterize_forward(P, params[5], S);
     return 0;
 }
+
+/* ------------------------------------------------------------------------ */
+/* Densification                                                             */
+/* ------------------------------------------------------------------------ */
+
+/*
+ * msplat_densify (core/metal/msplat_metal.mm:1337-1592) with its kernels
+ * restated in stage order: densify_classify_kernel (msplat_metal.metal:
+ * 3475-3509), inclusive prefix sums of the split and duplicate flags
+ * (block_reduce_kernel / block_scan_propagate_kernel :2368-2439),
+ * densify_append_split_kernel (:3514-3600), densify_append_dup_kernel
+ * (:3604-3651), densify_cull_classify_kernel (:3656-3694) over 3N slots, the
+ * keep prefix sum and the stable compaction of the 18 buffers
+ * (compact_scatter_kernel / compact_copy_back_kernel :3698-3729).
+ * bufs / exp_avg / exp_avg_sq: group order means, scales, quats,
+ * features_dc, features_rest (fr_stride floats per Gaussian), opacities, each
+ * with room for 3N rows.  random_samples: [2N, 3] standard normals, child k
+ * of the split with ordinal o takes row 2o + k.  The flag dumps may be NULL.
+ * Returns the new count, or -1 when 3N exceeds buf_capacity.
+ */
+int orc_densify(int N, int buf_capacity, float grad_thresh, float size_thresh,
+                float screen_thresh, int check_screen, float cull_alpha_thresh,
+                float cull_scale_thresh, float cull_screen_size, int check_huge,
+                const float *xys_grad_norm, const float *vis_counts, const float *max_2d_size,
+                float half_max_dim, float *bufs[6], int fr_stride, float *exp_avg[6],
+                float *exp_avg_sq[6], const float *random_samples, int *split_flag_out,
+                int *dup_flag_out, int *keep_flag_out)
+{
+    const int worst = 3 * N;
+    if (worst > buf_capacity) return -1;
+    const int strides[6] = {3, 3, 4, 3, fr_stride, 1};
+    const float log_size_fac = logf(1.6f);
+    int *split = (int *)calloc((size_t)(N > 0 ? N : 1), sizeof(int));
+    int *dup = (int *)calloc((size_t)(N > 0 ? N : 1), sizeof(int));
+    int *keep = (int *)calloc((size_t)(worst > 0 ? worst : 1), sizeof(int));
+    /* classify (:3475-3509) */
+    for (int i = 0; i < N; i++) {
+        const float vc = vis_counts[i];
+        if (vc <= 0.0f) continue;
+        const float avg_grad = (xys_grad_norm[i] / vc) * half_max_dim;
+        const int high_grad = avg_grad > grad_thresh;
+        const float *s = bufs[1] + 3 * (size_t)i;
+        const float max_scale = fmaxf(fmaxf(msp_expf(s[0]), msp_expf(s[1])), msp_expf(s[2]));
+        const int is_large = max_scale > size_thresh;
+        int do_split = is_large;
+        if (check_screen && max_2d_size[i] > screen_thresh) do_split = 1;
+        split[i] = do_split && high_grad;
+        dup[i] = !is_large && high_grad;
+    }
+    int n_split = 0, n_dup = 0;
+    int *split_ord = (int *)calloc((size_t)(N > 0 ? N : 1), sizeof(int));
+    int *dup_ord = (int *)calloc((size_t)(N > 0 ? N : 1), sizeof(int));
+    for (int i = 0; i < N; i++) {
+        split_ord[i] = n_split;
+        n_split += split[i];
+        dup_ord[i] = n_dup;
+        n_dup += dup[i];
+    }
+    /* split children (:3514-3600): child k at N + 2*ord + k */
+    for (int i = 0; i < N; i++) {
+        if (!split[i]) continue;
+        const int ord = split_ord[i];
+        float *q = bufs[2] + 4 * (size_t)i;
+        float qw = q[0], qx = q[1], qy = q[2], qz = q[3];
+        const float qlen = sqrtf(((qw * qw + qx * qx) + qy * qy) + qz * qz);
+        qw /= qlen; qx /= qlen; qy /= qlen; qz /= qlen;
+        float *sp = bufs[1] + 3 * (size_t)i;
+        const float sx = msp_expf(sp[0]), sy = msp_expf(sp[1]), sz = msp_expf(sp[2]);
+        for (int k = 0; k < 2; k++) {
+            const size_t child = (size_t)N + 2 * (size_t)ord + k;
+            const float *rs = random_samples + 3 * (size_t)(ord * 2 + k);
+            const float r0 = rs[0] * sx, r1 = rs[1] * sy, r2 = rs[2] * sz;
+            const float v0 = ((1.f - 2.f * (qy * qy + qz * qz)) * r0 + 2.f * (qx * qy - qw * qz) * r1) +
+                             2.f * (qx * qz + qw * qy) * r2;
+            const float v1 = (2.f * (qx * qy + qw * qz) * r0 + (1.f - 2.f * (qx * qx + qz * qz)) * r1) +
+                             2.f * (qy * qz - qw * qx) * r2;
+            const float v2 = (2.f * (qx * qz - qw * qy) * r0 + 2.f * (qy * qz + qw * qx) * r1) +
+                             (1.f - 2.f * (qx * qx + qy * qy)) * r2;
+            float *pm = bufs[0];
+            pm[child * 3] = pm[(size_t)i * 3] + v0;
+            pm[child * 3 + 1] = pm[(size_t)i * 3 + 1] + v1;
+            pm[child * 3 + 2] = pm[(size_t)i * 3 + 2] + v2;
+            for (int j = 0; j < 3; j++) bufs[1][child * 3 + j] = sp[j] - log_size_fac;
+            for (int j = 0; j < 4; j++) bufs[2][child * 4 + j] = q[j];
+            for (int j = 0; j < 3; j++) bufs[3][child * 3 + j] = bufs[3][(size_t)i * 3 + j];
+            for (int j = 0; j < fr_stride; j++)
+                bufs[4][child * fr_stride + j] = bufs[4][(size_t)i * fr_stride + j];
+            bufs[5][child] = bufs[5][i];
+            for (int g = 0; g < 6; g++)
+                for (int j = 0; j < strides[g]; j++) {
+                    exp_avg[g][child * strides[g] + j] = 0.f;
+                    exp_avg_sq[g][child * strides[g] + j] = 0.f;
+                }
+        }
+        for (int j = 0; j < 3; j++) sp[j] -= log_size_fac;
+    }
+    /* duplicates (:3604-3651): at N + 2*nSplits + ord, copied after the split
+     * stage (a parent that also splits is copied with its shrunk scale) */
+    for (int i = 0; i < N; i++) {
+        if (!dup[i]) continue;
+        const size_t dst = (size_t)N + 2 * (size_t)n_split + dup_ord[i];
+        for (int g = 0; g < 6; g++)
+            for (int j = 0; j < strides[g]; j++) {
+                bufs[g][dst * strides[g] + j] = bufs[g][(size_t)i * strides[g] + j];
+                exp_avg[g][dst * strides[g] + j] = 0.f;
+                exp_avg_sq[g][dst * strides[g] + j] = 0.f;
+            }
+    }
+    /* cull classification over the grown population (:3656-3694) */
+    const int n_new = N + 2 * n_split + n_dup;
+    for (int i = 0; i < n_new; i++) {
+        const float op = sigmoidf_ref(bufs[5][i]);
+        int cull = op < cull_alpha_thresh;
+        if (i < N && split[i]) cull = 1;
+        if (check_huge) {
+            const float *s = bufs[1] + 3 * (size_t)i;
+            const float max_s = fmaxf(fmaxf(msp_expf(s[0]), msp_expf(s[1])), msp_expf(s[2]));
+            if (max_s > cull_scale_thresh) cull = 1;
+            if (check_screen && i < N && max_2d_size[i] > cull_screen_size) cull = 1;
+        }
+        keep[i] = !cull;
+    }
+    /* stable compaction of the 18 buffers (:3698-3729) */
+    int n_keep = 0;
+    for (int i = 0; i < n_new; i++) {
+        if (!keep[i]) continue;
+        if (n_keep != i)
+            for (int g = 0; g < 6; g++) {
+                const int S = strides[g];
+                memmove(bufs[g] + (size_t)n_keep * S, bufs[g] + (size_t)i * S, sizeof(float) * S);
+                memmove(exp_avg[g] + (size_t)n_keep * S, exp_avg[g] + (size_t)i * S, sizeof(float) * S);
+                memmove(exp_avg_sq[g] + (size_t)n_keep * S, exp_avg_sq[g] + (size_t)i * S,
+                        sizeof(float) * S);
+            }
+        n_keep++;
+    }
+    if (split_flag_out) memcpy(split_flag_out, split, sizeof(int) * (size_t)N);
+    if (dup_flag_out) memcpy(dup_flag_out, dup, sizeof(int) * (size_t)N);
+    if (keep_flag_out) memcpy(keep_flag_out, keep, sizeof(int) * (size_t)worst);
+    free(split); free(dup); free(keep); free(split_ord); free(dup_ord);
+    return n_keep;
+}
+
+/*
+ * The opacity reset of Model::afterTrain (core/src/model.cpp:280-290):
+ * logits above logit(0.2) are lowered to it, and the opacity moments are
+ * zeroed.
+ */
+void orc_reset_opacity(float *opacities, float *exp_avg5, float *exp_avg_sq5, int n)
+{
+    const float reset_logit = -1.3862943611198906f;
+    for (int i = 0; i < n; i++) {
+        if (opacities[i] > reset_logit) opacities[i] = reset_logit;
+        exp_avg5[i] = 0.f;
+        exp_avg_sq5[i] = 0.f;
+    }
+}

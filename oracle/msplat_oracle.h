@@ -122,6 +122,16 @@ int orc_train_step(const orc_params *P, orc_state *S, float *params[6],
                    float *exp_avg[6], float *exp_avg_sq[6], const float *gt,
                    float *vis_counts, float *xys_grad_norm, float *max_2d_size);
 
+/* Densification, msplat_densify (bindings.h:69-84): see msplat_oracle.c. */
+int orc_densify(int N, int buf_capacity, float grad_thresh, float size_thresh,
+                float screen_thresh, int check_screen, float cull_alpha_thresh,
+                float cull_scale_thresh, float cull_screen_size, int check_huge,
+                const float *xys_grad_norm, const float *vis_counts, const float *max_2d_size,
+                float half_max_dim, float *bufs[6], int fr_stride, float *exp_avg[6],
+                float *exp_avg_sq[6], const float *random_samples, int *split_flag_out,
+                int *dup_flag_out, int *keep_flag_out);
+void orc_reset_opacity(float *opacities, float *exp_avg5, float *exp_avg_sq5, int n);
+
 /* Forward only (msplat_render): fills S->out_img / final_T / final_idx. */
 int orc_render(const orc_params *P, orc_state *S, const float *params[6]);
 

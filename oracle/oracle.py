@@ -57,7 +57,7 @@ def load_ref():
     global _ref
     if _ref is None and os.path.exists(REF_PATH):
         lib = C.CDLL(REF_PATH)
-        for name in ("ref_train_step", "ref_render", "ref_tile_cap"):
+        for name in ("ref_train_step", "ref_render", "ref_tile_cap", "ref_densify"):
             getattr(lib, name).restype = C.c_int
         lib.ref_set_threads.argtypes = [C.c_int]
         _ref = lib
@@ -80,7 +80,7 @@ def load():
         lib.orc_set_threads.argtypes = [C.c_int]
         lib.orc_chunk_k_max.restype = C.c_int32
         lib.orc_chunk_k_max.argtypes = [C.c_int32, C.c_int32]
-        for name in ("orc_train_step", "orc_render"):
+        for name in ("orc_train_step", "orc_render", "orc_densify"):
             getattr(lib, name).restype = C.c_int
         _lib = lib
     return _lib
@@ -193,3 +193,35 @@ def set_threads(n: int) -> None:
 
 def chunk_k_max(n: int, num_tiles: int) -> int:
     return int(load().orc_chunk_k_max(n, num_tiles))
+
+
+def densify(bufs, exp_avg, exp_avg_sq, n: int, xys_grad_norm, vis_counts, max_2d_size,
+            random_samples, half_max_dim: float, grad_thresh: float = 0.0002,
+            size_thresh: float = 0.01, screen_thresh: float = 0.05, check_screen: bool = True,
+            cull_alpha_thresh: float = 0.1, cull_scale_thresh: float = 0.5,
+            cull_screen_size: float = 0.15, check_huge: bool = True, impl: str = "oracle"):
+    """msplat_densify on float32 numpy buffers of >= 3n rows (updated in
+    place, group order means, scales, quats, features_dc, features_rest,
+    opacities).  impl "oracle" runs the C restatement, "reference" the
+    reference's kernels through the shim.  Returns (new_count, split flags,
+    duplicate flags, keep flags)."""
+    cap = min(b.shape[0] for b in bufs)
+    fr_stride = int(np.prod(bufs[4].shape[1:]))
+    split = np.zeros(max(n, 1), np.int32)
+    dup = np.zeros(max(n, 1), np.int32)
+    keep = np.zeros(max(3 * n, 1), np.int32)
+    pb = (_FP * 6)(*[_fp(b) for b in bufs])
+    pm = (_FP * 6)(*[_fp(b) for b in exp_avg])
+    pv = (_FP * 6)(*[_fp(b) for b in exp_avg_sq])
+    lib = load_ref() if impl == "reference" else load()
+    fn = lib.ref_densify if impl == "reference" else lib.orc_densify
+    fn.argtypes = [C.c_int, C.c_int, C.c_float, C.c_float, C.c_float, C.c_int, C.c_float,
+                   C.c_float, C.c_float, C.c_int, _FP, _FP, _FP, C.c_float, _FP * 6, C.c_int,
+                   _FP * 6, _FP * 6, _FP, _IP, _IP, _IP]
+    rc = fn(n, cap, grad_thresh, size_thresh, screen_thresh, int(check_screen),
+            cull_alpha_thresh, cull_scale_thresh, cull_screen_size, int(check_huge),
+            _fp(xys_grad_norm), _fp(vis_counts), _fp(max_2d_size), half_max_dim, pb, fr_stride,
+            pm, pv, _fp(random_samples), _ip(split), _ip(dup), _ip(keep))
+    if rc < 0:
+        raise RuntimeError("densify: 3N exceeds the buffers' capacity")
+    return int(rc), split[:n], dup[:n], keep[:3 * n]

@@ -12,7 +12,8 @@ C++ (each keeps the reference's arithmetic; see DESIGN.md for why):
      nothing, kernel -> nothing) and [[attributes]] are removed;
   2. overloads that differ only in address space (identical bodies) are kept
      once;
-  3. only the kernels msplat_train_step / msplat_render dispatch are kept;
+  3. only the kernels msplat_train_step / msplat_render / msplat_densify
+     dispatch are kept;
   4. each `threadgroup T name[...]` becomes a reference to per-threadgroup
      storage of the shim (filled with 0x7F bytes per threadgroup);
   5. MAX_TILE_ELEMS (the per-tile cap, 2048) becomes overridable; the default
@@ -50,6 +51,10 @@ KERNELS = {
     "ssim_fused_v_fwd_h_bwd_kernel", "ssim_v_bwd_kernel", "rasterize_backward_kernel",
     "compute_chunk_prefix_suffix_kernel", "rasterize_backward_chunked_kernel",
     "project_and_sh_backward_kernel", "fused_adam_kernel", "accumulate_grad_stats_kernel",
+    # msplat_densify
+    "densify_classify_kernel", "block_reduce_kernel", "block_scan_propagate_kernel",
+    "densify_append_split_kernel", "densify_append_dup_kernel", "densify_cull_classify_kernel",
+    "compact_scatter_kernel", "compact_copy_back_kernel",
 }
 BWD_KERNELS = {"rasterize_backward_kernel", "rasterize_backward_chunked_kernel"}
 

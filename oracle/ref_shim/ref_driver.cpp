@@ -12,6 +12,7 @@
 // msl_runtime.hpp and DESIGN.md.
 #include <omp.h>
 
+#include <cmath>
 #include <cstring>
 #include <vector>
 
@@ -322,6 +323,88 @@ int ref_train_step(const orc_params* P, orc_state* S, float* params[6], float* e
     std::memcpy(S->v_scale, g.v_scale.data(), sizeof(float) * 3 * N);
     std::memcpy(S->v_quat, g.v_quat.data(), sizeof(float) * 4 * N);
     return rc;
+}
+
+// msplat_densify (msplat_metal.mm:1337-1592): the nine stages in order,
+// with the scan kernels on 1024-thread threadgroups and the compaction of
+// the 18 buffers through the scratch buffer.  Same arguments as
+// orc_densify; returns the new count, or -1 when 3N exceeds the capacity.
+int ref_densify(int N, int buf_capacity, float grad_thresh, float size_thresh,
+                float screen_thresh, int check_screen, float cull_alpha_thresh,
+                float cull_scale_thresh, float cull_screen_size, int check_huge,
+                const float* xys_grad_norm, const float* vis_counts, const float* max_2d_size,
+                float half_max_dim, float* bufs[6], int fr_stride, float* exp_avg[6],
+                float* exp_avg_sq[6], const float* random_samples, int* split_flag_out,
+                int* dup_flag_out, int* keep_flag_out)
+{
+    const int worst = 3 * N;
+    if (worst > buf_capacity) return -1;
+    const int cap = std::max(buf_capacity, 1);
+    std::vector<int> split_flag(cap), dup_flag(cap), split_prefix(cap), dup_prefix(cap),
+        keep_flag(cap), keep_prefix(cap), block_totals((cap + 1023) / 1024 + 1);
+    std::vector<float> scratch((size_t)cap * std::max(fr_stride, 4));
+    const float log_size_fac = std::log(1.6f);
+    const uint N_u = (uint)N;
+    const uint K = (uint)((N + 1023) / 1024);
+    const int strides[6] = {3, 3, 4, 3, fr_stride, 1};
+    auto scan = [&](uint n, const int* in, int* out) {
+        const uint blocks = (n + 1023) / 1024;
+        dispatch_threadgroups(uint3(blocks, 1, 1), uint3(1024, 1, 1), [&](const ThreadIds& t) {
+            block_reduce_kernel(n, in, block_totals.data(), t.tgid.x, t.tr, t.sgid, t.lane);
+        });
+        dispatch_threadgroups(uint3(blocks, 1, 1), uint3(1024, 1, 1), [&](const ThreadIds& t) {
+            block_scan_propagate_kernel(n, in, out, block_totals.data(), t.tgid.x, t.tr, t.sgid,
+                                        t.lane, 32u);
+        });
+    };
+    dispatch_threads_1d(N_u, [&](uint i) {
+        densify_classify_kernel(N, xys_grad_norm, vis_counts, bufs[1], max_2d_size, half_max_dim,
+                                grad_thresh, size_thresh, screen_thresh, check_screen,
+                                split_flag.data(), dup_flag.data(), i);
+    });
+    (void)K;
+    scan(N_u, split_flag.data(), split_prefix.data());
+    scan(N_u, dup_flag.data(), dup_prefix.data());
+    dispatch_threads_1d(N_u, [&](uint i) {
+        densify_append_split_kernel(N, split_flag.data(), split_prefix.data(), random_samples,
+                                    log_size_fac, bufs[0], bufs[1], bufs[2], bufs[3], bufs[4],
+                                    bufs[5], fr_stride, exp_avg[0], exp_avg[1], exp_avg[2],
+                                    exp_avg[3], exp_avg[4], exp_avg[5], exp_avg_sq[0],
+                                    exp_avg_sq[1], exp_avg_sq[2], exp_avg_sq[3], exp_avg_sq[4],
+                                    exp_avg_sq[5], i);
+    });
+    dispatch_threads_1d(N_u, [&](uint i) {
+        densify_append_dup_kernel(N, dup_flag.data(), dup_prefix.data(), split_prefix.data(),
+                                  bufs[0], bufs[1], bufs[2], bufs[3], bufs[4], bufs[5], fr_stride,
+                                  exp_avg[0], exp_avg[1], exp_avg[2], exp_avg[3], exp_avg[4],
+                                  exp_avg[5], exp_avg_sq[0], exp_avg_sq[1], exp_avg_sq[2],
+                                  exp_avg_sq[3], exp_avg_sq[4], exp_avg_sq[5], i);
+    });
+    const uint wc = (uint)worst;
+    dispatch_threads_1d(wc, [&](uint i) {
+        densify_cull_classify_kernel(N, split_prefix.data(), dup_prefix.data(), split_flag.data(),
+                                     bufs[5], bufs[1], max_2d_size, cull_alpha_thresh,
+                                     cull_scale_thresh, cull_screen_size, check_huge,
+                                     check_screen, keep_flag.data(), i);
+    });
+    scan(wc, keep_flag.data(), keep_prefix.data());
+    for (int b = 0; b < 18; b++) {
+        float* buf = b < 6 ? bufs[b] : b < 12 ? exp_avg[b - 6] : exp_avg_sq[b - 12];
+        const uint stride = (uint)strides[b % 6];
+        const uint total = wc * stride;
+        dispatch_threads_1d(total, [&](uint t) {
+            compact_scatter_kernel(buf, scratch.data(), keep_prefix.data(), keep_flag.data(), wc,
+                                   stride, t);
+        });
+        const uint last = wc ? wc - 1 : 0;
+        dispatch_threads_1d(total, [&](uint t) {
+            compact_copy_back_kernel(scratch.data(), buf, keep_prefix.data(), last, stride, t);
+        });
+    }
+    if (split_flag_out) std::memcpy(split_flag_out, split_flag.data(), sizeof(int) * N);
+    if (dup_flag_out) std::memcpy(dup_flag_out, dup_flag.data(), sizeof(int) * N);
+    if (keep_flag_out) std::memcpy(keep_flag_out, keep_flag.data(), sizeof(int) * worst);
+    return worst ? keep_prefix[worst - 1] : 0;
 }
 
 }  // extern "C"
