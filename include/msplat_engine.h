@@ -290,6 +290,74 @@ int msplat_densify(
  */
 int msplat_reset_opacity(float *opacities, float *exp_avg, float *exp_avg_sq, int n);
 
+/* ---- model files ----------------------------------------------------------
+ * Every array below may be device memory (the engine's buffers; a save first
+ * waits for the engine's queued work, as msplat_gpu_sync does) or host
+ * memory.  `params`, `exp_avg`, `exp_avg_sq`: six pointers in group order
+ * means [N,3], scales [N,3], quats [N,4], features_dc [N,3], features_rest
+ * [N,B,3], opacities [N,1], B = features_rest_bases.  keep_crs/scale/
+ * translation are the model's CRS fields (keepCrs, scale, translation[3]).
+ */
+
+/* Writes a .msplat checkpoint, byte for byte Model::saveCheckpoint
+ * (core/src/model.cpp:361-399): magic 0x4C50534D, version 1, step,
+ * num_active, shDegree, adam_step_count (u32 each), adam_lr[6],
+ * means_lr_init, means_lr_final (f32), then 18 tensors (the six parameter
+ * groups, six exp_avg, six exp_avg_sq), each u32 ndim, i64 shape[ndim],
+ * u64 byte count, raw f32. */
+int msplat_save_checkpoint(const char *path, int step, int num_active, int sh_degree,
+                           int adam_step_count, const float *adam_lr, float means_lr_init,
+                           float means_lr_final, int features_rest_bases,
+                           const float *const *params, const float *const *exp_avg,
+                           const float *const *exp_avg_sq);
+
+/* Reads the scalar state of a checkpoint (model.cpp:401-422) and the SH-rest
+ * basis count B from its features_rest tensor, so the caller can size the
+ * buffers before msplat_load_checkpoint.  NULL outputs are skipped; adam_lr
+ * receives 6 floats.  0 or MSPLAT_ERR_ARG (bad magic or version: the
+ * reference's "Not a valid msplat checkpoint file" / "Unsupported checkpoint
+ * version"). */
+int msplat_read_checkpoint_header(const char *path, int *step, int *num_active, int *sh_degree,
+                                  int *adam_step_count, float *adam_lr, float *means_lr_init,
+                                  float *means_lr_final, int *features_rest_bases);
+
+/* Loads the 18 tensors of a checkpoint (model.cpp:424-435) into arrays with
+ * room for `capacity` rows each (the backing buffers; the reference
+ * allocates 4 * num_active of them, model.cpp:441-470).  Every tensor's
+ * shape is checked.  Returns the checkpoint's step (>= 0) or a negative
+ * code. */
+int msplat_load_checkpoint(const char *path, int capacity, float *const *params,
+                           float *const *exp_avg, float *const *exp_avg_sq);
+
+/* Writes a PLY of n Gaussians, byte for byte saveGaussianPly
+ * (core/src/loaders/save_gaussians.cpp:10-54): header comment
+ * "msplat v<step>", per vertex x y z, zero normals, f_dc_*, f_rest_* in
+ * [3, B] order, opacity, scale_0..2, rot_0..3; with keep_crs the means
+ * become m / scale + translation and the log-scales log(exp(s) / scale). */
+int msplat_save_ply(const char *path, int step, int n, int features_rest_bases,
+                    const float *const *params, int keep_crs, float scale,
+                    const float *translation);
+
+/* Writes a .splat file, byte for byte saveGaussianSplat
+ * (save_gaussians.cpp:56-97): 32-byte records (f32 position, f32 scale,
+ * u8 rgba, u8 quaternion) sorted by size * sigmoid(opacity), largest
+ * first.  params[4] (features_rest) is not read and may be NULL. */
+int msplat_save_splat(const char *path, int n, const float *const *params, int keep_crs,
+                      float scale, const float *translation);
+
+/* The header of loadGaussianPly (save_gaussians.cpp:99-130): vertex count,
+ * step (from a "comment Generated by msplat at iteration <k>" line, else 0)
+ * and B (f_rest properties / 3).  MSPLAT_ERR_ARG for a file that is not a
+ * PLY or has no vertices, as the reference throws. */
+int msplat_read_ply_header(const char *path, int *n, int *step, int *features_rest_bases);
+
+/* loadGaussianPly (save_gaussians.cpp:99-184) into arrays of >= capacity
+ * rows (group order as above; features_rest back to [N, B, 3]); with
+ * keep_crs the inverse CRS transform.  Returns the step or a negative
+ * code. */
+int msplat_load_ply(const char *path, int capacity, float *const *params, int keep_crs,
+                    float scale, const float *translation);
+
 /* ---- introspection (tests and benchmarks) ------------------------------- */
 
 /* Loss of the last step; waits for it when `sync` != 0, else returns the

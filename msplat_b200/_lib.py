@@ -76,6 +76,17 @@ SIGNATURES = {
         C.POINTER(_p), C.POINTER(_p), _p, _p, _p, _p, _p, _p, _p, _p, _p,
     ]),
     "msplat_reset_opacity": (_i, [_p, _p, _p, _i]),
+    "msplat_save_checkpoint": (_i, [
+        C.c_char_p, _i, _i, _i, _i, _fp, _f, _f, _i, C.POINTER(_p), C.POINTER(_p), C.POINTER(_p),
+    ]),
+    "msplat_read_checkpoint_header": (_i, [
+        C.c_char_p, _ip, _ip, _ip, _ip, _fp, _fp, _fp, _ip,
+    ]),
+    "msplat_load_checkpoint": (_i, [C.c_char_p, _i, C.POINTER(_p), C.POINTER(_p), C.POINTER(_p)]),
+    "msplat_save_ply": (_i, [C.c_char_p, _i, _i, _i, C.POINTER(_p), _i, _f, _fp]),
+    "msplat_save_splat": (_i, [C.c_char_p, _i, C.POINTER(_p), _i, _f, _fp]),
+    "msplat_read_ply_header": (_i, [C.c_char_p, _ip, _ip, _ip]),
+    "msplat_load_ply": (_i, [C.c_char_p, _i, C.POINTER(_p), _i, _f, _fp]),
     "msplat_render_noalloc": (_i, [
         _i, _p, _p, _f, _p, _fp, _fp, _f, _f, _f, _f, _u, _u, _ip, _f, _u, _u, _fp,
         _p, _p, _p, _fp, _p, _p,

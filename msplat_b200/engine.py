@@ -83,8 +83,13 @@ class GaussianModel:
         self._stats = [torch.zeros(cap, dtype=torch.float32, device=device) for _ in range(3)]
         self.num_active = n
         self.lr = [float(x) for x in lr]
+        self.means_lr_init, self.means_lr_final = float(LR_INIT[0]), float(MEANS_LR_FINAL)
         self.beta1, self.beta2, self.eps = 0.9, 0.999, 1e-8
         self.step_count = 0
+        # Model::shDegree: the SH degree the features_rest bases were sized for
+        self.sh_degree = int(round(math.sqrt(arrs[4].shape[1] + 1))) - 1
+        # CRS of the input data (Model::keepCrs, scale, translation), used by the exports
+        self.keep_crs, self.crs_scale, self.crs_translation = False, 1.0, (0.0, 0.0, 0.0)
         self._refresh()
 
     def _refresh(self) -> None:
@@ -112,8 +117,9 @@ class GaussianModel:
     def schedule_means_lr(self, step: int, max_steps: int) -> None:
         """Model::schedulersStep (model.cpp:179-182)."""
         t = min(max(f32(step) / f32(max_steps), f32(0.0)), f32(1.0))
-        self.lr[0] = float(f32(math.exp(float(f32(math.log(float(f32(LR_INIT[0])))) * (f32(1.0) - t)
-                                               + f32(math.log(float(f32(MEANS_LR_FINAL)))) * t))))
+        lo, hi = f32(self.means_lr_init), f32(self.means_lr_final)
+        self.lr[0] = float(f32(math.exp(float(f32(math.log(float(lo))) * (f32(1.0) - t)
+                                               + f32(math.log(float(hi))) * t))))
 
     def ensure_capacity(self, needed: int) -> None:
         """Model::ensureCapacity (model.cpp:197-225): grow every backing
@@ -174,6 +180,84 @@ class GaussianModel:
     def reset_stats(self) -> None:
         for st in self._stats:
             st.zero_()
+
+    # ---- model files (msplat_save_checkpoint & co.) ---------------------
+
+    @classmethod
+    def _blank(cls, n: int, rest_bases: int, device: str, capacity: int) -> "GaussianModel":
+        shapes = [(n, 3), (n, 3), (n, 4), (n, 3), (n, rest_bases, 3), (n, 1)]
+        return cls([np.zeros(s, np.float32) for s in shapes], device=device, capacity=capacity)
+
+    def _crs_args(self):
+        return int(self.keep_crs), float(self.crs_scale), _lib.farr(self.crs_translation)
+
+    def save_checkpoint(self, path: str, step: int) -> None:
+        """Model::saveCheckpoint (core/src/model.cpp:361-399)."""
+        _lib.check(_lib.load().msplat_save_checkpoint(
+            str(path).encode(), int(step), self.num_active, self.sh_degree, self.step_count,
+            _lib.farr(self.lr), self.means_lr_init, self.means_lr_final, self.rest_bases,
+            _ptr_array(self.params), _ptr_array(self.exp_avg), _ptr_array(self.exp_avg_sq)),
+            "msplat_save_checkpoint")
+
+    @classmethod
+    def load_checkpoint(cls, path: str, device: str = "cuda"):
+        """Model::loadCheckpoint (model.cpp:401-488): a model with the
+        checkpoint's parameters, Adam moments, step count and learning
+        rates in 4N-capacity buffers.  Returns (model, step)."""
+        lib = _lib.load()
+        step, n, deg, adam_steps, rb = (C.c_int() for _ in range(5))
+        lr = (C.c_float * 6)()
+        lr0, lr1 = C.c_float(), C.c_float()
+        _lib.check(lib.msplat_read_checkpoint_header(
+            str(path).encode(), C.byref(step), C.byref(n), C.byref(deg), C.byref(adam_steps), lr,
+            C.byref(lr0), C.byref(lr1), C.byref(rb)), "msplat_read_checkpoint_header")
+        model = cls._blank(n.value, rb.value, device, capacity=4 * n.value)
+        rc = lib.msplat_load_checkpoint(str(path).encode(), model.capacity, _ptr_array(model._bufs),
+                                        _ptr_array(model._m), _ptr_array(model._v))
+        if rc < 0:
+            _lib.check(rc, "msplat_load_checkpoint")
+        model.lr = [float(x) for x in lr]
+        model.means_lr_init, model.means_lr_final = float(lr0.value), float(lr1.value)
+        model.step_count = adam_steps.value
+        model.sh_degree = deg.value
+        return model, int(rc)
+
+    def save_ply(self, path: str, step: int) -> None:
+        """Model::savePly -> saveGaussianPly (core/src/loaders/save_gaussians.cpp:10-54)."""
+        _lib.check(_lib.load().msplat_save_ply(
+            str(path).encode(), int(step), self.n, self.rest_bases, _ptr_array(self.params),
+            *self._crs_args()), "msplat_save_ply")
+
+    def save_splat(self, path: str) -> None:
+        """Model::saveSplat -> saveGaussianSplat (save_gaussians.cpp:56-97)."""
+        _lib.check(_lib.load().msplat_save_splat(
+            str(path).encode(), self.n, _ptr_array(self.params), *self._crs_args()),
+            "msplat_save_splat")
+
+    def save(self, path: str, step: int) -> None:
+        """Model::save (model.cpp:298-305): .splat by extension, else PLY."""
+        if str(path).endswith(".splat"):
+            self.save_splat(path)
+        else:
+            self.save_ply(path, step)
+
+    @classmethod
+    def load_ply(cls, path: str, device: str = "cuda", keep_crs: bool = False,
+                 crs_scale: float = 1.0, crs_translation=(0.0, 0.0, 0.0)):
+        """Model::loadPly (model.cpp:319-329) -> loadGaussianPly: a model with
+        fresh Adam state.  Returns (model, step)."""
+        lib = _lib.load()
+        n, step, rb = C.c_int(), C.c_int(), C.c_int()
+        _lib.check(lib.msplat_read_ply_header(str(path).encode(), C.byref(n), C.byref(step),
+                                              C.byref(rb)), "msplat_read_ply_header")
+        model = cls._blank(n.value, rb.value, device, capacity=4 * n.value)
+        model.keep_crs, model.crs_scale = bool(keep_crs), float(crs_scale)
+        model.crs_translation = tuple(float(x) for x in crs_translation)
+        rc = lib.msplat_load_ply(str(path).encode(), model.capacity, _ptr_array(model._bufs),
+                                 *model._crs_args())
+        if rc < 0:
+            _lib.check(rc, "msplat_load_ply")
+        return model, int(rc)
 
 
 class Schedule:

@@ -228,5 +228,31 @@ def build(verbose: bool = False) -> str:
     return lib
 
 
+IO_SOURCE = os.path.join(REFERENCE, "core", "src", "loaders", "save_gaussians.cpp")
+
+
+def build_io(verbose: bool = False) -> str:
+    """oracle/_ref/libmsplat_ref_io.so: the reference's save_gaussians.cpp
+    (PLY / .splat writers, PLY reader) compiled as it is, with ref_io.cpp
+    supplying host versions of the three runtime calls it makes."""
+    if not os.path.exists(IO_SOURCE):
+        raise FileNotFoundError(f"reference Gaussian I/O not found at {IO_SOURCE}")
+    os.makedirs(OUT, exist_ok=True)
+    lib = os.path.join(OUT, "libmsplat_ref_io.so")
+    srcs = [os.path.join(HERE, "ref_io.cpp"), IO_SOURCE]
+    if os.path.exists(lib) and all(os.path.getmtime(d) <= os.path.getmtime(lib) for d in srcs):
+        return lib
+    cmd = ["g++", "-std=c++17", "-O2", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-shared",
+           "-Wno-return-type", f"-I{os.path.join(REFERENCE, 'core', 'include')}",
+           f"-I{os.path.join(REFERENCE, 'core', 'metal')}", "-o", lib, *srcs]
+    if verbose:
+        print(" ".join(cmd))
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"reference I/O build failed:\n{r.stderr[-6000:]}")
+    return lib
+
+
 if __name__ == "__main__":
     print(build(verbose="-v" in sys.argv))
+    print(build_io(verbose="-v" in sys.argv))
