@@ -358,6 +358,92 @@ int msplat_read_ply_header(const char *path, int *n, int *step, int *features_re
 int msplat_load_ply(const char *path, int capacity, float *const *params, int keep_crs,
                     float scale, const float *translation);
 
+/* ---- training images on the device ----------------------------------------
+ * The reference prepares ground truth on the host (core/src/loaders/
+ * image_io.cpp, core/src/input_data.cpp:17-75) and uploads it; these run on
+ * the engine's stream over device buffers, float RGB interleaved (H, W, 3).
+ */
+
+/* Bytes (1 = grey, 3 = RGB, 4 = RGBA with alpha ignored) -> floats v / 255,
+ * the conversion of imreadRGB (image_io.cpp:46-51). */
+int msplat_bytes_to_rgb(const unsigned char *src, int width, int height, int channels, float *dst);
+
+/* resizeArea (image_io.cpp:93-139): box-filter downscale, each output the
+ * area-weighted mean of the source pixels it covers.  Bit-identical. */
+int msplat_resize_area(const float *src, int src_w, int src_h, float *dst, int dst_w, int dst_h);
+
+/* The crop rectangle of undistortImage (image_io.cpp:203-270), on the host:
+ * roi = {x, y, width, height} of the inner rectangle of the undistorted
+ * border (the whole image when that rectangle is empty). */
+int msplat_undistort_roi(int w, int h, float fx, float fy, float cx, float cy, float k1, float k2,
+                         float p1, float p2, float k3, int *roi);
+
+/* undistortImage's resampling (image_io.cpp:141-201, 272-300): for each
+ * pixel of the roi, Brown-Conrady distortion of its ray and a bilinear,
+ * edge-clamped sample of `src` (w x h).  dst is roi[2] x roi[3].  The new
+ * intrinsics are fx, fy, cx - roi[0], cy - roi[1]. */
+int msplat_undistort(const float *src, int w, int h, float fx, float fy, float cx, float cy,
+                     float k1, float k2, float p1, float p2, float k3, const int *roi, float *dst);
+
+/* imreadRGB (image_io.cpp:12-56) into device memory: JPEG decoded by
+ * nvJPEG on the GPU, PNG (any bit depth, colour type, interlacing) on the
+ * host; RGBA composited over black.  msplat_image_info reads the size
+ * only.  dst holds capacity_floats floats (>= 3 W H).  Synchronous. */
+int msplat_image_info(const char *path, int *width, int *height);
+int msplat_image_decode(const char *path, float *dst, long long capacity_floats, int *width,
+                        int *height);
+
+/* ---- datasets -------------------------------------------------------------
+ * InputData (core/include/input_data.hpp) with its images resident in HBM.
+ * Not thread-safe; one caller per dataset.
+ */
+typedef struct MsplatDataset MsplatDataset;
+
+typedef struct MsplatCameraInfo {
+    int width, height;
+    float fx, fy, cx, cy;
+    float k1, k2, k3, p1, p2;
+    float cam_to_world[16]; /* row-major, OpenGL axes (y up, z back) */
+} MsplatCameraInfo;
+
+/* inputDataFromX (input_data.cpp:195-217): Nerfstudio (transforms.json),
+ * COLMAP (cameras.bin / sparse/0/cameras.bin; loadColmap,
+ * load_colmap.cpp:121-164) or Polycam (keyframes/corrected_cameras or
+ * cameras.json), then autoScaleAndCenter (input_data.cpp:79-123).  No
+ * images are read.  MSPLAT_ERR_ARG with the reference's message for an
+ * unknown layout, an unsupported COLMAP camera model or a bad file. */
+int msplat_dataset_open(const char *path, const char *colmap_image_path, MsplatDataset **out);
+void msplat_dataset_close(MsplatDataset *ds);
+int msplat_dataset_num_cameras(const MsplatDataset *ds);
+int msplat_dataset_camera(const MsplatDataset *ds, int index, MsplatCameraInfo *out);
+/* Camera::filePath; valid while the dataset is open. */
+const char *msplat_dataset_camera_path(const MsplatDataset *ds, int index);
+/* InputData::points (host memory owned by the dataset); returns the count. */
+long long msplat_dataset_points(const MsplatDataset *ds, const float **xyz,
+                                const unsigned char **rgb);
+/* InputData::scale and translation[3]. */
+int msplat_dataset_transform(const MsplatDataset *ds, float *scale, float *translation);
+/* splitTrainTest (input_data.cpp:148-158): index i is a test camera when
+ * i % test_every == 0.  The index arrays may be NULL (counts only). */
+int msplat_dataset_split(const MsplatDataset *ds, int test_every, int *train_idx, int *n_train,
+                         int *test_idx, int *n_test);
+/* getCameras(validate = true) (input_data.cpp:127-146): the held-out
+ * camera, std::mt19937(42)() % n for "random", else the first path that
+ * contains val_image, else 0. */
+int msplat_dataset_validation_camera(const MsplatDataset *ds, const char *val_image);
+/* Camera::loadImage (input_data.cpp:17-52) for every camera / one camera:
+ * decode, fit intrinsics to the decoded size, downscale by the factor (when
+ * > 1), undistort and crop; the image stays in HBM and the camera's
+ * intrinsics are updated. */
+int msplat_dataset_load_images(MsplatDataset *ds, float downscale_factor);
+int msplat_dataset_load_image(MsplatDataset *ds, int index, float downscale_factor);
+/* Camera::getGPUImage (input_data.cpp:54-75): the resident image, or its
+ * W/k x H/k area-downscaled copy (made on first use, then cached). */
+int msplat_dataset_gt(MsplatDataset *ds, int index, int downscale, const float **dev_rgb,
+                      int *width, int *height);
+/* Device bytes held by the dataset's images. */
+long long msplat_dataset_device_bytes(const MsplatDataset *ds);
+
 /* ---- introspection (tests and benchmarks) ------------------------------- */
 
 /* Loss of the last step; waits for it when `sync` != 0, else returns the

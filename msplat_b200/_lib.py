@@ -18,6 +18,16 @@ _p = C.c_void_p
 _fp = C.POINTER(C.c_float)
 _ip = C.POINTER(C.c_int)
 
+
+class CameraInfo(C.Structure):
+    """MsplatCameraInfo (include/msplat_engine.h)."""
+    _fields_ = [
+        ("width", C.c_int), ("height", C.c_int),
+        ("fx", C.c_float), ("fy", C.c_float), ("cx", C.c_float), ("cy", C.c_float),
+        ("k1", C.c_float), ("k2", C.c_float), ("k3", C.c_float), ("p1", C.c_float),
+        ("p2", C.c_float), ("cam_to_world", C.c_float * 16),
+    ]
+
 # name -> (restype, argtypes); mirrors include/msplat_engine.h
 SIGNATURES = {
     "msplat_last_error": (C.c_char_p, []),
@@ -87,6 +97,25 @@ SIGNATURES = {
     "msplat_save_splat": (_i, [C.c_char_p, _i, C.POINTER(_p), _i, _f, _fp]),
     "msplat_read_ply_header": (_i, [C.c_char_p, _ip, _ip, _ip]),
     "msplat_load_ply": (_i, [C.c_char_p, _i, C.POINTER(_p), _i, _f, _fp]),
+    "msplat_bytes_to_rgb": (_i, [_p, _i, _i, _i, _p]),
+    "msplat_resize_area": (_i, [_p, _i, _i, _p, _i, _i]),
+    "msplat_undistort_roi": (_i, [_i, _i, _f, _f, _f, _f, _f, _f, _f, _f, _f, _ip]),
+    "msplat_undistort": (_i, [_p, _i, _i, _f, _f, _f, _f, _f, _f, _f, _f, _f, _ip, _p]),
+    "msplat_image_info": (_i, [C.c_char_p, _ip, _ip]),
+    "msplat_image_decode": (_i, [C.c_char_p, _p, C.c_longlong, _ip, _ip]),
+    "msplat_dataset_open": (_i, [C.c_char_p, C.c_char_p, C.POINTER(_p)]),
+    "msplat_dataset_close": (None, [_p]),
+    "msplat_dataset_num_cameras": (_i, [_p]),
+    "msplat_dataset_camera": (_i, [_p, _i, C.POINTER(CameraInfo)]),
+    "msplat_dataset_camera_path": (C.c_char_p, [_p, _i]),
+    "msplat_dataset_points": (C.c_longlong, [_p, C.POINTER(_fp), C.POINTER(C.POINTER(C.c_ubyte))]),
+    "msplat_dataset_transform": (_i, [_p, _fp, _fp]),
+    "msplat_dataset_split": (_i, [_p, _i, _ip, _ip, _ip, _ip]),
+    "msplat_dataset_validation_camera": (_i, [_p, C.c_char_p]),
+    "msplat_dataset_load_images": (_i, [_p, _f]),
+    "msplat_dataset_load_image": (_i, [_p, _i, _f]),
+    "msplat_dataset_gt": (_i, [_p, _i, _i, C.POINTER(_p), _ip, _ip]),
+    "msplat_dataset_device_bytes": (C.c_longlong, [_p]),
     "msplat_render_noalloc": (_i, [
         _i, _p, _p, _f, _p, _fp, _fp, _f, _f, _f, _f, _u, _u, _ip, _f, _u, _u, _fp,
         _p, _p, _p, _fp, _p, _p,

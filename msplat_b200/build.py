@@ -78,7 +78,7 @@ def build(verbose: bool = False, force: bool = False) -> str:
     with ThreadPoolExecutor(max_workers=min(8, max(1, len(jobs)))) as ex:
         list(ex.map(run, jobs))
     if force or jobs or _stale(LIB, objs):
-        run([nvcc, *ARCH, "-shared", "-o", LIB, *objs, "-cudart", "static"])
+        run([nvcc, *ARCH, "-shared", "-o", LIB, *objs, "-cudart", "static", "-lz", "-ldl"])
     return LIB
 
 

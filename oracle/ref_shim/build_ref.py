@@ -253,6 +253,81 @@ def build_io(verbose: bool = False) -> str:
     return lib
 
 
+DATA_SOURCES = [os.path.join(REFERENCE, "core", "src", *p) for p in (
+    ("input_data.cpp",), ("loaders", "load_colmap.cpp"), ("loaders", "load_ply.cpp"),
+    ("loaders", "load_nerfstudio.cpp"), ("loaders", "load_polycam.cpp"))]
+IMAGE_IO = os.path.join(REFERENCE, "core", "src", "loaders", "image_io.cpp")
+
+
+def nlohmann_include() -> str:
+    """A directory holding nlohmann/json.hpp (the reference fetches it at
+    configure time; an unmodified copy ships inside cudnn_frontend)."""
+    import glob
+    import site
+    roots = site.getsitepackages() + [sys.prefix]
+    for root in roots:
+        for hit in glob.glob(os.path.join(root, "**", "nlohmann", "json.hpp"), recursive=True):
+            return os.path.dirname(os.path.dirname(hit))
+    raise FileNotFoundError("nlohmann/json.hpp not found")
+
+
+def strip_function(src: str, signature: str) -> str:
+    """Remove the definition that starts with `signature` (brace matched)."""
+    i = src.find(signature)
+    if i < 0:
+        raise ValueError(f"{signature!r} not found")
+    j = src.index("{", i)
+    depth = 0
+    for k in range(j, len(src)):
+        depth += {"{": 1, "}": -1}.get(src[k], 0)
+        if depth == 0:
+            return src[:i] + src[k + 1:]
+    raise ValueError("unbalanced braces")
+
+
+def image_io_transform(src: str) -> str:
+    """image_io.cpp without its CoreGraphics half: the two platform includes
+    and the CoreGraphics decoder / encoder (imreadRGB, imwriteRGB) are
+    dropped; resizeArea and undistortImage are kept as written."""
+    src = "\n".join(line for line in src.split("\n")
+                     if not re.match(r"\s*#include <(CoreGraphics|ImageIO)/", line))
+    src = strip_function(src, "Image imreadRGB(const std::string &path)")
+    return strip_function(src, "void imwriteRGB(const std::string &path, const Image &img)")
+
+
+def build_data(verbose: bool = False) -> str:
+    """oracle/_ref/libmsplat_ref_data.so: the reference's dataset loaders,
+    pose normalisation, splits, Camera image pipeline and the resize /
+    undistort code of image_io.cpp; ref_data.cpp stands in for the
+    CoreGraphics decoder and the Metal runtime calls."""
+    for src in DATA_SOURCES + [IMAGE_IO]:
+        if not os.path.exists(src):
+            raise FileNotFoundError(f"reference source not found: {src}")
+    os.makedirs(OUT, exist_ok=True)
+    gen = os.path.join(OUT, "image_io_ref.cpp")
+    code = image_io_transform(open(IMAGE_IO).read())
+    if not os.path.exists(gen) or open(gen).read() != code:
+        with open(gen, "w") as f:
+            f.write(code)
+    lib = os.path.join(OUT, "libmsplat_ref_data.so")
+    srcs = [os.path.join(HERE, "ref_data.cpp"), gen] + DATA_SOURCES
+    if os.path.exists(lib) and all(os.path.getmtime(d) <= os.path.getmtime(lib) for d in srcs):
+        return lib
+    cmd = ["g++", "-std=c++17", "-O2", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-shared",
+           "-Wno-return-type", f"-I{os.path.join(REFERENCE, 'core', 'include')}",
+           # headers the sources reach transitively through libc++ on macOS
+           "-include", "cmath", "-include", "stdexcept", "-include", "unordered_map",
+           f"-I{os.path.join(REFERENCE, 'core', 'metal')}", f"-I{nlohmann_include()}", "-o", lib,
+           *srcs]
+    if verbose:
+        print(" ".join(cmd))
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"reference data build failed:\n{r.stderr[-6000:]}")
+    return lib
+
+
 if __name__ == "__main__":
     print(build(verbose="-v" in sys.argv))
     print(build_io(verbose="-v" in sys.argv))
+    print(build_data(verbose="-v" in sys.argv))
