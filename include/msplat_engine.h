@@ -444,6 +444,16 @@ int msplat_dataset_gt(MsplatDataset *ds, int index, int downscale, const float *
 /* Device bytes held by the dataset's images. */
 long long msplat_dataset_device_bytes(const MsplatDataset *ds);
 
+/* ---- evaluation ------------------------------------------------------------
+ * The held-out metrics of evaluate() (python/bindings.cpp:186-216) on the
+ * device: ssim_eval (core/src/ssim.cpp:61-123; Gaussian window of
+ * window_size <= 11 taps and sigma, separable, edge-clamped), psnr and
+ * l1_loss (core/src/model.cpp:24-40) of two (H, W, 3) float images in
+ * device memory.  Synchronous; NULL outputs are skipped.
+ */
+int msplat_eval_metrics(const float *rendered, const float *gt, int height, int width,
+                        int window_size, float sigma, float *psnr, float *ssim, float *l1);
+
 /* ---- introspection (tests and benchmarks) ------------------------------- */
 
 /* Loss of the last step; waits for it when `sync` != 0, else returns the

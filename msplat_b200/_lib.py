@@ -116,6 +116,7 @@ SIGNATURES = {
     "msplat_dataset_load_image": (_i, [_p, _i, _f]),
     "msplat_dataset_gt": (_i, [_p, _i, _i, C.POINTER(_p), _ip, _ip]),
     "msplat_dataset_device_bytes": (C.c_longlong, [_p]),
+    "msplat_eval_metrics": (_i, [_p, _p, _i, _i, _i, _f, _fp, _fp, _fp]),
     "msplat_render_noalloc": (_i, [
         _i, _p, _p, _f, _p, _fp, _fp, _f, _f, _f, _f, _u, _u, _ip, _f, _u, _u, _fp,
         _p, _p, _p, _fp, _p, _p,

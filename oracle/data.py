@@ -1,8 +1,8 @@
 """The reference's data front end, compiled from its sources into
 oracle/_ref/libmsplat_ref_data.so (oracle/ref_shim/build_ref.py build_data):
 dataset loaders (COLMAP, Nerfstudio, Polycam), autoScaleAndCenter, the
-train/test splits, Camera::loadImage / getGPUImage, resizeArea and
-undistortImage.
+train/test splits, Camera::loadImage / getGPUImage, resizeArea,
+undistortImage and the evaluation metrics (ssim_eval, psnr, l1_loss).
 
 TEST INFRASTRUCTURE ONLY (tests/ use it as the checker for
 msplat_b200/csrc/dataset.cu and kernels_image.cu).  Images reach the
@@ -62,6 +62,7 @@ class RefDataset:
             lib.ref_camera_gt.argtypes = [C.c_void_p, C.c_int, C.c_int, _FP, C.c_longlong, _IP, _IP]
             lib.ref_resize_area.argtypes = [_FP, C.c_int, C.c_int, _FP, C.c_int, C.c_int]
             lib.ref_undistort.argtypes = [_FP, C.c_int, C.c_int] + [C.c_float] * 9 + [_FP, _FP, _IP]
+            lib.ref_eval.argtypes = [_FP, _FP, C.c_int, C.c_int, C.c_int, C.c_float, _FP]
             cls._lib = lib
         return cls._lib
 
@@ -152,3 +153,13 @@ def undistort(src: np.ndarray, fx, fy, cx, cy, k1, k2, p1, p2, k3):
                                    size.ctypes.data_as(_IP))
     rw, rh = int(size[0]), int(size[1])
     return out[:rw * rh * 3].reshape(rh, rw, 3), tuple(intr)
+
+
+def eval_metrics(rendered: np.ndarray, gt: np.ndarray, window: int = 11, sigma: float = 1.5):
+    """(psnr, ssim, l1) as the reference's evaluate() computes them."""
+    r = np.ascontiguousarray(rendered, np.float32)
+    g = np.ascontiguousarray(gt, np.float32)
+    out = np.zeros(3, np.float32)
+    RefDataset.lib().ref_eval(r.ctypes.data_as(_FP), g.ctypes.data_as(_FP), r.shape[0], r.shape[1],
+                              window, sigma, out.ctypes.data_as(_FP))
+    return out[0], out[1], out[2]

@@ -257,6 +257,7 @@ DATA_SOURCES = [os.path.join(REFERENCE, "core", "src", *p) for p in (
     ("input_data.cpp",), ("loaders", "load_colmap.cpp"), ("loaders", "load_ply.cpp"),
     ("loaders", "load_nerfstudio.cpp"), ("loaders", "load_polycam.cpp"))]
 IMAGE_IO = os.path.join(REFERENCE, "core", "src", "loaders", "image_io.cpp")
+SSIM_CPP = os.path.join(REFERENCE, "core", "src", "ssim.cpp")
 
 
 def nlohmann_include() -> str:
@@ -285,6 +286,32 @@ def strip_function(src: str, signature: str) -> str:
     raise ValueError("unbalanced braces")
 
 
+def extract_function(src: str, signature: str) -> str:
+    """The definition that starts with `signature` (brace matched)."""
+    i = src.find(signature)
+    if i < 0:
+        raise ValueError(f"{signature!r} not found")
+    j = src.index("{", i)
+    depth = 0
+    for k in range(j, len(src)):
+        depth += {"{": 1, "}": -1}.get(src[k], 0)
+        if depth == 0:
+            return src[i:k + 1]
+    raise ValueError("unbalanced braces")
+
+
+MODEL_CPP = os.path.join(REFERENCE, "core", "src", "model.cpp")
+
+
+def model_metrics_source() -> str:
+    """psnr and l1_loss of model.cpp (the rest of that file needs the Metal
+    runtime and nanoflann), taken verbatim."""
+    src = open(MODEL_CPP).read()
+    funcs = [extract_function(src, "float psnr(const MTensor& rendered, const MTensor& gt)"),
+             extract_function(src, "float l1_loss(const MTensor& rendered, const MTensor& gt)")]
+    return "#include <cmath>\n#include \"model.hpp\"\n\n" + "\n\n".join(funcs) + "\n"
+
+
 def image_io_transform(src: str) -> str:
     """image_io.cpp without its CoreGraphics half: the two platform includes
     and the CoreGraphics decoder / encoder (imreadRGB, imwriteRGB) are
@@ -297,20 +324,24 @@ def image_io_transform(src: str) -> str:
 
 def build_data(verbose: bool = False) -> str:
     """oracle/_ref/libmsplat_ref_data.so: the reference's dataset loaders,
-    pose normalisation, splits, Camera image pipeline and the resize /
-    undistort code of image_io.cpp; ref_data.cpp stands in for the
+    pose normalisation, splits, Camera image pipeline, the resize /
+    undistort code of image_io.cpp and the evaluation metrics (ssim.cpp,
+    psnr / l1_loss of model.cpp); ref_data.cpp stands in for the
     CoreGraphics decoder and the Metal runtime calls."""
-    for src in DATA_SOURCES + [IMAGE_IO]:
+    for src in DATA_SOURCES + [IMAGE_IO, SSIM_CPP, MODEL_CPP]:
         if not os.path.exists(src):
             raise FileNotFoundError(f"reference source not found: {src}")
     os.makedirs(OUT, exist_ok=True)
-    gen = os.path.join(OUT, "image_io_ref.cpp")
-    code = image_io_transform(open(IMAGE_IO).read())
-    if not os.path.exists(gen) or open(gen).read() != code:
-        with open(gen, "w") as f:
-            f.write(code)
+    gens = []
+    for name, code in (("image_io_ref.cpp", image_io_transform(open(IMAGE_IO).read())),
+                       ("model_metrics_ref.cpp", model_metrics_source())):
+        gen = os.path.join(OUT, name)
+        if not os.path.exists(gen) or open(gen).read() != code:
+            with open(gen, "w") as f:
+                f.write(code)
+        gens.append(gen)
     lib = os.path.join(OUT, "libmsplat_ref_data.so")
-    srcs = [os.path.join(HERE, "ref_data.cpp"), gen] + DATA_SOURCES
+    srcs = [os.path.join(HERE, "ref_data.cpp")] + gens + DATA_SOURCES + [SSIM_CPP]
     if os.path.exists(lib) and all(os.path.getmtime(d) <= os.path.getmtime(lib) for d in srcs):
         return lib
     cmd = ["g++", "-std=c++17", "-O2", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-shared",

@@ -1,12 +1,13 @@
 // ref_data.cpp -- C entry points over the reference's own data front end
 // (msplat core/src/input_data.cpp, core/src/loaders/load_colmap.cpp,
-// load_ply.cpp, load_nerfstudio.cpp, load_polycam.cpp and the resize /
-// undistort half of image_io.cpp), compiled from the reference's sources
-// into oracle/_ref/libmsplat_ref_data.so by build_ref.py build_data.
+// load_ply.cpp, load_nerfstudio.cpp, load_polycam.cpp, the resize /
+// undistort half of image_io.cpp, ssim.cpp and psnr / l1_loss of
+// model.cpp), compiled from the reference's sources into
+// oracle/_ref/libmsplat_ref_data.so by build_ref.py build_data.
 //
-// TEST INFRASTRUCTURE ONLY: the checker for the engine's dataset loaders
-// and device image preparation (msplat_b200/csrc/dataset.cu,
-// kernels_image.cu).
+// TEST INFRASTRUCTURE ONLY: the checker for the engine's dataset loaders,
+// device image preparation and evaluation metrics
+// (msplat_b200/csrc/dataset.cu, kernels_image.cu, kernels_eval.cu).
 //
 // The reference decodes images with CoreGraphics (macOS only).  Here
 // imreadRGB reads "<image path>.rgb8" instead -- a raw file the tests write
@@ -23,7 +24,9 @@
 
 #include "input_data.hpp"
 #include "loaders.hpp"
+#include "model.hpp"
 #include "msplat.hpp"
+#include "ssim.hpp"
 
 MTensor gpu_empty(std::vector<int64_t> shape, DType dtype) { return MTensor(std::move(shape), dtype); }
 
@@ -182,6 +185,19 @@ void ref_undistort(const float* src, int w, int h, float fx, float fy, float cx,
     intr_out[3] = r.cy;
     size_out[0] = r.width;
     size_out[1] = r.height;
+}
+
+// ssim_eval, psnr and l1_loss of the evaluation (bindings.cpp:199-201) on
+// host copies of two (H, W, 3) images: out = {psnr, ssim, l1}
+void ref_eval(const float* rendered, const float* gt, int H, int W, int window, float sigma,
+              float* out)
+{
+    MTensor r({H, W, 3}, DType::Float32), g({H, W, 3}, DType::Float32);
+    std::memcpy(r.data_ptr(), rendered, r.nbytes());
+    std::memcpy(g.data_ptr(), gt, g.nbytes());
+    out[0] = psnr(r, g);
+    out[1] = ssim_eval(r, g, window, sigma);
+    out[2] = l1_loss(r, g);
 }
 
 }  // extern "C"

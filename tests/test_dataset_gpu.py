@@ -84,26 +84,41 @@ def test_png_matches_pil_and_errors(tmp_path):
                                    100, None, None) < 0           # too small a buffer
 
 
-# nvJPEG and libjpeg (PIL) use different IDCT and chroma-upsampling
-# arithmetic; the decoded bytes may differ by a few levels at edges.
+# nvJPEG and libjpeg (PIL) use different IDCT arithmetic, and for 4:2:0
+# chroma libjpeg interpolates ("fancy" triangular upsampling) where nvJPEG
+# replicates; the decoded bytes differ by a few levels, and by more in the
+# chroma of subsampled images with per-pixel colour noise.  So: every
+# channel on a 4:4:4 or grey file and on a smooth 4:2:0 file, and luma only
+# on a noisy 4:2:0 file.
 JPEG_MAX_LEVELS = 12
 JPEG_MEAN_LEVELS = 0.75
 
 
-@pytest.mark.parametrize("mode,subsampling", [("RGB", 0), ("RGB", 2), ("L", 0)])
-def test_jpeg_decode_against_pil(tmp_path, mode, subsampling):
+def _smooth_pixels(w, h):
+    y, x = np.mgrid[0:h, 0:w].astype(np.float32)
+    rgb = np.stack([x / (w - 1), y / (h - 1), 0.5 + 0.4 * np.sin(x * 0.05 + y * 0.03)], -1)
+    return np.clip(rgb * 255.0 + 0.5, 0, 255).astype(np.uint8)
+
+
+@pytest.mark.parametrize("mode,subsampling,noisy", [("RGB", 0, True), ("RGB", 2, False),
+                                                    ("RGB", 2, True), ("L", 0, True)])
+def test_jpeg_decode_against_pil(tmp_path, mode, subsampling, noisy):
     from PIL import Image
-    px = dataset_case.image_pixels(203, 131, 11)
+    px = dataset_case.image_pixels(203, 131, 11) if noisy else _smooth_pixels(203, 131)
     im = Image.fromarray(px).convert(mode)
     kw = {"subsampling": subsampling} if mode == "RGB" else {}
     im.save(tmp_path / "a.jpg", quality=92, **kw)
-    ref = np.array(Image.open(tmp_path / "a.jpg").convert("RGB")).astype(np.int64)
+    ref = np.array(Image.open(tmp_path / "a.jpg").convert("RGB")).astype(np.float64)
     got = _decode(tmp_path / "a.jpg")
-    levels = np.abs(np.rint(got * 255.0).astype(np.int64) - ref)
+    # every value is a byte / 255
+    got8 = np.rint(got * 255.0)
+    assert got.tobytes() == _as_float(got8.astype(np.uint8)).tobytes()
+    if mode == "RGB" and subsampling == 2 and noisy:
+        luma = np.array([0.299, 0.587, 0.114])
+        got8, ref = got8 @ luma, ref @ luma
+    levels = np.abs(got8 - ref)
     assert levels.max() <= JPEG_MAX_LEVELS and levels.mean() <= JPEG_MEAN_LEVELS, (
         levels.max(), levels.mean())
-    # every value is a byte / 255
-    assert got.tobytes() == _as_float(np.rint(got * 255.0).astype(np.uint8)).tobytes()
 
 
 def _dev(a):
