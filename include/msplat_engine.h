@@ -397,7 +397,7 @@ int msplat_image_decode(const char *path, float *dst, long long capacity_floats,
  * InputData (core/include/input_data.hpp) with its images resident in HBM.
  * Not thread-safe; one caller per dataset.
  */
-typedef struct MsplatDataset MsplatDataset;
+typedef struct MsplatData MsplatData;
 
 typedef struct MsplatCameraInfo {
     int width, height;
@@ -412,37 +412,67 @@ typedef struct MsplatCameraInfo {
  * cameras.json), then autoScaleAndCenter (input_data.cpp:79-123).  No
  * images are read.  MSPLAT_ERR_ARG with the reference's message for an
  * unknown layout, an unsupported COLMAP camera model or a bad file. */
-int msplat_dataset_open(const char *path, const char *colmap_image_path, MsplatDataset **out);
-void msplat_dataset_close(MsplatDataset *ds);
-int msplat_dataset_num_cameras(const MsplatDataset *ds);
-int msplat_dataset_camera(const MsplatDataset *ds, int index, MsplatCameraInfo *out);
+int msplat_dataset_open(const char *path, const char *colmap_image_path, MsplatData **out);
+void msplat_dataset_close(MsplatData *ds);
+int msplat_dataset_num_cameras(const MsplatData *ds);
+int msplat_dataset_camera(const MsplatData *ds, int index, MsplatCameraInfo *out);
 /* Camera::filePath; valid while the dataset is open. */
-const char *msplat_dataset_camera_path(const MsplatDataset *ds, int index);
+const char *msplat_dataset_camera_path(const MsplatData *ds, int index);
 /* InputData::points (host memory owned by the dataset); returns the count. */
-long long msplat_dataset_points(const MsplatDataset *ds, const float **xyz,
+long long msplat_dataset_points(const MsplatData *ds, const float **xyz,
                                 const unsigned char **rgb);
 /* InputData::scale and translation[3]. */
-int msplat_dataset_transform(const MsplatDataset *ds, float *scale, float *translation);
+int msplat_dataset_transform(const MsplatData *ds, float *scale, float *translation);
 /* splitTrainTest (input_data.cpp:148-158): index i is a test camera when
  * i % test_every == 0.  The index arrays may be NULL (counts only). */
-int msplat_dataset_split(const MsplatDataset *ds, int test_every, int *train_idx, int *n_train,
+int msplat_dataset_split(const MsplatData *ds, int test_every, int *train_idx, int *n_train,
                          int *test_idx, int *n_test);
 /* getCameras(validate = true) (input_data.cpp:127-146): the held-out
  * camera, std::mt19937(42)() % n for "random", else the first path that
  * contains val_image, else 0. */
-int msplat_dataset_validation_camera(const MsplatDataset *ds, const char *val_image);
+int msplat_dataset_validation_camera(const MsplatData *ds, const char *val_image);
 /* Camera::loadImage (input_data.cpp:17-52) for every camera / one camera:
  * decode, fit intrinsics to the decoded size, downscale by the factor (when
  * > 1), undistort and crop; the image stays in HBM and the camera's
  * intrinsics are updated. */
-int msplat_dataset_load_images(MsplatDataset *ds, float downscale_factor);
-int msplat_dataset_load_image(MsplatDataset *ds, int index, float downscale_factor);
+int msplat_dataset_load_images(MsplatData *ds, float downscale_factor);
+int msplat_dataset_load_image(MsplatData *ds, int index, float downscale_factor);
 /* Camera::getGPUImage (input_data.cpp:54-75): the resident image, or its
  * W/k x H/k area-downscaled copy (made on first use, then cached). */
-int msplat_dataset_gt(MsplatDataset *ds, int index, int downscale, const float **dev_rgb,
+int msplat_dataset_gt(MsplatData *ds, int index, int downscale, const float **dev_rgb,
                       int *width, int *height);
 /* Device bytes held by the dataset's images. */
-long long msplat_dataset_device_bytes(const MsplatDataset *ds);
+long long msplat_dataset_device_bytes(const MsplatData *ds);
+
+/* Bridges from the trainer-level C API (include/msplat_c_api.h), no
+ * counterpart in the reference: the engine dataset behind an MsplatDataset
+ * handle (owned by it), and the dataset indices of its training (test = 0)
+ * or held-out (test = 1) cameras (up to max_out; returns the count). */
+MsplatData *msplat_dataset_data(void *c_api_dataset);
+/* msplat_trainer_load_checkpoint with the camera re-shuffle optional: the
+ * C++ Trainer re-shuffles on resume (msplat_api.mm:250-255), the Python
+ * binding's load_checkpoint (python/bindings.cpp:273-275) does not. */
+int msplat_trainer_load_checkpoint_ex(void *trainer, const char *path, int reshuffle);
+int msplat_dataset_indices(void *c_api_dataset, int test, int *out, int max_out);
+
+/* ---- initialisation from a point cloud ------------------------------------- */
+
+/* PointsTensor::scales (core/include/kdtree_tensor.hpp:27-41, a nanoflann
+ * k-d tree on the host) on the GPU: out[i] = mean of the square roots of
+ * the k-1 smallest squared distances from point i to the others (the k
+ * nearest include the point itself), by an exact grid search.  xyz (n,3)
+ * and out (n) are host arrays; 2 <= k <= 8.  Synchronous. */
+int msplat_knn_mean_distance(const float *xyz, long long n, int k, float *out);
+
+/* The initial Gaussians of Model::Model (core/src/model.cpp:42-118) from a
+ * point cloud (host xyz (n,3), 8-bit rgb (n,3)) into device arrays of >= n
+ * rows: means = xyz; scales = log(mean distance to the 3 nearest
+ * neighbours), repeated; random unit quaternions from std::mt19937(42);
+ * features_dc from the colours; features_rest zero ((n, (sh_degree+1)^2-1,
+ * 3)); opacities logit(0.1).  Synchronous. */
+int msplat_init_gaussians(const float *xyz, const unsigned char *rgb, long long n, int sh_degree,
+                          float *means, float *scales, float *quats, float *features_dc,
+                          float *features_rest, float *opacities);
 
 /* ---- evaluation ------------------------------------------------------------
  * The held-out metrics of evaluate() (python/bindings.cpp:186-216) on the

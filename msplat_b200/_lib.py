@@ -28,7 +28,32 @@ class CameraInfo(C.Structure):
         ("p2", C.c_float), ("cam_to_world", C.c_float * 16),
     ]
 
-# name -> (restype, argtypes); mirrors include/msplat_engine.h
+class MsplatConfig(C.Structure):
+    """MsplatConfig (include/msplat_c_api.h)."""
+    _fields_ = [
+        ("iterations", C.c_int), ("shDegree", C.c_int), ("shDegreeInterval", C.c_int),
+        ("ssimWeight", C.c_float), ("numDownscales", C.c_int), ("resolutionSchedule", C.c_int),
+        ("refineEvery", C.c_int), ("warmupLength", C.c_int), ("resetAlphaEvery", C.c_int),
+        ("densifyGradThresh", C.c_float), ("densifySizeThresh", C.c_float),
+        ("stopScreenSizeAt", C.c_int), ("splitScreenSize", C.c_float), ("keepCrs", C.c_bool),
+        ("downscaleFactor", C.c_float), ("bgColor", C.c_float * 3),
+    ]
+
+
+class MsplatStats(C.Structure):
+    _fields_ = [("iteration", C.c_int), ("splatCount", C.c_int), ("msPerStep", C.c_float)]
+
+
+class MsplatEvalMetrics(C.Structure):
+    _fields_ = [("psnr", C.c_float), ("ssim", C.c_float), ("l1", C.c_float),
+                ("numTest", C.c_int), ("numGaussians", C.c_int)]
+
+
+class MsplatPixelBuffer(C.Structure):
+    _fields_ = [("data", C.POINTER(C.c_float)), ("width", C.c_int), ("height", C.c_int)]
+
+
+# name -> (restype, argtypes); mirrors include/msplat_engine.h and msplat_c_api.h
 SIGNATURES = {
     "msplat_last_error": (C.c_char_p, []),
     "msplat_set_stream": (_i, [_p]),
@@ -117,6 +142,32 @@ SIGNATURES = {
     "msplat_dataset_gt": (_i, [_p, _i, _i, C.POINTER(_p), _ip, _ip]),
     "msplat_dataset_device_bytes": (C.c_longlong, [_p]),
     "msplat_eval_metrics": (_i, [_p, _p, _i, _i, _i, _f, _fp, _fp, _fp]),
+    "msplat_knn_mean_distance": (_i, [_p, C.c_longlong, _i, _p]),
+    "msplat_dataset_data": (_p, [_p]),
+    "msplat_dataset_indices": (_i, [_p, _i, _ip, _i]),
+    "msplat_dataset_create": (_p, [C.c_char_p, _f, C.c_bool, _i]),
+    "msplat_dataset_destroy": (None, [_p]),
+    "msplat_dataset_num_train": (_i, [_p]),
+    "msplat_dataset_num_test": (_i, [_p]),
+    "msplat_dataset_camera_pose": (None, [_p, _i, _fp]),
+    "msplat_trainer_create": (_p, [_p, MsplatConfig]),
+    "msplat_trainer_destroy": (None, [_p]),
+    "msplat_trainer_step": (MsplatStats, [_p]),
+    "msplat_trainer_train": (None, [_p]),
+    "msplat_trainer_evaluate": (MsplatEvalMetrics, [_p]),
+    "msplat_trainer_render": (MsplatPixelBuffer, [_p, _i, C.c_bool]),
+    "msplat_trainer_render_pose": (MsplatPixelBuffer, [_p, _fp, _i]),
+    "msplat_trainer_render_pose_to_buffer": (None, [_p, _fp, _i, C.POINTER(C.c_ubyte), _ip, _ip]),
+    "msplat_trainer_export_ply": (None, [_p, C.c_char_p]),
+    "msplat_trainer_export_splat": (None, [_p, C.c_char_p]),
+    "msplat_trainer_save_checkpoint": (None, [_p, C.c_char_p]),
+    "msplat_trainer_load_checkpoint": (_i, [_p, C.c_char_p]),
+    "msplat_trainer_load_checkpoint_ex": (_i, [_p, C.c_char_p, _i]),
+    "msplat_trainer_splat_count": (_i, [_p]),
+    "msplat_trainer_iteration": (_i, [_p]),
+    "msplat_sync": (None, []),
+    "msplat_cleanup": (None, []),
+    "msplat_init_gaussians": (_i, [_p, _p, C.c_longlong, _i, _p, _p, _p, _p, _p, _p]),
     "msplat_render_noalloc": (_i, [
         _i, _p, _p, _f, _p, _fp, _fp, _f, _f, _f, _f, _u, _u, _ip, _f, _u, _u, _fp,
         _p, _p, _p, _fp, _p, _p,

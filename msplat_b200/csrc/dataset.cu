@@ -303,12 +303,12 @@ struct Points {
 }  // namespace
 }  // namespace msp
 
-struct MsplatDataset {
+struct MsplatData {
     std::vector<msp::Cam> cams;
     float scale = 1.0f;
     float translation[3] = {0, 0, 0};
     msp::Points points;
-    ~MsplatDataset()
+    ~MsplatData()
     {
         for (auto& c : cams) {
             if (c.image.ptr) cudaFree(c.image.ptr);
@@ -615,9 +615,9 @@ void colmap_pose(const double q[4], const double t[3], float out[16])
     out[15] = 1;
 }
 
-void auto_scale_and_center(MsplatDataset& d);
+void auto_scale_and_center(MsplatData& d);
 
-void load_colmap(MsplatDataset& d, const std::string& root_s, const std::string& image_src)
+void load_colmap(MsplatData& d, const std::string& root_s, const std::string& image_src)
 {
     const fs::path root(root_s);
     const std::string sparse = fs::exists(root / "cameras.bin") ? root_s : (root / "sparse" / "0").string();
@@ -675,7 +675,7 @@ void read_matrix(const Json& tm, float out[16])
     }
 }
 
-void load_nerfstudio(MsplatDataset& d, const std::string& root_s)
+void load_nerfstudio(MsplatData& d, const std::string& root_s)
 {
     const fs::path root(root_s);
     const Json j = read_json((root / "transforms.json").string());
@@ -736,7 +736,7 @@ std::string polycam_image(const fs::path& dir, const std::string& stem)
     return (dir / (stem + ".png")).string();
 }
 
-void load_polycam(MsplatDataset& d, const std::string& root_s)
+void load_polycam(MsplatData& d, const std::string& root_s)
 {
     const fs::path root(root_s);
     const fs::path kf = root / "keyframes" / "corrected_cameras";
@@ -812,7 +812,7 @@ void load_polycam(MsplatDataset& d, const std::string& root_s)
 
 // Centre the camera positions on their mean and scale them into [-1, 1]
 // (by the largest absolute coordinate); the point cloud follows.
-void auto_scale_and_center(MsplatDataset& d)
+void auto_scale_and_center(MsplatData& d)
 {
     if (d.cams.empty()) return;
     float mean[3] = {0, 0, 0};
@@ -958,7 +958,7 @@ using namespace msp;
 
 extern "C" {
 
-int msplat_dataset_open(const char* path, const char* colmap_image_path, MsplatDataset** out)
+int msplat_dataset_open(const char* path, const char* colmap_image_path, MsplatData** out)
 {
     if (!path || !out) {
         set_error("msplat_dataset_open: invalid arguments");
@@ -966,7 +966,7 @@ int msplat_dataset_open(const char* path, const char* colmap_image_path, MsplatD
     }
     *out = nullptr;
     try {
-        auto d = std::make_unique<MsplatDataset>();
+        auto d = std::make_unique<MsplatData>();
         const fs::path root(path);
         if (fs::exists(root / "transforms.json"))
             load_nerfstudio(*d, path);
@@ -985,11 +985,11 @@ int msplat_dataset_open(const char* path, const char* colmap_image_path, MsplatD
     }
 }
 
-void msplat_dataset_close(MsplatDataset* d) { delete d; }
+void msplat_dataset_close(MsplatData* d) { delete d; }
 
-int msplat_dataset_num_cameras(const MsplatDataset* d) { return d ? (int)d->cams.size() : MSPLAT_ERR_ARG; }
+int msplat_dataset_num_cameras(const MsplatData* d) { return d ? (int)d->cams.size() : MSPLAT_ERR_ARG; }
 
-int msplat_dataset_camera(const MsplatDataset* d, int i, MsplatCameraInfo* out)
+int msplat_dataset_camera(const MsplatData* d, int i, MsplatCameraInfo* out)
 {
     if (!d || !out || i < 0 || i >= (int)d->cams.size()) {
         set_error("msplat_dataset_camera: index %d out of range", i);
@@ -1011,13 +1011,13 @@ int msplat_dataset_camera(const MsplatDataset* d, int i, MsplatCameraInfo* out)
     return MSPLAT_OK;
 }
 
-const char* msplat_dataset_camera_path(const MsplatDataset* d, int i)
+const char* msplat_dataset_camera_path(const MsplatData* d, int i)
 {
     if (!d || i < 0 || i >= (int)d->cams.size()) return nullptr;
     return d->cams[i].path.c_str();
 }
 
-long long msplat_dataset_points(const MsplatDataset* d, const float** xyz, const unsigned char** rgb)
+long long msplat_dataset_points(const MsplatData* d, const float** xyz, const unsigned char** rgb)
 {
     if (!d) return MSPLAT_ERR_ARG;
     if (xyz) *xyz = d->points.xyz.data();
@@ -1025,7 +1025,7 @@ long long msplat_dataset_points(const MsplatDataset* d, const float** xyz, const
     return d->points.count;
 }
 
-int msplat_dataset_transform(const MsplatDataset* d, float* scale, float* translation)
+int msplat_dataset_transform(const MsplatData* d, float* scale, float* translation)
 {
     if (!d) return MSPLAT_ERR_ARG;
     if (scale) *scale = d->scale;
@@ -1033,7 +1033,7 @@ int msplat_dataset_transform(const MsplatDataset* d, float* scale, float* transl
     return MSPLAT_OK;
 }
 
-int msplat_dataset_split(const MsplatDataset* d, int test_every, int* train_idx, int* n_train,
+int msplat_dataset_split(const MsplatData* d, int test_every, int* train_idx, int* n_train,
                          int* test_idx, int* n_test)
 {
     if (!d || test_every <= 0) {
@@ -1055,7 +1055,7 @@ int msplat_dataset_split(const MsplatDataset* d, int test_every, int* train_idx,
     return MSPLAT_OK;
 }
 
-int msplat_dataset_validation_camera(const MsplatDataset* d, const char* val_image)
+int msplat_dataset_validation_camera(const MsplatData* d, const char* val_image)
 {
     if (!d || d->cams.empty()) {
         set_error("msplat_dataset_validation_camera: no cameras");
@@ -1076,7 +1076,7 @@ int msplat_dataset_validation_camera(const MsplatDataset* d, const char* val_ima
     return idx < 0 ? 0 : idx;
 }
 
-int msplat_dataset_load_images(MsplatDataset* d, float downscale_factor)
+int msplat_dataset_load_images(MsplatData* d, float downscale_factor)
 {
     if (!d) return MSPLAT_ERR_ARG;
     for (auto& c : d->cams) {
@@ -1086,7 +1086,7 @@ int msplat_dataset_load_images(MsplatDataset* d, float downscale_factor)
     return MSPLAT_OK;
 }
 
-int msplat_dataset_load_image(MsplatDataset* d, int i, float downscale_factor)
+int msplat_dataset_load_image(MsplatData* d, int i, float downscale_factor)
 {
     if (!d || i < 0 || i >= (int)d->cams.size()) {
         set_error("msplat_dataset_load_image: index %d out of range", i);
@@ -1095,7 +1095,7 @@ int msplat_dataset_load_image(MsplatDataset* d, int i, float downscale_factor)
     return load_image(d->cams[i], downscale_factor);
 }
 
-int msplat_dataset_gt(MsplatDataset* d, int i, int downscale, const float** dev_rgb, int* width,
+int msplat_dataset_gt(MsplatData* d, int i, int downscale, const float** dev_rgb, int* width,
                       int* height)
 {
     if (!d || i < 0 || i >= (int)d->cams.size()) {
@@ -1129,7 +1129,7 @@ int msplat_dataset_gt(MsplatDataset* d, int i, int downscale, const float** dev_
     return MSPLAT_OK;
 }
 
-long long msplat_dataset_device_bytes(const MsplatDataset* d)
+long long msplat_dataset_device_bytes(const MsplatData* d)
 {
     if (!d) return 0;
     long long b = 0;

@@ -62,31 +62,49 @@ class Dataset:
     def __init__(self, path: str, downscale_factor: float = 1.0, eval_mode: bool = False,
                  test_every: int = 8, load_images: bool = True, colmap_image_path: str = ""):
         lib = _lib.load()
-        h = C.c_void_p()
-        _lib.check(lib.msplat_dataset_open(str(path).encode(), colmap_image_path.encode(),
-                                           C.byref(h)), "msplat_dataset_open")
-        self._h = h.value
         self.downscale_factor = float(downscale_factor)
-        if load_images:
-            _lib.check(lib.msplat_dataset_load_images(self._h, self.downscale_factor),
-                       "msplat_dataset_load_images")
-        n = lib.msplat_dataset_num_cameras(self._h)
-        self.cameras = [Camera(self, i) for i in range(n)]
-        if eval_mode:
-            tr = (C.c_int * max(n, 1))()
-            te = (C.c_int * max(n, 1))()
-            a, b = C.c_int(), C.c_int()
-            _lib.check(lib.msplat_dataset_split(self._h, int(test_every), tr, C.byref(a), te,
-                                                C.byref(b)), "msplat_dataset_split")
-            self.train_cams = [self.cameras[i] for i in tr[:a.value]]
-            self.test_cams = [self.cameras[i] for i in te[:b.value]]
+        self._c = None
+        if load_images and not colmap_image_path:
+            # the trainer-level dataset (msplat_dataset_create): images loaded, split made
+            self._c = lib.msplat_dataset_create(str(path).encode(), self.downscale_factor,
+                                                bool(eval_mode), int(test_every))
+            if not self._c:
+                raise _lib.EngineError("Dataset: " + lib.msplat_last_error().decode())
+            self._h = lib.msplat_dataset_data(self._c)
+            n = lib.msplat_dataset_num_cameras(self._h)
+            self.cameras = [Camera(self, i) for i in range(n)]
+            idx = (C.c_int * max(n, 1))()
+            tr = [idx[i] for i in range(lib.msplat_dataset_indices(self._c, 0, idx, n))]
+            te = [idx[i] for i in range(lib.msplat_dataset_indices(self._c, 1, idx, n))]
         else:
-            self.train_cams = list(self.cameras)
-            self.test_cams = []
+            h = C.c_void_p()
+            _lib.check(lib.msplat_dataset_open(str(path).encode(), colmap_image_path.encode(),
+                                               C.byref(h)), "msplat_dataset_open")
+            self._h = h.value
+            if load_images:
+                _lib.check(lib.msplat_dataset_load_images(self._h, self.downscale_factor),
+                           "msplat_dataset_load_images")
+            n = lib.msplat_dataset_num_cameras(self._h)
+            self.cameras = [Camera(self, i) for i in range(n)]
+            tr, te = list(range(n)), []
+            if eval_mode:
+                a_ = (C.c_int * max(n, 1))()
+                b_ = (C.c_int * max(n, 1))()
+                a, b = C.c_int(), C.c_int()
+                _lib.check(lib.msplat_dataset_split(self._h, int(test_every), a_, C.byref(a), b_,
+                                                    C.byref(b)), "msplat_dataset_split")
+                tr, te = list(a_[:a.value]), list(b_[:b.value])
+        self.train_cams = [self.cameras[i] for i in tr]
+        self.test_cams = [self.cameras[i] for i in te]
 
     def close(self) -> None:
-        if getattr(self, "_h", None):
-            _lib.load().msplat_dataset_close(self._h)
+        lib = _lib.load()
+        if getattr(self, "_c", None):
+            lib.msplat_dataset_destroy(self._c)   # owns the engine dataset
+            self._c = None
+            self._h = None
+        elif getattr(self, "_h", None):
+            lib.msplat_dataset_close(self._h)
             self._h = None
 
     def __del__(self):

@@ -358,7 +358,49 @@ def build_data(verbose: bool = False) -> str:
     return lib
 
 
+TRAINER_SOURCES = [os.path.join(REFERENCE, "core", "src", *p) for p in (
+    ("model.cpp",), ("ssim.cpp",), ("loaders", "save_gaussians.cpp"))] + DATA_SOURCES
+API_SOURCE = os.path.join(REFERENCE, "core", "src", "msplat_api.mm")
+
+
+def build_trainer(verbose: bool = False) -> str:
+    """oracle/_ref/libmsplat_ref_trainer.so: the reference's Model
+    (model.cpp), Trainer and C API (msplat_api.mm -- plain C++ despite its
+    extension) and data front end, over ref_backend.cpp, which implements
+    the backend seam (bindings.h) with the reference's kernels built through
+    the MSL shim (libmsplat_ref.so, linked).  nanoflann is absent; the
+    stand-in kdtree_tensor.hpp in stub_include/ searches exhaustively."""
+    ref_lib = build(verbose)
+    build_data(verbose)   # writes the generated image_io_ref.cpp
+    for src in TRAINER_SOURCES + [API_SOURCE]:
+        if not os.path.exists(src):
+            raise FileNotFoundError(f"reference source not found: {src}")
+    lib = os.path.join(OUT, "libmsplat_ref_trainer.so")
+    gen = os.path.join(OUT, "image_io_ref.cpp")
+    srcs = [os.path.join(HERE, "ref_backend.cpp"), gen] + TRAINER_SOURCES
+    deps = srcs + [API_SOURCE, ref_lib, os.path.join(HERE, "stub_include", "kdtree_tensor.hpp")]
+    if os.path.exists(lib) and all(os.path.getmtime(d) <= os.path.getmtime(lib) for d in deps):
+        return lib
+    cmd = ["g++", "-std=c++17", "-O2", "-ffp-contract=off", "-fno-fast-math", "-fopenmp", "-fPIC",
+           "-shared", "-Wno-return-type", "-Wno-unused-result",
+           f"-I{os.path.join(HERE, 'stub_include')}",
+           f"-I{os.path.join(REFERENCE, 'core', 'include')}",
+           "-include", "cmath", "-include", "stdexcept", "-include", "unordered_map",
+           "-include", "cstring", "-include", "algorithm",
+           f"-I{os.path.join(REFERENCE, 'core', 'metal')}",
+           f"-I{nlohmann_include()}", f"-I{ORACLE}", "-o", lib, *srcs,
+           "-x", "c++", API_SOURCE, "-x", "none",
+           f"-L{OUT}", "-lmsplat_ref", "-Wl,-rpath,$ORIGIN"]
+    if verbose:
+        print(" ".join(cmd))
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"reference trainer build failed:\n{r.stderr[-6000:]}")
+    return lib
+
+
 if __name__ == "__main__":
     print(build(verbose="-v" in sys.argv))
     print(build_io(verbose="-v" in sys.argv))
     print(build_data(verbose="-v" in sys.argv))
+    print(build_trainer(verbose="-v" in sys.argv))
