@@ -22,7 +22,7 @@ class _DeviceArray:
 
     def __init__(self, ptr: int, h: int, w: int):
         self.__cuda_array_interface__ = {
-            "shape": (h, w, 3), "typestr": "<f4", "data": (int(ptr), True), "version": 3,
+            "shape": (h, w, 3), "typestr": "<f4", "data": (int(ptr), False), "version": 3,
             "strides": None,
         }
 
