@@ -281,12 +281,18 @@ def run_ours(args, rank: int, world: int):
     # --- end to end through the public API with host buffers ----------------
     h, w = setups[0].height, setups[0].width
     host_gts = [t.cpu().pin_memory() for t in gts[:4]]
-    dev_gt = torch.empty_like(gts[0])
+    gt_bytes = host_gts[0].numel() * 4
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     losses = []
+    staged = C_void_p()
     for s in range(args.steps):
-        dev_gt.copy_(host_gts[s % len(host_gts)], non_blocking=True)
+        # msplat_stage_input: the upload of this step's target overlaps the
+        # previous step's kernels (copy stream, two staging buffers)
+        hg = host_gts[s % len(host_gts)]
+        _lib.check(lib.msplat_stage_input(C_void_p(hg.data_ptr()), gt_bytes, C_byref(staged)),
+                   "msplat_stage_input")
+        dev_gt = engine.DevicePtr(staged.value)
         if dist is None:
             engine.train_step(model, setups[view_of(s)], dev_gt)
         else:
@@ -440,6 +446,7 @@ def main():
 
 
 from ctypes import byref as C_byref, c_char_p as C_char_p, c_double as C_double, c_int as C_int  # noqa: E402
+from ctypes import c_void_p as C_void_p  # noqa: E402
 
 if __name__ == "__main__":
     main()

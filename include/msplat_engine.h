@@ -290,6 +290,18 @@ int msplat_densify(
  */
 int msplat_reset_opacity(float *opacities, float *exp_avg, float *exp_avg_sq, int n);
 
+/* ---- per-step host inputs ---------------------------------------------------
+ * msplat_stage_input: copy `bytes` of host memory (pinned, for the copy to
+ * overlap compute) into one of two engine-owned device buffers on a
+ * separate copy stream, and return that buffer to pass as this step's
+ * input (e.g. msplat_train_step's gt).  The copy waits only for the step
+ * that read the same buffer two stagings ago, and the kernels queued next
+ * on the engine stream wait for the copy, so with one staging per step the
+ * upload of step s runs under the kernels of step s-1.  The buffer is valid
+ * until the next-but-one staging.  No counterpart in the reference (its
+ * images are host-visible to the GPU). */
+int msplat_stage_input(const void *host, size_t bytes, const void **dev_out);
+
 /* ---- model files ----------------------------------------------------------
  * Every array below may be device memory (the engine's buffers; a save first
  * waits for the engine's queued work, as msplat_gpu_sync does) or host

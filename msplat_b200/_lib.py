@@ -111,6 +111,7 @@ SIGNATURES = {
         C.POINTER(_p), C.POINTER(_p), _p, _p, _p, _p, _p, _p, _p, _p, _p,
     ]),
     "msplat_reset_opacity": (_i, [_p, _p, _p, _i]),
+    "msplat_stage_input": (_i, [_p, C.c_size_t, C.POINTER(_p)]),
     "msplat_save_checkpoint": (_i, [
         C.c_char_p, _i, _i, _i, _i, _fp, _f, _f, _i, C.POINTER(_p), C.POINTER(_p), C.POINTER(_p),
     ]),

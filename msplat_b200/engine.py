@@ -301,6 +301,17 @@ class Schedule:
         return done
 
 
+class DevicePtr:
+    """A raw device address where the step functions expect a tensor (they
+    only read its data_ptr()), e.g. a buffer from msplat_stage_input."""
+
+    def __init__(self, address: int):
+        self.address = int(address)
+
+    def data_ptr(self) -> int:
+        return self.address
+
+
 def _ptr(t) -> C.c_void_p:
     return C.c_void_p(t.data_ptr())
 
