@@ -1,6 +1,7 @@
 """Benchmark of the training step (BASELINE.json metric) on synthetic C1.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  python bench.py --config C3 [--iterations 7000]     (training-run report)
 
 Workload (N=1): BASELINE.json config 1 -- 1,000,000 seeded synthetic
 Gaussians rendered at 1297x840 from 16 cameras on a radius-4 sphere, the
@@ -55,6 +56,11 @@ def parse():
                     help="N > 1: optimiser over NVLink peer memory, or NCCL all-reduce")
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the timed CPU oracle sample (profiling runs)")
+    ap.add_argument("--config", choices=("C1", "C3"), default="C1",
+                    help="C1 (default): the headline step benchmark; C3: BASELINE.json config 3, "
+                         "a 7000-iteration training run with densification, reporting steps/s "
+                         "and held-out PSNR/SSIM (one GPU)")
+    ap.add_argument("--iterations", type=int, default=7000, help="C3: training iterations")
     return ap.parse_args()
 
 
@@ -433,10 +439,105 @@ def run_reference(args, rank: int, world: int):
                     "d2h_bytes_per_step": 0}}
 
 
+def run_c3(args) -> dict:
+    """a full synthetic training run at 1024x768.
+    Ground truth: a seed-7 scene of 500,000 Gaussians drawn as in config 1,
+    rendered to 72 cameras on the radius-4 sphere (every 9th held out: 64
+    train, 8 test).  Student: 100,000 Gaussians, means U[-2,2]^3, the rest
+    as in config 0.  The reference's schedule (Model::afterTrain defaults):
+    densification every 100 steps from 500 until half the run, gradient
+    threshold 2e-4, opacity reset every 3000 steps, SH degree +1 every 1000
+    steps, means learning rate decayed over the run; one view per step in a
+    reshuffled order.  Timed on the device (CUDA events around the whole
+    run, densification included); held-out PSNR / SSIM by
+    msplat_eval_metrics on the 8 test views."""
+    import math as _m
+
+    import torch
+    from msplat_b200 import _lib, camera, engine, synthetic
+    lib = _lib.load()
+    engine.bind_stream()
+    w, h, iters = 1024, 768, args.iterations
+    cams = synthetic.fibonacci_cameras(72, 4.0, w, h)
+    test_idx = list(range(0, 72, 9))
+    train_idx = [i for i in range(72) if i not in test_idx]
+    final = [camera.prepare_camera(c, step=10**9, sh_degree=3, sh_degree_interval=1000,
+                                   rest_bases=15) for c in cams]
+    truth = synthetic.gaussians(500_000, 7, mean_range=2.0, log_scale_mu=_m.log(0.01),
+                                log_scale_sigma=0.4)
+    tmodel = engine.GaussianModel(truth.groups())
+    gts = []
+    for cs in final:
+        ptr = engine.render(tmodel, cs)
+        buf = torch.empty((h, w, 3), dtype=torch.float32, device="cuda")
+        _lib.check(lib.msplat_copy(buf.data_ptr(), ptr, buf.numel() * 4, 2, 0), "copy")
+        gts.append(buf)
+    torch.cuda.synchronize()
+    del tmodel
+    student = synthetic.gaussians(100_000, 8, mean_range=2.0, log_scale_mu=_m.log(0.02),
+                                  log_scale_sigma=0.3)
+    model = engine.GaussianModel(student.groups())
+    sched = engine.Schedule(max_steps=iters, num_cameras=len(train_idx))
+    rng = np.random.default_rng(42)
+    order = []
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    lib.msplat_kernel_launches(1)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e0.record(stream)
+    for step in range(1, iters + 1):
+        if not order:
+            order = list(rng.permutation(train_idx))
+        ci = int(order.pop())
+        cs = camera.prepare_camera(cams[ci], step=step, sh_degree=3, sh_degree_interval=1000,
+                                   rest_bases=15)
+        engine.train_step(model, cs, gts[ci])
+        model.schedule_means_lr(step, iters)
+        sched.after_train(model, step, w, h)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    clk = clocks.stop()
+    launches = int(lib.msplat_kernel_launches(1))
+    ms = e0.elapsed_time(e1)
+    psnr, ssim, l1 = [], [], []
+    for ci in test_idx:
+        cs = camera.prepare_camera(cams[ci], step=iters, sh_degree=3, sh_degree_interval=1000,
+                                   rest_bases=15)
+        ptr = engine.render(model, cs)
+        out = [C_float() for _ in range(3)]
+        _lib.check(lib.msplat_eval_metrics(C_void_p(ptr), C_void_p(gts[ci].data_ptr()), h, w, 11,
+                                           1.5, *[C_byref(o) for o in out]), "eval")
+        psnr.append(out[0].value)
+        ssim.append(out[1].value)
+        l1.append(out[2].value)
+    steps_per_s = iters / (ms / 1000.0)
+    return {
+        "metric": "C3 training run: steps/s + held-out PSNR/SSIM", "value": round(steps_per_s, 2),
+        "unit": "steps/s", "n_gpus": 1, "steps": iters, "warmup": 0,
+        "ms_per_step": round(ms / iters, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seed-7 ground-truth scene rendered to 72 cameras; seed-8 student)",
+        "config": {"workload": "C3: 100,000 -> densified Gaussians, 7000 iterations at 1024x768, "
+                               "64 train / 8 held-out cameras",
+                   "iterations": iters, "width": w, "height": h},
+        "heldout_psnr": round(float(np.mean(psnr)), 3), "heldout_ssim": round(float(np.mean(ssim)), 4),
+        "heldout_l1": round(float(np.mean(l1)), 5), "final_gaussians": model.n,
+        "wall_s": round(wall, 2), "gpu_launches": launches, "clocks": clk,
+    }
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    if args.config == "C3":
+        if rank == 0:
+            print(json.dumps(run_c3(args)), flush=True)
+        return
     if args.impl == "reference":
         res = run_reference(args, rank, world)
     else:
@@ -446,7 +547,7 @@ def main():
 
 
 from ctypes import byref as C_byref, c_char_p as C_char_p, c_double as C_double, c_int as C_int  # noqa: E402
-from ctypes import c_void_p as C_void_p  # noqa: E402
+from ctypes import c_float as C_float, c_void_p as C_void_p  # noqa: E402
 
 if __name__ == "__main__":
     main()
