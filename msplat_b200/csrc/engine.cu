@@ -136,7 +136,7 @@ static void free_buffers()
 {
     Buffers& B = g.B;
     void* ptrs[] = {B.proj.xy, B.proj.depth, B.proj.radii, B.proj.conic_op, B.proj.rgb, B.proj.rect,
-                    B.tile_count, B.tile_offset, B.keys, B.keys_alt, B.sorted_ids, B.out_img,
+                    B.tile_count, B.tile_offset, B.tile_order, B.keys, B.keys_alt, B.sorted_ids, B.out_img,
                     B.final_T, B.final_idx, B.v_rendered, B.grad_acc,
                     B.chunk_T, B.chunk_C, B.chunk_idx, B.prefix_T, B.after_C};
     for (void* p : ptrs)
@@ -187,6 +187,7 @@ static int ensure(long long N, long long W, long long H, long long T, int K, boo
     if (T > g.cap_T) {
         if ((rc = realloc_dev(B.tile_count, T * kCountPitch))) return rc;
         if ((rc = realloc_dev(B.tile_offset, T + 1))) return rc;
+        if ((rc = realloc_dev(B.tile_order, T))) return rc;
         MSP_CUDA(cudaMemsetAsync(B.tile_count, 0, sizeof(int) * T * kCountPitch, g.stream()));
         g.cap_T = T;
     }

@@ -60,6 +60,7 @@ struct Buffers {
     ProjOut proj;
     int* tile_count;       // [T * kCountPitch] zero between steps
     int* tile_offset;      // [T+1] exclusive scan
+    int* tile_order;       // [T] tiles by intersection count, largest first (CTA order)
     unsigned long long* keys;      // [capacity]
     unsigned long long* keys_alt;  // [capacity] merge scratch for tiles longer than one register-sorted run
     int* sorted_ids;       // [capacity]

@@ -94,7 +94,8 @@ __device__ __forceinline__ bool backprop(PixelBwd& s, float fpx, float fpy, cons
 template <bool CHUNKED, int PPT>
 __global__ void __launch_bounds__(256 / PPT, kBwdMinBlocks)
 raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
-                       const int* __restrict__ ids, const float2* __restrict__ g_xy,
+                       const int* __restrict__ order, const int* __restrict__ ids,
+                       const float2* __restrict__ g_xy,
                        const float4* __restrict__ g_co, const float4* __restrict__ g_rgb,
                        const float* __restrict__ final_T, const int* __restrict__ final_idx,
                        const float* __restrict__ v_rendered, const int* __restrict__ chunk_idx,
@@ -110,7 +111,7 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
     __shared__ int s_order[kRastBatch];
     __shared__ unsigned char s_band[kRastBatch];
     __shared__ int s_wcnt[kRastBatch / 32];
-    const int tile = blockIdx.x;
+    const int tile = order[blockIdx.x];
     const int tx_n = P->tiles_x;
     const int W = P->img_w, H = P->img_h;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -338,7 +339,7 @@ void launch_raster_backward(const StepParams* P, int num_tiles, int k_max, int W
     if (num_tiles <= 0) return;
     if (k_max <= 1) {
         raster_backward_kernel<false, kBwdPPT><<<num_tiles, 256 / kBwdPPT, 0, s>>>(
-            P, B.tile_offset, B.sorted_ids, B.proj.xy, B.proj.conic_op, B.proj.rgb, B.final_T,
+            P, B.tile_offset, B.tile_order, B.sorted_ids, B.proj.xy, B.proj.conic_op, B.proj.rgb, B.final_T,
             B.final_idx, B.v_rendered, nullptr, nullptr, nullptr, nullptr, B.grad_acc);
     } else {
         dim3 pgrid((W + 15) / 16, (H + 15) / 16);
@@ -346,7 +347,7 @@ void launch_raster_backward(const StepParams* P, int num_tiles, int k_max, int W
                                                          B.prefix_T, B.after_C);
         dim3 grid(num_tiles, k_max);
         raster_backward_kernel<true, kBwdPPT><<<grid, 256 / kBwdPPT, 0, s>>>(
-            P, B.tile_offset, B.sorted_ids, B.proj.xy, B.proj.conic_op, B.proj.rgb, B.final_T,
+            P, B.tile_offset, B.tile_order, B.sorted_ids, B.proj.xy, B.proj.conic_op, B.proj.rgb, B.final_T,
             nullptr, B.v_rendered, B.chunk_idx, B.prefix_T, B.chunk_T, B.after_C, B.grad_acc);
     }
 }
@@ -442,6 +443,76 @@ __device__ __forceinline__ void adam_slab(float* __restrict__ P, float* __restri
     }
 }
 
+// Per-Gaussian gradient slots in shared memory (phase 1 -> phase 2).
+constexpr int kGradSlots = 12;  // v_mean[3], v_scale[3], v_quat[4], v_opacity, pad
+constexpr int kBasisSlots = 19; // 15 SH-rest basis values + v_rgb[3] (odd stride: no bank conflicts)
+
+// Adam for one warp's 32 Gaussians over the small groups -- means, scales,
+// quats and opacity for every Gaussian, features_dc for the visible ones --
+// with every parameter, first- and second-moment load of all five groups
+// issued before the first update: 14 coalesced rounds of 32 elements, so a
+// warp waits for memory once instead of once per group.  Same element
+// updates as adam_slab group by group.
+constexpr int kSmallRounds = 14;
+// round -> group (means 3 rounds, scales 3, quats 4, opacity 1, dc 3), the
+// round's 32-element step within its group, and the group's floats per
+// Gaussian
+__host__ __device__ constexpr int round_group(int r)
+{
+    return r < 3 ? 0 : r < 6 ? 1 : r < 10 ? 2 : r < 11 ? 5 : 3;
+}
+__host__ __device__ constexpr int round_u(int r)
+{
+    return r < 3 ? r : r < 6 ? r - 3 : r < 10 ? r - 6 : r < 11 ? 0 : r - 11;
+}
+__host__ __device__ constexpr int group_stride(int grp) { return grp == 2 ? 4 : grp == 5 ? 1 : 3; }
+
+__device__ __forceinline__ void adam_small_groups(const AdamPtrs& A, const StepParams* __restrict__ P,
+                                                  int g0, int cnt, int lane,
+                                                  const float (*sg)[kGradSlots],
+                                                  const float (*sb)[kBasisSlots],
+                                                  const int* sv)
+{
+    float p[kSmallRounds], m[kSmallRounds], v[kSmallRounds], g[kSmallRounds];
+    unsigned on = 0;
+#pragma unroll
+    for (int r = 0; r < kSmallRounds; r++) {
+        const int grp = round_group(r), stride = group_stride(grp);
+        const int e = lane + 32 * round_u(r);
+        const int gl = e / stride, k = e - gl * stride;
+        bool active = A.numel[grp] > 0 && e < cnt * stride;
+        g[r] = 0.f;
+        if (active) {
+            if (grp == 0) g[r] = sg[gl][k];
+            else if (grp == 1) g[r] = sg[gl][3 + k];
+            else if (grp == 2) g[r] = sg[gl][6 + k];
+            else if (grp == 5) g[r] = sg[gl][10];
+            else {  // features_dc: visible Gaussians only
+                active = sv[gl] != 0;
+                g[r] = MSP_SH_C0 * sb[gl][15 + k];
+            }
+        }
+        if (active) {
+            const size_t idx = (size_t)g0 * stride + e;
+            p[r] = A.param[grp][idx];
+            m[r] = A.exp_avg[grp][idx];
+            v[r] = A.exp_avg_sq[grp][idx];
+            on |= 1u << r;
+        }
+    }
+    const float b1 = P->beta1, b2 = P->beta2, eps = P->eps;
+#pragma unroll
+    for (int r = 0; r < kSmallRounds; r++) {
+        if (!((on >> r) & 1u)) continue;
+        const int grp = round_group(r), stride = group_stride(grp);
+        adam_math(p[r], m[r], v[r], g[r], P->adam_step[grp], b1, b2, 1.0f / P->adam_bc2[grp], eps);
+        const size_t idx = (size_t)g0 * stride + lane + 32 * round_u(r);
+        A.param[grp][idx] = p[r];
+        A.exp_avg[grp][idx] = m[r];
+        A.exp_avg_sq[grp][idx] = v[r];
+    }
+}
+
 // Writes one warp's contiguous slab of a gradient group (same walk as
 // adam_slab); elements that grad_of declines are written as 0.
 template <int STRIDE, class G>
@@ -455,9 +526,6 @@ __device__ __forceinline__ void grad_slab(float* __restrict__ out, size_t e0, in
     }
 }
 
-// Per-Gaussian gradient slots in shared memory (phase 1 -> phase 2).
-constexpr int kGradSlots = 12;  // v_mean[3], v_scale[3], v_quat[4], v_opacity, pad
-constexpr int kBasisSlots = 19; // 15 SH-rest basis values + v_rgb[3] (odd stride: no bank conflicts)
 
 
 // Geometry and colour VJP of one visible Gaussian (project_and_sh_backward_kernel,
@@ -611,16 +679,18 @@ project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
                         ls2 = scales[3 * (size_t)i + 2];
             const float q0 = quats[4 * (size_t)i], q1 = quats[4 * (size_t)i + 1],
                         q2 = quats[4 * (size_t)i + 2], q3 = quats[4 * (size_t)i + 3];
+            // densification statistics (accumulate_grad_stats_kernel), read
+            // before the VJP so their loads overlap it
+            const float st_vis = St.vis_counts[i], st_norm = St.grad_norm[i], st_max = St.max_2d[i];
             // the SH-rest basis only when this kernel forms the rest gradient
             const bool with_basis =
                 GRAD_OUT ? !G.compact : (A.numel[4] > 0 && nb_rest > 0);
             gaussian_vjp(P, ga, g_co[i], p, ls0, ls1, ls2, q0, q1, q2, q3, gr, s_basis[tid],
                          with_basis);
             const float vx = ga[6], vy = ga[7];
-            // densification statistics (accumulate_grad_stats_kernel)
-            St.vis_counts[i] += 1.0f;
-            St.grad_norm[i] += sqrtf(vx * vx + vy * vy);
-            St.max_2d[i] = fmaxf(St.max_2d[i], (float)rad * P->inv_max_dim);
+            St.vis_counts[i] = st_vis + 1.0f;
+            St.grad_norm[i] = st_norm + sqrtf(vx * vx + vy * vy);
+            St.max_2d[i] = fmaxf(st_max, (float)rad * P->inv_max_dim);
         }
     }
 #pragma unroll
@@ -674,29 +744,9 @@ project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
         if (lane < cnt) G.vis[g0 + lane] = sv[lane] ? 1.f : 0.f;
         return;
     }
-    if (A.numel[0] > 0)  // means, every Gaussian (zero gradient when culled)
-        adam_slab<3>(A.param[0], A.exp_avg[0], A.exp_avg_sq[0], (size_t)g0 * 3, cnt * 3, lane,
-                     P->adam_step[0], b1, b2, 1.0f / P->adam_bc2[0], eps,
-                     [&](int gl, int k, float& g) { g = sg[gl][k]; return true; });
-    if (A.numel[1] > 0)  // scales (log)
-        adam_slab<3>(A.param[1], A.exp_avg[1], A.exp_avg_sq[1], (size_t)g0 * 3, cnt * 3, lane,
-                     P->adam_step[1], b1, b2, 1.0f / P->adam_bc2[1], eps,
-                     [&](int gl, int k, float& g) { g = sg[gl][3 + k]; return true; });
-    if (A.numel[2] > 0)  // quats
-        adam_slab<4>(A.param[2], A.exp_avg[2], A.exp_avg_sq[2], (size_t)g0 * 4, cnt * 4, lane,
-                     P->adam_step[2], b1, b2, 1.0f / P->adam_bc2[2], eps,
-                     [&](int gl, int k, float& g) { g = sg[gl][6 + k]; return true; });
-    if (A.numel[5] > 0)  // opacity logits
-        adam_slab<1>(A.param[5], A.exp_avg[5], A.exp_avg_sq[5], (size_t)g0, cnt, lane,
-                     P->adam_step[5], b1, b2, 1.0f / P->adam_bc2[5], eps,
-                     [&](int gl, int, float& g) { g = sg[gl][10]; return true; });
-    if (A.numel[3] > 0)  // features_dc, visible only
-        adam_slab<3>(A.param[3], A.exp_avg[3], A.exp_avg_sq[3], (size_t)g0 * 3, cnt * 3, lane,
-                     P->adam_step[3], b1, b2, 1.0f / P->adam_bc2[3], eps,
-                     [&](int gl, int k, float& g) {
-                         g = MSP_SH_C0 * sb[gl][15 + k];
-                         return sv[gl] != 0;
-                     });
+    // means, scales, quats, opacity (every Gaussian: zero gradient when
+    // culled) and features_dc (visible only)
+    adam_small_groups(A, P, g0, cnt, lane, sg, sb, sv);
     if (A.numel[4] > 0 && nb_rest > 0) {  // features_rest, visible only, degrees in use
         const int stride = P->rest_stride;
         const int used = nb_rest * 3;

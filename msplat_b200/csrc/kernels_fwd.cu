@@ -291,11 +291,15 @@ void launch_project_forward(const StepParams* P, int N, const float* means, cons
 // role of prefix_sum_kernel (msplat_metal.metal:2312-2364); ranges here are
 // [offset[t], offset[t+1]) with no per-tile cap.
 // ---------------------------------------------------------------------------
+constexpr int kOrderBuckets = 1024;  // = the scan CTA's threads
+__device__ __forceinline__ int order_bucket(int count) { return min(count >> 1, kOrderBuckets - 1); }
+
 __global__ void __launch_bounds__(1024)
 scan_tiles_kernel(const StepParams* __restrict__ P, int T, const int* __restrict__ count,
-                  int* __restrict__ offset, int* __restrict__ err)
+                  int* __restrict__ offset, int* __restrict__ order, int* __restrict__ err)
 {
     __shared__ int s_warp[32];
+    __shared__ int s_bucket[kOrderBuckets];
     const int tid = threadIdx.x;
     const int per = (T + 1023) / 1024;
     const int beg = min(tid * per, T), end = min(beg + per, T);
@@ -330,11 +334,48 @@ scan_tiles_kernel(const StepParams* __restrict__ P, int T, const int* __restrict
         offset[T] = run;
         if ((long long)run > P->capacity) atomicOr(err, kErrIsectOverflow);
     }
+    // CTA order of the per-tile kernels: tiles by intersection count, largest
+    // first (a counting sort on count/2, capped), so the longest tiles start
+    // in the first wave and the last wave holds short ones.  The order within
+    // a bucket is arbitrary; no result depends on it.
+    for (int b = tid; b < kOrderBuckets; b += 1024) s_bucket[b] = 0;
+    __syncthreads();
+    for (int i = beg; i < end; i++) atomicAdd(&s_bucket[order_bucket(count[i * kCountPitch])], 1);
+    __syncthreads();
+    {
+        // exclusive scan of the buckets from the largest down: one bucket per thread
+        const int b = kOrderBuckets - 1 - tid;
+        const int c = s_bucket[b];
+        int x = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += v;
+        }
+        if (lane == 31) s_warp[warp] = x;
+        __syncthreads();
+        if (warp == 0) {
+            const int v = s_warp[lane];
+            int wi = v;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int u = __shfl_up_sync(0xffffffffu, wi, o);
+                if (lane >= o) wi += u;
+            }
+            s_warp[lane] = wi - v;
+        }
+        __syncthreads();
+        s_bucket[b] = s_warp[warp] + x - c;
+    }
+    __syncthreads();
+    for (int i = beg; i < end; i++)
+        order[atomicAdd(&s_bucket[order_bucket(count[i * kCountPitch])], 1)] = i;
 }
 
 void launch_scan_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s)
 {
-    scan_tiles_kernel<<<1, 1024, 0, s>>>(P, num_tiles, B.tile_count, B.tile_offset, B.err);
+    scan_tiles_kernel<<<1, 1024, 0, s>>>(P, num_tiles, B.tile_count, B.tile_offset, B.tile_order,
+                                         B.err);
 }
 
 // ---------------------------------------------------------------------------
@@ -544,11 +585,11 @@ __device__ __forceinline__ int merge_path(const unsigned long long* a, int la,
 
 __global__ void __launch_bounds__(kSortThreads)
 sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
-                  unsigned long long* __restrict__ keys, unsigned long long* __restrict__ keys_alt,
-                  int* __restrict__ ids)
+                  const int* __restrict__ order, unsigned long long* __restrict__ keys,
+                  unsigned long long* __restrict__ keys_alt, int* __restrict__ ids)
 {
     __shared__ unsigned long long s[kSortRun + kSortRun / 16];
-    const int t = blockIdx.x;
+    const int t = order[blockIdx.x];
     const long long cap = P->capacity;
     const long long start = min((long long)offset[t], cap);
     const long long end = min((long long)offset[t + 1], cap);
@@ -595,7 +636,7 @@ sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offs
 void launch_sort_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s)
 {
     if (num_tiles <= 0) return;
-    sort_tiles_kernel<<<num_tiles, kSortThreads, 0, s>>>(P, B.tile_offset, B.keys, B.keys_alt,
+    sort_tiles_kernel<<<num_tiles, kSortThreads, 0, s>>>(P, B.tile_offset, B.tile_order, B.keys, B.keys_alt,
                                                         B.sorted_ids);
 }
 
@@ -612,7 +653,8 @@ void launch_sort_tiles(const StepParams* P, int num_tiles, const Buffers& B, cud
 template <bool CHUNKED>
 __global__ void __launch_bounds__(kTileThreads)
 raster_forward_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
-                      const int* __restrict__ ids, const float2* __restrict__ g_xy,
+                      const int* __restrict__ order, const int* __restrict__ ids,
+                      const float2* __restrict__ g_xy,
                       const float4* __restrict__ g_co, const float4* __restrict__ g_rgb,
                       float* __restrict__ out_img, float* __restrict__ final_T,
                       int* __restrict__ final_idx, float* __restrict__ chunk_T,
@@ -623,7 +665,7 @@ raster_forward_kernel(const StepParams* __restrict__ P, const int* __restrict__ 
     __shared__ float4 s_rgb[kTileThreads];
     __shared__ int s_idx[kTileThreads];
     __shared__ int s_wcnt[kTileThreads / 32];
-    const int tile = blockIdx.x;
+    const int tile = order[blockIdx.x];
     const int tx_n = P->tiles_x;
     const int W = P->img_w, H = P->img_h;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -773,12 +815,12 @@ void launch_raster_forward(const StepParams* P, int num_tiles, int k_max, int W,
     if (num_tiles <= 0) return;
     if (k_max <= 1) {
         raster_forward_kernel<false><<<num_tiles, kTileThreads, 0, s>>>(
-            P, B.tile_offset, B.sorted_ids, B.proj.xy, B.proj.conic_op, B.proj.rgb, B.out_img,
+            P, B.tile_offset, B.tile_order, B.sorted_ids, B.proj.xy, B.proj.conic_op, B.proj.rgb, B.out_img,
             B.final_T, B.final_idx, nullptr, nullptr, nullptr);
     } else {
         dim3 grid(num_tiles, k_max);
         raster_forward_kernel<true><<<grid, kTileThreads, 0, s>>>(
-            P, B.tile_offset, B.sorted_ids, B.proj.xy, B.proj.conic_op, B.proj.rgb, nullptr,
+            P, B.tile_offset, B.tile_order, B.sorted_ids, B.proj.xy, B.proj.conic_op, B.proj.rgb, nullptr,
             nullptr, nullptr, B.chunk_T, B.chunk_C, B.chunk_idx);
         dim3 mgrid((W + 15) / 16, (H + 15) / 16);
         merge_chunks_kernel<<<mgrid, 256, 0, s>>>(P, B.tile_offset, B.chunk_T, B.chunk_C,

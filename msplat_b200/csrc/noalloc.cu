@@ -47,7 +47,7 @@ inline size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 
 // Byte offsets of every buffer inside the array; capacity = intersections.
 struct Layout {
-    size_t params, err, xy, depth, radii, conic_op, rgb, rect, tile_count, tile_offset;
+    size_t params, err, xy, depth, radii, conic_op, rgb, rect, tile_count, tile_offset, tile_order;
     size_t final_T, final_idx, chunk_T, chunk_C, chunk_idx, keys, keys_alt, sorted_ids;
     size_t end;
     long long capacity;
@@ -75,6 +75,7 @@ Layout layout(long long N, long long P, long long T, int K, long long cap)
     L.rect = take(n * sizeof(uint2));
     L.tile_count = take((size_t)T * kCountPitch * sizeof(int));
     L.tile_offset = take((size_t)(T + 1) * sizeof(int));
+    L.tile_order = take((size_t)T * sizeof(int));
     L.final_T = take(px * sizeof(float));
     L.final_idx = take(px * sizeof(int));
     const size_t kp = K > 1 ? (size_t)K * px : 0;
@@ -179,6 +180,7 @@ extern "C" int msplat_render_noalloc(
     B.proj.rect = reinterpret_cast<uint2*>(base + L.rect);
     B.tile_count = reinterpret_cast<int*>(base + L.tile_count);
     B.tile_offset = reinterpret_cast<int*>(base + L.tile_offset);
+    B.tile_order = reinterpret_cast<int*>(base + L.tile_order);
     B.final_T = reinterpret_cast<float*>(base + L.final_T);
     B.final_idx = reinterpret_cast<int*>(base + L.final_idx);
     if (p.k_max > 1) {

@@ -1242,3 +1242,39 @@ void orc_reset_opacity(float *opacities, float *exp_avg5, float *exp_avg_sq5, in
         exp_avg_sq5[i] = 0.f;
     }
 }
+
+/*
+ * Mean distance to the k-1 nearest other points (PointsTensor::scales,
+ * core/include/kdtree_tensor.hpp:27-41, a nanoflann v1.5.5 k-d tree, which
+ * is exact): squared distances formed as nanoflann's L2_Simple_Adaptor
+ * forms them (result += diff * diff over x, y, z), the k smallest kept
+ * (the point itself is the first), then the mean of their square roots.
+ * Exhaustive search; test infrastructure for msplat_knn_mean_distance.
+ */
+void orc_knn_mean_distance(const float *xyz, int64_t n, int k, float *out)
+{
+#pragma omp parallel for schedule(dynamic, 64)
+    for (int64_t i = 0; i < n; i++) {
+        float best[8];
+        for (int j = 0; j < k; j++) best[j] = 3.402823466e38f;
+        const float *q = xyz + 3 * i;
+        for (int64_t j = 0; j < n; j++) {
+            float d = 0.0f;
+            for (int a = 0; a < 3; a++) {
+                const float diff = q[a] - xyz[3 * j + a];
+                d += diff * diff;
+            }
+            if (d < best[k - 1]) {
+                int m = k - 1;
+                while (m > 0 && best[m - 1] > d) {
+                    best[m] = best[m - 1];
+                    m--;
+                }
+                best[m] = d;
+            }
+        }
+        float sum = 0.0f;
+        for (int j = 1; j < k; j++) sum += sqrtf(best[j]);
+        out[i] = sum / (float)(k - 1);
+    }
+}

@@ -132,6 +132,9 @@ int orc_densify(int N, int buf_capacity, float grad_thresh, float size_thresh,
                 int *dup_flag_out, int *keep_flag_out);
 void orc_reset_opacity(float *opacities, float *exp_avg5, float *exp_avg_sq5, int n);
 
+/* Initial-scale k-NN (kdtree_tensor.hpp:27-41): see msplat_oracle.c. */
+void orc_knn_mean_distance(const float *xyz, int64_t n, int k, float *out);
+
 /* Forward only (msplat_render): fills S->out_img / final_T / final_idx. */
 int orc_render(const orc_params *P, orc_state *S, const float *params[6]);
 
