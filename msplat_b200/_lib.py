@@ -9,7 +9,9 @@ import ctypes as C
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libmsplat_b200.so")
+# MSPLAT_B200_LIB selects another build of the same library (e.g. a tuning
+# variant built elsewhere); by default the in-tree build.
+LIB_PATH = os.environ.get("MSPLAT_B200_LIB") or os.path.join(_HERE, "libmsplat_b200.so")
 
 _f = C.c_float
 _i = C.c_int

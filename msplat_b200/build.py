@@ -56,16 +56,19 @@ def _stale(target: str, inputs: list[str]) -> bool:
     return any(os.path.getmtime(i) > t for i in inputs)
 
 
-def build(verbose: bool = False, force: bool = False) -> str:
-    os.makedirs(BUILD, exist_ok=True)
+def build(verbose: bool = False, force: bool = False, out: str = LIB, build_dir: str = BUILD,
+          defines: tuple = ()) -> str:
+    """Compile every csrc/*.cu for sm_100a and link `out`.  `defines`
+    (-DNAME=VALUE strings) and a separate `build_dir` make a variant build."""
+    os.makedirs(build_dir, exist_ok=True)
     nvcc = _nvcc()
     deps = _deps()
     objs, jobs = [], []
     for src in sources():
-        obj = os.path.join(BUILD, os.path.basename(src)[:-3] + ".o")
+        obj = os.path.join(build_dir, os.path.basename(src)[:-3] + ".o")
         objs.append(obj)
         if force or _stale(obj, [src] + deps):
-            jobs.append([nvcc, *ARCH, *CFLAGS, fmad_flag(src), "-c", src, "-o", obj])
+            jobs.append([nvcc, *ARCH, *CFLAGS, *defines, fmad_flag(src), "-c", src, "-o", obj])
 
     def run(cmd):
         if verbose:
@@ -77,9 +80,9 @@ def build(verbose: bool = False, force: bool = False) -> str:
 
     with ThreadPoolExecutor(max_workers=min(8, max(1, len(jobs)))) as ex:
         list(ex.map(run, jobs))
-    if force or jobs or _stale(LIB, objs):
-        run([nvcc, *ARCH, "-shared", "-o", LIB, *objs, "-cudart", "static", "-lz", "-ldl"])
-    return LIB
+    if force or jobs or _stale(out, objs):
+        run([nvcc, *ARCH, "-shared", "-o", out, *objs, "-cudart", "static", "-lz", "-ldl"])
+    return out
 
 
 if __name__ == "__main__":

@@ -34,9 +34,19 @@ __device__ __forceinline__ float sel(bool c, float a, float b) { return c ? a : 
 // broadcasts, vote, warp reduction) per pixel; the 64-register cap (8 CTAs
 // of 128 threads per SM) keeps enough warps resident.  Measured at C1: 0.99
 // ms against 1.13 ms for one pixel per thread.
+// Tuning constants; a variant build may override them (-DMSP_BWD_MIN_BLOCKS=...).
+#ifndef MSP_BWD_MIN_BLOCKS
+#define MSP_BWD_MIN_BLOCKS 8
+#endif
+#ifndef MSP_RAST_BATCH
+#define MSP_RAST_BATCH 256
+#endif
+#ifndef MSP_PROJ_BWD_MIN_BLOCKS
+#define MSP_PROJ_BWD_MIN_BLOCKS 5
+#endif
 constexpr int kBwdPPT = 2;
-constexpr int kBwdMinBlocks = 8;
-constexpr int kRastBatch = 256;
+constexpr int kBwdMinBlocks = MSP_BWD_MIN_BLOCKS;
+constexpr int kRastBatch = MSP_RAST_BATCH;
 
 // Back-to-front state of one pixel.  Bs = sum_c (buffer_c + T_final*bg_c) *
 // v_out_c, the colour "behind" the current Gaussian weighted by the pixel's
@@ -649,7 +659,7 @@ __device__ __forceinline__ void gaussian_vjp(const StepParams* __restrict__ P,
 // GRAD_OUT = true: the data-parallel step, gradients written to G (the
 // same values Adam would have consumed) and no parameter touched.
 template <bool GRAD_OUT>
-__global__ void __launch_bounds__(kBwdThreads, 5)
+__global__ void __launch_bounds__(kBwdThreads, MSP_PROJ_BWD_MIN_BLOCKS)
 project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
                              const int* __restrict__ radii, const float4* __restrict__ g_co,
                              const float* __restrict__ grad_acc, AdamPtrs A, StatPtrs St,

@@ -61,7 +61,8 @@ def test_step_through_staged_input_matches_device_input():
     host = gt.contiguous().pin_memory()
     engine.train_step(b, cs, engine.DevicePtr(_stage(host)))
     lb = lib.msplat_last_loss(1)
-    assert la == lb
+    # the loss is a float-atomic sum over blocks: equal to a few ulp
+    assert abs(la - lb) <= 1e-6 * abs(la)
     for x, y in zip(a.params, b.params):
         bad, _ = harness.close(x.cpu().numpy(), y.cpu().numpy(), 1e-5, 1e-6)
         assert bad <= 3
