@@ -135,9 +135,9 @@ def peaks() -> dict:
 # (rest_adam_kernel + project_backward_adam_kernel) and warp instructions of
 # the issue-bound kernels.  Instruction counts vary a little with the view;
 # the capture's view stands for all.
-C1_OPT_STAGE_TRAFFIC = 510081536 + 344526592 + 235912960 + 118926592
-C1_WARP_INSTR = {"rast_fwd": ("raster_forward_kernel<0>", 374211050),
-                 "rast_bwd": ("raster_backward_kernel<0,2>", 667931406),
+C1_OPT_STAGE_TRAFFIC = 510096128 + 344680448 + 235900928 + 117620224
+C1_WARP_INSTR = {"rast_fwd": ("raster_forward_kernel<0>", 374177594),
+                 "rast_bwd": ("raster_backward_kernel<0,2>", 667897786),
                  "loss_fwd_bwd": ("ssim_loss_fused_kernel", 105998350)}
 SM_COUNT, ISSUE_PER_SM_CLK = 148, 4
 
