@@ -16,16 +16,19 @@ namespace msp {
 // (msplat_metal.metal:898-1099) and, for depth chunks,
 // compute_chunk_prefix_suffix_kernel (:2804-2840) plus
 // rasterize_backward_chunked_kernel (:2844-3031).
-// One CTA per 16x16 tile (per (tile, chunk)); each thread replays PPT
-// pixels, (x, y + 2h), back to front, so a warp owns a 16 x 2*PPT block.
+// One CTA per 16x16 tile (per (tile, chunk)); each warp owns one 8x8
+// quadrant and each thread replays two of its pixels, (x, y) and (x, y + 4),
+// back to front.
 // Each lane adds
 // its pixels' contributions, the warp sums its lanes with
 // a transposed butterfly (8 values in 9 shuffles, the opacity term in 5),
 // then 9 lanes issue one RED each into the Gaussian's 9 contiguous
 // accumulators: v_rgb[3] (gated by the clamp mask), v_conic[3], v_xy[2],
 // v_opacity (w.r.t. the logit).  Staged batches drop the Gaussians that cannot
-// reach any pixel of the tile (tile_may_contribute), as the forward does, and
-// each warp walks only those that can reach its rows (band_mask).
+// reach any pixel of the tile, as the forward does, and each warp walks only
+// those that can reach a pixel of its quadrant (quadrant_mask: the exact
+// least sigma over each 8x8 rectangle of pixel centres, with the forward's
+// conservative margins).
 // ---------------------------------------------------------------------------
 
 __device__ __forceinline__ float sel(bool c, float a, float b) { return c ? a : b; }
@@ -112,6 +115,7 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
                        const float* __restrict__ prefix_T, const float* __restrict__ chunk_T,
                        const float* __restrict__ after_C, float* __restrict__ grad_acc)
 {
+    static_assert(PPT == 2, "a warp's 32 lanes x 2 pixels cover one 8x8 quadrant");
     constexpr int kThreads = 256 / PPT;
     __shared__ int s_id[kRastBatch];
     __shared__ float2 s_xy[kRastBatch];
@@ -126,8 +130,10 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
     const int W = P->img_w, H = P->img_h;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int tx0 = (tile % tx_n) * kBlockX, ty0 = (tile / tx_n) * kBlockY;
-    const int px = tx0 + (lane & 15);
-    const int by = ty0 + warp * 2 * PPT;
+    // warp w owns the 8x8 quadrant (w & 1, w >> 1); lane: column lane & 7,
+    // rows lane >> 3 and + 4
+    const int px = tx0 + 8 * (warp & 1) + (lane & 7);
+    const int by = ty0 + 8 * (warp >> 1);
     const long long cap = P->capacity;
     const int fbeg = (int)min((long long)offset[tile], cap);
     const int fend = (int)min((long long)offset[tile + 1], cap);
@@ -145,7 +151,7 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
 #pragma unroll
     for (int h = 0; h < PPT; h++) {
         PixelBwd& s = st[h];
-        const int py = by + (lane >> 4) + 2 * h;
+        const int py = by + (lane >> 3) + 4 * h;
         s = PixelBwd{0.f, 0.f, 0.f, 0.f, 0.f, beg - 1};
         if (px < W && py < H) {
             const size_t pix = (size_t)py * W + px;
@@ -207,10 +213,11 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
                                  (raw.z + 0.5f >= 0.f ? 4 : 0);
                 s_rgb[slot] = make_float4(fmaxf(raw.x + 0.5f, 0.f), fmaxf(raw.y + 0.5f, 0.f),
                                           fmaxf(raw.z + 0.5f, 0.f), __int_as_float(mask));
-                const float lim = cull_limit(co);
-                keep = tile_may_contribute(xy, co, tx0f, ty0f, lim);
-                // warp w owns the 2*PPT rows from 2*PPT*w
-                s_band[slot] = (unsigned char)band_mask<2 * PPT>(xy, co, ty0f, lim);
+                // the quadrants (one per warp) the Gaussian can reach; none:
+                // it cannot reach the tile
+                const unsigned qm = quadrant_mask(xy, co, tx0f, ty0f, cull_limit(co));
+                keep = qm != 0u;
+                s_band[slot] = (unsigned char)qm;
             }
             const unsigned bal = __ballot_sync(0xffffffffu, keep);
             if (lane == 0) s_wcnt[h * (kThreads / 32) + warp] = __popc(bal);
@@ -260,7 +267,7 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
                 bool on = false;
 #pragma unroll
                 for (int h = 0; h < PPT; h++)
-                    on |= backprop(st[h], fpx, (float)(by + (lane >> 4) + 2 * h), xy, co, rc, idx, v);
+                    on |= backprop(st[h], fpx, (float)(by + (lane >> 3) + 4 * h), xy, co, rc, idx, v);
                 if (!__any_sync(0xffffffffu, on)) continue;
                 // Transposed butterfly: afterwards lane L holds the warp sum of
                 // value (L >> 2); the opacity term takes a plain butterfly.

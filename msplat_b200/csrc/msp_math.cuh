@@ -95,16 +95,16 @@ __device__ __forceinline__ float cull_limit(float4 co)
 }
 
 // Whether the Gaussian (centre xy, conic co) can reach any pixel centre of
-// the 16x16 tile whose first pixel centre is (x0, y0): the least sigma over
-// the rectangle of pixel centres (0 if the centre lies inside, else the
+// the w x h rectangle whose first pixel centre is (x0, y0): the least sigma
+// over the rectangle of pixel centres (0 if the centre lies inside, else the
 // least of the four edge minima, exact for a convex quadratic) against lim.
-__device__ __forceinline__ bool tile_may_contribute(float2 xy, float4 co, float x0, float y0,
-                                                    float lim)
+__device__ __forceinline__ bool rect_may_contribute(float2 xy, float4 co, float x0, float y0,
+                                                    float w1, float h1, float lim)
 {
     if (lim >= 1.0e38f) return true;
     const float a = co.x, b = co.y, c = co.z;
-    const float dxl = xy.x - (x0 + 15.f), dxh = xy.x - x0;
-    const float dyl = xy.y - (y0 + 15.f), dyh = xy.y - y0;
+    const float dxl = xy.x - (x0 + w1), dxh = xy.x - x0;
+    const float dyl = xy.y - (y0 + h1), dyh = xy.y - y0;
     if (dxl <= 0.f && dxh >= 0.f && dyl <= 0.f && dyh >= 0.f) return lim >= 0.f;
     const float ia = 1.f / a, ic = 1.f / c;
     float qmin = 3.0e38f;
@@ -117,6 +117,41 @@ __device__ __forceinline__ bool tile_may_contribute(float2 xy, float4 co, float 
     edge(fminf(fmaxf(-b * dyl * ia, dxl), dxh), dyl);
     edge(fminf(fmaxf(-b * dyh * ia, dxl), dxh), dyh);
     return qmin <= lim;
+}
+
+// The 16x16 tile whose first pixel centre is (x0, y0).
+__device__ __forceinline__ bool tile_may_contribute(float2 xy, float4 co, float x0, float y0,
+                                                    float lim)
+{
+    return rect_may_contribute(xy, co, x0, y0, 15.f, 15.f, lim);
+}
+
+// The 8x4 blocks of the tile (bit 2*by + bx, bx in 0..1, by in 0..3) that
+// the Gaussian can reach; zero exactly when tile_may_contribute is false.
+__device__ __forceinline__ unsigned block8x4_mask(float2 xy, float4 co, float x0, float y0,
+                                                  float lim)
+{
+    if (lim >= 1.0e38f) return 0xffu;
+    unsigned m = 0u;
+#pragma unroll
+    for (int q = 0; q < 8; q++)
+        if (rect_may_contribute(xy, co, x0 + 8.f * (q & 1), y0 + 4.f * (q >> 1), 7.f, 3.f, lim))
+            m |= 1u << q;
+    return m;
+}
+
+// The 8x8 quadrants of the tile (bit 2*qy + qx) that the Gaussian can reach;
+// zero exactly when tile_may_contribute is false.
+__device__ __forceinline__ unsigned quadrant_mask(float2 xy, float4 co, float x0, float y0,
+                                                  float lim)
+{
+    if (lim >= 1.0e38f) return 0xfu;
+    unsigned m = 0u;
+#pragma unroll
+    for (int q = 0; q < 4; q++)
+        if (rect_may_contribute(xy, co, x0 + 8.f * (q & 1), y0 + 8.f * (q >> 1), 7.f, 7.f, lim))
+            m |= 1u << q;
+    return m;
 }
 
 // Bands of ROWS pixel rows of the tile (bit w: rows y0 + ROWS*w ...) that
