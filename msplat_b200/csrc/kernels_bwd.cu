@@ -123,7 +123,7 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
     __shared__ float4 s_rgb[kRastBatch];
     __shared__ int s_wmax[kThreads / 32];
     __shared__ int s_order[kRastBatch];
-    __shared__ unsigned char s_band[kRastBatch];
+    __shared__ unsigned char s_quad[kRastBatch];
     __shared__ int s_wcnt[kRastBatch / 32];
     const int tile = order[blockIdx.x];
     const int tx_n = P->tiles_x;
@@ -217,7 +217,7 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
                 // it cannot reach the tile
                 const unsigned qm = quadrant_mask(xy, co, tx0f, ty0f, cull_limit(co));
                 keep = qm != 0u;
-                s_band[slot] = (unsigned char)qm;
+                s_quad[slot] = (unsigned char)qm;
             }
             const unsigned bal = __ballot_sync(0xffffffffu, keep);
             if (lane == 0) s_wcnt[h * (kThreads / 32) + warp] = __popc(bal);
@@ -253,7 +253,7 @@ raster_backward_kernel(const StepParams* __restrict__ P, const int* __restrict__
         for (int b = t0; b < m; b += 32) {
             const int oi = b + lane;
             const int my_slot = oi < m ? s_order[oi] : 0;
-            unsigned bits = __ballot_sync(0xffffffffu, oi < m && ((s_band[my_slot] >> warp) & 1u));
+            unsigned bits = __ballot_sync(0xffffffffu, oi < m && ((s_quad[my_slot] >> warp) & 1u));
             while (bits) {
                 const int t = __shfl_sync(0xffffffffu, my_slot, __ffs(bits) - 1);
                 bits &= bits - 1u;

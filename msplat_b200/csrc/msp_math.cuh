@@ -126,20 +126,6 @@ __device__ __forceinline__ bool tile_may_contribute(float2 xy, float4 co, float 
     return rect_may_contribute(xy, co, x0, y0, 15.f, 15.f, lim);
 }
 
-// The 8x4 blocks of the tile (bit 2*by + bx, bx in 0..1, by in 0..3) that
-// the Gaussian can reach; zero exactly when tile_may_contribute is false.
-__device__ __forceinline__ unsigned block8x4_mask(float2 xy, float4 co, float x0, float y0,
-                                                  float lim)
-{
-    if (lim >= 1.0e38f) return 0xffu;
-    unsigned m = 0u;
-#pragma unroll
-    for (int q = 0; q < 8; q++)
-        if (rect_may_contribute(xy, co, x0 + 8.f * (q & 1), y0 + 4.f * (q >> 1), 7.f, 3.f, lim))
-            m |= 1u << q;
-    return m;
-}
-
 // The 8x8 quadrants of the tile (bit 2*qy + qx) that the Gaussian can reach;
 // zero exactly when tile_may_contribute is false.
 __device__ __forceinline__ unsigned quadrant_mask(float2 xy, float4 co, float x0, float y0,
@@ -152,26 +138,6 @@ __device__ __forceinline__ unsigned quadrant_mask(float2 xy, float4 co, float x0
         if (rect_may_contribute(xy, co, x0 + 8.f * (q & 1), y0 + 8.f * (q >> 1), 7.f, 7.f, lim))
             m |= 1u << q;
     return m;
-}
-
-// Bands of ROWS pixel rows of the tile (bit w: rows y0 + ROWS*w ...) that
-// the Gaussian can reach: over any row the least sigma is
-// 0.5 * dy^2 * det / a, so only rows with |dy| <= sqrt(2 lim a / det) can.
-template <int ROWS>
-__device__ __forceinline__ unsigned band_mask(float2 xy, float4 co, float y0, float lim)
-{
-    constexpr int kBands = 16 / ROWS;
-    constexpr unsigned kAll = (1u << kBands) - 1u;
-    if (lim >= 1.0e38f) return kAll;
-    if (lim < 0.f) return 0u;
-    const float a = co.x, b = co.y, c = co.z;
-    const float ry = sqrtf(2.f * lim * a / (a * c - b * b)) * 1.001f + 0.01f;
-    const float inv = 1.f / (float)ROWS;
-    const float flo = floorf((xy.y - ry - y0) * inv), fhi = floorf((xy.y + ry - y0) * inv);
-    if (!(fhi == fhi && flo == flo)) return kAll;
-    if (fhi < 0.f || flo > (float)(kBands - 1)) return 0u;
-    const int lo = (int)fmaxf(flo, 0.f), hi = (int)fminf(fhi, (float)(kBands - 1));
-    return kAll & ((2u << hi) - 1u) & ~((1u << lo) - 1u);
 }
 
 __device__ __forceinline__ int num_sh_bases(int degree)
