@@ -39,7 +39,7 @@ __device__ __forceinline__ float sel(bool c, float a, float b) { return c ? a : 
 // ms against 1.13 ms for one pixel per thread.
 // Tuning constants; a variant build may override them (-DMSP_BWD_MIN_BLOCKS=...).
 #ifndef MSP_BWD_MIN_BLOCKS
-#define MSP_BWD_MIN_BLOCKS 7
+#define MSP_BWD_MIN_BLOCKS 8
 #endif
 #ifndef MSP_RAST_BATCH
 #define MSP_RAST_BATCH 256

@@ -9,8 +9,12 @@
 namespace msp {
 
 constexpr int kProjThreads = 128;
-constexpr int kSortThreads = 256;
-constexpr int kSortRun = 8 * kSortThreads;  // keys sorted in registers in one pass
+#ifndef MSP_SORT_THREADS
+#define MSP_SORT_THREADS 128
+#endif
+constexpr int kSortThreads = MSP_SORT_THREADS;
+constexpr int kSortRun = 2048;                   // keys sorted in registers in one pass
+constexpr int kSortKMax = kSortRun / kSortThreads;  // keys per thread at most
 
 // ---------------------------------------------------------------------------
 // Projection + SH colour + tile counting.
@@ -568,7 +572,8 @@ __device__ __forceinline__ void sort_small(const unsigned long long* keys, int n
     if (n <= kSortThreads) sort_run<1>(keys, n, s, out_keys, out_ids);
     else if (n <= 2 * kSortThreads) sort_run<2>(keys, n, s, out_keys, out_ids);
     else if (n <= 4 * kSortThreads) sort_run<4>(keys, n, s, out_keys, out_ids);
-    else sort_run<8>(keys, n, s, out_keys, out_ids);
+    else if (kSortKMax == 8 || n <= 8 * kSortThreads) sort_run<8>(keys, n, s, out_keys, out_ids);
+    else if constexpr (kSortKMax >= 16) sort_run<16>(keys, n, s, out_keys, out_ids);
 }
 
 __device__ __forceinline__ int merge_path(const unsigned long long* a, int la,
