@@ -443,6 +443,7 @@ void cleanup_msplat_cuda(void)
     if (!g.ready) return;
     cudaStreamSynchronize(g.stream());
     free_buffers();
+    stage_release();
     g.growth_isect = 0;
 }
 

@@ -147,6 +147,7 @@ std::mutex& engine_mutex();          // the engine's lock (take it in every entr
 int engine_init();                   // idempotent; MSPLAT_OK or an error code
 cudaStream_t engine_stream();        // stream all engine work goes to
 void engine_add_launches(int n);     // for msplat_kernel_launches
+void stage_release();                // frees msplat_stage_input's buffers (engine lock held)
 
 // Host helpers shared by the entry points (engine.cu).
 void set_error(const char* fmt, ...);                  // text for msplat_last_error()

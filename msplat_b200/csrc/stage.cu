@@ -60,6 +60,22 @@ int stage_init()
 }
 
 }  // namespace
+
+void stage_release()
+{
+    Stage& S = s_stage;
+    if (!S.ready) return;
+    cudaStreamSynchronize(S.copy);
+    for (int k = 0; k < 2; k++) {
+        if (S.buf[k]) cudaFree(S.buf[k]);
+        S.buf[k] = nullptr;
+        S.bytes[k] = 0;
+        S.consumed_recorded[k] = false;
+    }
+    S.next = 0;
+    S.stagings = 0;
+}
+
 }  // namespace msp
 
 using namespace msp;

@@ -378,8 +378,11 @@ struct Model {
             std::mt19937 rng(step);
             std::normal_distribution<float> dist(0.0f, 1.0f);
             for (auto& x : smp) x = dist(rng);
-            cudaMemcpyAsync(samples, smp.data(), smp.size() * sizeof(float), cudaMemcpyHostToDevice,
-                            engine_stream());
+            if (cudaMemcpyAsync(samples, smp.data(), smp.size() * sizeof(float),
+                                cudaMemcpyHostToDevice, engine_stream()) != cudaSuccess) {
+                set_error("uploading the split samples failed");
+                return MSPLAT_ERR_CUDA;
+            }
             const float half_max_dim = 0.5f * static_cast<float>(std::max(lastWidth, lastHeight));
             const int check_screen = step < stopScreenSizeAt ? 1 : 0;
             const bool check_huge = step > refineEvery * resetAlphaEvery;
