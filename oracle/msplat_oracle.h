@@ -14,8 +14,8 @@
  * per-tile sort order and the forward image are bit-exact):
  *   - no FMA contraction (compiled with -ffp-contract=off); fma() of the
  *     reference is fmaf();
- *   - exp() is msp_expf(): Cody & Waite argument reduction plus a degree-7
- *     Taylor polynomial (see msplat_oracle.c);
+ *   - exp() is msp_expf(): Cody & Waite argument reduction plus a degree-6
+ *     minimax polynomial (see msplat_oracle.c);
  *   - sqrt, division are IEEE round-to-nearest; rsqrt(x) is 1.0f/sqrtf(x);
  *   - float->int conversion truncates, saturates and maps NaN to 0.
  */

@@ -45,8 +45,9 @@ msl_fiber_trampoline:
 
 namespace msl {
 
-// exp(x): the oracle's method (Cody & Waite reduction, degree-7 Taylor
-// polynomial, exact two-step scale), so every side evaluates the same bits.
+// exp(x): the oracle's method (Cody & Waite reduction with k read from
+// fma(x, log2e, 1.5*2^23), degree-6 minimax polynomial, exact two-step
+// scale), so every side evaluates the same bits.
 float ref_expf(float x)
 {
     if (x != x) return x + x;
@@ -55,18 +56,21 @@ float ref_expf(float x)
     const float log2e = 1.44269502162933349609375f;
     const float ln2_hi = 0.693145751953125f;
     const float ln2_lo = 1.428606765330187045e-06f;
-    float k = rintf(x * log2e);
+    const float round_const = 12582912.0f;
+    const float t = fmaf(x, log2e, round_const);
+    const float k = t - round_const;
     float r = fmaf(-k, ln2_hi, x);
     r = fmaf(-k, ln2_lo, r);
-    float p = 1.98412698412698413e-04f;
-    p = fmaf(p, r, 1.38888888888888889e-03f);
-    p = fmaf(p, r, 8.33333333333333333e-03f);
-    p = fmaf(p, r, 4.16666666666666667e-02f);
-    p = fmaf(p, r, 1.66666666666666667e-01f);
-    p = fmaf(p, r, 0.5f);
+    float p = 0.0013814594130963087f;
+    p = fmaf(p, r, 0.0083687193691730499f);
+    p = fmaf(p, r, 0.041668388992547989f);
+    p = fmaf(p, r, 0.1666652113199234f);
+    p = fmaf(p, r, 0.49999994039535522f);
     p = fmaf(p, r, 1.0f);
     p = fmaf(p, r, 1.0f);
-    const int ki = (int)k;
+    uint32_t tb;
+    std::memcpy(&tb, &t, 4);
+    const int ki = (int)(tb - 0x4B400000u);
     const int e1 = ki / 2, e2 = ki - e1;
     auto pow2 = [](int e) {
         uint32_t u = (uint32_t)(e + 127) << 23;

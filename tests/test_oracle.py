@@ -23,7 +23,7 @@ def test_expf_accuracy():
     xs = np.concatenate([np.linspace(-87.0, 88.0, 20001), np.linspace(-6.0, 0.0, 20001),
                          np.array([0.0, -0.0, 1e-8, -1e-8, 0.5, -0.5])]).astype(np.float32)
     worst = max(_ulp_err(oracle.expf(float(x)), math.exp(float(x))) for x in xs)
-    assert worst <= 2.0, worst
+    assert worst <= 1.0, worst
 
 
 def test_expf_special_values():
