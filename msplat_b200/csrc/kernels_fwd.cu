@@ -13,6 +13,9 @@ constexpr int kProjThreads = 128;
 #define MSP_SORT_THREADS 128
 #endif
 constexpr int kSortThreads = MSP_SORT_THREADS;
+#ifndef MSP_SORT_RADIX
+#define MSP_SORT_RADIX 1
+#endif
 constexpr int kSortRun = 2048;                   // keys sorted in registers in one pass
 constexpr int kSortKMax = kSortRun / kSortThreads;  // keys per thread at most
 
@@ -588,12 +591,163 @@ __device__ __forceinline__ int merge_path(const unsigned long long* a, int la,
     return lo;
 }
 
+// Per-tile LSD radix sort of the 32-bit depths (the ids ride along) for
+// 2 <= n <= kSortRun keys: 8-bit digits, one pass per byte that is not the
+// same for every key of the tile.  Each pass is stable: warp w ranks its
+// contiguous share of the keys 32 at a time (__match_any_sync groups the
+// lanes with equal digits), and the per-(digit, warp) counts are scanned
+// digit-major, warp-minor.  Stability keeps equal depths in input order,
+// which the scatter's atomics leave arbitrary, so a tile holding two equal
+// depths reports it and is sorted by the bitonic network on the full
+// (depth, id) keys instead; both give the order of the 64-bit keys.
+constexpr int kRadixWarps = kSortThreads / 32;
+constexpr int kRadixChunks = kSortRun / kSortThreads;  // 32-key chunks per warp at most
+
+struct RadixSmem {
+    unsigned key[kSortRun];
+    int val[kSortRun];
+    int hist[256 * kRadixWarps];  // [digit * kRadixWarps + warp]
+    int wsum[kRadixWarps];
+    unsigned red[2 * kRadixWarps];
+};
+
+// Exclusive prefix sum of S.hist in place (256 * kRadixWarps counters).
+__device__ __forceinline__ void radix_scan(RadixSmem& S)
+{
+    constexpr int kPer = 256 * kRadixWarps / kSortThreads;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int c[kPer];
+    int sum = 0;
+#pragma unroll
+    for (int i = 0; i < kPer; i++) {
+        c[i] = S.hist[tid * kPer + i];
+        sum += c[i];
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += u;
+    }
+    if (lane == 31) S.wsum[warp] = incl;
+    __syncthreads();
+    int base = incl - sum;
+#pragma unroll
+    for (int w = 0; w < kRadixWarps; w++) base += w < warp ? S.wsum[w] : 0;
+#pragma unroll
+    for (int i = 0; i < kPer; i++) {
+        S.hist[tid * kPer + i] = base;
+        base += c[i];
+    }
+}
+
+// Returns false (and writes nothing) when two keys of the tile have equal
+// depths; otherwise writes the ids in ascending (depth, id) order.
+__device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __restrict__ keys, int n,
+                                                RadixSmem& S, int* __restrict__ out_ids)
+{
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const unsigned lt = (1u << lane) - 1u;
+    const int C = (n + kSortThreads - 1) / kSortThreads;  // chunks per warp
+    const int w0 = warp * C * 32;                          // this warp's first element
+    unsigned k[kRadixChunks];
+    int v[kRadixChunks];
+    unsigned pe[kRadixChunks];
+    unsigned ko = 0u, ka = ~0u;
+#pragma unroll
+    for (int c = 0; c < kRadixChunks; c++) {
+        k[c] = ~0u;  // padding sorts last and stays behind equal real keys
+        v[c] = 0;
+        const int e = w0 + c * 32 + lane;
+        if (c < C && e < n) {
+            const unsigned long long kv = keys[e];
+            k[c] = (unsigned)(kv >> 32);
+            v[c] = (int)(unsigned)(kv & 0xffffffffull);
+            ko |= k[c];
+            ka &= k[c];
+        }
+    }
+    ko = __reduce_or_sync(0xffffffffu, ko);
+    ka = __reduce_and_sync(0xffffffffu, ka);
+    if (lane == 0) {
+        S.red[warp] = ko;
+        S.red[kRadixWarps + warp] = ka;
+    }
+    __syncthreads();
+    unsigned all_or = 0u, all_and = ~0u;
+#pragma unroll
+    for (int w = 0; w < kRadixWarps; w++) {
+        all_or |= S.red[w];
+        all_and &= S.red[kRadixWarps + w];
+    }
+    const unsigned varying = all_or ^ all_and;
+    if (varying == 0u) return false;  // n >= 2 equal depths
+    for (int shift = 0; shift < 32; shift += 8) {
+        if (((varying >> shift) & 0xffu) == 0u) continue;
+        for (int d = lane; d < 256; d += 32) S.hist[d * kRadixWarps + warp] = 0;
+        __syncwarp();
+#pragma unroll
+        for (int c = 0; c < kRadixChunks; c++) {
+            if (c >= C) break;
+            const unsigned d = (k[c] >> shift) & 0xffu;
+            pe[c] = __match_any_sync(0xffffffffu, d);
+            if ((pe[c] & lt) == 0u) S.hist[d * kRadixWarps + warp] += __popc(pe[c]);
+            __syncwarp();
+        }
+        __syncthreads();
+        radix_scan(S);
+        __syncthreads();
+#pragma unroll
+        for (int c = 0; c < kRadixChunks; c++) {
+            if (c >= C) break;
+            const unsigned d = (k[c] >> shift) & 0xffu;
+            const int slot = d * kRadixWarps + warp;
+            const int base = S.hist[slot];
+            __syncwarp();
+            if ((pe[c] & lt) == 0u) S.hist[slot] = base + __popc(pe[c]);
+            const int pos = base + __popc(pe[c] & lt);
+            S.key[pos] = k[c];
+            S.val[pos] = v[c];
+            __syncwarp();
+        }
+        __syncthreads();
+#pragma unroll
+        for (int c = 0; c < kRadixChunks; c++) {
+            if (c >= C) break;
+            const int e = w0 + c * 32 + lane;
+            k[c] = S.key[e];
+            v[c] = S.val[e];
+        }
+    }
+    // S.key holds the sorted depths (at least one pass ran): any equal
+    // neighbours among the real keys?
+    bool tie = false;
+#pragma unroll
+    for (int c = 0; c < kRadixChunks; c++) {
+        if (c >= C) break;
+        const int e = w0 + c * 32 + lane;
+        if (e + 1 < n && k[c] == S.key[e + 1]) tie = true;
+    }
+    if (__syncthreads_or(tie)) return false;
+#pragma unroll
+    for (int c = 0; c < kRadixChunks; c++) {
+        if (c >= C) break;
+        const int e = w0 + c * 32 + lane;
+        if (e < n) out_ids[e] = v[c];
+    }
+    return true;
+}
+
 __global__ void __launch_bounds__(kSortThreads)
 sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
                   const int* __restrict__ order, unsigned long long* __restrict__ keys,
                   unsigned long long* __restrict__ keys_alt, int* __restrict__ ids)
 {
-    __shared__ unsigned long long s[kSortRun + kSortRun / 16];
+    __shared__ union {
+        unsigned long long bitonic[kSortRun + kSortRun / 16];
+        RadixSmem radix;
+    } sm;
+    unsigned long long* s = sm.bitonic;
     const int t = order[blockIdx.x];
     const long long cap = P->capacity;
     const long long start = min((long long)offset[t], cap);
@@ -601,6 +755,10 @@ sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offs
     const int n = (int)(end - start);
     if (n <= 0) return;
     if (n <= kSortRun) {
+        if (MSP_SORT_RADIX && n > kSortThreads) {
+            if (radix_sort_tile(keys + start, n, sm.radix, ids + start)) return;
+            __syncthreads();
+        }
         sort_small(keys + start, n, s, nullptr, ids + start);
         return;
     }
