@@ -16,6 +16,12 @@ constexpr int kSortThreads = MSP_SORT_THREADS;
 #ifndef MSP_SORT_RADIX
 #define MSP_SORT_RADIX 1
 #endif
+#ifndef MSP_RADIX_KEEP_PEERS
+#define MSP_RADIX_KEEP_PEERS 0
+#endif
+#ifndef MSP_SORT_MIN_BLOCKS
+#define MSP_SORT_MIN_BLOCKS 8
+#endif
 constexpr int kSortRun = 2048;                   // keys sorted in registers in one pass
 constexpr int kSortKMax = kSortRun / kSortThreads;  // keys per thread at most
 
@@ -652,7 +658,9 @@ __device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __rest
     const int w0 = warp * C * 32;                          // this warp's first element
     unsigned k[kRadixChunks];
     int v[kRadixChunks];
+#if MSP_RADIX_KEEP_PEERS
     unsigned pe[kRadixChunks];
+#endif
     unsigned ko = 0u, ka = ~0u;
 #pragma unroll
     for (int c = 0; c < kRadixChunks; c++) {
@@ -686,13 +694,17 @@ __device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __rest
         if (((varying >> shift) & 0xffu) == 0u) continue;
         for (int d = lane; d < 256; d += 32) S.hist[d * kRadixWarps + warp] = 0;
         __syncwarp();
+        // counts need no order: shared-memory atomics, no chain between chunks
 #pragma unroll
         for (int c = 0; c < kRadixChunks; c++) {
             if (c >= C) break;
             const unsigned d = (k[c] >> shift) & 0xffu;
+#if MSP_RADIX_KEEP_PEERS
             pe[c] = __match_any_sync(0xffffffffu, d);
-            if ((pe[c] & lt) == 0u) S.hist[d * kRadixWarps + warp] += __popc(pe[c]);
-            __syncwarp();
+            if ((pe[c] & lt) == 0u) atomicAdd(&S.hist[d * kRadixWarps + warp], __popc(pe[c]));
+#else
+            atomicAdd(&S.hist[d * kRadixWarps + warp], 1);
+#endif
         }
         __syncthreads();
         radix_scan(S);
@@ -701,11 +713,16 @@ __device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __rest
         for (int c = 0; c < kRadixChunks; c++) {
             if (c >= C) break;
             const unsigned d = (k[c] >> shift) & 0xffu;
+#if MSP_RADIX_KEEP_PEERS
+            const unsigned peers = pe[c];
+#else
+            const unsigned peers = __match_any_sync(0xffffffffu, d);
+#endif
             const int slot = d * kRadixWarps + warp;
             const int base = S.hist[slot];
             __syncwarp();
-            if ((pe[c] & lt) == 0u) S.hist[slot] = base + __popc(pe[c]);
-            const int pos = base + __popc(pe[c] & lt);
+            if ((peers & lt) == 0u) S.hist[slot] = base + __popc(peers);
+            const int pos = base + __popc(peers & lt);
             S.key[pos] = k[c];
             S.val[pos] = v[c];
             __syncwarp();
@@ -738,7 +755,7 @@ __device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __rest
     return true;
 }
 
-__global__ void __launch_bounds__(kSortThreads)
+__global__ void __launch_bounds__(kSortThreads, MSP_SORT_MIN_BLOCKS)
 sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
                   const int* __restrict__ order, unsigned long long* __restrict__ keys,
                   unsigned long long* __restrict__ keys_alt, int* __restrict__ ids)
