@@ -65,6 +65,7 @@ struct Engine {
     float* h_loss = nullptr;    // pinned [2]: loss_sum, isect total (as float bits unused)
     int* h_misc = nullptr;      // pinned [2]: err, isect total
     cudaEvent_t readback_ev = nullptr;
+    SideStream side{};
     bool readback_pending = false;
     float last_loss = 0.f;
     double last_loss_scale = 1.0;
@@ -106,6 +107,9 @@ static int init_engine()
     memset(g.h_loss, 0, sizeof(float) * 4);
     memset(g.h_misc, 0, sizeof(int) * 4);
     MSP_CUDA(cudaEventCreateWithFlags(&g.readback_ev, cudaEventDisableTiming));
+    MSP_CUDA(cudaStreamCreateWithFlags(&g.side.stream, cudaStreamNonBlocking));
+    MSP_CUDA(cudaEventCreateWithFlags(&g.side.fork, cudaEventDisableTiming));
+    MSP_CUDA(cudaEventCreateWithFlags(&g.side.join, cudaEventDisableTiming));
     for (int s = 0; s <= kStages; s++)
         for (int r = 0; r < kRing; r++) MSP_CUDA(cudaEventCreate(&g.st_ev[s][r]));
     MSP_CUDA(cudaMalloc(&g.B.loss_sum, sizeof(float) * 4));
@@ -120,6 +124,7 @@ static int init_engine()
 std::mutex& engine_mutex() { return g_mu; }
 int engine_init() { return init_engine(); }
 cudaStream_t engine_stream() { return g.stream(); }
+const SideStream& engine_side() { return g.side; }
 void engine_add_launches(int n) { g.launches += n; }
 
 template <typename T>
@@ -136,7 +141,7 @@ static void free_buffers()
 {
     Buffers& B = g.B;
     void* ptrs[] = {B.proj.xy, B.proj.depth, B.proj.radii, B.proj.conic_op, B.proj.rgb, B.proj.rect,
-                    B.tile_count, B.tile_offset, B.tile_order, B.keys, B.keys_alt, B.sorted_ids, B.out_img,
+                    B.proj.sh_mean, B.tile_count, B.tile_offset, B.tile_order, B.keys, B.keys_alt, B.sorted_ids, B.out_img,
                     B.final_T, B.final_idx, B.v_rendered, B.grad_acc,
                     B.chunk_T, B.chunk_C, B.chunk_idx, B.prefix_T, B.after_C};
     for (void* p : ptrs)
@@ -167,6 +172,7 @@ static int ensure(long long N, long long W, long long H, long long T, int K, boo
     if (train && N > g.cap_grad_N) {
         long long n = std::max(N, g.cap_N);
         if ((rc = realloc_dev(B.grad_acc, (size_t)n * kGradStride))) return rc;
+        if ((rc = realloc_dev(B.proj.sh_mean, (size_t)n * 3))) return rc;
         g.cap_grad_N = n;
     }
     long long want_isect = std::max(16 * N, g.growth_isect);

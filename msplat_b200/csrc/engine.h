@@ -54,6 +54,8 @@ struct ProjOut {
     float4* conic_op;    // conic a, b, c and sigmoid(opacity)
     float4* rgb;         // raw SH colour (w unused)
     uint2* rect;         // tile rect: x0 | y0<<16, x1 | y1<<16 (exclusive max)
+    float* sh_mean;      // [N*3] training only: the means as projected (SH-rest Adam reads
+                         // them while the projection VJP updates the means)
 };
 
 struct Buffers {
@@ -145,7 +147,14 @@ struct CamArgs {
 // Engine state shared with the other host files (engine.cu).
 std::mutex& engine_mutex();          // the engine's lock (take it in every entry point)
 int engine_init();                   // idempotent; MSPLAT_OK or an error code
-cudaStream_t engine_stream();        // stream all engine work goes to
+cudaStream_t engine_stream();
+// Second stream for work that overlaps the engine stream within a step,
+// with the events that fork it from and join it back to the engine stream.
+struct SideStream {
+    cudaStream_t stream;
+    cudaEvent_t fork, join;
+};
+const SideStream& engine_side();        // stream all engine work goes to
 void engine_add_launches(int n);     // for msplat_kernel_launches
 void stage_release();                // frees msplat_stage_input's buffers (engine lock held)
 

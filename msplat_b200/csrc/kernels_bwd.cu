@@ -801,8 +801,11 @@ int rest_bases_updated(int degrees_to_use, int rest_stride)
 // SH-rest Adam (the fused SH update of project_and_sh_backward_kernel,
 // msplat_metal.metal:1931-1985, for features_rest only), as its own
 // streaming kernel: 75% of the optimiser's bytes, and it needs nothing from
-// the geometry VJP -- only the view direction (from the mean, before the
-// means are updated, so this runs first), v_rgb and visibility.  Each lane
+// the geometry VJP -- only the view direction (from the forward's copy of
+// the mean, so the VJP may update the means meanwhile), v_rgb and
+// visibility.  It runs on the engine's side stream, concurrently with
+// project_backward_adam_kernel: this kernel streams at the bandwidth bound
+// while the other waits on its VJP's latency.  Each lane
 // first builds its Gaussian's 15 basis values in shared memory; then each
 // warp streams its 32 Gaussians' contiguous rest slab, kU independent
 // elements per lane per round so every lane keeps 3*kU loads in flight.
@@ -813,7 +816,7 @@ constexpr int kRestThreads = 256;
 template <int RS>
 __global__ void __launch_bounds__(kRestThreads)
 rest_adam_kernel(const StepParams* __restrict__ P, int N, const int* __restrict__ radii,
-                 const float* __restrict__ grad_acc, const float* __restrict__ means,
+                 const float* __restrict__ grad_acc, const float* __restrict__ sh_mean,
                  float* __restrict__ rest, float* __restrict__ rest_m, float* __restrict__ rest_v,
                  int used)
 {
@@ -826,7 +829,8 @@ rest_adam_kernel(const StepParams* __restrict__ P, int N, const int* __restrict_
     bool vis = false;
     if (i < N && radii[i] > 0) {
         vis = true;
-        const float p[3] = {means[3 * (size_t)i], means[3 * (size_t)i + 1], means[3 * (size_t)i + 2]};
+        const float p[3] = {sh_mean[3 * (size_t)i], sh_mean[3 * (size_t)i + 1],
+                            sh_mean[3 * (size_t)i + 2]};
         sh_rest_basis(P->cam_pos, p, s_b[tid]);
         const float* ga = grad_acc + (size_t)i * kGradStride;
         s_c[tid][0] = ga[0];
@@ -881,13 +885,19 @@ int launch_project_backward_adam(const StepParams* P, int N, int degrees_to_use_
     const int nb = rest_bases_updated(degrees_to_use_host, rest_stride_host);
     AdamPtrs A2 = A;
     int launches = 1;
+    bool joined = false;
+    const SideStream& side = engine_side();
     if (A.numel[4] > 0 && nb > 0) {
         const int grid = (N + kRestThreads - 1) / kRestThreads;
         const int used = nb * 3;
-#define MSP_REST(RS)                                                                           \
-    rest_adam_kernel<RS><<<grid, kRestThreads, 0, s>>>(P, N, B.proj.radii, B.grad_acc,       \
-                                                       A.param[0], A.param[4], A.exp_avg[4],  \
-                                                       A.exp_avg_sq[4], used)
+        // fork: the side stream starts after everything queued so far
+        const bool forked = cudaEventRecord(side.fork, s) == cudaSuccess &&
+                            cudaStreamWaitEvent(side.stream, side.fork, 0) == cudaSuccess;
+        const cudaStream_t rs = forked ? side.stream : s;
+#define MSP_REST(RS)                                                                            \
+    rest_adam_kernel<RS><<<grid, kRestThreads, 0, rs>>>(P, N, B.proj.radii, B.grad_acc,       \
+                                                        B.proj.sh_mean, A.param[4], A.exp_avg[4], \
+                                                        A.exp_avg_sq[4], used)
         bool done = true;
         switch (rest_stride_host) {
             case 45: MSP_REST(45); break;
@@ -901,10 +911,16 @@ int launch_project_backward_adam(const StepParams* P, int N, int degrees_to_use_
             A2.numel[4] = 0;  // the rest group is done
             launches++;
         }
+        // join: what the engine stream queues after this stage waits for it
+        if (forked) {
+            if (cudaEventRecord(side.join, side.stream) == cudaSuccess) joined = true;
+            else cudaStreamSynchronize(side.stream);
+        }
     }
     const int grid = (N + kBwdThreads - 1) / kBwdThreads;
     project_backward_adam_kernel<false><<<grid, kBwdThreads, 0, s>>>(
         P, N, B.proj.radii, B.proj.conic_op, B.grad_acc, A2, St, GradOut{}, nb);
+    if (joined) cudaStreamWaitEvent(s, side.join, 0);
     return launches;
 }
 

@@ -267,6 +267,11 @@ project_forward_kernel(const StepParams* __restrict__ P, int N, const float* __r
     float dcv[3] = {s_dc[3 * tid], s_dc[3 * tid + 1], s_dc[3 * tid + 2]};
     sh_to_color(P->degrees_to_use, d0 * dn, d1 * dn, d2 * dn, dcv, s_rest + tid * rest_stride, col);
     out.rgb[i] = make_float4(col[0], col[1], col[2], 0.f);
+    if (ZERO_GRADS) {  // training: the SH-rest Adam's copy of the mean
+        out.sh_mean[3 * (size_t)i] = p[0];
+        out.sh_mean[3 * (size_t)i + 1] = p[1];
+        out.sh_mean[3 * (size_t)i + 2] = p[2];
+    }
     const int tx_n = P->tiles_x;
     for (int ty = y0; ty < y1; ty++)
         for (int tx = x0; tx < x1; tx++) atomicAdd(&tile_count[(ty * tx_n + tx) * kCountPitch], 1);
