@@ -19,6 +19,9 @@ constexpr int kSortThreads = MSP_SORT_THREADS;
 #ifndef MSP_RADIX_KEEP_PEERS
 #define MSP_RADIX_KEEP_PEERS 0
 #endif
+#ifndef MSP_SCATTER_ROUNDS
+#define MSP_SCATTER_ROUNDS 2
+#endif
 #ifndef MSP_SORT_MIN_BLOCKS
 #define MSP_SORT_MIN_BLOCKS 8
 #endif
@@ -435,7 +438,8 @@ scatter_kernel(const StepParams* __restrict__ P, int N, const int* __restrict__ 
     const int tx_n = P->tiles_x;
     // kRounds rounds of 32 pairs per iteration: their atomics are issued
     // together, so a lane waits for one atomic latency per kRounds pairs.
-    constexpr int kRounds = 4;
+    // Measured at C1: 2 rounds beat 4 and 8 (fewer registers, more warps).
+    constexpr int kRounds = MSP_SCATTER_ROUNDS;
     for (int p0 = 0; p0 < total; p0 += 32 * kRounds) {
         int tile[kRounds];
         unsigned long long kv[kRounds];
