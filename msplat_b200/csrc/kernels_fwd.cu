@@ -19,8 +19,11 @@ constexpr int kSortThreads = MSP_SORT_THREADS;
 #ifndef MSP_RADIX_KEEP_PEERS
 #define MSP_RADIX_KEEP_PEERS 0
 #endif
+#ifndef MSP_FWD_MIN_BLOCKS
+#define MSP_FWD_MIN_BLOCKS 6
+#endif
 #ifndef MSP_SCATTER_ROUNDS
-#define MSP_SCATTER_ROUNDS 2
+#define MSP_SCATTER_ROUNDS 1
 #endif
 #ifndef MSP_SORT_MIN_BLOCKS
 #define MSP_SORT_MIN_BLOCKS 8
@@ -438,7 +441,9 @@ scatter_kernel(const StepParams* __restrict__ P, int N, const int* __restrict__ 
     const int tx_n = P->tiles_x;
     // kRounds rounds of 32 pairs per iteration: their atomics are issued
     // together, so a lane waits for one atomic latency per kRounds pairs.
-    // Measured at C1: 2 rounds beat 4 and 8 (fewer registers, more warps).
+    // Measured at C1 (bin+sort): 1 round 0.195 ms, 2: 0.197, 3: 0.200,
+    // 4: 0.202, 8: 0.206 -- fewer registers and more warps beat more
+    // atomics in flight per warp.
     constexpr int kRounds = MSP_SCATTER_ROUNDS;
     for (int p0 = 0; p0 < total; p0 += 32 * kRounds) {
         int tile[kRounds];
@@ -839,8 +844,10 @@ void launch_sort_tiles(const StepParams* P, int num_tiles, const Buffers& B, cud
 // (tile_may_contribute), which changes no result: those never pass the
 // per-pixel tests.
 // ---------------------------------------------------------------------------
+// Six resident CTAs per SM (40 registers): 0.377 ms at C1 against 0.385
+// with 47 registers (5 CTAs) and 0.379 with 32 (8 CTAs, spilling).
 template <bool CHUNKED>
-__global__ void __launch_bounds__(kTileThreads)
+__global__ void __launch_bounds__(kTileThreads, MSP_FWD_MIN_BLOCKS)
 raster_forward_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
                       const int* __restrict__ order, const int* __restrict__ ids,
                       const float2* __restrict__ g_xy,
