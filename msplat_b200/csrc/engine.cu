@@ -9,6 +9,7 @@
 
 #include <algorithm>
 #include <cstdarg>
+#include <cstddef>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -48,6 +49,16 @@ constexpr int kStages = 6;
 static const char* kStageNames[kStages] = {"proj_sh_fwd", "bin_sort", "rast_fwd",
                                            "loss_fwd_bwd", "rast_bwd", "proj_bwd_adam"};
 
+// The step's parameters and, after them, the step's counters: one upload per
+// step sets the parameters and zeroes the counters, one readback returns
+// them (loss sum, error bits, intersections).
+struct alignas(64) ParamSlot {
+    StepParams p;
+    alignas(64) int counters[16];
+};
+constexpr int kCtrLoss = 0, kCtrErr = 4, kCtrIsect = 8, kCtrRead = 12;
+static_assert(offsetof(ParamSlot, p) == 0, "the parameters lead the slot");
+
 struct Engine {
     bool ready = false;
     int device = -1;
@@ -57,16 +68,17 @@ struct Engine {
     // allocated sizes
     long long cap_N = 0, cap_grad_N = 0, cap_pix = 0, cap_T = 0, cap_isect = 0, cap_chunk = 0;
     Buffers B{};
-    StepParams* d_params = nullptr;
-    StepParams* h_ring = nullptr;
+    ParamSlot* d_slot = nullptr;
+    StepParams* d_params = nullptr;  // &d_slot->p
+    ParamSlot* h_ring = nullptr;
     cudaEvent_t ring_ev[kRing] = {};
     int ring_pos = 0;
-    // readback
-    float* h_loss = nullptr;    // pinned [2]: loss_sum, isect total (as float bits unused)
-    int* h_misc = nullptr;      // pinned [2]: err, isect total
+    // readback: pinned copy of the counters (kCtrRead ints)
+    int* h_ctr = nullptr;
     cudaEvent_t readback_ev = nullptr;
     SideStream side{};
     bool readback_pending = false;
+    bool readback_has_loss = false;  // a training step's readback (a render has no loss)
     float last_loss = 0.f;
     double last_loss_scale = 1.0;
     long long growth_isect = 0;  // requested capacity after an overflow
@@ -83,6 +95,12 @@ struct Engine {
 };
 
 static Engine g;
+// Device address of the counters that follow the parameters in d_slot.
+static int* d_counters()
+{
+    return reinterpret_cast<int*>(reinterpret_cast<char*>(g.d_slot) + offsetof(ParamSlot, counters));
+}
+
 static std::mutex g_mu;
 
 static int init_engine()
@@ -99,22 +117,22 @@ static int init_engine()
     // A blocking stream: ordered with the legacy default stream, so callers
     // that never pick a stream still see their own prior work completed.
     MSP_CUDA(cudaStreamCreateWithFlags(&g.own_stream, cudaStreamDefault));
-    MSP_CUDA(cudaMalloc(&g.d_params, sizeof(StepParams)));
-    MSP_CUDA(cudaMallocHost(&g.h_ring, sizeof(StepParams) * kRing));
+    MSP_CUDA(cudaMalloc(&g.d_slot, sizeof(ParamSlot)));
+    MSP_CUDA(cudaMemset(g.d_slot, 0, sizeof(ParamSlot)));
+    g.d_params = reinterpret_cast<StepParams*>(g.d_slot);
+    MSP_CUDA(cudaMallocHost(&g.h_ring, sizeof(ParamSlot) * kRing));
     for (int i = 0; i < kRing; i++) MSP_CUDA(cudaEventCreateWithFlags(&g.ring_ev[i], cudaEventDisableTiming));
-    MSP_CUDA(cudaMallocHost(&g.h_loss, sizeof(float) * 4));
-    MSP_CUDA(cudaMallocHost(&g.h_misc, sizeof(int) * 4));
-    memset(g.h_loss, 0, sizeof(float) * 4);
-    memset(g.h_misc, 0, sizeof(int) * 4);
+    MSP_CUDA(cudaMallocHost(&g.h_ctr, sizeof(int) * kCtrRead));
+    memset(g.h_ctr, 0, sizeof(int) * kCtrRead);
     MSP_CUDA(cudaEventCreateWithFlags(&g.readback_ev, cudaEventDisableTiming));
     MSP_CUDA(cudaStreamCreateWithFlags(&g.side.stream, cudaStreamNonBlocking));
     MSP_CUDA(cudaEventCreateWithFlags(&g.side.fork, cudaEventDisableTiming));
     MSP_CUDA(cudaEventCreateWithFlags(&g.side.join, cudaEventDisableTiming));
     for (int s = 0; s <= kStages; s++)
         for (int r = 0; r < kRing; r++) MSP_CUDA(cudaEventCreate(&g.st_ev[s][r]));
-    MSP_CUDA(cudaMalloc(&g.B.loss_sum, sizeof(float) * 4));
-    MSP_CUDA(cudaMalloc(&g.B.err, sizeof(int) * 4));
-    MSP_CUDA(cudaMemset(g.B.err, 0, sizeof(int) * 4));
+    g.B.loss_sum = reinterpret_cast<float*>(d_counters() + kCtrLoss);
+    g.B.err = d_counters() + kCtrErr;
+    g.B.isect_total = d_counters() + kCtrIsect;
     MSP_CUDA(cudaDeviceSynchronize());
     g.ready = true;
     return MSPLAT_OK;
@@ -148,9 +166,11 @@ static void free_buffers()
         if (p) cudaFree(p);
     float* ls = B.loss_sum;
     int* er = B.err;
+    int* it = B.isect_total;
     B = Buffers{};
     B.loss_sum = ls;
     B.err = er;
+    B.isect_total = it;
     g.cap_N = g.cap_grad_N = g.cap_pix = g.cap_T = g.cap_isect = g.cap_chunk = 0;
 }
 
@@ -233,11 +253,16 @@ static void poll_readback(bool wait)
         return;
     }
     g.readback_pending = false;
-    g.last_loss = (float)((double)g.h_loss[0] * g.last_loss_scale);
-    if (g.h_misc[0] & kErrStageTimeout)
+    if (g.readback_has_loss) {
+        float loss_sum;
+        memcpy(&loss_sum, &g.h_ctr[kCtrLoss], sizeof(float));
+        g.last_loss = (float)((double)loss_sum * g.last_loss_scale);
+    }
+    const int err = g.h_ctr[kCtrErr];
+    if (err & kErrStageTimeout)
         fprintf(stderr, "msplat: a shared-memory bulk copy timed out; the step is incomplete\n");
-    if (g.h_misc[0] & kErrIsectOverflow) {
-        const long long need = (long long)g.h_misc[1];
+    if (err & kErrIsectOverflow) {
+        const long long need = (long long)g.h_ctr[kCtrIsect];
         if (need > g.growth_isect) {
             g.growth_isect = need + need / 4;
             fprintf(stderr, "msplat: intersection buffer overflow (%lld > %lld); growing\n", need,
@@ -291,8 +316,9 @@ static int upload_params(const StepParams& p, cudaStream_t st)
     const int slot = g.ring_pos;
     g.ring_pos = (g.ring_pos + 1) % kRing;
     MSP_CUDA(cudaEventSynchronize(g.ring_ev[slot]));
-    g.h_ring[slot] = p;
-    MSP_CUDA(cudaMemcpyAsync(g.d_params, &g.h_ring[slot], sizeof(StepParams), cudaMemcpyHostToDevice, st));
+    g.h_ring[slot].p = p;
+    memset(g.h_ring[slot].counters, 0, sizeof(g.h_ring[slot].counters));
+    MSP_CUDA(cudaMemcpyAsync(g.d_slot, &g.h_ring[slot], sizeof(ParamSlot), cudaMemcpyHostToDevice, st));
     MSP_CUDA(cudaEventRecord(g.ring_ev[slot], st));
     return MSPLAT_OK;
 }
@@ -358,12 +384,11 @@ static int run_forward(const StepParams& p, const float* means, const float* sca
 
 static int queue_readback(cudaStream_t st, const StepParams& p)
 {
-    MSP_CUDA(cudaMemcpyAsync(g.h_loss, g.B.loss_sum, sizeof(float), cudaMemcpyDeviceToHost, st));
-    MSP_CUDA(cudaMemcpyAsync(g.h_misc, g.B.err, sizeof(int), cudaMemcpyDeviceToHost, st));
-    MSP_CUDA(cudaMemcpyAsync(g.h_misc + 1, g.B.tile_offset + p.num_tiles, sizeof(int),
+    MSP_CUDA(cudaMemcpyAsync(g.h_ctr, d_counters(), sizeof(int) * kCtrRead,
                              cudaMemcpyDeviceToHost, st));
     MSP_CUDA(cudaEventRecord(g.readback_ev, st));
     g.readback_pending = true;
+    g.readback_has_loss = true;
     g.last_loss_scale = 1.0 / (3.0 * (double)p.img_w * (double)p.img_h);
     return MSPLAT_OK;
 }
@@ -540,8 +565,6 @@ static int train_common(const char* who, int num_points, float* means3d, float* 
     p.capacity = g.cap_isect;
     StageMarks tm = begin_timing();
     if ((rc = upload_params(p, st))) return rc;
-    MSP_CUDA(cudaMemsetAsync(g.B.err, 0, sizeof(int), st));
-    MSP_CUDA(cudaMemsetAsync(g.B.loss_sum, 0, sizeof(float), st));
     if ((rc = run_forward(p, means3d, scales, quats, features_dc, features_rest, opacities, true,
                           tm, st)))
         return rc;
@@ -784,16 +807,15 @@ int msplat_render(int num_points, const float* means3d, const float* scales, flo
     p.capacity = g.cap_isect;
     StageMarks tm = begin_timing();
     if ((rc = upload_params(p, st))) return rc;
-    MSP_CUDA(cudaMemsetAsync(g.B.err, 0, sizeof(int), st));
     if ((rc = run_forward(p, means3d, scales, quats, features_dc, features_rest, opacities, false,
                           tm, st)))
         return rc;
     for (int s = 3; s <= 6; s++) tm.mark(s, st);
-    MSP_CUDA(cudaMemcpyAsync(g.h_misc, g.B.err, sizeof(int), cudaMemcpyDeviceToHost, st));
-    MSP_CUDA(cudaMemcpyAsync(g.h_misc + 1, g.B.tile_offset + p.num_tiles, sizeof(int),
+    MSP_CUDA(cudaMemcpyAsync(g.h_ctr, d_counters(), sizeof(int) * kCtrRead,
                              cudaMemcpyDeviceToHost, st));
     MSP_CUDA(cudaEventRecord(g.readback_ev, st));
     g.readback_pending = true;
+    g.readback_has_loss = false;
     if (out_img) *out_img = g.B.out_img;
     return MSPLAT_OK;
 }
@@ -812,7 +834,7 @@ long long msplat_num_intersections(void)
     if (!g.ready) return 0;
     cudaStreamSynchronize(g.stream());
     poll_readback(true);
-    return (long long)g.h_misc[1];
+    return (long long)g.h_ctr[kCtrIsect];
 }
 
 int msplat_device_errors(void)
@@ -821,7 +843,7 @@ int msplat_device_errors(void)
     if (!g.ready) return 0;
     cudaStreamSynchronize(g.stream());
     poll_readback(true);
-    return g.h_misc[0];
+    return g.h_ctr[kCtrErr];
 }
 
 int msplat_debug_buffer(const char* name, void** dev_ptr, long long* count)

@@ -78,6 +78,7 @@ struct Buffers {
     float* after_C;        // [K*H*W*3]
     float* loss_sum;       // [1]
     int* err;              // [1]
+    int* isect_total;      // [1] intersections of the view (scan output), or null
 };
 
 // Device pointers of the optimiser, one entry per group.

@@ -320,7 +320,8 @@ __device__ __forceinline__ int order_bucket(int count) { return min(count >> 1, 
 
 __global__ void __launch_bounds__(1024)
 scan_tiles_kernel(const StepParams* __restrict__ P, int T, const int* __restrict__ count,
-                  int* __restrict__ offset, int* __restrict__ order, int* __restrict__ err)
+                  int* __restrict__ offset, int* __restrict__ order, int* __restrict__ err,
+                  int* __restrict__ isect_total)
 {
     __shared__ int s_warp[32];
     __shared__ int s_bucket[kOrderBuckets];
@@ -356,6 +357,7 @@ scan_tiles_kernel(const StepParams* __restrict__ P, int T, const int* __restrict
     }
     if (tid == 1023) {
         offset[T] = run;
+        if (isect_total) *isect_total = run;
         if ((long long)run > P->capacity) atomicOr(err, kErrIsectOverflow);
     }
     // CTA order of the per-tile kernels: tiles by intersection count, largest
@@ -399,7 +401,7 @@ scan_tiles_kernel(const StepParams* __restrict__ P, int T, const int* __restrict
 void launch_scan_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s)
 {
     scan_tiles_kernel<<<1, 1024, 0, s>>>(P, num_tiles, B.tile_count, B.tile_offset, B.tile_order,
-                                         B.err);
+                                         B.err, B.isect_total);
 }
 
 // ---------------------------------------------------------------------------
