@@ -137,9 +137,9 @@ def peaks() -> dict:
 # (rest_adam_kernel + project_backward_adam_kernel) and warp instructions of
 # the issue-bound kernels.  Instruction counts vary a little with the view;
 # the capture's view stands for all.
-C1_OPT_STAGE_TRAFFIC = 510137344 + 346369792 + 235895040 + 117955328
-C1_WARP_INSTR = {"rast_fwd": ("raster_forward_kernel<0>", 374177594),
-                 "rast_bwd": ("raster_backward_kernel<0,2>", 572705112),
+C1_OPT_STAGE_TRAFFIC = 510080000 + 344294912 + 235875840 + 117640448
+C1_WARP_INSTR = {"rast_fwd": ("raster_forward_kernel<0>", 364023216),
+                 "rast_bwd": ("raster_backward_kernel<0,2>", 564315330),
                  "loss_fwd_bwd": ("ssim_loss_fused_kernel", 105998350)}
 SM_COUNT, ISSUE_PER_SM_CLK = 148, 4
 
