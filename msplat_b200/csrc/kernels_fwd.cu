@@ -16,8 +16,8 @@ constexpr int kSortThreads = MSP_SORT_THREADS;
 #ifndef MSP_SORT_RADIX
 #define MSP_SORT_RADIX 1
 #endif
-#ifndef MSP_RADIX_KEEP_PEERS
-#define MSP_RADIX_KEEP_PEERS 0
+#ifndef MSP_RADIX_SPLIT
+#define MSP_RADIX_SPLIT 1
 #endif
 #ifndef MSP_FWD_MIN_BLOCKS
 #define MSP_FWD_MIN_BLOCKS 6
@@ -624,19 +624,25 @@ __device__ __forceinline__ int merge_path(const unsigned long long* a, int la,
 // (depth, id) keys instead; both give the order of the 64-bit keys.
 constexpr int kRadixWarps = kSortThreads / 32;
 constexpr int kRadixChunks = kSortRun / kSortThreads;  // 32-key chunks per warp at most
+// Each warp's keys form kRadixSplit consecutive sub-ranges with their own
+// digit counters, so its scatter runs kRadixSplit independent chains of
+// counter reads and updates instead of one.
+constexpr int kRadixSplit = MSP_RADIX_SPLIT;
+constexpr int kRadixCols = kRadixWarps * kRadixSplit;
+static_assert(kRadixChunks % kRadixSplit == 0, "sub-ranges of whole chunks");
 
 struct RadixSmem {
     unsigned key[kSortRun];
     int val[kSortRun];
-    int hist[256 * kRadixWarps];  // [digit * kRadixWarps + warp]
+    int hist[256 * kRadixCols];  // [digit * kRadixCols + column], column = warp * split + sub-range
     int wsum[kRadixWarps];
     unsigned red[2 * kRadixWarps];
 };
 
-// Exclusive prefix sum of S.hist in place (256 * kRadixWarps counters).
+// Exclusive prefix sum of S.hist in place (256 * kRadixCols counters).
 __device__ __forceinline__ void radix_scan(RadixSmem& S)
 {
-    constexpr int kPer = 256 * kRadixWarps / kSortThreads;
+    constexpr int kPer = 256 * kRadixCols / kSortThreads;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     int c[kPer];
     int sum = 0;
@@ -665,30 +671,33 @@ __device__ __forceinline__ void radix_scan(RadixSmem& S)
 
 // Returns false (and writes nothing) when two keys of the tile have equal
 // depths; otherwise writes the ids in ascending (depth, id) order.
+// Register r of a lane holds element w0 + ((r % split) * cv + r / split) * 32
+// + lane: sub-range r % split, its chunk r / split.
 __device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __restrict__ keys, int n,
                                                 RadixSmem& S, int* __restrict__ out_ids)
 {
+    constexpr int V = kRadixSplit;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const unsigned lt = (1u << lane) - 1u;
     const int C = (n + kSortThreads - 1) / kSortThreads;  // chunks per warp
-    const int w0 = warp * C * 32;                          // this warp's first element
+    const int cv = (C + V - 1) / V;                        // chunks per sub-range
+    const int nr = cv * V;                                 // registers in use
+    const int w0 = warp * nr * 32;                         // this warp's first element
+    auto elem = [&](int r) { return w0 + ((r % V) * cv + r / V) * 32 + lane; };
     unsigned k[kRadixChunks];
     int v[kRadixChunks];
-#if MSP_RADIX_KEEP_PEERS
-    unsigned pe[kRadixChunks];
-#endif
     unsigned ko = 0u, ka = ~0u;
 #pragma unroll
-    for (int c = 0; c < kRadixChunks; c++) {
-        k[c] = ~0u;  // padding sorts last and stays behind equal real keys
-        v[c] = 0;
-        const int e = w0 + c * 32 + lane;
-        if (c < C && e < n) {
+    for (int r = 0; r < kRadixChunks; r++) {
+        k[r] = ~0u;  // padding sorts last and stays behind equal real keys
+        v[r] = 0;
+        const int e = elem(r);
+        if (r < nr && e < n) {
             const unsigned long long kv = keys[e];
-            k[c] = (unsigned)(kv >> 32);
-            v[c] = (int)(unsigned)(kv & 0xffffffffull);
-            ko |= k[c];
-            ka &= k[c];
+            k[r] = (unsigned)(kv >> 32);
+            v[r] = (int)(unsigned)(kv & 0xffffffffull);
+            ko |= k[r];
+            ka &= k[r];
         }
     }
     ko = __reduce_or_sync(0xffffffffu, ko);
@@ -708,65 +717,66 @@ __device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __rest
     if (varying == 0u) return false;  // n >= 2 equal depths
     for (int shift = 0; shift < 32; shift += 8) {
         if (((varying >> shift) & 0xffu) == 0u) continue;
-        for (int d = lane; d < 256; d += 32) S.hist[d * kRadixWarps + warp] = 0;
+        for (int i = lane; i < 256 * V; i += 32)
+            S.hist[(i / V) * kRadixCols + warp * V + (i % V)] = 0;
         __syncwarp();
         // counts need no order: shared-memory atomics, no chain between chunks
 #pragma unroll
-        for (int c = 0; c < kRadixChunks; c++) {
-            if (c >= C) break;
-            const unsigned d = (k[c] >> shift) & 0xffu;
-#if MSP_RADIX_KEEP_PEERS
-            pe[c] = __match_any_sync(0xffffffffu, d);
-            if ((pe[c] & lt) == 0u) atomicAdd(&S.hist[d * kRadixWarps + warp], __popc(pe[c]));
-#else
-            atomicAdd(&S.hist[d * kRadixWarps + warp], 1);
-#endif
+        for (int r = 0; r < kRadixChunks; r++) {
+            if (r >= nr) break;
+            const unsigned d = (k[r] >> shift) & 0xffu;
+            atomicAdd(&S.hist[d * kRadixCols + warp * V + r % V], 1);
         }
         __syncthreads();
         radix_scan(S);
         __syncthreads();
+        // V independent chains: chunk r0 / V of every sub-range at once
 #pragma unroll
-        for (int c = 0; c < kRadixChunks; c++) {
-            if (c >= C) break;
-            const unsigned d = (k[c] >> shift) & 0xffu;
-#if MSP_RADIX_KEEP_PEERS
-            const unsigned peers = pe[c];
-#else
-            const unsigned peers = __match_any_sync(0xffffffffu, d);
-#endif
-            const int slot = d * kRadixWarps + warp;
-            const int base = S.hist[slot];
+        for (int r0 = 0; r0 < kRadixChunks; r0 += V) {
+            if (r0 >= nr) break;
+            unsigned peers[V];
+            int slot[V], base[V];
+#pragma unroll
+            for (int u = 0; u < V; u++) {
+                const unsigned d = (k[r0 + u] >> shift) & 0xffu;
+                peers[u] = __match_any_sync(0xffffffffu, d);
+                slot[u] = d * kRadixCols + warp * V + u;
+                base[u] = S.hist[slot[u]];
+            }
             __syncwarp();
-            if ((peers & lt) == 0u) S.hist[slot] = base + __popc(peers);
-            const int pos = base + __popc(peers & lt);
-            S.key[pos] = k[c];
-            S.val[pos] = v[c];
+#pragma unroll
+            for (int u = 0; u < V; u++) {
+                if ((peers[u] & lt) == 0u) S.hist[slot[u]] = base[u] + __popc(peers[u]);
+                const int pos = base[u] + __popc(peers[u] & lt);
+                S.key[pos] = k[r0 + u];
+                S.val[pos] = v[r0 + u];
+            }
             __syncwarp();
         }
         __syncthreads();
 #pragma unroll
-        for (int c = 0; c < kRadixChunks; c++) {
-            if (c >= C) break;
-            const int e = w0 + c * 32 + lane;
-            k[c] = S.key[e];
-            v[c] = S.val[e];
+        for (int r = 0; r < kRadixChunks; r++) {
+            if (r >= nr) break;
+            const int e = elem(r);
+            k[r] = S.key[e];
+            v[r] = S.val[e];
         }
     }
     // S.key holds the sorted depths (at least one pass ran): any equal
     // neighbours among the real keys?
     bool tie = false;
 #pragma unroll
-    for (int c = 0; c < kRadixChunks; c++) {
-        if (c >= C) break;
-        const int e = w0 + c * 32 + lane;
-        if (e + 1 < n && k[c] == S.key[e + 1]) tie = true;
+    for (int r = 0; r < kRadixChunks; r++) {
+        if (r >= nr) break;
+        const int e = elem(r);
+        if (e + 1 < n && k[r] == S.key[e + 1]) tie = true;
     }
     if (__syncthreads_or(tie)) return false;
 #pragma unroll
-    for (int c = 0; c < kRadixChunks; c++) {
-        if (c >= C) break;
-        const int e = w0 + c * 32 + lane;
-        if (e < n) out_ids[e] = v[c];
+    for (int r = 0; r < kRadixChunks; r++) {
+        if (r >= nr) break;
+        const int e = elem(r);
+        if (e < n) out_ids[e] = v[r];
     }
     return true;
 }
