@@ -102,6 +102,34 @@ def test_big_tiles_merge_sort_bitexact():
     harness.assert_forward_bitexact(run, eng, cs)
 
 
+@pytest.mark.parametrize("levels", [1, 3])
+def test_tied_depths_sort_bitexact(levels):
+    # Every mean on one of `levels` planes facing the camera: most tiles hold
+    # many keys with the same depth, whose order is the ids' (the radix sort
+    # of depths reports the ties and those tiles take the bitonic sort of the
+    # full (depth, id) keys).  One level: every key of a tile ties.
+    g, cs = _scene(20_000, 640, 480, seed=9, log_mu=math.log(0.03))
+    planes = np.linspace(-0.2, 0.2, levels).astype(np.float32)
+    g.means[:, 2] = planes[np.arange(g.n) % levels]
+    run, eng = _render_pair(g, cs)
+    counts = np.diff(run.tile_bins.reshape(-1, 2), axis=1)[:, 0]
+    assert run.P.k_max == 1 and (counts > 128).sum() > 100
+    harness.assert_forward_bitexact(run, eng, cs)
+    depths = run.depths[run.radii > 0]
+    assert len(np.unique(depths)) == levels
+
+
+def test_distinct_depths_radix_sizes_bitexact():
+    # Tiles from a few keys up to the 2,048 the shared-memory sorts hold
+    # (radix above 128 keys, bitonic at or below), distinct depths.
+    g, cs = _scene(60_000, 640, 480, seed=10, log_mu=math.log(0.025), log_sigma=0.5)
+    run, eng = _render_pair(g, cs)
+    counts = np.diff(run.tile_bins.reshape(-1, 2), axis=1)[:, 0]
+    assert 1024 < run.S.max_tile_count <= 2048
+    assert ((counts > 0) & (counts <= 128)).sum() > 100 and (counts > 1024).sum() > 100
+    harness.assert_forward_bitexact(run, eng, cs)
+
+
 def test_render_all_culled():
     g, cs = _scene(1_000, 64, 64, seed=7, distance=-3.0)  # everything behind the camera
     run, eng = _render_pair(g, cs)
