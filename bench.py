@@ -2,6 +2,7 @@
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   python bench.py --config C3 [--iterations 7000]     (training-run report)
+  python bench.py --config C4 [--gpus N] [--steps K]  (batched views, 8 per step)
 
 Workload (N=1): BASELINE.json config 1 -- 1,000,000 seeded synthetic
 Gaussians rendered at 1297x840 from 16 cameras on a radius-4 sphere, the
@@ -18,9 +19,17 @@ upload overlaps the previous step) and the loss read back every step;
 wall clock over K steps, median of three runs after W untimed ones.
 
 Under torchrun (N > 1) every rank trains its own view of the same scene
-each step and the ranks exchange the 59-float-per-Gaussian gradient with an
-NCCL all-reduce before Adam (msplat_b200.multigpu); per-GPU work is fixed,
-so scaling is weak.
+each step and the ranks combine their gradients before Adam
+(msplat_b200.multigpu): by default one kernel per rank sums its shard of the
+gradients over NVLink peer memory, applies Adam and writes the shard into
+every replica (--dp-mode nccl: an NCCL all-reduce, then Adam on every
+replica); per-GPU work is fixed, so scaling is weak.
+
+--config C4 is BASELINE.json's batched-view configuration: 6,000,000
+Gaussians, a batch of 8 views at 1920x1080 per step, each of N in
+{1, 2, 4, 8} GPUs training 8/N of them (gradients accumulated per rank),
+one exchange and one Adam update per step; the batch is fixed, so scaling
+is strong.  It reports views/s and the exchange's time and NVLink bytes.
 
 --impl reference times the reference's CPU implementation of the path (the
 oracle port, or oracle/_ref when the reference was compiled) on the host
@@ -58,10 +67,11 @@ def parse():
                     help="N > 1: optimiser over NVLink peer memory, or NCCL all-reduce")
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the timed CPU oracle sample (profiling runs)")
-    ap.add_argument("--config", choices=("C1", "C3"), default="C1",
+    ap.add_argument("--config", choices=("C1", "C3", "C4"), default="C1",
                     help="C1 (default): the headline step benchmark; C3: BASELINE.json config 3, "
                          "a 7000-iteration training run with densification, reporting steps/s "
-                         "and held-out PSNR/SSIM (one GPU)")
+                         "and held-out PSNR/SSIM (one GPU); C4: BASELINE.json config 4, "
+                         "6M Gaussians, 8 views of 1920x1080 per step over N GPUs")
     ap.add_argument("--iterations", type=int, default=7000, help="C3: training iterations")
     return ap.parse_args()
 
@@ -163,14 +173,37 @@ def issue_rooflines(stage_ms: dict, sm_mhz: float) -> list:
 
 # ---------------------------------------------------------------------------
 
-def build_workload(device_gt: bool = True):
+def scene(config: str, seed: int = 0):
+    """synthetic.scene(config, seed=seed), kept as .npz files in the directory
+    MSPLAT_BENCH_SCENE_CACHE names (when set) so that several runs in one
+    session draw each large scene once; a file is written whole under a
+    temporary name and then renamed, so concurrent ranks never read a
+    partial one."""
+    from msplat_b200 import synthetic
+    cache = os.environ.get("MSPLAT_BENCH_SCENE_CACHE")
+    if not cache:
+        return synthetic.scene(config, seed=seed)
+    path = os.path.join(cache, f"{config}_seed{seed}.npz")
+    _, cams = synthetic.scene(config, n=1, seed=seed)
+    if os.path.exists(path):
+        with np.load(path) as z:
+            return synthetic.Gaussians(*[z[f"g{i}"] for i in range(6)]), cams
+    g, cams = synthetic.scene(config, seed=seed)
+    os.makedirs(cache, exist_ok=True)
+    tmp = f"{path}.{os.getpid()}.tmp.npz"
+    np.savez(tmp, **{f"g{i}": a for i, a in enumerate(g.groups())})
+    os.replace(tmp, path)
+    return g, cams
+
+
+def build_workload(config: str = CONFIG):
     import torch
-    from msplat_b200 import camera, engine, synthetic
-    g, cams = synthetic.scene(CONFIG)
+    from msplat_b200 import camera, engine
+    g, cams = scene(config)
     setups = [camera.prepare_camera(c, step=10**9, sh_degree=3, sh_degree_interval=1000,
                                     rest_bases=15) for c in cams]
     # targets: renders of an independent seed-1 scene, one per camera
-    tgt, _ = synthetic.scene(CONFIG, seed=1)
+    tgt, _ = scene(config, seed=1)
     tmodel = engine.GaussianModel(tgt.groups())
     gts = []
     h, w = setups[0].height, setups[0].width
@@ -586,6 +619,129 @@ def run_c3(args) -> dict:
     }
 
 
+def exchange_bytes(n: int, world: int, compact: bool, mode: str) -> int:
+    """Bytes one rank moves over NVLink per step in the optimiser exchange.
+    peer: it reads its 1/world shard of every other rank's gradient buffer
+    (60 floats per Gaussian, or 15 in the compact layout) and writes its
+    updated shard of the 59 parameter floats into every other replica.
+    nccl: a ring all-reduce of the 60-float buffer sends 2 (world-1)/world of
+    it per rank."""
+    if world <= 1:
+        return 0
+    share = (world - 1) / world
+    if mode == "nccl":
+        return int(2 * share * n * 60 * 4)
+    return int(share * n * ((15 if compact else 60) + 59) * 4)
+
+
+def run_c4(args, rank: int, world: int) -> dict:
+    """BASELINE.json config 4, multi-GPU batched views: 6,000,000 Gaussians
+    drawn as in config 1 (seed 0), 8 cameras on the radius-4 sphere at
+    1920x1080, targets rendered from an independent seed-1 scene of the same
+    size.  A step trains the batch of all 8 views: rank r of N takes views
+    r, r + N, ... (8/N of them), accumulating their gradients of the batch's
+    mean loss; then one exchange over NVLink and one Adam update
+    (multigpu.DataParallel.train_views; on one GPU multigpu.train_batch).
+    Timed on the device, max over ranks; the exchange is timed in a second
+    pass over the same number of steps with CUDA events around it."""
+    import torch
+    from msplat_b200 import _lib, engine, multigpu
+    batch = 8
+    if world not in (1, 2, 4, 8):
+        raise SystemExit("C4 runs its batch of 8 views on 1, 2, 4 or 8 GPUs")
+    vpr = batch // world
+    lib = _lib.load()
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    engine.bind_stream()
+    g, setups, gts, model = build_workload("C4")
+    mine = [rank + k * world for k in range(vpr)]
+    cams = [setups[v] for v in mine]
+    tgts = [gts[v] for v in mine]
+    dist = None
+    if world == 1:
+        grad = torch.empty(multigpu.grad_floats(model.n, model.rest_bases), dtype=torch.float32,
+                           device="cuda")
+
+        def one_step():
+            multigpu.train_batch(model, cams, tgts, grad)
+    else:
+        dist = multigpu.DataParallel(model, rank, world, mode=args.dp_mode, views_per_rank=vpr)
+
+        def one_step():
+            dist.train_views(cams, tgts)
+    steps = args.steps
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    lib.msplat_kernel_launches(1)
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(steps):
+        one_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    launches = int(lib.msplat_kernel_launches(1))
+    ms = e0.elapsed_time(e1)
+    ms_max = dist.max_over_ranks(ms) if dist is not None else ms
+    # second pass: the exchange (peer kernel or all-reduce) plus Adam, timed
+    # per step between the rank's last backward and the step's end
+    ex_ms = None
+    if dist is not None:
+        dist.barrier()
+        torch.cuda.synchronize()
+        evs = []
+        for _ in range(steps):
+            model.step_count += 1
+            multigpu.accumulate_views(dist.ops, model, cams, tgts, dist.grad, dist.compact)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            dist.apply(cams[0])
+            b.record(stream)
+            evs.append((a, b))
+        torch.cuda.synchronize()
+        ex_ms = dist.max_over_ranks(float(np.mean([a.elapsed_time(b) for a, b in evs])))
+    n_isect = int(lib.msplat_num_intersections())
+    xbytes = exchange_bytes(model.n, world, dist.compact if dist else False, args.dp_mode)
+    result = {
+        "metric": "C4 batched views: views/s (8 views per step, 6M Gaussians, 1920x1080)",
+        "value": round(batch * steps / (ms_max / 1000.0), 2), "unit": "views/s",
+        "n_gpus": world, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_max / steps, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded C4 scene; targets are renders of a seed-1 scene)",
+        "config": {"workload": "C4: 6,000,000 Gaussians, SH degree 3, 8 views of 1920x1080 per "
+                               "step on a radius-4 sphere",
+                   "gaussians": model.n, "width": setups[0].width, "height": setups[0].height,
+                   "views_per_step": batch, "views_per_gpu": vpr,
+                   "l2": "inputs larger than L2 (parameters and moments ~4.2 GB)",
+                   "parallelism": "single GPU" if world == 1 else (
+                       f"dp{world}: replicated Gaussians, " + (
+                           "peer-memory reduce + Adam + parameter write-back"
+                           + (" (compact v_rgb exchange)" if dist.compact else "")
+                           if args.dp_mode == "peer" else "NCCL all-reduce, Adam on every replica"))},
+        "exchange": None if dist is None else {
+            "mode": args.dp_mode, "ms_per_step": round(ex_ms, 3),
+            "nvlink_bytes_per_rank": xbytes,
+            "gbs_per_rank": round(xbytes / (ex_ms / 1000.0) / 1e9, 1) if ex_ms else None,
+            "timing": "CUDA events around the exchange + Adam of each step (includes waiting "
+                      "for the slowest rank's gradients), mean over steps, max over ranks"},
+        "intersections_last_view": n_isect,
+        "gpu_launches": launches, "clocks": clk,
+    }
+    if dist is not None:
+        if dist.mode == "peer" and dist.peer_errors():
+            raise RuntimeError("peer-memory optimiser reported a timed-out wait: run invalid")
+        dist.shutdown()
+    return result
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -593,6 +749,17 @@ def main():
     if args.config == "C3":
         if rank == 0:
             print(json.dumps(run_c3(args)), flush=True)
+        return
+    if args.config == "C4":
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable":
+                                  "C4 is a multi-GPU configuration; the reference trains one "
+                                  "view on one device"}), flush=True)
+            return
+        res = run_c4(args, rank, world)
+        if rank == 0:
+            print(json.dumps(res), flush=True)
         return
     if args.impl == "reference":
         res = run_reference(args, rank, world)

@@ -161,6 +161,26 @@ int msplat_train_step_grads_compact(
     float inv_max_dim, const int32_t **radii_out, float *loss_out);
 
 /*
+ * The gradient half for a batch of several views per step.  No counterpart
+ * in the reference (one view per step).  Same arguments and buffer layout as
+ * msplat_train_step_grads, but this view's gradients are ADDED to what
+ * grad_out holds (the previous views of the step, written by
+ * msplat_train_step_grads for the first one) and each visible Gaussian's
+ * visibility entry grows by 1; Gaussians this view culls are neither read
+ * nor written.  For the mean loss over a batch of V views pass loss_inv_n =
+ * 1 / (H * W * 3 * V) to every view's call.
+ */
+int msplat_train_step_grads_accumulate(
+    int num_points, float *means3d, float *scales, float glob_scale, float *quats,
+    const float *viewmat, const float *projmat, float fx, float fy, float cx, float cy,
+    unsigned img_height, unsigned img_width, const int *tile_bounds, float clip_thresh,
+    unsigned degree, unsigned degrees_to_use, const float *cam_pos,
+    float *features_dc, float *features_rest, float *opacities, const float *background,
+    const float *gt, float ssim_weight, float loss_inv_n, int features_rest_bases,
+    float *grad_out, float *vis_counts, float *xys_grad_norm, float *max_2d_size,
+    float inv_max_dim, const int32_t **radii_out, float *loss_out);
+
+/*
  * Data-parallel training, optimiser half: Adam on Gaussians [begin, end)
  * from a gradient buffer in the msplat_train_step_grads layout (typically
  * summed over ranks), each gradient multiplied by grad_scale.  The update,

@@ -96,6 +96,10 @@ SIGNATURES = {
         _i, _p, _p, _f, _p, _fp, _fp, _f, _f, _f, _f, _u, _u, _ip, _f, _u, _u, _fp,
         _p, _p, _p, _fp, _p, _f, _f, _i, _p, _p, _p, _p, _f, C.POINTER(_p), _fp,
     ]),
+    "msplat_train_step_grads_accumulate": (_i, [
+        _i, _p, _p, _f, _p, _fp, _fp, _f, _f, _f, _f, _u, _u, _ip, _f, _u, _u, _fp,
+        _p, _p, _p, _fp, _p, _f, _f, _i, _p, _p, _p, _p, _f, C.POINTER(_p), _fp,
+    ]),
     "msplat_adam_apply": (_i, [
         _i, _i, _u, _u, _p, _f, _i, _i, _i, C.POINTER(_p), C.POINTER(_p), C.POINTER(_p),
         _fp, _fp, _f, _f, _f,

@@ -637,7 +637,7 @@ int msplat_train_step(
 }
 
 static int train_grads_common(
-    bool compact, int num_points, float* means3d, float* scales, float glob_scale, float* quats,
+    int mode, int num_points, float* means3d, float* scales, float glob_scale, float* quats,
     const float* viewmat, const float* projmat, float fx, float fy, float cx, float cy,
     unsigned img_height, unsigned img_width, const int* tile_bounds, float clip_thresh,
     unsigned degree, unsigned degrees_to_use, const float* cam_pos, float* features_dc,
@@ -656,7 +656,7 @@ int msplat_train_step_grads(
     float* vis_counts, float* xys_grad_norm, float* max_2d_size, float inv_max_dim,
     const int32_t** radii_out, float* loss_out)
 {
-    return train_grads_common(false, num_points, means3d, scales, glob_scale, quats, viewmat,
+    return train_grads_common(0, num_points, means3d, scales, glob_scale, quats, viewmat,
                               projmat, fx, fy, cx, cy, img_height, img_width, tile_bounds,
                               clip_thresh, degree, degrees_to_use, cam_pos, features_dc,
                               features_rest, opacities, background, gt, ssim_weight, loss_inv_n,
@@ -674,7 +674,25 @@ int msplat_train_step_grads_compact(
     float* vis_counts, float* xys_grad_norm, float* max_2d_size, float inv_max_dim,
     const int32_t** radii_out, float* loss_out)
 {
-    return train_grads_common(true, num_points, means3d, scales, glob_scale, quats, viewmat,
+    return train_grads_common(1, num_points, means3d, scales, glob_scale, quats, viewmat,
+                              projmat, fx, fy, cx, cy, img_height, img_width, tile_bounds,
+                              clip_thresh, degree, degrees_to_use, cam_pos, features_dc,
+                              features_rest, opacities, background, gt, ssim_weight, loss_inv_n,
+                              features_rest_bases, grad_out, vis_counts, xys_grad_norm,
+                              max_2d_size, inv_max_dim, radii_out, loss_out);
+}
+
+int msplat_train_step_grads_accumulate(
+    int num_points, float* means3d, float* scales, float glob_scale, float* quats,
+    const float* viewmat, const float* projmat, float fx, float fy, float cx, float cy,
+    unsigned img_height, unsigned img_width, const int* tile_bounds, float clip_thresh,
+    unsigned degree, unsigned degrees_to_use, const float* cam_pos, float* features_dc,
+    float* features_rest, float* opacities, const float* background, const float* gt,
+    float ssim_weight, float loss_inv_n, int features_rest_bases, float* grad_out,
+    float* vis_counts, float* xys_grad_norm, float* max_2d_size, float inv_max_dim,
+    const int32_t** radii_out, float* loss_out)
+{
+    return train_grads_common(2, num_points, means3d, scales, glob_scale, quats, viewmat,
                               projmat, fx, fy, cx, cy, img_height, img_width, tile_bounds,
                               clip_thresh, degree, degrees_to_use, cam_pos, features_dc,
                               features_rest, opacities, background, gt, ssim_weight, loss_inv_n,
@@ -683,7 +701,7 @@ int msplat_train_step_grads_compact(
 }
 
 static int train_grads_common(
-    bool compact, int num_points, float* means3d, float* scales, float glob_scale, float* quats,
+    int mode, int num_points, float* means3d, float* scales, float glob_scale, float* quats,
     const float* viewmat, const float* projmat, float fx, float fy, float cx, float cy,
     unsigned img_height, unsigned img_width, const int* tile_bounds, float clip_thresh,
     unsigned degree, unsigned degrees_to_use, const float* cam_pos, float* features_dc,
@@ -693,9 +711,12 @@ static int train_grads_common(
     const int32_t** radii_out, float* loss_out)
 {
     std::lock_guard<std::mutex> lk(g_mu);
+    static const char* const kNames[3] = {"msplat_train_step_grads",
+                                          "msplat_train_step_grads_compact",
+                                          "msplat_train_step_grads_accumulate"};
+    const bool compact = mode == 1;
     if (!grad_out || features_rest_bases < 0) {
-        set_error("%s: missing gradient buffer",
-                  compact ? "msplat_train_step_grads_compact" : "msplat_train_step_grads");
+        set_error("%s: missing gradient buffer", kNames[mode]);
         return MSPLAT_ERR_ARG;
     }
     StepParams p;
@@ -721,8 +742,9 @@ static int train_grads_common(
         G.g[4] = G.g[3] + 3 * n;
         G.g[5] = G.g[4] + rs * n;
         G.vis = G.g[5] + n;
+        G.accumulate = mode == 2;
     }
-    return train_common("msplat_train_step_grads", num_points, means3d, scales, glob_scale, quats,
+    return train_common(kNames[mode], num_points, means3d, scales, glob_scale, quats,
                         viewmat, projmat, fx, fy, cx, cy, img_height, img_width, tile_bounds,
                         clip_thresh, degree, degrees_to_use, cam_pos, features_dc, features_rest,
                         opacities, background, gt, ssim_weight, loss_inv_n, features_rest_bases,

@@ -103,11 +103,16 @@ struct StatPtrs {
 // gradient, from which every SH coefficient's gradient follows with the view
 // direction), g[4] is unused, and cam (3 floats) receives the camera
 // position of the step.
+//
+// Accumulating form (several views per rank and step, full layout only):
+// each visible Gaussian's gradients are added to what the buffer holds and
+// its vis entry grows by 1; culled Gaussians are neither read nor written.
 struct GradOut {
     float* g[kGroups];
     float* vis;
     float* cam;
     int compact;
+    int accumulate;
 };
 
 // Adam over a range of Gaussians [begin, end) from a gradient buffer laid

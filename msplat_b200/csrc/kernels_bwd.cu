@@ -543,6 +543,29 @@ __device__ __forceinline__ void grad_slab(float* __restrict__ out, size_t e0, in
     }
 }
 
+// The accumulating form of grad_slab: adds each visible Gaussian's
+// gradients (sv[gl] != 0) to the slab and leaves the rest untouched; four
+// elements per lane per round, loads issued before the adds.
+template <int STRIDE, class G>
+__device__ __forceinline__ void grad_slab_add(float* __restrict__ out, size_t e0, int total, int lane,
+                                              const int* sv, G grad_of)
+{
+    constexpr int kU = 4;
+    for (int eb = lane; eb < total; eb += 32 * kU) {
+        float g[kU], o[kU];
+        bool on[kU];
+#pragma unroll
+        for (int u = 0; u < kU; u++) {
+            const int e = eb + 32 * u;
+            on[u] = e < total && sv[e / STRIDE] != 0 && grad_of(e / STRIDE, e % STRIDE, g[u]);
+            if (on[u]) o[u] = out[e0 + e];
+        }
+#pragma unroll
+        for (int u = 0; u < kU; u++)
+            if (on[u]) out[e0 + eb + 32 * u] = o[u] + g[u];
+    }
+}
+
 
 
 // Geometry and colour VJP of one visible Gaussian (project_and_sh_backward_kernel,
@@ -724,6 +747,37 @@ project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
     const int* sv = s_vis + wbase;
     if constexpr (GRAD_OUT) {
         const size_t gb = (size_t)g0;
+        if (G.accumulate) {
+            // another view of the same step: add the visible Gaussians'
+            // gradients to the buffer, count the view in vis
+            if (!__any_sync(0xffffffffu, lane < cnt && sv[lane])) return;
+            grad_slab_add<3>(G.g[0], gb * 3, cnt * 3, lane, sv,
+                             [&](int gl, int k, float& g) { g = sg[gl][k]; return true; });
+            grad_slab_add<3>(G.g[1], gb * 3, cnt * 3, lane, sv,
+                             [&](int gl, int k, float& g) { g = sg[gl][3 + k]; return true; });
+            grad_slab_add<4>(G.g[2], gb * 4, cnt * 4, lane, sv,
+                             [&](int gl, int k, float& g) { g = sg[gl][6 + k]; return true; });
+            grad_slab_add<1>(G.g[5], gb, cnt, lane, sv,
+                             [&](int gl, int, float& g) { g = sg[gl][10]; return true; });
+            grad_slab_add<3>(G.g[3], gb * 3, cnt * 3, lane, sv, [&](int gl, int k, float& g) {
+                g = MSP_SH_C0 * sb[gl][15 + k];
+                return true;
+            });
+            const int stride = P->rest_stride;
+            const int used = nb_rest * 3;
+            auto rest_add = [&](int gl, int kk, float& g) {
+                if (kk >= used) return false;
+                const int b = kk / 3, c = kk - 3 * b;
+                g = sb[gl][b] * sb[gl][15 + c];
+                return true;
+            };
+            if (stride == 45) grad_slab_add<45>(G.g[4], gb * 45, cnt * 45, lane, sv, rest_add);
+            else if (stride == 24) grad_slab_add<24>(G.g[4], gb * 24, cnt * 24, lane, sv, rest_add);
+            else if (stride == 9) grad_slab_add<9>(G.g[4], gb * 9, cnt * 9, lane, sv, rest_add);
+            else if (stride == 72) grad_slab_add<72>(G.g[4], gb * 72, cnt * 72, lane, sv, rest_add);
+            if (lane < cnt && sv[lane]) G.vis[g0 + lane] += 1.f;
+            return;
+        }
         grad_slab<3>(G.g[0], gb * 3, cnt * 3, lane,
                      [&](int gl, int k, float& g) { g = sg[gl][k]; return true; });
         grad_slab<3>(G.g[1], gb * 3, cnt * 3, lane,

@@ -15,6 +15,13 @@ point where views interact -- the optimiser:
      the multi-view form of the reference's visible-only SH update.
 
 With world = 1 the two halves reproduce msplat_train_step bit for bit.
+
+A step may also train a batch of several views per rank (the batched-view
+configuration: 8 views per step on 1, 2, 4 or 8 GPUs): the rank's first
+view writes the gradient buffer, the others add to it
+(msplat_train_step_grads_accumulate), every view's loss is normalised by
+the rank's view count, and the exchange above completes the mean over the
+batch.  train_batch() is the same step on one device.
 Densification statistics stay per rank during training; sync_stats() sums
 vis_counts / xys_grad_norm and takes the max of max_2d_size across ranks
 before a densification pass reads them.
@@ -69,16 +76,18 @@ class EngineOps:
         import torch
         return torch.empty(count, dtype=torch.float32, device="cuda")
 
-    def grads(self, model: GaussianModel, cam, gt, out, ssim_weight, background, glob_scale,
-              clip_thresh) -> float:
+    def _grads(self, fn: str, model: GaussianModel, cam, gt, out, ssim_weight, background,
+               glob_scale, clip_thresh, batch: int) -> float:
         lib = _lib.load()
         h, w = cam.height, cam.width
-        loss_inv_n = float(f32(1.0) / f32(h * w * 3))
+        # the mean over the pixels and channels of `batch` views (a division
+        # by a power-of-two batch is exact)
+        loss_inv_n = float(f32(f32(1.0) / f32(h * w * 3)) / f32(batch))
         inv_max_dim = float(f32(1.0) / f32(max(h, w)))
         p = model.params
         radii = C.c_void_p()
         loss = C.c_float()
-        rc = lib.msplat_train_step_grads(
+        rc = getattr(lib, fn)(
             model.n, _ptr(p[0]), _ptr(p[1]), glob_scale, _ptr(p[2]),
             _lib.farr(cam.viewmat), _lib.farr(cam.projmat), cam.fx, cam.fy, cam.cx, cam.cy,
             h, w, _lib.iarr(cam.tile_bounds), clip_thresh, cam.degree, cam.degrees_to_use,
@@ -86,28 +95,21 @@ class EngineOps:
             _ptr(gt), ssim_weight, loss_inv_n, model.rest_bases, _ptr(out),
             _ptr(model.vis_counts), _ptr(model.xys_grad_norm), _ptr(model.max_2d_size),
             inv_max_dim, C.byref(radii), C.byref(loss))
-        _lib.check(rc, "msplat_train_step_grads")
+        _lib.check(rc, fn)
         return float(loss.value)
+
+    def grads(self, model: GaussianModel, cam, gt, out, ssim_weight, background, glob_scale,
+              clip_thresh, accumulate: bool = False, batch: int = 1) -> float:
+        """This view's gradients into `out` (full layout); with `accumulate`
+        added to what it holds.  `batch`: views per rank in the step."""
+        fn = "msplat_train_step_grads_accumulate" if accumulate else "msplat_train_step_grads"
+        return self._grads(fn, model, cam, gt, out, ssim_weight, background, glob_scale,
+                           clip_thresh, batch)
 
     def grads_compact(self, model: GaussianModel, cam, gt, out, ssim_weight, background,
                       glob_scale, clip_thresh) -> float:
-        lib = _lib.load()
-        h, w = cam.height, cam.width
-        loss_inv_n = float(f32(1.0) / f32(h * w * 3))
-        inv_max_dim = float(f32(1.0) / f32(max(h, w)))
-        p = model.params
-        radii = C.c_void_p()
-        loss = C.c_float()
-        rc = lib.msplat_train_step_grads_compact(
-            model.n, _ptr(p[0]), _ptr(p[1]), glob_scale, _ptr(p[2]),
-            _lib.farr(cam.viewmat), _lib.farr(cam.projmat), cam.fx, cam.fy, cam.cx, cam.cy,
-            h, w, _lib.iarr(cam.tile_bounds), clip_thresh, cam.degree, cam.degrees_to_use,
-            _lib.farr(cam.cam_pos), _ptr(p[3]), _ptr(p[4]), _ptr(p[5]), _lib.farr(background),
-            _ptr(gt), ssim_weight, loss_inv_n, model.rest_bases, _ptr(out),
-            _ptr(model.vis_counts), _ptr(model.xys_grad_norm), _ptr(model.max_2d_size),
-            inv_max_dim, C.byref(radii), C.byref(loss))
-        _lib.check(rc, "msplat_train_step_grads_compact")
-        return float(loss.value)
+        return self._grads("msplat_train_step_grads_compact", model, cam, gt, out, ssim_weight,
+                           background, glob_scale, clip_thresh, 1)
 
     def adam_apply(self, model: GaussianModel, cam, grad, scale: float) -> None:
         lib = _lib.load()
@@ -118,6 +120,41 @@ class EngineOps:
             _ptr_array(model.exp_avg_sq), _lib.farr(steps), _lib.farr(bc2s), model.beta1,
             model.beta2, model.eps)
         _lib.check(rc, "msplat_adam_apply")
+
+
+def accumulate_views(ops, model: GaussianModel, cams, gts, out, compact: bool = False,
+                     ssim_weight: float = 0.2, background=DEFAULT_BG, glob_scale: float = 1.0,
+                     clip_thresh: float = 0.01) -> float:
+    """Gradient of one rank's share of a batched step: its views in order,
+    the first written into `out`, the others added to it, each with the loss
+    normalised by the rank's view count (the exchange's 1/world completes the
+    mean over the batch).  Returns the sum of the views' losses so scaled."""
+    if compact and len(cams) != 1:
+        raise ValueError("the compact gradient layout carries one view per rank")
+    loss = 0.0
+    for k, (cam, gt) in enumerate(zip(cams, gts)):
+        if compact:
+            loss += ops.grads_compact(model, cam, gt, out, ssim_weight, background, glob_scale,
+                                      clip_thresh)
+        else:
+            loss += ops.grads(model, cam, gt, out, ssim_weight, background, glob_scale,
+                              clip_thresh, accumulate=k > 0, batch=len(cams))
+    return loss
+
+
+def train_batch(model: GaussianModel, cams, gts, grad, ops=None, ssim_weight: float = 0.2,
+                background=DEFAULT_BG, glob_scale: float = 1.0,
+                clip_thresh: float = 0.01) -> float:
+    """One step on a batch of views on a single device: the gradient of the
+    mean loss over the views (accumulated in `grad`, a grad_floats buffer),
+    then one Adam update.  With one view it equals msplat_train_step within
+    the parity bar (the fused step is faster there)."""
+    ops = ops if ops is not None else EngineOps()
+    model.step_count += 1
+    loss = accumulate_views(ops, model, cams, gts, grad, False, ssim_weight, background,
+                            glob_scale, clip_thresh)
+    ops.adam_apply(model, cams[0], grad, 1.0)
+    return loss
 
 
 class DeviceBuffer:
@@ -159,7 +196,7 @@ def _open_handle(h: bytes) -> int:
 
 
 class DataParallel:
-    """Replicated Gaussians, one view per rank per step.
+    """Replicated Gaussians, views_per_rank views per rank per step.
 
     mode "peer" (GPUs): the gradient buffers, parameter arrays and flag
     arrays of all ranks are mapped into every process, and one kernel per
@@ -178,7 +215,7 @@ class DataParallel:
 
     def __init__(self, model: GaussianModel, rank: int, world: int, ops=None,
                  backend: str | None = None, timeout_s: float = 120.0, mode: str | None = None,
-                 peer_timeout_s: float = 10.0, compact: bool = True):
+                 peer_timeout_s: float = 10.0, compact: bool = True, views_per_rank: int = 1):
         import torch
         import torch.distributed as dist
         self.model, self.rank, self.world = model, rank, world
@@ -189,7 +226,11 @@ class DataParallel:
             raise ValueError(f"unknown data-parallel mode {self.mode!r}")
         self.peer_timeout_s = float(peer_timeout_s)
         # peer mode: exchange v_rgb instead of the 48 SH gradients per Gaussian
-        self.compact = bool(compact) and self.mode == "peer"
+        # (one view per rank: v_rgb is tied to its view's camera)
+        self.views_per_rank = int(views_per_rank)
+        if self.views_per_rank < 1:
+            raise ValueError("views_per_rank must be >= 1")
+        self.compact = bool(compact) and self.mode == "peer" and self.views_per_rank == 1
         self._bufs = []
         if not dist.is_initialized():
             be = backend or ("nccl" if torch.cuda.is_available() else "gloo")
@@ -241,11 +282,20 @@ class DataParallel:
     def train_step(self, cam, gt, ssim_weight: float = 0.2, background=DEFAULT_BG,
                    glob_scale: float = 1.0, clip_thresh: float = 0.01) -> float:
         """One data-parallel step; every rank passes its own view."""
+        return self.train_views([cam], [gt], ssim_weight, background, glob_scale, clip_thresh)
+
+    def train_views(self, cams, gts, ssim_weight: float = 0.2, background=DEFAULT_BG,
+                    glob_scale: float = 1.0, clip_thresh: float = 0.01) -> float:
+        """One data-parallel step over a batch of world * views_per_rank
+        views; every rank passes its own views_per_rank of them.  Adam
+        follows the gradient of the mean loss over the whole batch."""
+        if len(cams) != self.views_per_rank or len(gts) != len(cams):
+            raise ValueError(f"expected {self.views_per_rank} views per rank, got {len(cams)}")
         self.model.step_count += 1
-        grads = self.ops.grads_compact if self.compact else self.ops.grads
-        self.last_loss = grads(self.model, cam, gt, self.grad, ssim_weight, background,
-                               glob_scale, clip_thresh)
-        self.apply(cam)
+        self.last_loss = accumulate_views(self.ops, self.model, cams, gts, self.grad,
+                                          self.compact, ssim_weight, background, glob_scale,
+                                          clip_thresh)
+        self.apply(cams[0])
         return self.last_loss
 
     def apply(self, cam) -> None:

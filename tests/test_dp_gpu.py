@@ -13,6 +13,10 @@
    GPUs), through NCCL and through the peer-memory kernel: the replicas must
    be bit-identical to each other, and within the same bar of a one-GPU
    emulation that sums the two views' gradients and applies scale 1/2.
+   Batched steps (two views per rank, gradients accumulated with
+   msplat_train_step_grads_accumulate): within the bar of one GPU training
+   the same four-view batches (multigpu.train_batch), and on one GPU the
+   accumulated buffer within the one-step bar of the mean of its views.
 3. The peer-memory optimiser: at world 1 bit-identical to msplat_adam_apply
    on the same gradients; its compact exchange (v_rgb instead of the SH
    gradients) within the bar of the full one; and its cross-GPU waits give
@@ -117,6 +121,38 @@ def test_split_step_equals_fused_step(case):
     # the visible-only rule: Gaussians never seen keep their SH moments at 0
     never = a["vis"] == 0
     assert not b["m3"][never].any() and not b["m4"][never].any()
+
+
+@pytest.mark.parametrize("case", ["chunked", "mono"])
+def test_accumulated_views_equal_mean_of_views(case):
+    """A batch of two views through msplat_train_step_grads_accumulate
+    (multigpu.accumulate_views: the first view writes, the second adds, each
+    loss normalised by 2) equals the mean of the two views' own gradients
+    within the one-step gradient bar (the runs differ only in the order of
+    the raster backward's atomics); the visibility entries are exact counts."""
+    import torch
+    n, w, h = (20_000, 256, 192) if case == "chunked" else (30_000, 640, 480)
+    g, cams = _scene(n, w, h)
+    model = engine.GaussianModel(g.groups())
+    ops = multigpu.EngineOps()
+    nf = multigpu.grad_floats(n, model.rest_bases)
+    ga, gb, acc = (ops.alloc(nf) for _ in range(3))
+    css = [harness.setup_cam(cams[k]) for k in range(2)]
+    gts = [_gt(cs, 10 + k) for k, cs in enumerate(css)]
+    ops.grads(model, css[0], gts[0], ga, 0.2, engine.DEFAULT_BG, 1.0, 0.01)
+    ops.grads(model, css[1], gts[1], gb, 0.2, engine.DEFAULT_BG, 1.0, 0.01)
+    acc.fill_(float("nan"))  # every entry must be written by the first view
+    multigpu.accumulate_views(ops, model, css, gts, acc)
+    torch.cuda.synchronize()
+    (sa, va), (sb, vb), (sc, vc) = (multigpu.grad_views(t, n, model.rest_bases)
+                                    for t in (ga, gb, acc))
+    np.testing.assert_array_equal(vc.cpu().numpy(), (va + vb).cpu().numpy())
+    assert ((va > 0) != (vb > 0)).any(), "the two views should see different Gaussians"
+    for gi in range(6):
+        want = (0.5 * (sa[gi] + sb[gi])).cpu().numpy()
+        got = sc[gi].cpu().numpy()
+        assert np.isfinite(got).all(), f"group {gi}: unwritten entries"
+        _assert_close(got, want, STAT_RTOL, STAT_ATOL_FRAC, f"{case}: group {gi}")
 
 
 def _single_rank_group():
@@ -274,3 +310,37 @@ def test_two_rank_nccl_matches_summed_views():
         for k, v in want.items():
             np.testing.assert_array_equal(got[0][k], got[1][k], err_msg=f"{mode}: replicas differ: {k}")
             _assert_close(got[0][k], v, PARAM_RTOL, PARAM_ATOL_FRAC, f"{mode} vs emulation: {k}")
+
+
+def test_two_rank_batched_views_match_single_gpu_batch():
+    """Two ranks, two views each per step (a batch of four; full-layout
+    exchange with accumulated gradients) through the peer kernel and NCCL:
+    replicas bit-identical, and within the bar of one GPU training the same
+    batches with multigpu.train_batch."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    n, w, h = 20_000, 320, 240
+    g, cams = _scene(n, w, h, seed=6)
+    model = engine.GaussianModel(g.groups())
+    buf = multigpu.EngineOps().alloc(multigpu.grad_floats(n, model.rest_bases))
+    for step in range(3):
+        css = [harness.setup_cam(cams[(step * 4 + b) % 3]) for b in range(4)]
+        gts = [_gt(cs, (step * 4 + b) % 3) for b, cs in enumerate(css)]
+        multigpu.train_batch(model, css, gts, buf)
+    torch.cuda.synchronize()
+    want = {f"p{i}": model.params[i].cpu().numpy() for i in range(6)}
+    for mode, port in (("nccl", 29563), ("peer", 29564)):
+        with tempfile.TemporaryDirectory() as d:
+            cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                   "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(port),
+                   os.path.join(ROOT, "tests", "dp_worker.py"), d, str(n), str(w), str(h), "6",
+                   mode, "2"]
+            env = dict(os.environ, PYTHONPATH=ROOT)
+            res = subprocess.run(["timeout", "-k", "30", "300"] + cmd, cwd=ROOT, env=env,
+                                 capture_output=True, text=True)
+            assert res.returncode == 0, mode + res.stdout[-3000:] + res.stderr[-3000:]
+            got = [dict(np.load(os.path.join(d, f"rank{r}.npz"))) for r in range(2)]
+        for k, v in want.items():
+            np.testing.assert_array_equal(got[0][k], got[1][k], err_msg=f"{mode}: replicas differ: {k}")
+            _assert_close(got[0][k], v, PARAM_RTOL, PARAM_ATOL_FRAC, f"{mode} vs one GPU: {k}")

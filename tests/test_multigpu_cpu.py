@@ -73,8 +73,14 @@ class FakeOps:
     def alloc(self, count):
         return torch.empty(count, dtype=torch.float32)
 
-    def grads(self, model, cam, gt, out, *args):
-        fake_grads(model, cam.view, out)
+    def grads(self, model, cam, gt, out, *args, accumulate=False, batch=1):
+        # the engine's contract: gradients of the loss normalised by the
+        # rank's view count; `accumulate` adds them (and the visibility) to out
+        tmp = torch.empty_like(out) if accumulate else out
+        fake_grads(model, cam.view, tmp)
+        tmp[:-model.n] /= batch
+        if accumulate:
+            out += tmp
         model.vis_counts += 1.0
         model.xys_grad_norm += float(cam.view)
         model.max_2d_size.copy_(torch.maximum(model.max_2d_size,
@@ -90,14 +96,20 @@ def _model():
     return engine.GaussianModel(g.groups(), device="cpu")
 
 
-def _worker(rank, world, port, out_dir):
+def _worker(rank, world, port, out_dir, vpr=1):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     model = _model()
-    dp = multigpu.DataParallel(model, rank, world, ops=FakeOps(), backend="gloo", timeout_s=60)
+    dp = multigpu.DataParallel(model, rank, world, ops=FakeOps(), backend="gloo", timeout_s=60,
+                               views_per_rank=vpr)
     losses = []
     for s in range(STEPS):
-        losses.append(dp.train_step(FakeCam(s * world + rank), None))
+        if vpr == 1:
+            losses.append(dp.train_step(FakeCam(s * world + rank), None))
+        else:
+            # rank r takes views r, r + world, ... of the step's batch
+            cams = [FakeCam(s * world * vpr + k * world + rank) for k in range(vpr)]
+            losses.append(dp.train_views(cams, [None] * vpr))
     dp.barrier()
     mx = dp.max_over_ranks(float(rank) + 0.5)
     dp.sync_stats()
@@ -122,6 +134,41 @@ def two_ranks():
         mp.start_processes(_worker, args=(2, _free_port(), d), nprocs=2, join=True,
                            start_method="spawn")
         yield [dict(np.load(os.path.join(d, f"rank{r}.npz"))) for r in range(2)]
+
+
+@pytest.fixture(scope="module")
+def two_ranks_batched():
+    """Two ranks, two views each per step (a batch of four)."""
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_worker, args=(2, _free_port(), d, 2), nprocs=2, join=True,
+                           start_method="spawn")
+        yield [dict(np.load(os.path.join(d, f"rank{r}.npz"))) for r in range(2)]
+
+
+def test_batched_views_match_single_device_batch(two_ranks_batched):
+    """world 2 x 2 views per rank == one device training the same batches of
+    four views (multigpu.train_batch), and the replicas stay identical."""
+    r0, r1 = two_ranks_batched
+    for k in r0:
+        if k.startswith(("p", "m", "v")) and k[1:].isdigit():
+            np.testing.assert_array_equal(r0[k], r1[k], err_msg=k)
+    model = _model()
+    buf = torch.empty(multigpu.grad_floats(N, REST_BASES))
+    batch = 4
+    for s in range(STEPS):
+        cams = [FakeCam(s * batch + v) for v in range(batch)]
+        multigpu.train_batch(model, cams, [None] * batch, buf, ops=FakeOps())
+    for i in range(6):
+        np.testing.assert_allclose(r0[f"p{i}"], model.params[i].numpy(), rtol=1e-6, atol=1e-7,
+                                   err_msg=f"group {i}")
+    # every view of every step counted once across the ranks
+    np.testing.assert_array_equal(r0["vis"], np.full(N, batch * STEPS, np.float32))
+
+
+def test_batched_views_reject_wrong_count_and_compact():
+    with pytest.raises(ValueError):
+        multigpu.accumulate_views(FakeOps(), _model(), [FakeCam(0), FakeCam(1)], [None, None],
+                                  torch.empty(multigpu.grad_floats(N, REST_BASES)), compact=True)
 
 
 def test_replicas_identical(two_ranks):
