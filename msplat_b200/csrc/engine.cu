@@ -374,10 +374,10 @@ static int run_forward(const StepParams& p, const float* means, const float* sca
     tm.mark(1, st);
     launch_scan_tiles(g.d_params, p.num_tiles, B, st);
     launch_scatter(g.d_params, p.num_points, B, st);
-    launch_sort_tiles(g.d_params, p.num_tiles, B, st);
+    const int sort_launches = launch_sort_tiles(g.d_params, p.num_tiles, B, st);
     tm.mark(2, st);
     launch_raster_forward(g.d_params, p.num_tiles, p.k_max, p.img_w, p.img_h, B, st);
-    g.launches += 4 + (p.k_max > 1 ? 2 : 1);
+    g.launches += 3 + sort_launches + (p.k_max > 1 ? 2 : 1);
     MSP_CUDA(cudaGetLastError());
     return MSPLAT_OK;
 }
@@ -576,7 +576,7 @@ static int train_common(const char* who, int num_points, float* means3d, float* 
     StatPtrs S{vis_counts, xys_grad_norm, max_2d_size};
     int bwd_launches = 1;
     if (G)
-        launch_project_backward_grads(g.d_params, num_points, p.degrees_to_use, p.rest_stride,
+        bwd_launches = launch_project_backward_grads(g.d_params, num_points, p.degrees_to_use, p.rest_stride,
                                       g.B, A, S, *G, st);
     else
         bwd_launches = launch_project_backward_adam(g.d_params, num_points, p.degrees_to_use,

@@ -113,6 +113,7 @@ struct GradOut {
     float* cam;
     int compact;
     int accumulate;
+    int rest_done;  // the SH-rest group is written by rest_grads_kernel
 };
 
 // Adam over a range of Gaussians [begin, end) from a gradient buffer laid
@@ -176,7 +177,7 @@ void launch_project_forward(const StepParams* P, int N, const float* means, cons
                             int degrees_to_use_host, int rest_stride_host, cudaStream_t s);
 void launch_scan_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s);
 void launch_scatter(const StepParams* P, int N, const Buffers& B, cudaStream_t s);
-void launch_sort_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s);
+int launch_sort_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s);
 void launch_raster_forward(const StepParams* P, int num_tiles, int k_max, int W, int H,
                            const Buffers& B, cudaStream_t s);
 void launch_ssim(const StepParams* P, int W, int H, const float* gt, const Buffers& B,
@@ -187,7 +188,7 @@ void launch_raster_backward(const StepParams* P, int num_tiles, int k_max, int W
 int launch_project_backward_adam(const StepParams* P, int N, int degrees_to_use_host,
                                  int rest_stride_host, const Buffers& B, const AdamPtrs& A,
                                  const StatPtrs& St, cudaStream_t s);
-void launch_project_backward_grads(const StepParams* P, int N, int degrees_to_use_host,
+int launch_project_backward_grads(const StepParams* P, int N, int degrees_to_use_host,
                                    int rest_stride_host, const Buffers& B, const AdamPtrs& A,
                                    const StatPtrs& St, const GradOut& G, cudaStream_t s);
 int rest_bases_updated(int degrees_to_use, int rest_stride);

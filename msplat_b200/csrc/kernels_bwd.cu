@@ -724,7 +724,7 @@ project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
             const float st_vis = St.vis_counts[i], st_norm = St.grad_norm[i], st_max = St.max_2d[i];
             // the SH-rest basis only when this kernel forms the rest gradient
             const bool with_basis =
-                GRAD_OUT ? !G.compact : (A.numel[4] > 0 && nb_rest > 0);
+                GRAD_OUT ? !(G.compact || G.rest_done) : (A.numel[4] > 0 && nb_rest > 0);
             gaussian_vjp(P, ga, g_co[i], p, ls0, ls1, ls2, q0, q1, q2, q3, gr, s_basis[tid],
                          with_basis);
             const float vx = ga[6], vy = ga[7];
@@ -763,6 +763,10 @@ project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
                 g = MSP_SH_C0 * sb[gl][15 + k];
                 return true;
             });
+            if (G.rest_done) {
+                if (lane < cnt && sv[lane]) G.vis[g0 + lane] += 1.f;
+                return;
+            }
             const int stride = P->rest_stride;
             const int used = nb_rest * 3;
             auto rest_add = [&](int gl, int kk, float& g) {
@@ -800,6 +804,10 @@ project_backward_adam_kernel(const StepParams* __restrict__ P, int N,
             g = MSP_SH_C0 * sb[gl][15 + k];
             return sv[gl] != 0;
         });
+        if (G.rest_done) {
+            if (lane < cnt) G.vis[g0 + lane] = sv[lane] ? 1.f : 0.f;
+            return;
+        }
         const int stride = P->rest_stride;
         const int used = nb_rest * 3;
         auto rest_grad = [&](int gl, int kk, float& g) {
@@ -931,6 +939,69 @@ rest_adam_kernel(const StepParams* __restrict__ P, int N, const int* __restrict_
     }
 }
 
+// SH-rest gradients of the data-parallel step in the full layout: the
+// gradient half's counterpart of rest_adam_kernel (75% of the gradient
+// bytes), streamed on the side stream beside the projection VJP.  Element
+// (i, b, c) is basis_b(view direction of the forward's mean) * v_rgb_c, the
+// product project_backward_adam_kernel<true> forms.  Overwrite: every
+// element is written (0 for culled Gaussians and for degrees not in use).
+// Accumulate: the visible Gaussians' used elements are added; nothing else
+// is touched.
+template <int RS>
+__global__ void __launch_bounds__(kRestThreads)
+rest_grads_kernel(const StepParams* __restrict__ P, int N, const int* __restrict__ radii,
+                  const float* __restrict__ grad_acc, const float* __restrict__ sh_mean,
+                  float* __restrict__ out, int used, int accumulate)
+{
+    __shared__ float s_b[kRestThreads][17];  // 15 basis values + pad (odd stride)
+    __shared__ float s_c[kRestThreads][3];   // v_rgb
+    __shared__ int s_vis[kRestThreads];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int base = blockIdx.x * kRestThreads;
+    const int i = base + tid;
+    bool vis = false;
+    if (i < N && radii[i] > 0) {
+        vis = true;
+        const float p[3] = {sh_mean[3 * (size_t)i], sh_mean[3 * (size_t)i + 1],
+                            sh_mean[3 * (size_t)i + 2]};
+        sh_rest_basis(P->cam_pos, p, s_b[tid]);
+        const float* ga = grad_acc + (size_t)i * kGradStride;
+        s_c[tid][0] = ga[0];
+        s_c[tid][1] = ga[1];
+        s_c[tid][2] = ga[2];
+    }
+    s_vis[tid] = vis;
+    __syncthreads();
+    const int wbase = warp * 32;
+    const int g0 = base + wbase;
+    if (g0 >= N) return;
+    const int cnt = min(32, N - g0);
+    if (accumulate && !__any_sync(0xffffffffu, s_vis[wbase + (lane < cnt ? lane : 0)])) return;
+    const size_t e0 = (size_t)g0 * RS;
+    const int total = cnt * RS;
+    constexpr int kU = 8;
+    for (int eb = lane; eb < total; eb += 32 * kU) {
+        float g[kU], o[kU];
+        bool on[kU];
+#pragma unroll
+        for (int u = 0; u < kU; u++) {
+            const int e = eb + 32 * u;
+            const int gl = e / RS, kk = e - gl * RS;
+            const bool real = e < total && kk < used && s_vis[wbase + gl];
+            g[u] = 0.f;
+            if (real) {
+                const int b = kk / 3, c = kk - 3 * b;
+                g[u] = s_b[wbase + gl][b] * s_c[wbase + gl][c];
+            }
+            on[u] = accumulate ? real : e < total;
+            if (accumulate && on[u]) o[u] = out[e0 + e];
+        }
+#pragma unroll
+        for (int u = 0; u < kU; u++)
+            if (on[u]) out[e0 + eb + 32 * u] = accumulate ? o[u] + g[u] : g[u];
+    }
+}
+
 int launch_project_backward_adam(const StepParams* P, int N, int degrees_to_use_host,
                                  int rest_stride_host, const Buffers& B, const AdamPtrs& A,
                                  const StatPtrs& St, cudaStream_t s)
@@ -978,15 +1049,47 @@ int launch_project_backward_adam(const StepParams* P, int N, int degrees_to_use_
     return launches;
 }
 
-void launch_project_backward_grads(const StepParams* P, int N, int degrees_to_use_host,
-                                   int rest_stride_host, const Buffers& B, const AdamPtrs& A,
-                                   const StatPtrs& St, const GradOut& G, cudaStream_t s)
+int launch_project_backward_grads(const StepParams* P, int N, int degrees_to_use_host,
+                                  int rest_stride_host, const Buffers& B, const AdamPtrs& A,
+                                  const StatPtrs& St, const GradOut& G, cudaStream_t s)
 {
-    if (N <= 0) return;
+    if (N <= 0) return 0;
     const int nb = rest_bases_updated(degrees_to_use_host, rest_stride_host);
+    GradOut G2 = G;
+    int launches = 1;
+    bool joined = false;
+    const bool full = !G.compact && rest_stride_host > 0;
+    const SideStream& side = engine_side();
+    if (full && (rest_stride_host == 45 || rest_stride_host == 24 || rest_stride_host == 9 ||
+                 rest_stride_host == 72)) {
+        const int grid = (N + kRestThreads - 1) / kRestThreads;
+        const int used = nb * 3;
+        const bool forked = cudaEventRecord(side.fork, s) == cudaSuccess &&
+                            cudaStreamWaitEvent(side.stream, side.fork, 0) == cudaSuccess;
+        const cudaStream_t rs = forked ? side.stream : s;
+#define MSP_REST(RS)                                                                         \
+    rest_grads_kernel<RS><<<grid, kRestThreads, 0, rs>>>(P, N, B.proj.radii, B.grad_acc,    \
+                                                         B.proj.sh_mean, G.g[4], used,      \
+                                                         G.accumulate)
+        switch (rest_stride_host) {
+            case 45: MSP_REST(45); break;
+            case 24: MSP_REST(24); break;
+            case 9: MSP_REST(9); break;
+            case 72: MSP_REST(72); break;
+        }
+#undef MSP_REST
+        G2.rest_done = 1;
+        launches++;
+        if (forked) {
+            if (cudaEventRecord(side.join, side.stream) == cudaSuccess) joined = true;
+            else cudaStreamSynchronize(side.stream);
+        }
+    }
     const int grid = (N + kBwdThreads - 1) / kBwdThreads;
     project_backward_adam_kernel<true><<<grid, kBwdThreads, 0, s>>>(
-        P, N, B.proj.radii, B.proj.conic_op, B.grad_acc, A, St, G, nb);
+        P, N, B.proj.radii, B.proj.conic_op, B.grad_acc, A, St, G2, nb);
+    if (joined) cudaStreamWaitEvent(s, side.join, 0);
+    return launches;
 }
 
 // ---------------------------------------------------------------------------

@@ -614,35 +614,43 @@ __device__ __forceinline__ int merge_path(const unsigned long long* a, int la,
 }
 
 // Per-tile LSD radix sort of the 32-bit depths (the ids ride along) for
-// 2 <= n <= kSortRun keys: 8-bit digits, one pass per byte that is not the
-// same for every key of the tile.  Each pass is stable: warp w ranks its
-// contiguous share of the keys 32 at a time (__match_any_sync groups the
-// lanes with equal digits), and the per-(digit, warp) counts are scanned
-// digit-major, warp-minor.  Stability keeps equal depths in input order,
-// which the scatter's atomics leave arbitrary, so a tile holding two equal
-// depths reports it and is sorted by the bitonic network on the full
-// (depth, id) keys instead; both give the order of the 64-bit keys.
-constexpr int kRadixWarps = kSortThreads / 32;
-constexpr int kRadixChunks = kSortRun / kSortThreads;  // 32-key chunks per warp at most
-// Each warp's keys form kRadixSplit consecutive sub-ranges with their own
-// digit counters, so its scatter runs kRadixSplit independent chains of
-// counter reads and updates instead of one.
+// 2 <= n <= RUN keys with T threads: 8-bit digits, one pass per byte that
+// is not the same for every key of the tile.  Each pass is stable: warp w
+// ranks its contiguous share of the keys 32 at a time (__match_any_sync
+// groups the lanes with equal digits), and the per-(digit, warp) counts are
+// scanned digit-major, warp-minor.  Stability keeps equal depths in input
+// order, which the scatter's atomics leave arbitrary, so each run of equal
+// depths is then put in id order by one thread (insertion sort in shared
+// memory); the result is the order of the 64-bit keys (depth << 32 | id).
+// A tile whose depths are all equal, or that holds a run of more than
+// kMaxTieRun equal depths, is reported and sorted by the bitonic / merge
+// path on the full keys instead.
 constexpr int kRadixSplit = MSP_RADIX_SPLIT;
-constexpr int kRadixCols = kRadixWarps * kRadixSplit;
-static_assert(kRadixChunks % kRadixSplit == 0, "sub-ranges of whole chunks");
+constexpr int kMaxTieRun = 32;
 
-struct RadixSmem {
-    unsigned key[kSortRun];
-    int val[kSortRun];
-    int hist[256 * kRadixCols];  // [digit * kRadixCols + column], column = warp * split + sub-range
-    int wsum[kRadixWarps];
-    unsigned red[2 * kRadixWarps];
+template <int T, int RUN>
+struct RadixSmemT {
+    static constexpr int kWarps = T / 32;
+    static constexpr int kChunks = RUN / T;  // 32-key chunks per warp at most
+    static constexpr int kCols = kWarps * kRadixSplit;
+    // Each warp's keys form kRadixSplit consecutive sub-ranges with their
+    // own digit counters, so its scatter runs kRadixSplit independent chains
+    // of counter reads and updates instead of one.
+    static_assert(kChunks % kRadixSplit == 0, "sub-ranges of whole chunks");
+    unsigned key[RUN];
+    int val[RUN];
+    int hist[256 * kCols];  // [digit * kCols + column], column = warp * split + sub-range
+    int wsum[kWarps];
+    unsigned red[2 * kWarps];
 };
+using RadixSmem = RadixSmemT<kSortThreads, kSortRun>;
 
-// Exclusive prefix sum of S.hist in place (256 * kRadixCols counters).
-__device__ __forceinline__ void radix_scan(RadixSmem& S)
+// Exclusive prefix sum of S.hist in place (256 * kCols counters).
+template <int T, int RUN>
+__device__ __forceinline__ void radix_scan(RadixSmemT<T, RUN>& S)
 {
-    constexpr int kPer = 256 * kRadixCols / kSortThreads;
+    using SM = RadixSmemT<T, RUN>;
+    constexpr int kPer = 256 * SM::kCols / T;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     int c[kPer];
     int sum = 0;
@@ -661,7 +669,7 @@ __device__ __forceinline__ void radix_scan(RadixSmem& S)
     __syncthreads();
     int base = incl - sum;
 #pragma unroll
-    for (int w = 0; w < kRadixWarps; w++) base += w < warp ? S.wsum[w] : 0;
+    for (int w = 0; w < SM::kWarps; w++) base += w < warp ? S.wsum[w] : 0;
 #pragma unroll
     for (int i = 0; i < kPer; i++) {
         S.hist[tid * kPer + i] = base;
@@ -669,26 +677,31 @@ __device__ __forceinline__ void radix_scan(RadixSmem& S)
     }
 }
 
-// Returns false (and writes nothing) when two keys of the tile have equal
-// depths; otherwise writes the ids in ascending (depth, id) order.
+// Returns false (and writes nothing) when the tile cannot be sorted here
+// (all depths equal, or a run of equal depths longer than kMaxTieRun);
+// otherwise writes the ids in ascending (depth, id) order.
 // Register r of a lane holds element w0 + ((r % split) * cv + r / split) * 32
 // + lane: sub-range r % split, its chunk r / split.
+template <int T, int RUN>
 __device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __restrict__ keys, int n,
-                                                RadixSmem& S, int* __restrict__ out_ids)
+                                                RadixSmemT<T, RUN>& S, int* __restrict__ out_ids)
 {
+    using SM = RadixSmemT<T, RUN>;
     constexpr int V = kRadixSplit;
+    constexpr int kChunks = SM::kChunks;
+    constexpr int kCols = SM::kCols;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const unsigned lt = (1u << lane) - 1u;
-    const int C = (n + kSortThreads - 1) / kSortThreads;  // chunks per warp
-    const int cv = (C + V - 1) / V;                        // chunks per sub-range
-    const int nr = cv * V;                                 // registers in use
-    const int w0 = warp * nr * 32;                         // this warp's first element
+    const int C = (n + T - 1) / T;     // chunks per warp
+    const int cv = (C + V - 1) / V;    // chunks per sub-range
+    const int nr = cv * V;             // registers in use
+    const int w0 = warp * nr * 32;     // this warp's first element
     auto elem = [&](int r) { return w0 + ((r % V) * cv + r / V) * 32 + lane; };
-    unsigned k[kRadixChunks];
-    int v[kRadixChunks];
+    unsigned k[kChunks];
+    int v[kChunks];
     unsigned ko = 0u, ka = ~0u;
 #pragma unroll
-    for (int r = 0; r < kRadixChunks; r++) {
+    for (int r = 0; r < kChunks; r++) {
         k[r] = ~0u;  // padding sorts last and stays behind equal real keys
         v[r] = 0;
         const int e = elem(r);
@@ -704,35 +717,35 @@ __device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __rest
     ka = __reduce_and_sync(0xffffffffu, ka);
     if (lane == 0) {
         S.red[warp] = ko;
-        S.red[kRadixWarps + warp] = ka;
+        S.red[SM::kWarps + warp] = ka;
     }
     __syncthreads();
     unsigned all_or = 0u, all_and = ~0u;
 #pragma unroll
-    for (int w = 0; w < kRadixWarps; w++) {
+    for (int w = 0; w < SM::kWarps; w++) {
         all_or |= S.red[w];
-        all_and &= S.red[kRadixWarps + w];
+        all_and &= S.red[SM::kWarps + w];
     }
     const unsigned varying = all_or ^ all_and;
     if (varying == 0u) return false;  // n >= 2 equal depths
     for (int shift = 0; shift < 32; shift += 8) {
         if (((varying >> shift) & 0xffu) == 0u) continue;
         for (int i = lane; i < 256 * V; i += 32)
-            S.hist[(i / V) * kRadixCols + warp * V + (i % V)] = 0;
+            S.hist[(i / V) * kCols + warp * V + (i % V)] = 0;
         __syncwarp();
         // counts need no order: shared-memory atomics, no chain between chunks
 #pragma unroll
-        for (int r = 0; r < kRadixChunks; r++) {
+        for (int r = 0; r < kChunks; r++) {
             if (r >= nr) break;
             const unsigned d = (k[r] >> shift) & 0xffu;
-            atomicAdd(&S.hist[d * kRadixCols + warp * V + r % V], 1);
+            atomicAdd(&S.hist[d * kCols + warp * V + r % V], 1);
         }
         __syncthreads();
         radix_scan(S);
         __syncthreads();
         // V independent chains: chunk r0 / V of every sub-range at once
 #pragma unroll
-        for (int r0 = 0; r0 < kRadixChunks; r0 += V) {
+        for (int r0 = 0; r0 < kChunks; r0 += V) {
             if (r0 >= nr) break;
             unsigned peers[V];
             int slot[V], base[V];
@@ -740,7 +753,7 @@ __device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __rest
             for (int u = 0; u < V; u++) {
                 const unsigned d = (k[r0 + u] >> shift) & 0xffu;
                 peers[u] = __match_any_sync(0xffffffffu, d);
-                slot[u] = d * kRadixCols + warp * V + u;
+                slot[u] = d * kCols + warp * V + u;
                 base[u] = S.hist[slot[u]];
             }
             __syncwarp();
@@ -755,7 +768,7 @@ __device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __rest
         }
         __syncthreads();
 #pragma unroll
-        for (int r = 0; r < kRadixChunks; r++) {
+        for (int r = 0; r < kChunks; r++) {
             if (r >= nr) break;
             const int e = elem(r);
             k[r] = S.key[e];
@@ -766,14 +779,45 @@ __device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __rest
     // neighbours among the real keys?
     bool tie = false;
 #pragma unroll
-    for (int r = 0; r < kRadixChunks; r++) {
+    for (int r = 0; r < kChunks; r++) {
         if (r >= nr) break;
         const int e = elem(r);
         if (e + 1 < n && k[r] == S.key[e + 1]) tie = true;
     }
-    if (__syncthreads_or(tie)) return false;
+    if (__syncthreads_or(tie)) {
+        // each run of equal depths, in id order: the thread holding the
+        // run's first element sorts its ids in place (runs are disjoint)
+        bool too_long = false;
 #pragma unroll
-    for (int r = 0; r < kRadixChunks; r++) {
+        for (int r = 0; r < kChunks; r++) {
+            if (r >= nr) break;
+            const int e = elem(r);
+            if (e + 1 >= n || k[r] != S.key[e + 1] || (e > 0 && S.key[e - 1] == k[r])) continue;
+            int end = e + 2;
+            while (end < n && end - e <= kMaxTieRun && S.key[end] == k[r]) end++;
+            if (end - e > kMaxTieRun) {
+                too_long = true;
+                continue;
+            }
+            for (int a = e + 1; a < end; a++) {
+                const int x = S.val[a];
+                int b = a - 1;
+                while (b >= e && (unsigned)S.val[b] > (unsigned)x) {
+                    S.val[b + 1] = S.val[b];
+                    b--;
+                }
+                S.val[b + 1] = x;
+            }
+        }
+        if (__syncthreads_or(too_long)) return false;
+#pragma unroll
+        for (int r = 0; r < kChunks; r++) {
+            if (r >= nr) break;
+            v[r] = S.val[elem(r)];
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < kChunks; r++) {
         if (r >= nr) break;
         const int e = elem(r);
         if (e < n) out_ids[e] = v[r];
@@ -781,10 +825,42 @@ __device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __rest
     return true;
 }
 
+// Tiles of kSortRun + 1 .. kLargeRun keys: the same radix sort with 512
+// threads and 80 KB of dynamic shared memory, two CTAs per SM, each CTA
+// walking the tile list (largest first) and taking every gridDim.x-th tile.
+// Slot 1 of a tile's counter line (slot 0 is the count) records whether the
+// tile is left to sort_tiles_kernel (1) or done (0); it is written for every
+// tile in this range and read only for those.
+constexpr int kLargeThreads = 512;
+constexpr int kLargeRun = 8192;
+using LargeSmem = RadixSmemT<kLargeThreads, kLargeRun>;
+
+__global__ void __launch_bounds__(kLargeThreads, 2)
+sort_large_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
+                        const int* __restrict__ order, int num_tiles,
+                        const unsigned long long* __restrict__ keys, int* __restrict__ ids,
+                        int* __restrict__ tile_line)
+{
+    extern __shared__ __align__(16) unsigned char s_large[];
+    LargeSmem& S = *reinterpret_cast<LargeSmem*>(s_large);
+    const long long cap = P->capacity;
+    for (int i = blockIdx.x; i < num_tiles; i += gridDim.x) {
+        const int t = order[i];
+        const long long start = min((long long)offset[t], cap);
+        const long long end = min((long long)offset[t + 1], cap);
+        const int n = (int)(end - start);
+        if (n <= kSortRun || n > kLargeRun) continue;
+        __syncthreads();  // the previous tile's last reads of S
+        const bool ok = radix_sort_tile(keys + start, n, S, ids + start);
+        if (threadIdx.x == 0) tile_line[t * kCountPitch + 1] = ok ? 0 : 1;
+    }
+}
+
 __global__ void __launch_bounds__(kSortThreads, MSP_SORT_MIN_BLOCKS)
 sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
                   const int* __restrict__ order, unsigned long long* __restrict__ keys,
-                  unsigned long long* __restrict__ keys_alt, int* __restrict__ ids)
+                  unsigned long long* __restrict__ keys_alt, int* __restrict__ ids,
+                  const int* __restrict__ tile_line)
 {
     __shared__ union {
         unsigned long long bitonic[kSortRun + kSortRun / 16];
@@ -805,6 +881,9 @@ sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offs
         sort_small(keys + start, n, s, nullptr, ids + start);
         return;
     }
+    // kSortRun < n <= kLargeRun: sorted by sort_large_tiles_kernel unless
+    // it left the tile here
+    if (n <= kLargeRun && tile_line[t * kCountPitch + 1] == 0) return;
     // Large tile: sorted runs of kSortRun, then pairwise merges.
     unsigned long long* src = keys + start;
     unsigned long long* dst = keys_alt + start;
@@ -839,11 +918,27 @@ sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offs
         ids[start + i] = (int)(unsigned)(src[i] & 0xffffffffull);
 }
 
-void launch_sort_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s)
+// Two launches: the tiles of kSortRun + 1 .. kLargeRun keys first (a grid
+// of two CTAs per SM walking the tile list), then every other tile.
+int launch_sort_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s)
 {
-    if (num_tiles <= 0) return;
+    if (num_tiles <= 0) return 0;
+    static int sms[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+    if (sms[dev] == 0) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cudaFuncSetAttribute(sort_large_tiles_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(LargeSmem));
+        sms[dev] = n > 0 ? n : 148;
+    }
+    const int grid = std::min(num_tiles, 2 * sms[dev]);
+    sort_large_tiles_kernel<<<grid, kLargeThreads, sizeof(LargeSmem), s>>>(
+        P, B.tile_offset, B.tile_order, num_tiles, B.keys, B.sorted_ids, B.tile_count);
     sort_tiles_kernel<<<num_tiles, kSortThreads, 0, s>>>(P, B.tile_offset, B.tile_order, B.keys, B.keys_alt,
-                                                        B.sorted_ids);
+                                                        B.sorted_ids, B.tile_count);
+    return 2;
 }
 
 // ---------------------------------------------------------------------------

@@ -105,9 +105,10 @@ def test_big_tiles_merge_sort_bitexact():
 @pytest.mark.parametrize("levels", [1, 3])
 def test_tied_depths_sort_bitexact(levels):
     # Every mean on one of `levels` planes facing the camera: most tiles hold
-    # many keys with the same depth, whose order is the ids' (the radix sort
-    # of depths reports the ties and those tiles take the bitonic sort of the
-    # full (depth, id) keys).  One level: every key of a tile ties.
+    # long runs of keys with the same depth, whose order is the ids' (the
+    # radix sort of depths reports runs longer than it orders itself and
+    # those tiles take the bitonic sort of the full (depth, id) keys).  One
+    # level: every key of a tile ties.
     g, cs = _scene(20_000, 640, 480, seed=9, log_mu=math.log(0.03))
     planes = np.linspace(-0.2, 0.2, levels).astype(np.float32)
     g.means[:, 2] = planes[np.arange(g.n) % levels]
@@ -127,6 +128,38 @@ def test_distinct_depths_radix_sizes_bitexact():
     counts = np.diff(run.tile_bins.reshape(-1, 2), axis=1)[:, 0]
     assert 1024 < run.S.max_tile_count <= 2048
     assert ((counts > 0) & (counts <= 128)).sum() > 100 and (counts > 1024).sum() > 100
+    harness.assert_forward_bitexact(run, eng, cs)
+
+
+@pytest.mark.parametrize("levels", [0, 20_000, 60])
+def test_sort_sizes_and_depth_ties_bitexact(levels):
+    # Tiles of 129-2,048 keys (128-thread radix sort) and 2,049-6,400 keys
+    # (512-thread radix sort).  levels = 0: distinct means, yet most large
+    # tiles hold a few equal depths (a tile of 4,000 float depths usually
+    # does); 20,000 depth planes: runs of up to ~6 equal depths, put in id
+    # order inside the radix sorts; 60 planes: runs of ~100, longer than the
+    # radix sorts order, so those tiles fall back to the bitonic (small) and
+    # merge (large) sorts of the full (depth, id) keys.
+    g, cs = _scene(250_000, 640, 480, seed=12, log_mu=math.log(0.03), log_sigma=0.5)
+    if levels:
+        planes = np.linspace(-0.5, 0.5, levels).astype(np.float32)
+        g.means[:, 2] = planes[np.arange(g.n) % levels]
+    run, eng = _render_pair(g, cs)
+    counts = np.diff(run.tile_bins.reshape(-1, 2), axis=1)[:, 0]
+    assert run.P.k_max == 1
+    assert ((counts > 128) & (counts <= 2048)).sum() > 100
+    assert ((counts > 2048) & (counts <= 8192)).sum() > 100
+    harness.assert_forward_bitexact(run, eng, cs)
+
+
+def test_sort_tiles_beyond_large_radix_bitexact():
+    # Two dense clusters: tiles of more than 8,192 keys (merge path) beside
+    # tiles the two radix sorts take, single-pass raster.
+    g, cs = _scene(150_000, 640, 480, seed=12, log_mu=math.log(0.03), log_sigma=0.5, clusters=2)
+    run, eng = _render_pair(g, cs)
+    counts = np.diff(run.tile_bins.reshape(-1, 2), axis=1)[:, 0]
+    assert run.P.k_max == 1 and (counts > 8192).sum() > 10
+    assert ((counts > 2048) & (counts <= 8192)).sum() > 10
     harness.assert_forward_bitexact(run, eng, cs)
 
 
