@@ -639,13 +639,23 @@ struct RadixSmemT {
     static_assert(kChunks % kRadixSplit == 0, "sub-ranges of whole chunks");
     unsigned key[RUN];
     int val[RUN];
-    int hist[256 * kCols];  // [digit * kCols + column], column = warp * split + sub-range
+    // [column * 256 + digit], column = warp * split + sub-range: a warp's
+    // lanes with different digits touch different banks
+    int hist[256 * kCols];
     int wsum[kWarps];
     unsigned red[2 * kWarps];
 };
 using RadixSmem = RadixSmemT<kSortThreads, kSortRun>;
 
-// Exclusive prefix sum of S.hist in place (256 * kCols counters).
+// Exclusive prefix sum of S.hist in place, over the counters in
+// digit-major, column-minor order (256 * kCols counters).
+template <int T, int RUN>
+__device__ __forceinline__ int hist_at(int logical)
+{
+    constexpr int kCols = RadixSmemT<T, RUN>::kCols;
+    return (logical % kCols) * 256 + logical / kCols;
+}
+
 template <int T, int RUN>
 __device__ __forceinline__ void radix_scan(RadixSmemT<T, RUN>& S)
 {
@@ -656,7 +666,7 @@ __device__ __forceinline__ void radix_scan(RadixSmemT<T, RUN>& S)
     int sum = 0;
 #pragma unroll
     for (int i = 0; i < kPer; i++) {
-        c[i] = S.hist[tid * kPer + i];
+        c[i] = S.hist[hist_at<T, RUN>(tid * kPer + i)];
         sum += c[i];
     }
     int incl = sum;
@@ -672,7 +682,7 @@ __device__ __forceinline__ void radix_scan(RadixSmemT<T, RUN>& S)
     for (int w = 0; w < SM::kWarps; w++) base += w < warp ? S.wsum[w] : 0;
 #pragma unroll
     for (int i = 0; i < kPer; i++) {
-        S.hist[tid * kPer + i] = base;
+        S.hist[hist_at<T, RUN>(tid * kPer + i)] = base;
         base += c[i];
     }
 }
@@ -689,7 +699,6 @@ __device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __rest
     using SM = RadixSmemT<T, RUN>;
     constexpr int V = kRadixSplit;
     constexpr int kChunks = SM::kChunks;
-    constexpr int kCols = SM::kCols;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const unsigned lt = (1u << lane) - 1u;
     const int C = (n + T - 1) / T;     // chunks per warp
@@ -730,15 +739,14 @@ __device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __rest
     if (varying == 0u) return false;  // n >= 2 equal depths
     for (int shift = 0; shift < 32; shift += 8) {
         if (((varying >> shift) & 0xffu) == 0u) continue;
-        for (int i = lane; i < 256 * V; i += 32)
-            S.hist[(i / V) * kCols + warp * V + (i % V)] = 0;
+        for (int i = lane; i < 256 * V; i += 32) S.hist[warp * V * 256 + i] = 0;
         __syncwarp();
         // counts need no order: shared-memory atomics, no chain between chunks
 #pragma unroll
         for (int r = 0; r < kChunks; r++) {
             if (r >= nr) break;
             const unsigned d = (k[r] >> shift) & 0xffu;
-            atomicAdd(&S.hist[d * kCols + warp * V + r % V], 1);
+            atomicAdd(&S.hist[(warp * V + r % V) * 256 + d], 1);
         }
         __syncthreads();
         radix_scan(S);
@@ -753,7 +761,7 @@ __device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __rest
             for (int u = 0; u < V; u++) {
                 const unsigned d = (k[r0 + u] >> shift) & 0xffu;
                 peers[u] = __match_any_sync(0xffffffffu, d);
-                slot[u] = d * kCols + warp * V + u;
+                slot[u] = (warp * V + u) * 256 + d;
                 base[u] = S.hist[slot[u]];
             }
             __syncwarp();
