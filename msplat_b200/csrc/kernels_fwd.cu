@@ -500,8 +500,9 @@ void launch_scatter(const StepParams* P, int N, const Buffers& B, cudaStream_t s
 // and sorted by a bitonic network whose element e = thread*K + r lives in
 // register r of `thread` (K = npow / 256): compare-exchange distances below K
 // stay in registers, distances below 32K use warp shuffles, larger ones go
-// through shared memory.  Larger tiles sort kSortRun runs that way and merge
-// them pairwise along merge paths.
+// through shared memory.  Larger tiles that the radix sorts below do not take
+// (more than kLargeRun keys, or refused) sort kSortRun runs that way and
+// merge them pairwise along merge paths.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void cmpx(unsigned long long& lo, unsigned long long& hi, bool up)
 {
