@@ -634,6 +634,33 @@ def exchange_bytes(n: int, world: int, compact: bool, mode: str) -> int:
     return int(share * n * ((15 if compact else 60) + 59) * 4)
 
 
+# Peer copy bandwidth per direction between two B200s of one node over
+# NVLink 5 / NVSwitch, as measured on this pool (nominal: 900 GB/s).
+NVLINK_PEER_GBS = 770.0
+
+
+def exchange_roofline(n: int, world: int, compact: bool, mode: str, ms: float):
+    """The exchange's NVLink bound: the larger of the bytes one rank receives
+    and sends per step (links are full duplex), at the measured per-direction
+    peer bandwidth, against the measured exchange time.  peer: receives its
+    shard of every other rank's gradient rows, sends its updated parameter
+    shard to every other replica; nccl ring all-reduce: 2 (world-1)/world of
+    the 60-float buffer each way."""
+    if world <= 1 or not ms:
+        return None
+    share = (world - 1) / world
+    if mode == "nccl":
+        rx = tx = 2 * share * n * 60 * 4
+    else:
+        rx = share * n * (15 if compact else 60) * 4
+        tx = share * n * 59 * 4
+    bound_ms = max(rx, tx) / (NVLINK_PEER_GBS * 1e9) * 1e3
+    return {"bound": "nvlink", "peak_gbs_per_direction": NVLINK_PEER_GBS,
+            "peak_source": "measured peer copy on this pool", "bytes_in": int(rx),
+            "bytes_out": int(tx), "bound_ms": round(bound_ms, 3),
+            "frac": round(bound_ms / ms, 4)}
+
+
 def run_c4(args, rank: int, world: int) -> dict:
     """BASELINE.json config 4, multi-GPU batched views: 6,000,000 Gaussians
     drawn as in config 1 (seed 0), 8 cameras on the radius-4 sphere at
@@ -730,6 +757,7 @@ def run_c4(args, rank: int, world: int) -> dict:
             "mode": args.dp_mode, "ms_per_step": round(ex_ms, 3),
             "nvlink_bytes_per_rank": xbytes,
             "gbs_per_rank": round(xbytes / (ex_ms / 1000.0) / 1e9, 1) if ex_ms else None,
+            "roofline": exchange_roofline(model.n, world, dist.compact, args.dp_mode, ex_ms),
             "timing": "CUDA events around the exchange + Adam of each step (includes waiting "
                       "for the slowest rank's gradients), mean over steps, max over ranks"},
         "intersections_last_view": n_isect,

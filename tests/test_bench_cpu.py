@@ -41,3 +41,15 @@ def test_exchange_bytes():
     assert bench.exchange_bytes(n, 8, True, "peer") == int(7 / 8 * n * 74 * 4)
     # ring all-reduce of the 60-float buffer
     assert bench.exchange_bytes(n, 4, False, "nccl") == int(2 * 0.75 * n * 60 * 4)
+
+
+def test_exchange_roofline():
+    n = 6_000_000
+    assert bench.exchange_roofline(n, 1, False, "peer", 1.0) is None
+    r = bench.exchange_roofline(n, 8, True, "peer", 2.967)
+    # compact at 8 ranks: the parameter write-back (59 floats) is the larger way
+    assert r["bytes_out"] == int(7 / 8 * n * 59 * 4) and r["bytes_in"] == int(7 / 8 * n * 15 * 4)
+    assert abs(r["bound_ms"] - r["bytes_out"] / 770e9 * 1e3) < 1e-3
+    assert 0.5 < r["frac"] < 0.6
+    r = bench.exchange_roofline(n, 4, False, "peer", 3.907)
+    assert r["bytes_in"] > r["bytes_out"]          # 60 gradient floats in, 59 out
