@@ -607,12 +607,17 @@ int msplat_dp_reduce_adam(int rank, int world, int num_points, int features_rest
         dp_wait_kernel<<<1, 32, 0, s>>>(a, 0, kDpWaitGrads);
 #define MSP_COMPACT(W)                                                                          \
     do {                                                                                        \
-        static bool set = false;                                                                \
-        if (!set) {                                                                             \
-            DP_CUDA(cudaFuncSetAttribute(dp_compact_kernel<W>,                                   \
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024)); \
-            set = true;                                                                         \
-        }                                                                                       \
+        static std::once_flag once_[kMaxDeviceSlots];                                           \
+        static cudaError_t set_err_[kMaxDeviceSlots];                                           \
+        int dev_ = 0;                                                                           \
+        if (!once_per_device(once_, [](int d) {                                                 \
+                set_err_[d] = cudaFuncSetAttribute(dp_compact_kernel<W>,                        \
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                                   96 * 1024);                                  \
+            }))                                                                                 \
+            DP_CUDA(cudaErrorNoDevice);                                                         \
+        DP_CUDA(cudaGetDevice(&dev_));                                                          \
+        DP_CUDA(set_err_[dev_]);                                                                \
         dp_compact_kernel<W><<<grid, kDpThreads, smem, s>>>(a);                                 \
     } while (0)
         switch (world) {

@@ -5,6 +5,8 @@
 
 #include <mutex>
 
+#include "errors.h"
+
 namespace msp {
 
 constexpr int kGroups = 6;        // means, scales, quats, features_dc, features_rest, opacities
@@ -37,12 +39,6 @@ struct StepParams {
     int num_adam_groups;
     int pad0;
     long long capacity;
-};
-
-// Device error word bits (read back by the host after a step).
-enum ErrorBits : int {
-    kErrIsectOverflow = 1,   // intersections exceeded the key buffer
-    kErrStageTimeout = 2,    // a bulk copy into shared memory did not complete in time
 };
 
 // Per-Gaussian geometry written by the projection and read by binning and
@@ -135,6 +131,20 @@ struct ApplyArgs {
 inline int num_sh_bases_host(int degree)
 {
     return degree <= 0 ? 1 : degree == 1 ? 4 : degree == 2 ? 9 : degree == 3 ? 16 : 25;
+}
+
+// Per-device one-time set-up (kernel attributes such as the dynamic
+// shared-memory limit are per device; entry points may be called from
+// several host threads, some without the engine lock).  Runs f(dev) once for
+// the current device and table; false when there is no usable device.
+constexpr int kMaxDeviceSlots = 64;
+template <class F>
+inline bool once_per_device(std::once_flag (&flags)[kMaxDeviceSlots], F&& f)
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDeviceSlots) return false;
+    std::call_once(flags[dev], f, dev);
+    return true;
 }
 
 // Camera arguments of one call, as passed through the C-ABI.

@@ -932,16 +932,18 @@ sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offs
 int launch_sort_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s)
 {
     if (num_tiles <= 0) return 0;
-    static int sms[64] = {0};
+    static std::once_flag once[kMaxDeviceSlots];
+    static int sms[kMaxDeviceSlots];
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
-    if (sms[dev] == 0) {
-        int n = 0;
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        cudaFuncSetAttribute(sort_large_tiles_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)sizeof(LargeSmem));
-        sms[dev] = n > 0 ? n : 148;
-    }
+    if (!once_per_device(once, [](int d) {
+            int n = 0;
+            cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
+            cudaFuncSetAttribute(sort_large_tiles_kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)sizeof(LargeSmem));
+            sms[d] = n > 0 ? n : 148;
+        }) || cudaGetDevice(&dev) != cudaSuccess)
+        return 0;
     const int grid = std::min(num_tiles, 2 * sms[dev]);
     sort_large_tiles_kernel<<<grid, kLargeThreads, sizeof(LargeSmem), s>>>(
         P, B.tile_offset, B.tile_order, num_tiles, B.keys, B.sorted_ids, B.tile_count);

@@ -242,13 +242,12 @@ ssim_loss_fused_kernel(const StepParams* __restrict__ P, const float* __restrict
 void launch_ssim(const StepParams* P, int W, int H, const float* gt, const Buffers& B,
                  cudaStream_t s)
 {
-    static bool configured = false;
+    static std::once_flag once[kMaxDeviceSlots];
     const int smem = (int)sizeof(SsimSmem);
-    if (!configured) {
+    once_per_device(once, [smem](int) {
         cudaFuncSetAttribute(ssim_loss_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              smem);
-        configured = true;
-    }
+    });
     dim3 grid((W + kT - 1) / kT, (H + kT - 1) / kT);
     ssim_loss_fused_kernel<<<grid, kSsimThreads, smem, s>>>(P, B.out_img, gt, B.v_rendered,
                                                              B.loss_sum);

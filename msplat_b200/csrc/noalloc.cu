@@ -213,11 +213,15 @@ extern "C" int msplat_render_noalloc(
     NA_CUDA(cudaMemcpyAsync(&h_check[1], B.tile_offset + p.num_tiles, sizeof(int),
                             cudaMemcpyDeviceToHost, st));
     NA_CUDA(cudaStreamSynchronize(st));
-    if (h_check[0] & kErrIsectOverflow) {
+    const char* what = nullptr;
+    rc = render_status(h_check[0], &what);
+    if (rc == MSPLAT_ERR_OVERFLOW) {
         set_error("msplat_render_noalloc: %d tile intersections exceed the %lld slots of the "
                   "static scratch; the image is incomplete",
                   h_check[1], cap);
-        return MSPLAT_ERR_OVERFLOW;
+    } else if (rc != MSPLAT_OK) {
+        set_error("msplat_render_noalloc: %s (error word 0x%x); the image is incomplete", what,
+                  (unsigned)h_check[0]);
     }
-    return MSPLAT_OK;
+    return rc;
 }

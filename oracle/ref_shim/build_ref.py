@@ -6,7 +6,7 @@ writes only under oracle/_ref/ (git-ignored; it travels to the GPU box).
 Nothing of the reference is copied into the repository.
 
 Mechanical transforms applied to the kernel source before compiling it as
-C++ (each keeps the reference's arithmetic; see DESIGN.md for why):
+C++ (each keeps the reference's arithmetic):
   1. the Metal header include and `using namespace metal` are dropped;
      address-space qualifiers become C++ (constant -> const, device/thread ->
      nothing, kernel -> nothing) and [[attributes]] are removed;
@@ -40,7 +40,10 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE = os.path.dirname(HERE)
 OUT = os.path.join(ORACLE, "_ref")
-REFERENCE = os.environ.get("MSPLAT_REFERENCE", "/root/reference")
+# The reference checkout: $MSPLAT_REFERENCE, else a "reference" directory
+# beside this repository.
+REFERENCE = os.environ.get("MSPLAT_REFERENCE") or os.path.join(
+    os.path.dirname(os.path.dirname(ORACLE)), "reference")
 METAL = os.path.join(REFERENCE, "core", "metal", "msplat_metal.metal")
 REF_TILE_CAP = int(os.environ.get("REF_TILE_CAP", "16384"))
 

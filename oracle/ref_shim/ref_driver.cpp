@@ -8,8 +8,9 @@
 // chunk rule (:873-889), the SH Adam hyper-parameter block (:1078-1092) and
 // fused_adam over groups 0, 1, 2, 5 (:1117-1139).  The only departure is
 // that threadgroups at the right/bottom image edge of the 16x16
-// dispatchThreads grids (SSIM passes) get all 256 threads; see
-// msl_runtime.hpp and DESIGN.md.
+// dispatchThreads grids (SSIM passes) get all 256 threads (the kernels'
+// cooperative tile loads stride by 256 and would otherwise leave part of
+// the tile unwritten; every access is bounds-checked); see msl_runtime.hpp.
 #include <omp.h>
 
 #include <cmath>

@@ -69,3 +69,42 @@ def close(a, b, rtol, atol_frac):
     tol = rtol * np.maximum(np.abs(a), np.abs(b)) + atol_frac * scale
     bad = np.abs(a - b) > tol
     return int(bad.sum()), float((np.abs(a - b) / scale).max()) if a.size else 0.0
+
+
+# Gradient bar (north star: 1e-4 relative), with an absolute floor for the
+# float-atomic sums: |a-b| <= GRAD_RTOL*max(|a|,|b|) + GRAD_ATOL_FRAC*max|ref|.
+# No outliers are allowed on gradients.
+GRAD_RTOL = 1e-4
+GRAD_ATOL_FRAC = 2e-6
+
+
+def engine_geometry_grads(groups, cs, gt_dev, ssim_weight=0.2):
+    """The engine's pre-Adam gradients of one step from `groups` (a fresh
+    model, so the fused step's in-place update does not interfere), through
+    msplat_train_step_grads: the same forward, backward and projection VJP
+    as msplat_train_step, with the Adam phase replaced by a gradient write.
+    Returns v_mean3d [N,3], v_scale [N,3] (log-space), v_quat [N,4] and
+    v_opacity [N,1] (logit), zero for culled Gaussians."""
+    import torch
+
+    from msplat_b200 import multigpu
+    model = engine.GaussianModel(groups)
+    buf = torch.zeros(multigpu.grad_floats(model.n, model.rest_bases), dtype=torch.float32,
+                      device="cuda")
+    multigpu.EngineOps().grads(model, cs, gt_dev, buf, ssim_weight, BG, 1.0, 0.01)
+    torch.cuda.synchronize()
+    views, _ = multigpu.grad_views(buf, model.n, model.rest_bases)
+    out = {"v_mean3d": views[0], "v_scale": views[1], "v_quat": views[2], "v_opacity": views[5]}
+    return {k: v.cpu().numpy() for k, v in out.items()}
+
+
+def assert_geometry_grads(eng, run, label=""):
+    """Geometry gradients against the oracle's at the gradient bar, every
+    entry (no outlier allowance)."""
+    n = eng["v_mean3d"].shape[0]
+    ref = {"v_mean3d": run.v_mean3d.reshape(n, 3), "v_scale": run.v_scale.reshape(n, 3),
+           "v_quat": run.v_quat.reshape(n, 4), "v_opacity": run.v_opacity.reshape(n, 1)}
+    for key, want in ref.items():
+        bad, worst = close(eng[key], want, GRAD_RTOL, GRAD_ATOL_FRAC)
+        print(f"  {label}{key}: out-of-tolerance={bad} worst|diff|/max={worst:.3g}")
+        assert bad == 0, f"{label}{key}: {bad} entries out of tolerance (worst {worst:.3g} of max)"

@@ -28,8 +28,8 @@ from tests import harness
 
 pytestmark = pytest.mark.gpu
 
-GRAD_RTOL = 1e-4
-GRAD_ATOL_FRAC = 2e-6     # absolute floor, as a fraction of the tensor's max |value|
+GRAD_RTOL = harness.GRAD_RTOL            # 1e-4
+GRAD_ATOL_FRAC = harness.GRAD_ATOL_FRAC  # absolute floor, as a fraction of the tensor's max |value|
 PARAM_RTOL = 1e-4
 PARAM_OUTLIER_FRAC, PARAM_OUTLIER_CAP = 2e-6, 1e-4
 
@@ -244,6 +244,16 @@ def _check_train(model, run, params, m, v, st, cs, check_grads=True, exact_forwa
         assert bad == 0, f"{label}: {bad} out of tolerance (worst {worst:.3g})"
 
 
+def _check_geometry_grads(g, cs, gt, run, ssim_weight=0.2):
+    """The projection VJP's outputs (v_mean3d, v_scale, v_quat) and the
+    opacity gradient before Adam, from msplat_train_step_grads on the same
+    inputs, against the oracle's first step at the gradient bar, every entry."""
+    import torch
+    eng = harness.engine_geometry_grads(g.groups(), cs, torch.as_tensor(gt).cuda().contiguous(),
+                                        ssim_weight)
+    harness.assert_geometry_grads(eng, run)
+
+
 def test_train_step_c0():
     g, cams = synthetic.scene("C0")
     cs = harness.setup_cam(cams[0])
@@ -252,19 +262,24 @@ def test_train_step_c0():
     _check_train(*out, cs)
     run = out[1]
     assert abs(_lib.load().msplat_last_loss(1) - run.loss) <= 1e-4 * abs(run.loss)
+    _check_geometry_grads(g, cs, gt, run)
 
 
 def test_train_step_monolithic():
     g, cs = _scene(40_000, 640, 480, seed=9)
     gt = synthetic.target_image(cs.width, cs.height, 2)
-    _check_train(*_train_pair(g, cs, gt), cs)
+    out = _train_pair(g, cs, gt)
+    _check_train(*out, cs)
+    _check_geometry_grads(g, cs, gt, out[1])
 
 
 @pytest.mark.parametrize("dtu", [0, 1, 2])
 def test_train_step_partial_sh(dtu):
     g, cs = _scene(8_000, 160, 120, seed=10 + dtu)
     gt = synthetic.target_image(cs.width, cs.height, 3)
-    _check_train(*_train_pair(g, cs, gt, dtu=dtu), cs)
+    out = _train_pair(g, cs, gt, dtu=dtu)
+    _check_train(*out, cs)
+    _check_geometry_grads(g, cs, gt, out[1])
 
 
 def test_train_three_steps():
@@ -276,4 +291,6 @@ def test_train_three_steps():
 def test_train_step_l1_only():
     g, cs = _scene(8_000, 128, 96, seed=13)
     gt = synthetic.target_image(cs.width, cs.height, 5)
-    _check_train(*_train_pair(g, cs, gt, ssim_weight=0.0), cs)
+    out = _train_pair(g, cs, gt, ssim_weight=0.0)
+    _check_train(*out, cs)
+    _check_geometry_grads(g, cs, gt, out[1], ssim_weight=0.0)

@@ -15,6 +15,7 @@ from __future__ import annotations
 
 import ctypes as C
 import math
+import re
 
 import numpy as np
 import pytest
@@ -87,3 +88,37 @@ def test_noalloc_matches_render_twice(case):
         got = out.cpu().numpy()
         np.testing.assert_allclose(got, expect, rtol=RTOL, atol=ATOL,
                                    err_msg=f"{case}: call {call}")
+
+
+@pytest.mark.gpu
+def test_noalloc_reports_intersection_overflow():
+    """4,000 large Gaussians in front of a 1280x720 camera each cover most
+    of its 3,600 tiles: 12.7M intersections, more than the ~2.9M slots left
+    in the static array once the per-pixel buffers are carved out.  The
+    size check passes (it budgets 16 slots per Gaussian); the overflow is
+    found on the device and reported, not returned as success."""
+    import torch
+    assert torch.cuda.is_available(), "no-alloc render test needs a CUDA device"
+    engine.bind_stream()
+    g = synthetic.gaussians(4_000, 11, mean_range=0.2, log_scale_mu=math.log(0.5),
+                            log_scale_sigma=0.1)
+    cs = harness.setup_cam(synthetic.front_camera(1280, 720, 3.0))
+    model = engine.GaussianModel(g.groups())
+    out = torch.empty(cs.height * cs.width * 3, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    lib = _lib.load()
+    rc = _call_noalloc(model, cs, out.data_ptr(), stream)
+    msg = lib.msplat_last_error().decode()
+    assert rc == -3, (rc, msg)          # MSPLAT_ERR_OVERFLOW
+    m = re.search(r"(\d+) tile intersections exceed the (\d+) slots of the static scratch", msg)
+    assert m, msg
+    n_isect, slots = int(m.group(1)), int(m.group(2))
+    assert n_isect > slots > 16 * g.n, msg
+    # the next call on a size that fits is unaffected
+    g2 = synthetic.gaussians(5_000, 12, mean_range=1.0, log_scale_mu=math.log(0.02),
+                             log_scale_sigma=0.3)
+    model2 = engine.GaussianModel(g2.groups())
+    expect = engine.download(engine.render(model2, cs), cs.height * cs.width * 3, np.float32)
+    rc = _call_noalloc(model2, cs, out.data_ptr(), stream)
+    assert rc == 0, lib.msplat_last_error().decode()
+    np.testing.assert_allclose(out.cpu().numpy(), expect, rtol=RTOL, atol=ATOL)
