@@ -532,6 +532,16 @@ int msplat_device_errors(void);
 int msplat_debug_buffer(const char *name, void **dev_ptr, long long *count);
 /* Number of kernel launches the engine issued since the last reset. */
 long long msplat_kernel_launches(int reset);
+/* Raster work of the last forward (render or training step), for
+ * benchmarks; no counterpart in the reference.  Replays the reference's
+ * per-pixel loop (nd_rasterize_forward_kernel, msplat_metal.metal:472-585)
+ * over the engine's sorted lists and writes four sums over the image:
+ * out[0] list positions visited before termination, out[1] pairs whose
+ * sigma passes (0 <= sigma < 5.55), out[2] pairs blended into the pixel
+ * (E, the contributing pixel.Gaussian evaluations), out[3] positions the
+ * backward walks (rasterize_backward_kernel, :898-1099).  Synchronous.
+ * MSPLAT_ERR_ARG when no forward ran yet or the last one was depth-chunked. */
+int msplat_count_raster_work(unsigned long long *out);
 
 #ifdef __cplusplus
 }

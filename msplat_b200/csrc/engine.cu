@@ -82,6 +82,9 @@ struct Engine {
     float last_loss = 0.f;
     double last_loss_scale = 1.0;
     long long growth_isect = 0;  // requested capacity after an overflow
+    int last_k_max = 0;          // depth chunks of the last forward (0: none yet)
+    int last_num_tiles = 0;
+    unsigned long long* d_work = nullptr;  // msplat_count_raster_work's counters
     // timing
     bool timing = false;
     cudaEvent_t st_ev[kStages + 1][kRing] = {};
@@ -377,6 +380,8 @@ static int run_forward(const StepParams& p, const float* means, const float* sca
     const int sort_launches = launch_sort_tiles(g.d_params, p.num_tiles, B, st);
     tm.mark(2, st);
     launch_raster_forward(g.d_params, p.num_tiles, p.k_max, p.img_w, p.img_h, B, st);
+    g.last_k_max = p.k_max;
+    g.last_num_tiles = p.num_tiles;
     g.launches += 3 + sort_launches + (p.k_max > 1 ? 2 : 1);
     MSP_CUDA(cudaGetLastError());
     return MSPLAT_OK;
@@ -475,6 +480,9 @@ void cleanup_msplat_cuda(void)
     cudaStreamSynchronize(g.stream());
     free_buffers();
     stage_release();
+    if (g.d_work) cudaFree(g.d_work);
+    g.d_work = nullptr;
+    g.last_k_max = 0;
     g.growth_isect = 0;
 }
 
@@ -895,6 +903,30 @@ int msplat_debug_buffer(const char* name, void** dev_ptr, long long* count)
     }
     set_error("unknown buffer '%s'", name);
     return MSPLAT_ERR_ARG;
+}
+
+int msplat_count_raster_work(unsigned long long* out)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g.ready || !out) {
+        set_error("msplat_count_raster_work: engine not initialised or null output");
+        return MSPLAT_ERR_ARG;
+    }
+    if (g.last_k_max != 1) {
+        set_error("msplat_count_raster_work: the last forward was %s",
+                  g.last_k_max == 0 ? "never run" : "depth-chunked (counts cover the single-pass "
+                                                    "path only)");
+        return MSPLAT_ERR_ARG;
+    }
+    cudaStream_t st = g.stream();
+    if (!g.d_work) MSP_CUDA(cudaMalloc(&g.d_work, 4 * sizeof(unsigned long long)));
+    MSP_CUDA(cudaMemsetAsync(g.d_work, 0, 4 * sizeof(unsigned long long), st));
+    launch_count_raster_work(g.d_params, g.last_num_tiles, g.B, g.d_work, st);
+    MSP_CUDA(cudaGetLastError());
+    MSP_CUDA(cudaMemcpyAsync(out, g.d_work, 4 * sizeof(unsigned long long),
+                             cudaMemcpyDeviceToHost, st));
+    MSP_CUDA(cudaStreamSynchronize(st));
+    return MSPLAT_OK;
 }
 
 long long msplat_kernel_launches(int reset)

@@ -188,6 +188,8 @@ void launch_project_forward(const StepParams* P, int N, const float* means, cons
 void launch_scan_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s);
 void launch_scatter(const StepParams* P, int N, const Buffers& B, cudaStream_t s);
 int launch_sort_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s);
+void launch_count_raster_work(const StepParams* P, int num_tiles, const Buffers& B,
+                              unsigned long long* d_out, cudaStream_t s);
 void launch_raster_forward(const StepParams* P, int num_tiles, int k_max, int W, int H,
                            const Buffers& B, cudaStream_t s);
 void launch_ssim(const StepParams* P, int W, int H, const float* gt, const Buffers& B,

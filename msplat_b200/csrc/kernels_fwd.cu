@@ -1123,6 +1123,73 @@ merge_chunks_kernel(const StepParams* __restrict__ P, const int* __restrict__ of
     out_img[3 * pix + 2] = saturatef_ref(fmaf(P->bg[2], Tr, r2));
 }
 
+// ---------------------------------------------------------------------------
+// Work counts of the last single-pass forward, for the benchmark's
+// instruction-per-evaluation and FP32 rooflines (not on the training path).
+// Each pixel replays the reference's per-pixel loop over its tile's sorted
+// list (nd_rasterize_forward_kernel, msplat_metal.metal:472-585) with the
+// forward's arithmetic and counts, summed over the image:
+//   out[0] list positions the loop visits (the terminating one included),
+//   out[1] of those, pairs with 0 <= sigma < 5.55 (the exp is evaluated),
+//   out[2] pairs blended into the pixel (alpha >= 1/255, not terminating):
+//          E, the contributing pixel.Gaussian evaluations,
+//   out[3] list positions the reference's backward walks for the pixel
+//          (rasterize_backward_kernel, :898-1099: from the last contributor
+//          back to the list start).
+// One CTA per tile in plain tile order, list entries read from global memory.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kTileThreads)
+count_raster_work_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
+                         const int* __restrict__ ids, const float2* __restrict__ g_xy,
+                         const float4* __restrict__ g_co, unsigned long long* __restrict__ out)
+{
+    const int tile = blockIdx.x;
+    const int tx_n = P->tiles_x;
+    const int px = (tile % tx_n) * kBlockX + (threadIdx.x & 15);
+    const int py = (tile / tx_n) * kBlockY + (threadIdx.x >> 4);
+    const long long cap = P->capacity;
+    const int beg = (int)min((long long)offset[tile], cap);
+    const int end = (int)min((long long)offset[tile + 1], cap);
+    unsigned visited = 0, passed = 0, blended = 0, walk = 0;
+    if (px < P->img_w && py < P->img_h) {
+        const float fpx = (float)px, fpy = (float)py;
+        float T = 1.f;
+        int last = beg - 1;
+        for (int i = beg; i < end; i++) {
+            visited++;
+            const int g = ids[i];
+            const float4 co = g_co[g];
+            const float2 xy = g_xy[g];
+            const float dx = xy.x - fpx, dy = xy.y - fpy;
+            const float sigma = fmaf(0.5f, fmaf(co.x, dx * dx, co.z * dy * dy), co.y * dx * dy);
+            if (sigma < 0.f || sigma >= 5.55f) continue;
+            passed++;
+            const float alpha = fminf(0.999f, co.w * msp_expf_normal(-sigma));
+            if (alpha < 1.f / 255.f) continue;
+            const float next_T = T * (1.f - alpha);
+            if (next_T <= 1e-4f) break;
+            blended++;
+            T = next_T;
+            last = i;
+        }
+        walk = (unsigned)(last - beg + 1);
+    }
+    const unsigned v[4] = {visited, passed, blended, walk};
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        const unsigned s = __reduce_add_sync(0xffffffffu, v[k]);
+        if ((threadIdx.x & 31) == 0 && s) atomicAdd(&out[k], (unsigned long long)s);
+    }
+}
+
+void launch_count_raster_work(const StepParams* P, int num_tiles, const Buffers& B,
+                              unsigned long long* d_out, cudaStream_t s)
+{
+    if (num_tiles <= 0) return;
+    count_raster_work_kernel<<<num_tiles, kTileThreads, 0, s>>>(P, B.tile_offset, B.sorted_ids,
+                                                               B.proj.xy, B.proj.conic_op, d_out);
+}
+
 void launch_raster_forward(const StepParams* P, int num_tiles, int k_max, int W, int H,
                            const Buffers& B, cudaStream_t s)
 {
