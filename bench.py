@@ -3,6 +3,9 @@
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   python bench.py --config C3 [--iterations 7000]     (training-run report)
   python bench.py --config C4 [--gpus N] [--steps K]  (batched views, 8 per step)
+  python bench.py --config C2                         (3M clustered Gaussians, 1920x1080)
+  python bench.py --profile-step                      (one C1 step for ncu)
+  python bench.py --summarize-ncu CSV... --hash-file F (per-kernel counter summary)
 
 Workload (N=1): BASELINE.json config 1 -- 1,000,000 seeded synthetic
 Gaussians rendered at 1297x840 from 16 cameras on a radius-4 sphere, the
@@ -30,6 +33,15 @@ Gaussians, a batch of 8 views at 1920x1080 per step, each of N in
 {1, 2, 4, 8} GPUs training 8/N of them (gradients accumulated per rank),
 one exchange and one Adam update per step; the batch is fixed, so scaling
 is strong.  It reports views/s and the exchange's time and NVLink bytes.
+The default C1 run appends the same C4 measurement on the same N GPUs as
+its `c4` object (--no-c4 skips it).
+
+Rooflines: `roofline` is the HBM-bound optimiser stage; `hbm_rooflines`
+adds the projection forward; `issue_roofline` the issue-bound stages
+(instruction counts from the committed per-kernel ncu summary
+profiles/counters_c1_train_step.txt, used only when its build hash equals
+this build's); `raster_work` the engine's count of the reference loop's
+pixel.Gaussian work (E) and the rasterizers' FP32 rooflines.
 
 --impl reference times the reference's CPU implementation of the path (the
 oracle port, or oracle/_ref when the reference was compiled) on the host
@@ -67,12 +79,23 @@ def parse():
                     help="N > 1: optimiser over NVLink peer memory, or NCCL all-reduce")
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the timed CPU oracle sample (profiling runs)")
-    ap.add_argument("--config", choices=("C1", "C3", "C4"), default="C1",
-                    help="C1 (default): the headline step benchmark; C3: BASELINE.json config 3, "
+    ap.add_argument("--config", choices=("C1", "C2", "C3", "C4"), default="C1",
+                    help="C1 (default): the headline step benchmark, followed by a C4 leg "
+                         "(--no-c4 skips it); C2: BASELINE.json config 2, the same step on 3M "
+                         "clustered Gaussians at 1920x1080; C3: BASELINE.json config 3, "
                          "a 7000-iteration training run with densification, reporting steps/s "
                          "and held-out PSNR/SSIM (one GPU); C4: BASELINE.json config 4, "
                          "6M Gaussians, 8 views of 1920x1080 per step over N GPUs")
     ap.add_argument("--iterations", type=int, default=7000, help="C3: training iterations")
+    ap.add_argument("--no-c4", action="store_true",
+                    help="C1: skip the C4 batched-view leg reported under 'c4'")
+    ap.add_argument("--profile-step", action="store_true",
+                    help="for ncu: the C1 workload, W warm-up steps, then one training step "
+                         "between cudaProfilerStart and cudaProfilerStop; prints the build hash")
+    ap.add_argument("--summarize-ncu", nargs="+", metavar="CSV",
+                    help="write the per-kernel counter summary from ncu --csv logs of "
+                         "--profile-step runs (no GPU needed)")
+    ap.add_argument("--hash-file", help="--summarize-ncu: the JSON line --profile-step printed")
     return ap.parse_args()
 
 
@@ -142,32 +165,157 @@ def peaks() -> dict:
     return {"hbm_gbs": 6650.0, "source": "fallback"}
 
 
-# Per-step figures from one ncu capture of the first C1 training step
-# (profiles/kernels_c1_train_step.md): DRAM bytes of the optimiser stage
-# (rest_adam_kernel + project_backward_adam_kernel) and warp instructions of
-# the issue-bound kernels.  Instruction counts vary a little with the view;
-# the capture's view stands for all.
-C1_OPT_STAGE_TRAFFIC = 510080000 + 344294912 + 235875840 + 117640448
-C1_WARP_INSTR = {"rast_fwd": ("raster_forward_kernel<0>", 364023216),
-                 "rast_bwd": ("raster_backward_kernel<0,2>", 564315330),
-                 "loss_fwd_bwd": ("ssim_loss_fused_kernel", 105998350)}
-SM_COUNT, ISSUE_PER_SM_CLK = 148, 4
+# ---------------------------------------------------------------------------
+# Per-kernel counters of one C1 training step, from ncu.  They live in a
+# committed text summary, one row per kernel, tagged with the hash of the
+# sources they were captured from; a run whose sources hash differently
+# reports them as stale and derives nothing from them.
+#
+# Capture (one GPU, one kernel per ncu command, one launch each; the step is
+# bracketed by cudaProfilerStart/Stop in --profile-step mode):
+#   python bench.py --profile-step > gpurun_out/profile_step.json &&
+#   ncu --profile-from-start off --clock-control none --kernel-name-base function \
+#       -k regex:<KERNEL> -c 1 --metrics <COUNTER_METRICS> --csv --print-units base \
+#       --log-file gpurun_out/ctr_<KERNEL>.csv python bench.py --profile-step
+# Summary:
+#   python bench.py --summarize-ncu gpurun_out/ctr_*.csv \
+#       --hash-file gpurun_out/profile_step.json
+# ---------------------------------------------------------------------------
+COUNTERS_FILE = os.path.join(ROOT, "profiles", "counters_c1_train_step.txt")
+COUNTER_METRICS = ("dram__bytes_read.sum", "dram__bytes_write.sum", "smsp__inst_executed.sum",
+                   "gpu__time_duration.sum")
+# kernel (ncu base name) -> stage of the engine's stage timer it runs in
+PROFILED_KERNELS = {
+    "project_forward_kernel": "proj_sh_fwd",
+    "scan_tiles_kernel": "bin_sort",
+    "scatter_kernel": "bin_sort",
+    "sort_large_tiles_kernel": "bin_sort",
+    "sort_tiles_kernel": "bin_sort",
+    "raster_forward_kernel": "rast_fwd",
+    "ssim_loss_fused_kernel": "loss_fwd_bwd",
+    "raster_backward_kernel": "rast_bwd",
+    "project_backward_adam_kernel": "proj_bwd_adam",
+    "rest_adam_kernel": "proj_bwd_adam",
+}
+SM_COUNT, ISSUE_PER_SM_CLK, FP32_LANES_PER_SM = 148, 4, 128
 
 
-def issue_rooflines(stage_ms: dict, sm_mhz: float) -> list:
-    """Achieved warp-instruction issue rate of the issue-bound kernels
-    against the SMs' issue slots (148 SMs x 4 schedulers x 1/clock at the SM
-    clock sampled during the timed region)."""
+def build_hash() -> str:
+    """First 12 hex digits of the SHA-256 of the engine's sources (kernels,
+    host code, headers and the build recipe), files in name order."""
+    import hashlib
+    h = hashlib.sha256()
+    for d in (os.path.join("msplat_b200", "csrc"), "include"):
+        base = os.path.join(ROOT, d)
+        for f in sorted(os.listdir(base)):
+            if f.endswith((".cu", ".cuh", ".h", ".hpp")):
+                h.update(f.encode())
+                with open(os.path.join(base, f), "rb") as fh:
+                    h.update(fh.read())
+    with open(os.path.join(ROOT, "msplat_b200", "build.py"), "rb") as fh:
+        h.update(fh.read())
+    return h.hexdigest()[:12]
+
+
+def load_counters(path: str = COUNTERS_FILE) -> dict:
+    """{"build": hash, "view": camera index, "kernels": {name: {...}}} from
+    the committed summary, or {} when it is absent."""
+    if not os.path.exists(path):
+        return {}
+    out = {"build": None, "view": None, "kernels": {}}
+    cols = None
+    with open(path) as f:
+        for line in f:
+            line = line.rstrip("\n")
+            if line.startswith("# build "):
+                out["build"] = line.split()[2]
+            elif line.startswith("# view "):
+                out["view"] = int(line.split()[2])
+            elif not line or line.startswith("#"):
+                continue
+            elif cols is None:
+                cols = line.split("\t")
+            else:
+                row = dict(zip(cols, line.split("\t")))
+                out["kernels"][row["kernel"]] = {
+                    k: (v if k in ("kernel", "launch") else float(v)) for k, v in row.items()}
+    return out
+
+
+def summarize_ncu(csv_paths, hash_file: str, out_path: str = COUNTERS_FILE) -> str:
+    """Write the counters summary from ncu --csv logs of --profile-step runs
+    (one kernel each).  The build hash and the profiled view come from the
+    JSON line --profile-step printed."""
+    import csv as _csv
+    with open(hash_file) as f:
+        info = json.loads([ln for ln in f if ln.strip().startswith("{")][-1])
+    rows = {}
+    for pth in csv_paths:
+        with open(pth) as f:
+            lines = [ln for ln in f if ln.startswith('"')]
+        for rec in _csv.DictReader(lines):
+            name = rec.get("Kernel Name", "")
+            base = name.split("(")[0].split("<")[0].split("::")[-1].strip()
+            if base not in PROFILED_KERNELS:
+                continue
+            r = rows.setdefault(base, {"kernel": base, "launch": name.split("(")[0].strip()})
+            metric, val = rec.get("Metric Name"), rec.get("Metric Value", "").replace(",", "")
+            if metric in COUNTER_METRICS:
+                r[metric] = float(val)
+    cols = ["kernel", "launch", "dram_read_bytes", "dram_write_bytes", "warp_instructions",
+            "duration_ns"]
+    keys = dict(zip(cols[2:], COUNTER_METRICS))
+    lines = ["# ncu counters of one C1 training step: one launch of each kernel, captured",
+             "# alone (--clock-control none; durations are cold-cache and serialised).",
+             f"# build {info['build_hash']}",
+             f"# view {info['view']}",
+             "# command, per kernel K (repository root, one GPU):",
+             "#   python bench.py --profile-step > gpurun_out/profile_step.json &&",
+             "#   ncu --profile-from-start off --clock-control none --kernel-name-base function \\",
+             f"#       -k regex:K -c 1 --metrics {','.join(COUNTER_METRICS)} \\",
+             "#       --csv --print-units base \\",
+             "#       --log-file gpurun_out/ctr_K.csv python bench.py --profile-step",
+             "# summary: python bench.py --summarize-ncu gpurun_out/ctr_*.csv "
+             "--hash-file gpurun_out/profile_step.json",
+             "\t".join(cols)]
+    for k in PROFILED_KERNELS:
+        if k in rows and all(m in rows[k] for m in COUNTER_METRICS):
+            r = rows[k]
+            lines.append("\t".join([r["kernel"], r["launch"]] +
+                                   [str(int(r[keys[c]])) for c in cols[2:]]))
+    with open(out_path, "w") as f:
+        f.write("\n".join(lines) + "\n")
+    return out_path
+
+
+def counters_status(ctr: dict) -> dict:
+    here = build_hash()
+    return {"source": os.path.relpath(COUNTERS_FILE, ROOT) if ctr else None,
+            "captured_build": ctr.get("build"), "this_build": here,
+            "matches_this_build": bool(ctr) and ctr.get("build") == here,
+            "profiled_view": ctr.get("view")}
+
+
+def issue_rooflines(stage_ms: dict, sm_mhz: float, ctr: dict, scale: dict) -> list:
+    """Achieved warp-instruction issue rate of the issue-bound stages against
+    the SMs' issue slots (148 SMs x 4 schedulers x 1/clock at the SM clock
+    sampled during the timed region).  Instructions: the profiled view's
+    ncu counts, scaled to the timed steps' mean work (`scale[stage]`: mean
+    over the timed views of the stage's work unit -- E for the rasterizers,
+    intersections for binning and sort -- over the profiled view's)."""
     peak = SM_COUNT * ISSUE_PER_SM_CLK * sm_mhz * 1e6 / 1e9   # G warp-instr/s
     out = []
-    for stage, (kernel, instr) in C1_WARP_INSTR.items():
+    for stage in ("rast_fwd", "rast_bwd", "loss_fwd_bwd", "bin_sort"):
+        kern = [k for k, st in PROFILED_KERNELS.items() if st == stage and k in ctr]
         ms = stage_ms.get(stage, 0.0)
-        if ms <= 0:
+        if not kern or ms <= 0:
             continue
+        instr = sum(ctr[k]["warp_instructions"] for k in kern) * scale.get(stage, 1.0)
         ach = instr / (ms / 1000.0) / 1e9
-        out.append({"bound": "issue", "kernel": kernel, "achieved": round(ach, 1),
+        out.append({"bound": "issue", "stage": stage, "kernels": kern, "achieved": round(ach, 1),
                     "peak": round(peak, 1), "unit": "G warp-instr/s", "frac": round(ach / peak, 4),
-                    "launch_ms": round(ms, 4), "warp_instructions": instr})
+                    "launch_ms": round(ms, 4), "warp_instructions": int(instr),
+                    "work_scale": round(scale.get(stage, 1.0), 4)})
     return out
 
 
@@ -242,13 +390,20 @@ def algorithmic_bytes_proj_bwd_grads(n_total: int, n_vis: int, rest_floats: int)
     return float(n_total * per_all + n_vis * per_vis)
 
 
-def run_ours(args, rank: int, world: int):
+WORKLOADS = {
+    "C1": "C1: 1,000,000 Gaussians, SH degree 3, 1297x840, 16 cameras, one view per GPU per step",
+    "C2": "C2: 3,000,000 Gaussians (70% in 10 clusters), SH degree 3, 1920x1080, one camera at "
+          "distance 3, one view per GPU per step",
+}
+
+
+def run_ours(args, rank: int, world: int, config: str = CONFIG):
     import torch
     from msplat_b200 import _lib, engine
     lib = _lib.load()
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
     engine.bind_stream()
-    g, setups, gts, model = build_workload()
+    g, setups, gts, model = build_workload(config)
     dist = None
     if world > 1:
         from msplat_b200 import multigpu
@@ -346,6 +501,21 @@ def run_ours(args, rank: int, world: int):
     radii = engine.debug_buffer("radii", model.n, np.int32)
     n_vis = int((radii > 0).sum())
 
+    # --- raster work of the timed steps, replayed from the same state: per
+    # step the engine's count of the reference loop's pixel.Gaussian work
+    # (msplat_count_raster_work) and the intersections --------------------
+    restore(start_state)
+    if dist is not None:
+        dist.barrier()
+    work = np.zeros((args.steps, 4), np.float64)
+    step_isect = np.zeros(args.steps, np.float64)
+    wbuf = (C_ulonglong * 4)()
+    for s in range(args.steps):
+        one_step(args.warmup + s)
+        if lib.msplat_count_raster_work(wbuf) == 0:
+            work[s] = [float(x) for x in wbuf]
+        step_isect[s] = float(lib.msplat_num_intersections())
+
     # --- end to end through the public API with host buffers ----------------
     h, w = setups[0].height, setups[0].width
     host_gts = [t.cpu().pin_memory() for t in gts[:4]]
@@ -387,6 +557,26 @@ def run_ours(args, rank: int, world: int):
         runs.append(views / e2e_s)
     e2e_value = statistics.median(runs)
 
+    # --- per-kernel counters of the profiled step (committed ncu summary) ----
+    ctr_all = load_counters()
+    ctr_state = counters_status(ctr_all)
+    use_ctr = ctr_state["matches_this_build"] and config == "C1" and world == 1
+    ctr = ctr_all.get("kernels", {}) if use_ctr else {}
+    # work of the profiled step (the first timed step: same state and view as
+    # --profile-step after the same warm-up) against the timed steps' mean
+    prof = work[0] if args.steps else np.zeros(4)
+    mean_w = work.mean(axis=0) if args.steps else np.zeros(4)
+    same_view = ctr_all.get("view") == view_of(args.warmup)
+    scale = {}
+    if use_ctr and same_view and prof[0] > 0:
+        scale = {"rast_fwd": mean_w[0] / prof[0], "rast_bwd": mean_w[3] / max(prof[3], 1.0),
+                 "bin_sort": float(step_isect.mean() / max(step_isect[0], 1.0)),
+                 "loss_fwd_bwd": 1.0}
+    elif use_ctr:
+        use_ctr, ctr = False, {}
+        ctr_state["note"] = "profiled view differs from the first timed view: counters unused"
+    sm_mhz = float(clk.get("sm_mhz") or 1965.0)
+
     # --- roofline of the dominant HBM-bound kernel ---------------------------
     pk = peaks()
     dom = "proj_bwd_adam"
@@ -398,20 +588,76 @@ def run_ours(args, rank: int, world: int):
     achieved = algo / (dom_ms / 1000.0) / 1e9 if dom_ms > 0 else 0.0
     kname = ("rest_adam_kernel + project_backward_adam_kernel<false> (projection VJP + Adam)"
              if world == 1 else "project_backward_adam_kernel<true> (gradient output)")
+    stage_traffic = None
+    if ctr and all(k in ctr for k in ("project_backward_adam_kernel", "rest_adam_kernel")):
+        stage_traffic = int(sum(ctr[k]["dram_read_bytes"] + ctr[k]["dram_write_bytes"]
+                                for k in ("project_backward_adam_kernel", "rest_adam_kernel")))
     roofline = {"bound": "hbm", "kernel": kname, "achieved": round(achieved, 1),
                 "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
                 "peak_source": pk["source"], "algorithmic_bytes": algo, "launch_ms": round(dom_ms, 4),
-                "traffic": C1_OPT_STAGE_TRAFFIC if world == 1 else None,
-                "traffic_source": "ncu dram__bytes_read+write of the stage's kernels, first C1 step"
-                if world == 1 else None}
+                "traffic": stage_traffic,
+                "traffic_source": "ncu dram__bytes_read+write of the stage's two kernels, profiled "
+                                  "step (profile_counters)" if stage_traffic else None}
+    # the projection forward against HBM: every Gaussian reads its mean,
+    # scale and rotation (40 B) to be culled or kept; a kept one reads its
+    # opacity, dc and SH-rest (196 B) and writes its 56 B record; a culled
+    # one writes its zero radius
+    pf_ms = stage_ms.get("proj_sh_fwd", 0.0)
+    pf_algo = float(model.n * 40 + n_vis * (196 + 56) + (model.n - n_vis) * 4)
+    pf_ach = pf_algo / (pf_ms / 1000.0) / 1e9 if pf_ms > 0 else 0.0
+    pf_traffic = None
+    if ctr and "project_forward_kernel" in ctr:
+        k = ctr["project_forward_kernel"]
+        pf_traffic = int(k["dram_read_bytes"] + k["dram_write_bytes"])
+    hbm_more = [{"bound": "hbm", "kernel": "project_forward_kernel", "achieved": round(pf_ach, 1),
+                 "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(pf_ach / pk["hbm_gbs"], 4),
+                 "algorithmic_bytes": pf_algo, "launch_ms": round(pf_ms, 4),
+                 "traffic": pf_traffic}]
+
+    # --- raster work: E and what the rasterizers spend on it -----------------
+    fp32_peak = SM_COUNT * FP32_LANES_PER_SM * sm_mhz * 1e6 / 1e9    # G lane-ops/s
+    V, S_, E, Wk = (float(x) for x in mean_w)
+    fwd_ops = 9 * V + 4 * S_ + 7 * E
+    bwd_ops = 9 * Wk + 56 * E
+    raster_work = {
+        "definition": "per step, summed over pixels (msplat_count_raster_work): visited = list "
+                      "positions the reference's forward loop visits; sigma_passed = pairs with "
+                      "0 <= sigma < 5.55; E = pairs blended into the pixel (contributing "
+                      "pixel.Gaussian evaluations); bwd_walk = positions the reference's "
+                      "backward walks",
+        "visited": round(V), "sigma_passed": round(S_), "E": round(E), "bwd_walk": round(Wk),
+        "steps_counted": int(args.steps),
+        "fp32_roofline": [], "instructions_per_evaluation": None,
+    }
+    for stage, ops, label in (("rast_fwd", fwd_ops, "9 per visited + 4 per sigma-passed "
+                                                     "(exp as 1) + 7 per E"),
+                              ("rast_bwd", bwd_ops, "9 per walked position + 56 per E")):
+        ms_ = stage_ms.get(stage, 0.0)
+        if ms_ > 0 and ops > 0:
+            ach = ops / (ms_ / 1000.0) / 1e9
+            raster_work["fp32_roofline"].append({
+                "stage": stage, "algorithmic_fp32_ops": round(ops), "ops_count": label,
+                "achieved": round(ach, 1), "peak": round(fp32_peak, 1),
+                "unit": "G FP32 lane-ops/s", "frac": round(ach / fp32_peak, 4)})
+    if ctr and prof[2] > 0:
+        per = {}
+        for kern, unit_idx in (("raster_forward_kernel", 2), ("raster_backward_kernel", 2)):
+            if kern in ctr:
+                thr = ctr[kern]["warp_instructions"] * 32.0
+                per[kern] = {"thread_instr_per_E": round(thr / prof[unit_idx], 2),
+                             "thread_instr_per_visited" if kern.startswith("raster_forward")
+                             else "thread_instr_per_walked":
+                             round(thr / prof[0 if kern.startswith("raster_forward") else 3], 2)}
+        raster_work["instructions_per_evaluation"] = per
+        raster_work["profiled_step"] = {"visited": int(prof[0]), "sigma_passed": int(prof[1]),
+                                        "E": int(prof[2]), "bwd_walk": int(prof[3])}
 
     result = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic (seeded C1 scene; targets are renders of a seed-1 scene)",
-        "config": {"workload": "C1: 1,000,000 Gaussians, SH degree 3, 1297x840, 16 cameras, "
-                               "one view per GPU per step",
+        "data": f"synthetic (seeded {config} scene; targets are renders of a seed-1 scene)",
+        "config": {"workload": WORKLOADS[config],
                    "gaussians": model.n, "width": w, "height": h, "cameras": ncam,
                    "l2": "inputs larger than L2 (per-step footprint ~2 GB)",
                    "parallelism": (f"dp{world}: replicated Gaussians; " + (
@@ -431,13 +677,20 @@ def run_ours(args, rank: int, world: int):
                           "starting model state and views, restored before each run), median "
                           "of 3 runs after W untimed steps"},
         "roofline": roofline,
-        "issue_roofline": issue_rooflines(stage_ms, float(clk.get("sm_mhz") or 1965.0)),
+        "issue_roofline": issue_rooflines(stage_ms, sm_mhz, ctr, scale),
+        "hbm_rooflines": hbm_more,
+        "raster_work": raster_work,
+        "build_hash": ctr_state["this_build"],
+        "profile_counters": ctr_state,
         "gpu_launches": launches,
         "clocks": clk,
         "loss": float(lib.msplat_last_loss(1)),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        result["cpu_baseline"] = cpu_baseline(g, setups, gts)
+        v0 = view_of(args.warmup)
+        cap = int(max(16 * model.n, 2 * (step_isect.max() if args.steps else 0)))
+        result["cpu_baseline"] = cpu_baseline(g, [setups[v0]], [gts[v0]], config=config,
+                                              isect_capacity=cap)
     if dist is not None:
         if dist.mode == "peer":
             errs = dist.peer_errors()
@@ -453,11 +706,13 @@ def _oracle_kind():
     return ("reference", ref) if os.path.exists(ref) else ("port", None)
 
 
-def cpu_baseline(g, setups, gts, steps: int = 1, warmup: int = 0) -> dict:
-    """One C1 training step of the CPU implementation on all host threads."""
+def cpu_baseline(g, setups, gts, steps: int = 1, config: str = CONFIG,
+                 isect_capacity: int | None = None) -> dict:
+    """One training step of the CPU port (the oracle's C restatement) on all
+    host threads, on the GPU arm's first timed view: same scene, target and
+    Adam scalars (first step of a fresh model)."""
+    from msplat_b200 import engine
     from oracle import oracle
-    kind, _ = _oracle_kind()
-    kind = "port"  # the reference shim is timed by --impl reference
     threads = os.cpu_count() or 1
     oracle.set_threads(threads)
     cs = setups[0]
@@ -466,64 +721,81 @@ def cpu_baseline(g, setups, gts, steps: int = 1, warmup: int = 0) -> dict:
     m = [np.zeros_like(x) for x in params]
     v = [np.zeros_like(x) for x in params]
     st = [np.zeros(g.n, np.float32) for _ in range(3)]
-    run = oracle.Run(cs, g.n, adam_steps=[1e-3] * 6, adam_bc2=[0.0316] * 6)
-    for _ in range(warmup):
+    dt = 0.0
+    for k in range(steps):
+        sz, bc2 = engine.adam_scalars(k + 1, engine.LR_INIT)
+        run = oracle.Run(cs, g.n, adam_steps=sz, adam_bc2=bc2, isect_capacity=isect_capacity)
+        t0 = time.perf_counter()
         run.train_step(params, m, v, gt, *st)
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        run.train_step(params, m, v, gt, *st)
-    dt = time.perf_counter() - t0
-    return {"value": round(steps / dt, 4), "unit": UNIT, "cores": threads, "kind": kind,
-            "sample": f"{steps} full C1 training step(s) of one 1297x840 view, 1M Gaussians "
-                      f"(CPU oracle, OpenMP over {threads} threads)"}
+        dt += time.perf_counter() - t0
+    h, w = cs.height, cs.width
+    return {"value": round(steps / dt, 4), "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{steps} full {config} training step(s) of one {w}x{h} view, {g.n:,} "
+                      f"Gaussians, the GPU arm's target (CPU oracle, OpenMP over {threads} "
+                      "threads)"}
 
 
 def run_reference(args, rank: int, world: int):
+    """The reference's own CPU implementation of the step on this host's
+    cores, on the GPU arm's workload: the C1 scene, its 16 cameras in the
+    same order (step s trains camera s mod 16), targets rendered from the
+    seed-1 scene (by the oracle, bit-exact with the engine's renders the GPU
+    arm trains on), Adam scalars of a model at step s + 1, W untimed and K
+    timed full steps in sequence on one evolving model.  The kernels are the
+    reference's Metal source compiled for the CPU (oracle/_ref, MSL shim)
+    when that build is present, else the C port."""
     if rank != 0:
         return None
-    from msplat_b200 import camera, synthetic
+    from msplat_b200 import camera, engine
     from oracle import oracle
-    g, cams = synthetic.scene(CONFIG)
-    setups = [camera.prepare_camera(c, step=10**9, sh_degree=3, sh_degree_interval=1000,
-                                    rest_bases=15) for c in cams]
-    gts = [synthetic.target_image(setups[0].width, setups[0].height, 1 + i) for i in range(2)]
     threads = os.cpu_count() or 1
     oracle.set_threads(threads)
+    kind, _ = _oracle_kind()
+    impl = "reference" if kind == "reference" else "oracle"
+    g, cams = scene(CONFIG)
+    setups = [camera.prepare_camera(c, step=10**9, sh_degree=3, sh_degree_interval=1000,
+                                    rest_bases=15) for c in cams]
+    ncam = len(setups)
+    h, w = setups[0].height, setups[0].width
+    tg, _ = scene(CONFIG, seed=1)
+    gts = {}
+    for vi in sorted({s % ncam for s in range(args.warmup + args.steps)}):
+        r = oracle.Run(setups[vi], tg.n)
+        r.render(tg.groups())
+        gts[vi] = r.out_img.reshape(h, w, 3).copy()
+    del tg
     params = [x.copy() for x in g.groups()]
     m = [np.zeros_like(x) for x in params]
     v = [np.zeros_like(x) for x in params]
     st = [np.zeros(g.n, np.float32) for _ in range(3)]
-    # the reference's own kernels (oracle/_ref, built from its Metal source)
-    # when present -- about 15x slower than the C port, so fewer steps --
-    # else the C port
-    kind, _ = _oracle_kind()
-    impl = "reference" if kind == "reference" else "oracle"
-    steps = max(1, min(args.steps, 3 if impl == "reference" else 8))
-    warm = max(0, min(args.warmup, 1))
     times = []
-    for s in range(warm + steps):
-        cs = setups[s % len(setups)]
-        run = oracle.Run(cs, g.n, adam_steps=[1e-3] * 6, adam_bc2=[0.0316] * 6)
+    for s in range(args.warmup + args.steps):
+        vi = s % ncam
+        sz, bc2 = engine.adam_scalars(s + 1, engine.LR_INIT)
+        run = oracle.Run(setups[vi], g.n, adam_steps=sz, adam_bc2=bc2)
         t0 = time.perf_counter()
-        run.train_step(params, m, v, gts[s % 2], *st, impl=impl)
-        if s >= warm:
-            times.append(time.perf_counter() - t0)
+        rc = run.train_step(params, m, v, gts[vi], *st, impl=impl)
+        dt = time.perf_counter() - t0
+        if rc != 0:
+            raise RuntimeError("reference step reported a per-tile overflow")
+        if s >= args.warmup:
+            times.append(dt)
     value = len(times) / sum(times)
+    what = ("the reference's Metal kernels compiled for the CPU (MSL shim: SIMD lanes as "
+            "fibers, OpenMP over threadgroups)" if impl == "reference" else
+            "the C restatement of the reference's kernels")
     return {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT,
-            "n_gpus": world, "steps": len(times), "warmup": warm,
+            "n_gpus": world, "steps": len(times), "warmup": args.warmup,
             "ms_per_step": round(1000 * sum(times) / len(times), 2), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "C1: 1,000,000 Gaussians, SH degree 3, 1297x840, one view "
-                                   "per step (CPU)"},
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded C1 scene; targets are renders of a seed-1 scene)",
+            "config": {"workload": WORKLOADS[CONFIG], "gaussians": g.n, "width": w, "height": h,
+                       "cameras": ncam, "parallelism": f"CPU, {threads} threads (rank 0 only)"},
             "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads,
-                             "kind": "port" if kind == "port" else "reference",
-                             "sample": f"{len(times)} full C1 training steps (capped at "
-                                       f"{3 if impl == 'reference' else 8} of --steps "
-                                       f"{args.steps}); " + (
-                                           "the reference's Metal kernels compiled for the CPU "
-                                           "(MSL shim: SIMD lanes as fibers, OpenMP over "
-                                           "threadgroups)" if impl == "reference" else
-                                           "the C restatement of the reference's kernels")},
+                             "kind": kind,
+                             "sample": f"{len(times)} full C1 training steps after "
+                                       f"{args.warmup} untimed ones, views in the GPU arm's "
+                                       f"order; {what}"},
             "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
 
@@ -770,10 +1042,36 @@ def run_c4(args, rank: int, world: int) -> dict:
     return result
 
 
+def profile_step(args) -> dict:
+    """One C1 training step after W warm-up steps, alone between
+    cudaProfilerStart and cudaProfilerStop (ncu --profile-from-start off)."""
+    import torch
+    from msplat_b200 import engine
+    torch.cuda.set_device(0)
+    engine.bind_stream()
+    g, setups, gts, model = build_workload(CONFIG)
+    ncam = len(setups)
+    for s in range(args.warmup):
+        engine.train_step(model, setups[s % ncam], gts[s % ncam])
+    torch.cuda.synchronize()
+    view = args.warmup % ncam
+    torch.cuda.profiler.start()
+    engine.train_step(model, setups[view], gts[view])
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    return {"build_hash": build_hash(), "view": view, "warmup": args.warmup, "config": CONFIG}
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
+    if args.summarize_ncu:
+        print(summarize_ncu(args.summarize_ncu, args.hash_file))
+        return
+    if args.profile_step:
+        print(json.dumps(profile_step(args)), flush=True)
+        return
     if args.config == "C3":
         if rank == 0:
             print(json.dumps(run_c3(args)), flush=True)
@@ -790,15 +1088,53 @@ def main():
             print(json.dumps(res), flush=True)
         return
     if args.impl == "reference":
+        if args.config != "C1":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable":
+                                  f"the reference arm times the headline C1 workload only "
+                                  f"({args.config} requested)"}), flush=True)
+            return
         res = run_reference(args, rank, world)
     else:
-        res = run_ours(args, rank, world)
+        res = run_ours(args, rank, world, args.config)
+        if args.config == "C1" and not args.no_c4:
+            res["c4"] = c4_leg(args, rank, world)
     if rank == 0 and res is not None:
         print(json.dumps(res), flush=True)
 
 
+def c4_leg(args, rank: int, world: int) -> dict:
+    """BASELINE.json config 4 beside the headline line: the batched-view step
+    (8 views of 1920x1080 per step, 6M Gaussians) on the same N GPUs, with
+    the same K and W; its scenes are drawn once per host and kept in a cache
+    directory (MSPLAT_BENCH_SCENE_CACHE, else one under the system temporary
+    directory) so that the runs at several N reuse them."""
+    import gc
+
+    import torch
+    from msplat_b200 import _lib
+    gc.collect()
+    torch.cuda.empty_cache()
+    _lib.load().cleanup_msplat_cuda()
+    if not os.environ.get("MSPLAT_BENCH_SCENE_CACHE"):
+        import tempfile
+        os.environ["MSPLAT_BENCH_SCENE_CACHE"] = os.path.join(tempfile.gettempdir(),
+                                                              "msplat_bench_scenes")
+    if world not in (1, 2, 4, 8):
+        return {"skipped": f"C4 splits its batch of 8 views over 1, 2, 4 or 8 GPUs, not {world}"}
+    r = run_c4(args, rank, world)
+    keep = ("value", "unit", "ms_per_step", "steps", "warmup", "scaling", "exchange",
+            "gpu_launches", "clocks")
+    out = {k: r[k] for k in keep if k in r}
+    out["metric"] = r["metric"]
+    out["workload"] = r["config"]["workload"]
+    out["views_per_gpu"] = r["config"]["views_per_gpu"]
+    out["parallelism"] = r["config"]["parallelism"]
+    return out
+
+
 from ctypes import byref as C_byref, c_char_p as C_char_p, c_double as C_double, c_int as C_int  # noqa: E402
-from ctypes import c_float as C_float, c_void_p as C_void_p  # noqa: E402
+from ctypes import c_float as C_float, c_ulonglong as C_ulonglong, c_void_p as C_void_p  # noqa: E402
 
 if __name__ == "__main__":
     main()

@@ -53,3 +53,47 @@ def test_exchange_roofline():
     assert 0.5 < r["frac"] < 0.6
     r = bench.exchange_roofline(n, 4, False, "peer", 3.907)
     assert r["bytes_in"] > r["bytes_out"]          # 60 gradient floats in, 59 out
+
+
+def _ncu_csv(path, kernel, values):
+    hdr = ('"ID","Process ID","Process Name","Host Name","Kernel Name","Context","Stream",'
+           '"Block Size","Grid Size","Device","CC","Section Name","Metric Name","Metric Unit",'
+           '"Metric Value"\n')
+    rows = []
+    for metric, unit, val in values:
+        rows.append(f'"0","11","python3","127.0.0.1","{kernel}","1","7","(256, 1, 1)",'
+                    f'"(4346, 1, 1)","0","10.0","Command line profiler metrics","{metric}",'
+                    f'"{unit}","{val}"\n')
+    path.write_text("==PROF== Connected to process 11\n" + hdr + "".join(rows))
+
+
+def test_counter_summary_round_trip(tmp_path, monkeypatch):
+    """--summarize-ncu writes the per-kernel summary bench.py reads back;
+    the build hash decides whether a run may use it."""
+    csvs = []
+    for kern, rd in (("void msp::raster_forward_kernel<0>(const msp::StepParams *, int)", 1000),
+                     ("msp::sort_tiles_kernel(const msp::StepParams *, const int *)", 2000)):
+        p = tmp_path / f"{rd}.csv"
+        _ncu_csv(p, kern, [("dram__bytes_read.sum", "byte", f"{rd:,}"),
+                           ("dram__bytes_write.sum", "byte", "500"),
+                           ("smsp__inst_executed.sum", "inst", "123,456"),
+                           ("gpu__time_duration.sum", "nsecond", "98765")])
+        csvs.append(str(p))
+    hf = tmp_path / "h.json"
+    hf.write_text('loading\n{"build_hash": "%s", "view": 5, "warmup": 5}\n' % bench.build_hash())
+    out = str(tmp_path / "counters.txt")
+    bench.summarize_ncu(csvs, str(hf), out)
+    ctr = bench.load_counters(out)
+    assert ctr["view"] == 5 and ctr["build"] == bench.build_hash()
+    k = ctr["kernels"]
+    assert set(k) == {"raster_forward_kernel", "sort_tiles_kernel"}
+    assert k["raster_forward_kernel"]["dram_read_bytes"] == 1000
+    assert k["sort_tiles_kernel"]["warp_instructions"] == 123456
+    assert k["sort_tiles_kernel"]["duration_ns"] == 98765
+    monkeypatch.setattr(bench, "COUNTERS_FILE", out)
+    assert bench.counters_status(ctr)["matches_this_build"]
+    assert not bench.counters_status(dict(ctr, build="0" * 12))["matches_this_build"]
+    roof = bench.issue_rooflines({"rast_fwd": 0.4, "bin_sort": 0.1}, 1965.0, k,
+                                 {"rast_fwd": 2.0})
+    fwd = [r for r in roof if r["stage"] == "rast_fwd"][0]
+    assert fwd["warp_instructions"] == 2 * 123456 and fwd["work_scale"] == 2.0
