@@ -255,10 +255,13 @@ def summarize_ncu(csv_paths, hash_file: str, out_path: str = COUNTERS_FILE) -> s
             lines = [ln for ln in f if ln.startswith('"')]
         for rec in _csv.DictReader(lines):
             name = rec.get("Kernel Name", "")
-            base = name.split("(")[0].split("<")[0].split("::")[-1].strip()
+            head = name.split("(")[0].strip()            # "void ns::kernel<0, 2>"
+            if head.startswith("void "):
+                head = head[5:]
+            base = head.split("<")[0].split("::")[-1].strip()
             if base not in PROFILED_KERNELS:
                 continue
-            r = rows.setdefault(base, {"kernel": base, "launch": name.split("(")[0].strip()})
+            r = rows.setdefault(base, {"kernel": base, "launch": head.split("::")[-1]})
             metric, val = rec.get("Metric Name"), rec.get("Metric Value", "").replace(",", "")
             if metric in COUNTER_METRICS:
                 r[metric] = float(val)

@@ -55,6 +55,17 @@ void *msplat_device(void);
  * `bytes`, zero-filled when `zero` != 0.  Free with msplat_gpu_free. */
 void *msplat_gpu_alloc(size_t bytes, int zero);
 void msplat_gpu_free(void *ptr);
+/* Memory that the host and the engine's kernels both address (CUDA managed
+ * memory): the counterpart of the MTLResourceStorageModeShared buffers
+ * behind the reference's MTensor (metal_tensor.hpp:43-55), for hosts that
+ * read and write tensors in place as the reference's Model does.  Before
+ * an engine call reads a range the host has touched, move it to the device
+ * with msplat_shared_prefetch (queued on the engine stream; the host must
+ * not touch the range until msplat_gpu_sync).  Zeroed on the host when
+ * `zero` != 0.  Free with msplat_shared_free. */
+void *msplat_shared_alloc(size_t bytes, int zero);
+void msplat_shared_free(void *ptr);
+int msplat_shared_prefetch(const void *ptr, size_t bytes);
 /* Host<->device copies on the engine stream (Metal's shared storage made
  * these implicit); `kind` 0 = host to device, 1 = device to host,
  * 2 = device to device.  Synchronous when `sync` != 0. */

@@ -185,6 +185,9 @@ SIGNATURES = {
     "msplat_debug_buffer": (_i, [C.c_char_p, C.POINTER(_p), C.POINTER(C.c_longlong)]),
     "msplat_kernel_launches": (C.c_longlong, [_i]),
     "msplat_count_raster_work": (_i, [C.POINTER(C.c_ulonglong)]),
+    "msplat_shared_alloc": (_p, [C.c_size_t, _i]),
+    "msplat_shared_free": (None, [_p]),
+    "msplat_shared_prefetch": (_i, [_p, C.c_size_t]),
 }
 
 _lib = None

@@ -451,6 +451,40 @@ void msplat_gpu_free(void* ptr)
     cudaFree(ptr);
 }
 
+void* msplat_shared_alloc(size_t bytes, int zero)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (init_engine()) return nullptr;
+    void* p = nullptr;
+    const size_t n = bytes ? bytes : 4;
+    cudaError_t e = cudaMallocManaged(&p, n, cudaMemAttachGlobal);
+    if (e != cudaSuccess) {
+        set_error("cudaMallocManaged(%zu) failed: %s", n, cudaGetErrorString(e));
+        return nullptr;
+    }
+    // first touched by the host (the caller fills it), so zero it there too
+    if (zero) memset(p, 0, n);
+    return p;
+}
+
+void msplat_shared_free(void* ptr)
+{
+    if (!ptr) return;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (g.ready) cudaStreamSynchronize(g.stream());
+    cudaFree(ptr);
+}
+
+int msplat_shared_prefetch(const void* ptr, size_t bytes)
+{
+    if (!ptr || bytes == 0) return MSPLAT_OK;
+    std::lock_guard<std::mutex> lk(g_mu);
+    int rc = init_engine();
+    if (rc) return rc;
+    MSP_CUDA(cudaMemPrefetchAsync(ptr, bytes, g.device, g.stream()));
+    return MSPLAT_OK;
+}
+
 int msplat_copy(void* dst, const void* src, size_t bytes, int kind, int sync)
 {
     std::lock_guard<std::mutex> lk(g_mu);

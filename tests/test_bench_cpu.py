@@ -71,7 +71,7 @@ def test_counter_summary_round_trip(tmp_path, monkeypatch):
     """--summarize-ncu writes the per-kernel summary bench.py reads back;
     the build hash decides whether a run may use it."""
     csvs = []
-    for kern, rd in (("void msp::raster_forward_kernel<0>(const msp::StepParams *, int)", 1000),
+    for kern, rd in (("void raster_forward_kernel<0>(const StepParams *, int)", 1000),
                      ("msp::sort_tiles_kernel(const msp::StepParams *, const int *)", 2000)):
         p = tmp_path / f"{rd}.csv"
         _ncu_csv(p, kern, [("dram__bytes_read.sum", "byte", f"{rd:,}"),
