@@ -292,10 +292,14 @@ class DataParallel:
         if len(cams) != self.views_per_rank or len(gts) != len(cams):
             raise ValueError(f"expected {self.views_per_rank} views per rank, got {len(cams)}")
         self.model.step_count += 1
-        self.last_loss = accumulate_views(self.ops, self.model, cams, gts, self.grad,
-                                          self.compact, ssim_weight, background, glob_scale,
-                                          clip_thresh)
-        self.apply(cams[0])
+        try:
+            self.last_loss = accumulate_views(self.ops, self.model, cams, gts, self.grad,
+                                              self.compact, ssim_weight, background, glob_scale,
+                                              clip_thresh)
+            self.apply(cams[0])
+        except PeerLostError:
+            self.model.step_count -= 1   # the step did not happen
+            raise
         return self.last_loss
 
     def apply(self, cam) -> None:
@@ -314,7 +318,13 @@ class DataParallel:
             _lib.check(rc, "msplat_dp_reduce_adam")
             return
         if self.world > 1:
-            dist.all_reduce(self.grad, op=dist.ReduceOp.SUM)
+            try:
+                dist.all_reduce(self.grad, op=dist.ReduceOp.SUM)
+            except RuntimeError as e:   # timed out, or a peer's connection closed
+                raise PeerLostError(
+                    f"rank {self.rank}: the gradient exchange of step {self.model.step_count} "
+                    f"failed (a peer exited or stalled past the process group's timeout); "
+                    f"no parameter was updated: {e}") from e
         self.ops.adam_apply(self.model, cam, self.grad, 1.0 / self.world)
 
     def peer_errors(self, reset: bool = False) -> int:
@@ -367,6 +377,11 @@ class DataParallel:
         if self._owns_group and dist.is_initialized():
             dist.destroy_process_group()
         self._owns_group = False
+
+
+class PeerLostError(RuntimeError):
+    """A data-parallel step could not complete because another rank left or
+    stalled between steps; the local replica is left as before the step."""
 
 
 def rank_and_world() -> tuple[int, int]:

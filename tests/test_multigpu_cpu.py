@@ -209,3 +209,48 @@ def test_grad_buffer_layout():
                                     4, 15)
     assert [tuple(b.shape) for b in bufs] == [(4, 3), (4, 3), (4, 4), (4, 3), (4, 45), (4, 1)]
     assert vis.shape == (4,) and vis[0].item() == 59 * 4
+
+
+# ---- a rank that leaves or stalls between steps ---------------------------------
+
+def _failure_worker(rank, world, port, out_dir, how):
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    model = _model()
+    dp = multigpu.DataParallel(model, rank, world, ops=FakeOps(), backend="gloo", timeout_s=3)
+    dp.train_step(FakeCam(rank), None)      # one complete step on both ranks
+    if rank == 1:
+        if how == "stall":
+            time.sleep(8)                   # between steps, nothing in flight
+        os._exit(0)                         # leaves without shutting down
+    after_one = [t.clone() for t in model.params + model.exp_avg + model.exp_avg_sq]
+    t0 = time.monotonic()
+    err = ""
+    try:
+        dp.train_step(FakeCam(world + rank), None)
+    except multigpu.PeerLostError as e:
+        err = str(e)
+    elapsed = time.monotonic() - t0
+    now = model.params + model.exp_avg + model.exp_avg_sq
+    unchanged = all(torch.equal(a, b) for a, b in zip(after_one, now))
+    np.savez(os.path.join(out_dir, "rank0.npz"), elapsed=np.array([elapsed]),
+             unchanged=np.array([unchanged]), step=np.array([model.step_count]),
+             err=np.array([err]))
+    os._exit(0)                             # the group is broken: skip its teardown
+
+
+@pytest.mark.parametrize("how", ["exit", "stall"])
+def test_survivor_reports_a_lost_peer(how):
+    """Rank 1 completes a step, then exits (or stalls for 8 s) between
+    steps.  Rank 0's next step fails on the host within the process group's
+    3 s timeout (or as soon as the connection closes) with PeerLostError, and
+    its replica and step count are those of the last complete step."""
+    with tempfile.TemporaryDirectory() as d:
+        mp.start_processes(_failure_worker, args=(2, _free_port(), d, how), nprocs=2,
+                           join=True, start_method="spawn")
+        r = np.load(os.path.join(d, "rank0.npz"))
+        assert "no parameter was updated" in str(r["err"][0]), r["err"]
+        assert bool(r["unchanged"][0])
+        assert int(r["step"][0]) == 1
+        assert float(r["elapsed"][0]) < 15.0
