@@ -917,18 +917,19 @@ NVLINK_PEER_GBS = 770.0
 def exchange_roofline(n: int, world: int, compact: bool, mode: str, ms: float):
     """The exchange's NVLink bound: the larger of the bytes one rank receives
     and sends per step (links are full duplex), at the measured per-direction
-    peer bandwidth, against the measured exchange time.  peer: receives its
-    shard of every other rank's gradient rows, sends its updated parameter
-    shard to every other replica; nccl ring all-reduce: 2 (world-1)/world of
-    the 60-float buffer each way."""
+    peer bandwidth, against the measured exchange time.  peer: a rank
+    receives its shard of every other rank's gradient rows and every other
+    rank's updated parameter shard (59 floats per Gaussian) into its
+    replica, and sends as much (its gradient rows to the shards' owners, its
+    own shard to every other replica); nccl ring all-reduce: 2 (world-1)/world
+    of the 60-float buffer each way."""
     if world <= 1 or not ms:
         return None
     share = (world - 1) / world
     if mode == "nccl":
         rx = tx = 2 * share * n * 60 * 4
     else:
-        rx = share * n * (15 if compact else 60) * 4
-        tx = share * n * 59 * 4
+        rx = tx = share * n * ((15 if compact else 60) + 59) * 4
     bound_ms = max(rx, tx) / (NVLINK_PEER_GBS * 1e9) * 1e3
     return {"bound": "nvlink", "peak_gbs_per_direction": NVLINK_PEER_GBS,
             "peak_source": "measured peer copy on this pool", "bytes_in": int(rx),

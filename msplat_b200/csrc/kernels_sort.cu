@@ -92,27 +92,86 @@ __device__ __forceinline__ unsigned cta_excl_scan(unsigned v, unsigned* s_wsum, 
     return before + x - v;
 }
 
-// Decoupled look-back: the sum of `slot` over every block before `b`, from
-// words published under `epoch`.  False when a wait ran out.
+__device__ __forceinline__ bool os_ready(unsigned long long w, unsigned epoch)
+{
+    return os_epoch(w) == epoch && (w >> 62) != 0;
+}
+
+// Decoupled look-back by one thread: the sum of `slot` over every block
+// before `b`, from words published under `epoch`, reading kOsWindow
+// predecessors per round (their loads in flight together: every block of a
+// wave starts at once, so the nearest inclusive prefix can be far back).
+// False when a wait ran out.
+constexpr int kOsWindow = 8;
 __device__ __forceinline__ bool os_lookback(const unsigned long long* status, long long b,
                                             int stride, int slot, unsigned epoch,
                                             unsigned long long& excl)
 {
     excl = 0;
-    long long j = b - 1;
+    long long j = b - 1;   // nearest predecessor not yet summed
     unsigned long long t0 = 0;
     while (j >= 0) {
-        const unsigned long long w =
-            *reinterpret_cast<const volatile unsigned long long*>(status + j * stride + slot);
-        if (os_epoch(w) != epoch || (w >> 62) == 0) {
+        unsigned long long w[kOsWindow];
+#pragma unroll
+        for (int k = 0; k < kOsWindow; k++)
+            w[k] = j - k >= 0 ? *reinterpret_cast<const volatile unsigned long long*>(
+                                    status + (j - k) * stride + slot)
+                              : os_word(kOsPrefix, epoch, 0);
+        int used = 0;
+        bool done = false, stalled = false;
+#pragma unroll
+        for (int k = 0; k < kOsWindow; k++) {
+            if (done || stalled) continue;
+            if (!os_ready(w[k], epoch)) {
+                stalled = true;
+                continue;
+            }
+            excl += os_count(w[k]);
+            used++;
+            done = (w[k] & kOsPrefix) != 0;
+        }
+        if (done) return true;
+        j -= used;
+        if (used == 0) {
             const unsigned long long now = os_now();
             if (t0 == 0) t0 = now;
             else if (now - t0 > kOsLookbackNs) return false;
-            continue;
         }
-        excl += os_count(w);
-        if ((w & kOsPrefix) != 0) break;
-        j--;
+    }
+    return true;
+}
+
+// The same for a single value per block, by a whole warp: lane k reads
+// predecessor j - k, 32 per round.  Every lane returns the same result.
+__device__ __forceinline__ bool os_lookback_warp(const unsigned long long* status, long long b,
+                                                 unsigned epoch, unsigned long long& excl)
+{
+    const int lane = threadIdx.x & 31;
+    excl = 0;
+    long long j = b - 1;
+    unsigned long long t0 = 0;
+    while (j >= 0) {
+        const long long idx = j - lane;
+        const unsigned long long w =
+            idx >= 0 ? *reinterpret_cast<const volatile unsigned long long*>(status + idx)
+                     : os_word(kOsPrefix, epoch, 0);
+        const bool ready = os_ready(w, epoch);
+        const unsigned notready = __ballot_sync(0xffffffffu, !ready);
+        const unsigned prefix = __ballot_sync(0xffffffffu, ready && (w & kOsPrefix) != 0);
+        const int fnr = notready ? __ffs(notready) - 1 : 32;
+        const int fp = prefix ? __ffs(prefix) - 1 : 32;
+        const int take = fp < fnr ? fp + 1 : fnr;   // lanes [0, take) are summed
+        unsigned long long c = lane < take ? os_count(w) : 0ull;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xffffffffu, c, o);
+        excl += c;
+        if (fp < fnr) return true;
+        j -= take;
+        if (take == 0) {
+            const unsigned long long now = os_now();
+            if (t0 == 0) t0 = now;
+            else if (now - t0 > kOsLookbackNs) return false;
+        }
     }
     return true;
 }
@@ -318,16 +377,19 @@ pair_kernel(const StepParams* __restrict__ P, int N, const unsigned* __restrict_
         unsigned btotal = 0;
         const unsigned wex = cta_excl_scan(lane == 0 ? wsum : 0u, s_wsum, &btotal);
         const unsigned warp_base = __shfl_sync(0xffffffffu, wex, 0);
-        if (tid == 0) {
-            os_publish(status, b, 1, 0, os_word(b == 0 ? kOsPrefix : kOsAgg, epoch, btotal));
+        if (warp == 0) {
+            if (lane == 0)
+                os_publish(status, b, 1, 0, os_word(b == 0 ? kOsPrefix : kOsAgg, epoch, btotal));
             unsigned long long excl = 0;
             bool ok = true;
             if (b > 0) {
-                ok = os_lookback(status, b, 1, 0, epoch, excl);
-                os_publish(status, b, 1, 0, os_word(kOsPrefix, epoch, excl + btotal));
+                ok = os_lookback_warp(status, b, epoch, excl);
+                if (lane == 0) os_publish(status, b, 1, 0, os_word(kOsPrefix, epoch, excl + btotal));
             }
-            if (!ok) atomicOr(err, kErrSortTimeout);
-            s_base = ok ? excl : ~0ull;
+            if (lane == 0) {
+                if (!ok) atomicOr(err, kErrSortTimeout);
+                s_base = ok ? excl : ~0ull;
+            }
         }
         __syncthreads();
         const unsigned long long bbase = s_base;
