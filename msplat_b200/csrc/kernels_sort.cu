@@ -446,23 +446,30 @@ namespace {
 
 std::atomic<unsigned> g_epoch{8};
 
-int resident_blocks(const void* kernel)
+// Blocks of `kernel` (kOsThreads threads) resident on the current device at
+// once: the persistent grid size.  One lookup per kernel and device.
+template <const void* (*KERNEL)()>
+int resident_blocks()
 {
     static std::once_flag once[kMaxDeviceSlots];
-    static int sms[kMaxDeviceSlots];
+    static int blocks[kMaxDeviceSlots];
     int dev = 0;
     if (!once_per_device(once, [](int d) {
-            int n = 0;
-            cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
-            sms[d] = n > 0 ? n : 148;
+            int sms = 0, per = 0;
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, d);
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, KERNEL(), kOsThreads, 0) !=
+                    cudaSuccess ||
+                per < 1)
+                per = 1;
+            blocks[d] = (sms > 0 ? sms : 148) * per;
         }) || cudaGetDevice(&dev) != cudaSuccess)
         return 148;
-    int per = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, kernel, kOsThreads, 0) != cudaSuccess ||
-        per < 1)
-        per = 1;
-    return sms[dev] * per;
+    return blocks[dev];
 }
+
+template <class Src, class KeyT, bool WK>
+const void* onesweep_ptr() { return (const void*)onesweep_kernel<Src, KeyT, WK>; }
+const void* pair_ptr() { return (const void*)pair_kernel; }
 
 template <class Src, class KeyT, bool WK>
 void launch_pass(Src src, KeyT* keys_out, unsigned* vals_out, const unsigned* hist,
@@ -471,8 +478,8 @@ void launch_pass(Src src, KeyT* keys_out, unsigned* vals_out, const unsigned* hi
                  cudaStream_t s)
 {
     const long long tiles = (max_items + kOsTile - 1) / kOsTile;
-    const int grid = (int)std::max(1LL, std::min(tiles, (long long)resident_blocks(
-                                                           (const void*)onesweep_kernel<Src, KeyT, WK>)));
+    const int grid = (int)std::max(
+        1LL, std::min(tiles, (long long)resident_blocks<onesweep_ptr<Src, KeyT, WK>>()));
     onesweep_kernel<Src, KeyT, WK><<<grid, kOsThreads, 0, s>>>(
         src, keys_out, vals_out, hist, S.status, S.ctrl + ticket, n_dev, n_host, cap, shift, epoch,
         err);
@@ -514,8 +521,7 @@ int launch_bin_sort(const StepParams* P, int N, int num_tiles, long long cap, co
     // pairs in depth order
     {
         const long long tiles = (N + kOsTile - 1) / kOsTile;
-        const int grid = (int)std::max(1LL, std::min(tiles, (long long)resident_blocks(
-                                                                (const void*)pair_kernel)));
+        const int grid = (int)std::max(1LL, std::min(tiles, (long long)resident_blocks<pair_ptr>()));
         pair_kernel<<<grid, kOsThreads, 0, s>>>(P, N, S.dval_a, B.proj.radii, B.proj.rect,
                                                 S.pkey_a, S.pval_a, hist_p, S.status,
                                                 S.ctrl + 4, epoch + 4, B.err);
