@@ -207,7 +207,7 @@ static int ensure(long long N, long long W, long long H, long long T, int K, boo
         if ((rc = realloc_dev(B.proj.sh_mean, (size_t)n * 3))) return rc;
         g.cap_grad_N = n;
     }
-    // the sort's look-back words count in 30 bits
+    // the sort counts intersections in 32-bit words
     long long want_isect = std::min(std::max(16 * N, g.growth_isect), (1LL << 30) - 1);
     if (want_isect > g.cap_isect) {
         if ((rc = realloc_dev(B.sort.pkey_a, want_isect))) return rc;
@@ -220,8 +220,6 @@ static int ensure(long long N, long long W, long long H, long long T, int K, boo
     const long long words = sort_status_words(g.cap_N, g.cap_isect);
     if (words > g.cap_status) {
         if ((rc = realloc_dev(B.sort.status, words))) return rc;
-        // look-back words carry the launch's epoch; stale memory must not
-        MSP_CUDA(cudaMemsetAsync(B.sort.status, 0, sizeof(unsigned long long) * words, g.stream()));
         g.cap_status = words;
     }
     const long long P = W * H;

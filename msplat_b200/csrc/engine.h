@@ -55,8 +55,8 @@ struct ProjOut {
 };
 
 // Working arrays of the binning sort (kernels_sort.cu).  ctrl holds the
-// passes' tickets and digit histograms: kSortCtrlWords words zeroed by the
-// scan of the tile counts each step.
+// passes' digit histograms: kSortCtrlWords words zeroed by the scan of the
+// tile counts each step.
 constexpr int kSortCtrlHistDepth = 8;                              // [4][256]
 constexpr int kSortCtrlHistPair = kSortCtrlHistDepth + 4 * 256;    // [2][256]
 constexpr int kSortCtrlWords = kSortCtrlHistPair + 2 * 256;
@@ -69,7 +69,7 @@ struct SortBuffers {
     unsigned short* pkey_b;
     unsigned* pval_a;
     unsigned* pval_b;
-    unsigned long long* status;  // [sort_status_words(N, capacity)] look-back words, zeroed once
+    unsigned long long* status;  // [sort_status_words(N, capacity)] per-tile digit counts and offsets
     unsigned* ctrl;              // [kSortCtrlWords]
 };
 

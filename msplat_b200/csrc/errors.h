@@ -13,7 +13,6 @@ namespace msp {
 enum ErrorBits : int {
     kErrIsectOverflow = 1,   // intersections exceeded the key buffer
     kErrStageTimeout = 2,    // a bulk copy into shared memory did not complete in time
-    kErrSortTimeout = 4,     // a sort block's look-back wait ran out (its keys are not written)
 };
 
 // Status of a synchronous render whose error word read back as `err`.
@@ -28,10 +27,6 @@ inline int render_status(int err, const char** what)
 {
     *what = nullptr;
     if (err == 0) return MSPLAT_OK;
-    if (err & kErrSortTimeout) {
-        *what = "a sort block's look-back wait timed out; the tile lists are incomplete";
-        return MSPLAT_ERR_CUDA;
-    }
     if (err & kErrStageTimeout) {
         *what = (err & kErrIsectOverflow)
                     ? "a shared-memory bulk copy timed out and the intersections overflowed"

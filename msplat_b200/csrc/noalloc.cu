@@ -216,13 +216,11 @@ extern "C" int msplat_render_noalloc(
     // The parameter block goes from this stack frame; a copy from pageable
     // memory has been staged by the time cudaMemcpyAsync returns.
     NA_CUDA(cudaMemcpyAsync(d_params, &p, sizeof(StepParams), cudaMemcpyHostToDevice, st));
-    // Only the tile counters, the error word and the sort's look-back words
-    // must start at zero; every other buffer is written before it is read
-    // (the scan of the tile counts clears the sort's tickets and histograms).
+    // Only the tile counters and the error word must start at zero; every
+    // other buffer is written before it is read (the scan of the tile
+    // counts clears the sort's histograms).
     NA_CUDA(cudaMemsetAsync(B.err, 0, 4 * sizeof(int), st));
     NA_CUDA(cudaMemsetAsync(B.tile_count, 0, sizeof(int) * (size_t)p.num_tiles * kCountPitch, st));
-    // the sort's look-back words: this region may hold another call's data
-    NA_CUDA(cudaMemsetAsync(B.sort.status, 0, sizeof(unsigned long long) * L.status_words, st));
     launch_project_forward(d_params, p.num_points, means3d, scales, quats, features_dc,
                            features_rest, opacities, B, false, p.degrees_to_use, p.rest_stride, st);
     launch_scan_tiles(d_params, p.num_tiles, B, st);
