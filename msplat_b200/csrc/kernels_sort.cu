@@ -239,12 +239,14 @@ digit_scatter_kernel(Src src, KeyT* __restrict__ keys_out, unsigned* __restrict_
             tot += c;
         }
         s_bexcl[tid] = cta_excl_scan(tot, s_wsum, nullptr);
+        __syncthreads();   // every digit's tile offset before any thread reads it
         // the tile grouped by digit in shared memory, then written in runs
 #pragma unroll
         for (int r = 0; r < kOsItems; r++) {
             if (base + r * 32 + lane >= n) continue;
             const unsigned d = (key[r] >> shift) & 0xffu;
             const unsigned lp = s_bexcl[d] + s_whist[warp][d] + rnk[r];
+            if (lp >= (unsigned)kOsTile) continue;   // cannot happen: lp < the tile's count
             s_key[lp] = key[r];
             s_val[lp] = val[r];
         }
