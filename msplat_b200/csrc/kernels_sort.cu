@@ -140,14 +140,17 @@ digit_count_kernel(Src src, const int* __restrict__ n_dev, long long n_host, lon
         for (int i = lane; i < kOsRadix; i += 32) s_whist[warp][i] = 0;
         __syncwarp();
         const long long base = b * kOsTile + (long long)warp * (kOsItems * 32);
-#pragma unroll 4
-        for (int r = 0; r < kOsItems; r++) {
+        unsigned key[kOsItems];
+#pragma unroll
+        for (int r = 0; r < kOsItems; r++) {   // every load in flight before any count
             const long long i = base + r * 32 + lane;
-            if (i >= n) break;
-            unsigned key, val;
-            src.load(i, key, val);
-            atomicAdd(&s_whist[warp][(key >> shift) & 0xffu], 1u);
+            unsigned val;
+            key[r] = 0;
+            if (i < n) src.load(i, key[r], val);
         }
+#pragma unroll
+        for (int r = 0; r < kOsItems; r++)
+            if (base + r * 32 + lane < n) atomicAdd(&s_whist[warp][(key[r] >> shift) & 0xffu], 1u);
         __syncthreads();
         unsigned c = 0;
 #pragma unroll
@@ -264,126 +267,125 @@ digit_scatter_kernel(Src src, KeyT* __restrict__ keys_out, unsigned* __restrict_
     }
 }
 
-// Sum of the rect areas of each tile of 4096 depth-ordered ranks (the
-// Gaussian ids[r]; culled ones have none): sums[b].
+// Rect area of each rank (Gaussian ids[r] of the depth order; culled ones
+// have none), summed per group of 32 consecutive ranks: sums[r / 32].
+__device__ __forceinline__ unsigned rank_area(const unsigned* ids, const int* radii,
+                                              const uint2* rect, long long r, long long N,
+                                              unsigned& g, uint2& rc)
+{
+    g = 0;
+    rc = make_uint2(0u, 0u);
+    if (r >= N) return 0u;
+    g = ids[r];
+    if (radii[g] <= 0) return 0u;
+    rc = rect[g];
+    return ((rc.y & 0xffffu) - (rc.x & 0xffffu)) * ((rc.y >> 16) - (rc.x >> 16));
+}
+
 __global__ void __launch_bounds__(kOsThreads)
 rank_area_kernel(int N, const unsigned* __restrict__ ids, const int* __restrict__ radii,
                  const uint2* __restrict__ rect, unsigned* __restrict__ sums)
 {
-    __shared__ unsigned s_wsum[kOsWarps];
-    const long long tiles = ((long long)N + kOsTile - 1) / kOsTile;
-    for (long long b = blockIdx.x; b < tiles; b += gridDim.x) {
-        unsigned a = 0;
-#pragma unroll 4
-        for (int q = 0; q < kOsItems; q++) {
-            const long long r = b * kOsTile + (long long)q * kOsThreads + threadIdx.x;
-            if (r >= N) break;
-            const unsigned g = ids[r];
-            if (radii[g] > 0) {
-                const uint2 rc = rect[g];
-                a += ((rc.y & 0xffffu) - (rc.x & 0xffffu)) * ((rc.y >> 16) - (rc.x >> 16));
-            }
+    const long long r = (long long)blockIdx.x * kOsThreads + threadIdx.x;
+    unsigned g;
+    uint2 rc;
+    const unsigned a = __reduce_add_sync(0xffffffffu, rank_area(ids, radii, rect, r, N, g, rc));
+    if ((threadIdx.x & 31) == 0 && r < N) sums[r >> 5] = a;
+}
+
+// Exclusive prefix of sums[0, n) into offs, one CTA of 1024 threads: each
+// thread adds up a contiguous run, the CTA scans the run totals, each
+// thread writes its run's prefixes.
+__global__ void __launch_bounds__(1024)
+group_scan_kernel(const unsigned* __restrict__ sums, unsigned* __restrict__ offs, long long n)
+{
+    __shared__ unsigned s_w[32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const long long per = (n + 1023) / 1024;
+    const long long beg = min((long long)tid * per, n), end = min(beg + per, n);
+    unsigned local = 0;
+    for (long long i = beg; i < end; i++) local += sums[i];
+    unsigned x = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned u = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += u;
+    }
+    if (lane == 31) s_w[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        const unsigned v = s_w[lane];
+        unsigned y = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned u = __shfl_up_sync(0xffffffffu, y, o);
+            if (lane >= o) y += u;
         }
-        unsigned total = 0;
-        cta_excl_scan(a, s_wsum, &total);
-        if (threadIdx.x == 0) sums[b] = total;
+        s_w[lane] = y - v;
+    }
+    __syncthreads();
+    unsigned run = s_w[warp] + x - local;
+    for (long long i = beg; i < end; i++) {
+        offs[i] = run;
+        run += sums[i];
     }
 }
 
 // The pairs of the depth-ordered Gaussians: rank r (Gaussian ids[r]) writes
 // tile id (u16) and Gaussian id for each tile of its rect, row-major, at
-// the prefix sum of the areas of the ranks before it (the block's start is
-// the sum of sums[0..b) from rank_area_kernel); the tiles' low and high
-// bytes are counted into hist[2][256] for the tile sort.  Pairs at or
-// beyond cap are not written (nor counted): the scan of the tile counts has
-// flagged the overflow.
+// the prefix sum of the areas of the ranks before it.  One warp per group
+// of 32 ranks (its first pair at offs[group]), the group's pairs dealt to
+// the lanes 32 at a time; the tiles' low and high bytes are counted into
+// hist[2][256] for the tile sort.  Pairs at or beyond cap are not written
+// (nor counted): the scan of the tile counts has flagged the overflow.
 __global__ void __launch_bounds__(kOsThreads)
 pair_kernel(const StepParams* __restrict__ P, int N, const unsigned* __restrict__ ids,
             const int* __restrict__ radii, const uint2* __restrict__ rect,
-            const unsigned* __restrict__ sums, unsigned short* __restrict__ pkey,
+            const unsigned* __restrict__ offs, unsigned short* __restrict__ pkey,
             unsigned* __restrict__ pval, unsigned* __restrict__ hist)
 {
     __shared__ unsigned s_hist[2 * kOsRadix];
-    __shared__ unsigned s_wsum[kOsWarps];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x, lane = tid & 31;
     for (int i = tid; i < 2 * kOsRadix; i += kOsThreads) s_hist[i] = 0;
+    __syncthreads();
     const long long cap = P->capacity;
-    const int tx_n = P->tiles_x;
-    const long long tiles = ((long long)N + kOsTile - 1) / kOsTile;
-    for (long long b = blockIdx.x; b < tiles; b += gridDim.x) {
-        // this tile's first pair: the areas of every earlier tile
-        unsigned long long before = 0;
-        for (long long t = tid; t < b; t += kOsThreads) before += sums[t];
+    const unsigned tx_n = (unsigned)P->tiles_x;
+    const long long r = (long long)blockIdx.x * kOsThreads + tid;
+    unsigned g;
+    uint2 rc;
+    const unsigned area = rank_area(ids, radii, rect, r, N, g, rc);
+    unsigned incl = area;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) before += __shfl_xor_sync(0xffffffffu, before, o);
-        if (lane == 0) s_wsum[warp] = (unsigned)before;   // < 2^30 pairs in all
-        __syncthreads();
-        unsigned long long tile_base = 0;
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned u = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += u;
+    }
+    const unsigned total = __shfl_sync(0xffffffffu, incl, 31);
+    const unsigned long long off = r - lane < N ? offs[(r - lane) >> 5] : 0ull;
+    for (unsigned p0 = 0; p0 < total; p0 += 32) {
+        const unsigned pidx = p0 + lane;
+        int owner = 0;
 #pragma unroll
-        for (int w = 0; w < kOsWarps; w++) tile_base += s_wsum[w];
-        __syncthreads();
-        // the warp's 512 ranks, 16 groups of 32 (rank-major over lanes)
-        const long long base = b * kOsTile + (long long)warp * (kOsItems * 32);
-        unsigned area[kOsItems];
-        uint2 rcs[kOsItems];
-        unsigned gid[kOsItems];
-        unsigned wsum = 0;
-#pragma unroll
-        for (int q = 0; q < kOsItems; q++) {
-            const long long r = base + q * 32 + lane;
-            area[q] = 0;
-            rcs[q] = make_uint2(0u, 0u);
-            gid[q] = 0;
-            if (r < N) {
-                const unsigned g = ids[r];
-                gid[q] = g;
-                if (radii[g] > 0) {
-                    rcs[q] = rect[g];
-                    area[q] = ((rcs[q].y & 0xffffu) - (rcs[q].x & 0xffffu)) *
-                              ((rcs[q].y >> 16) - (rcs[q].x >> 16));
-                }
-            }
-            wsum += __reduce_add_sync(0xffffffffu, area[q]);
+        for (int step = 16; step > 0; step >>= 1) {
+            const unsigned probe = __shfl_sync(0xffffffffu, incl, owner + step - 1);
+            if (probe <= pidx) owner += step;
         }
-        const unsigned wex = cta_excl_scan(lane == 0 ? wsum : 0u, s_wsum, nullptr);
-        unsigned long long off = tile_base + __shfl_sync(0xffffffffu, wex, 0);
-        // deal each group's pairs to the lanes, 32 at a time
-#pragma unroll
-        for (int q = 0; q < kOsItems; q++) {
-            unsigned incl = area[q];
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const unsigned u = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += u;
-            }
-            const unsigned total = __shfl_sync(0xffffffffu, incl, 31);
-            for (unsigned p0 = 0; p0 < total; p0 += 32) {
-                const unsigned pidx = p0 + lane;
-                int owner = 0;
-#pragma unroll
-                for (int step = 16; step > 0; step >>= 1) {
-                    const unsigned probe = __shfl_sync(0xffffffffu, incl, owner + step - 1);
-                    if (probe <= pidx) owner += step;
-                }
-                const unsigned o_incl = __shfl_sync(0xffffffffu, incl, owner);
-                const unsigned o_area = __shfl_sync(0xffffffffu, area[q], owner);
-                const unsigned o_g = __shfl_sync(0xffffffffu, gid[q], owner);
-                const unsigned o_rx = __shfl_sync(0xffffffffu, rcs[q].x, owner);
-                const unsigned o_ry = __shfl_sync(0xffffffffu, rcs[q].y, owner);
-                if (pidx >= total) continue;
-                const unsigned k = pidx - (o_incl - o_area);
-                const unsigned x0 = o_rx & 0xffffu, y0 = o_rx >> 16;
-                const unsigned w = (o_ry & 0xffffu) - x0;
-                const unsigned tile = (y0 + k / w) * (unsigned)tx_n + x0 + k % w;
-                const unsigned long long idx = off + pidx;
-                if (idx < (unsigned long long)cap) {
-                    pkey[idx] = (unsigned short)tile;
-                    pval[idx] = o_g;
-                    atomicAdd(&s_hist[tile & 0xffu], 1u);
-                    atomicAdd(&s_hist[kOsRadix + (tile >> 8)], 1u);
-                }
-            }
-            off += total;
+        const unsigned o_incl = __shfl_sync(0xffffffffu, incl, owner);
+        const unsigned o_area = __shfl_sync(0xffffffffu, area, owner);
+        const unsigned o_g = __shfl_sync(0xffffffffu, g, owner);
+        const unsigned o_rx = __shfl_sync(0xffffffffu, rc.x, owner);
+        const unsigned o_ry = __shfl_sync(0xffffffffu, rc.y, owner);
+        if (pidx >= total) continue;
+        const unsigned k = pidx - (o_incl - o_area);
+        const unsigned x0 = o_rx & 0xffffu, y0 = o_rx >> 16;
+        const unsigned w = (o_ry & 0xffffu) - x0;
+        const unsigned tile = (y0 + k / w) * tx_n + x0 + k % w;
+        const unsigned long long idx = off + pidx;
+        if (idx < (unsigned long long)cap) {
+            pkey[idx] = (unsigned short)tile;
+            pval[idx] = o_g;
+            atomicAdd(&s_hist[tile & 0xffu], 1u);
+            atomicAdd(&s_hist[kOsRadix + (tile >> 8)], 1u);
         }
     }
     __syncthreads();
@@ -419,8 +421,6 @@ template <class Src>
 const void* count_ptr() { return (const void*)digit_count_kernel<Src>; }
 template <class Src, class KeyT, bool WK>
 const void* scatter_ptr() { return (const void*)digit_scatter_kernel<Src, KeyT, WK>; }
-const void* area_ptr() { return (const void*)rank_area_kernel; }
-const void* pair_ptr() { return (const void*)pair_kernel; }
 
 int grid_for(long long max_items, int per_launch)
 {
@@ -480,12 +480,15 @@ int launch_bin_sort(const StepParams* P, int N, int num_tiles, long long cap, co
     launch_pass<ArraySource<unsigned>, unsigned, false>(ArraySource<unsigned>{S.dkey_b, S.dval_b},
                                                         nullptr, S.dval_a, hist_d + 768, S, ts,
                                                         nullptr, N, N, N, 24, s);
-    // pairs in depth order; the area sums live in the counts half of status
+    // pairs in depth order: area sums per 32 ranks (in the counts half of
+    // status), their prefix (in the offsets half), then the pairs
     unsigned* sums = reinterpret_cast<unsigned*>(S.status);
-    rank_area_kernel<<<grid_for(N, loop_grid<area_ptr>()), kOsThreads, 0, s>>>(
-        N, S.dval_a, B.proj.radii, B.proj.rect, sums);
-    pair_kernel<<<grid_for(N, loop_grid<pair_ptr>()), kOsThreads, 0, s>>>(
-        P, N, S.dval_a, B.proj.radii, B.proj.rect, sums, S.pkey_a, S.pval_a, hist_p);
+    unsigned* goffs = sums + (size_t)kOsRadix * ts;
+    const int rgrid = (N + kOsThreads - 1) / kOsThreads;
+    rank_area_kernel<<<rgrid, kOsThreads, 0, s>>>(N, S.dval_a, B.proj.radii, B.proj.rect, sums);
+    group_scan_kernel<<<1, 1024, 0, s>>>(sums, goffs, ((long long)N + 31) / 32);
+    pair_kernel<<<rgrid, kOsThreads, 0, s>>>(P, N, S.dval_a, B.proj.radii, B.proj.rect, goffs,
+                                             S.pkey_a, S.pval_a, hist_p);
     // stable sort of the pairs by tile id: one pass per byte of the tile ids
     const int* n_dev = B.tile_offset + num_tiles;
     unsigned* ids = reinterpret_cast<unsigned*>(B.sorted_ids);
@@ -493,7 +496,7 @@ int launch_bin_sort(const StepParams* P, int N, int num_tiles, long long cap, co
         launch_pass<ArraySource<unsigned short>, unsigned short, false>(
             ArraySource<unsigned short>{S.pkey_a, S.pval_a}, nullptr, ids, hist_p, S, ts, n_dev, 0,
             cap, cap, 0, s);
-        return 1 + 12 + 2 + 3;
+        return 1 + 12 + 3 + 3;
     }
     launch_pass<ArraySource<unsigned short>, unsigned short, true>(
         ArraySource<unsigned short>{S.pkey_a, S.pval_a}, S.pkey_b, S.pval_b, hist_p, S, ts, n_dev, 0,
@@ -501,7 +504,7 @@ int launch_bin_sort(const StepParams* P, int N, int num_tiles, long long cap, co
     launch_pass<ArraySource<unsigned short>, unsigned short, false>(
         ArraySource<unsigned short>{S.pkey_b, S.pval_b}, nullptr, ids, hist_p + kOsRadix, S, ts,
         n_dev, 0, cap, cap, 8, s);
-    return 1 + 12 + 2 + 6;
+    return 1 + 12 + 3 + 6;
 }
 
 }  // namespace msp
