@@ -268,9 +268,9 @@ int msplat_render(
  * MSPLAT_NOALLOC_SCRATCH_BYTES per device.
  *
  * Limit: the call is rejected with MSPLAT_ERR_ARG, before any CUDA call,
- * when 72 bytes per Gaussian + 8 per pixel + 20 per depth-chunk pixel
- * (chunked path only) + 132 per tile + 16 intersections of 16.5 bytes per
- * Gaussian do not fit the array (about 175k Gaussians at 1280x720).  Spare
+ * when 56 bytes per Gaussian + 8 per pixel + 20 per depth-chunk pixel
+ * (chunked path only) + 132 per tile + 16 intersections of 20 bytes per
+ * Gaussian do not fit the array (about 160k Gaussians at 1280x720).  Spare
  * bytes become extra intersection slots; more intersections than slots
  * return MSPLAT_ERR_OVERFLOW.  The first call on a device (with it current)
  * does the set-up and should precede any stream capture.  Calls on one

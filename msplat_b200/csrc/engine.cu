@@ -67,7 +67,6 @@ struct Engine {
     bool user_stream_set = false;
     // allocated sizes
     long long cap_N = 0, cap_grad_N = 0, cap_pix = 0, cap_T = 0, cap_isect = 0, cap_chunk = 0;
-    long long cap_status = 0;
     Buffers B{};
     ParamSlot* d_slot = nullptr;
     StepParams* d_params = nullptr;  // &d_slot->p
@@ -163,11 +162,9 @@ static void free_buffers()
 {
     Buffers& B = g.B;
     void* ptrs[] = {B.proj.xy, B.proj.depth, B.proj.radii, B.proj.conic_op, B.proj.rgb, B.proj.rect,
-                    B.proj.sh_mean, B.tile_count, B.tile_offset, B.tile_order, B.sorted_ids, B.out_img,
+                    B.proj.sh_mean, B.tile_count, B.tile_offset, B.tile_order, B.keys, B.keys_alt, B.sorted_ids, B.out_img,
                     B.final_T, B.final_idx, B.v_rendered, B.grad_acc,
-                    B.chunk_T, B.chunk_C, B.chunk_idx, B.prefix_T, B.after_C,
-                    B.sort.dkey_a, B.sort.dval_a, B.sort.dkey_b, B.sort.dval_b, B.sort.pkey_a,
-                    B.sort.pkey_b, B.sort.pval_a, B.sort.pval_b, B.sort.status, B.sort.ctrl};
+                    B.chunk_T, B.chunk_C, B.chunk_idx, B.prefix_T, B.after_C};
     for (void* p : ptrs)
         if (p) cudaFree(p);
     float* ls = B.loss_sum;
@@ -178,7 +175,6 @@ static void free_buffers()
     B.err = er;
     B.isect_total = it;
     g.cap_N = g.cap_grad_N = g.cap_pix = g.cap_T = g.cap_isect = g.cap_chunk = 0;
-    g.cap_status = 0;
 }
 
 // Buffer cache: grow-only, like FusedTensorCache::ensure_* (msplat_metal.mm:383-452).
@@ -194,33 +190,20 @@ static int ensure(long long N, long long W, long long H, long long T, int K, boo
         if ((rc = realloc_dev(B.proj.conic_op, n))) return rc;
         if ((rc = realloc_dev(B.proj.rgb, n))) return rc;
         if ((rc = realloc_dev(B.proj.rect, n))) return rc;
-        if ((rc = realloc_dev(B.sort.dkey_a, n))) return rc;
-        if ((rc = realloc_dev(B.sort.dval_a, n))) return rc;
-        if ((rc = realloc_dev(B.sort.dkey_b, n))) return rc;
-        if ((rc = realloc_dev(B.sort.dval_b, n))) return rc;
         g.cap_N = n;
     }
-    if (!B.sort.ctrl && (rc = realloc_dev(B.sort.ctrl, kSortCtrlWords))) return rc;
     if (train && N > g.cap_grad_N) {
         long long n = std::max(N, g.cap_N);
         if ((rc = realloc_dev(B.grad_acc, (size_t)n * kGradStride))) return rc;
         if ((rc = realloc_dev(B.proj.sh_mean, (size_t)n * 3))) return rc;
         g.cap_grad_N = n;
     }
-    // the sort counts intersections in 32-bit words
-    long long want_isect = std::min(std::max(16 * N, g.growth_isect), (1LL << 30) - 1);
+    long long want_isect = std::max(16 * N, g.growth_isect);
     if (want_isect > g.cap_isect) {
-        if ((rc = realloc_dev(B.sort.pkey_a, want_isect))) return rc;
-        if ((rc = realloc_dev(B.sort.pkey_b, want_isect))) return rc;
-        if ((rc = realloc_dev(B.sort.pval_a, want_isect))) return rc;
-        if ((rc = realloc_dev(B.sort.pval_b, want_isect))) return rc;
+        if ((rc = realloc_dev(B.keys, want_isect))) return rc;
+        if ((rc = realloc_dev(B.keys_alt, want_isect))) return rc;
         if ((rc = realloc_dev(B.sorted_ids, want_isect))) return rc;
         g.cap_isect = want_isect;
-    }
-    const long long words = sort_status_words(g.cap_N, g.cap_isect);
-    if (words > g.cap_status) {
-        if ((rc = realloc_dev(B.sort.status, words))) return rc;
-        g.cap_status = words;
     }
     const long long P = W * H;
     if (P > g.cap_pix) {
@@ -375,10 +358,6 @@ int fill_params(StepParams& p, const CamArgs& a)
         return MSPLAT_ERR_ARG;
     }
     p.num_tiles = p.tiles_x * p.tiles_y;
-    if (p.num_tiles > 65536) {   // tile ids are sorted as 16-bit keys
-        set_error("image too large: %d tiles of 16x16 (at most 65536)", p.num_tiles);
-        return MSPLAT_ERR_ARG;
-    }
     p.degree = (int)a.degree;
     p.degrees_to_use = (int)std::min(a.degrees_to_use, a.degree);
     p.rest_stride = a.rest_stride;
@@ -397,13 +376,13 @@ static int run_forward(const StepParams& p, const float* means, const float* sca
                            p.degrees_to_use, p.rest_stride, st);
     tm.mark(1, st);
     launch_scan_tiles(g.d_params, p.num_tiles, B, st);
-    const int sort_launches =
-        launch_bin_sort(g.d_params, p.num_points, p.num_tiles, g.cap_isect, B, st);
+    launch_scatter(g.d_params, p.num_points, B, st);
+    const int sort_launches = launch_sort_tiles(g.d_params, p.num_tiles, B, st);
     tm.mark(2, st);
     launch_raster_forward(g.d_params, p.num_tiles, p.k_max, p.img_w, p.img_h, B, st);
     g.last_k_max = p.k_max;
     g.last_num_tiles = p.num_tiles;
-    g.launches += 2 + sort_launches + (p.k_max > 1 ? 2 : 1);
+    g.launches += 3 + sort_launches + (p.k_max > 1 ? 2 : 1);
     MSP_CUDA(cudaGetLastError());
     return MSPLAT_OK;
 }

@@ -54,31 +54,13 @@ struct ProjOut {
                          // them while the projection VJP updates the means)
 };
 
-// Working arrays of the binning sort (kernels_sort.cu).  ctrl holds the
-// passes' digit histograms: kSortCtrlWords words zeroed by the scan of the
-// tile counts each step.
-constexpr int kSortCtrlHistDepth = 8;                              // [4][256]
-constexpr int kSortCtrlHistPair = kSortCtrlHistDepth + 4 * 256;    // [2][256]
-constexpr int kSortCtrlWords = kSortCtrlHistPair + 2 * 256;
-struct SortBuffers {
-    unsigned* dkey_a;      // [N] depth keys / Gaussian ids, ping-pong
-    unsigned* dval_a;
-    unsigned* dkey_b;
-    unsigned* dval_b;
-    unsigned short* pkey_a;  // [capacity] tile ids / Gaussian ids of the pairs, ping-pong
-    unsigned short* pkey_b;
-    unsigned* pval_a;
-    unsigned* pval_b;
-    unsigned long long* status;  // [sort_status_words(N, capacity)] per-tile digit counts and offsets
-    unsigned* ctrl;              // [kSortCtrlWords]
-};
-
 struct Buffers {
     ProjOut proj;
-    SortBuffers sort;
     int* tile_count;       // [T * kCountPitch] zero between steps
     int* tile_offset;      // [T+1] exclusive scan
     int* tile_order;       // [T] tiles by intersection count, largest first (CTA order)
+    unsigned long long* keys;      // [capacity]
+    unsigned long long* keys_alt;  // [capacity] merge scratch for tiles longer than one register-sorted run
     int* sorted_ids;       // [capacity]
     float* out_img;        // [H*W*3]
     float* final_T;        // [H*W]
@@ -204,12 +186,8 @@ void launch_project_forward(const StepParams* P, int N, const float* means, cons
                             const float* opac, const Buffers& B, bool zero_grads,
                             int degrees_to_use_host, int rest_stride_host, cudaStream_t s);
 void launch_scan_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s);
-// Binning and per-tile depth order (kernels_sort.cu): the Gaussian ids of
-// every tile, in (depth, id) order, into B.sorted_ids.  Returns the kernels
-// launched.  sort_status_words: length of SortBuffers::status.
-int launch_bin_sort(const StepParams* P, int N, int num_tiles, long long capacity,
-                    const Buffers& B, cudaStream_t s);
-long long sort_status_words(long long N, long long capacity);
+void launch_scatter(const StepParams* P, int N, const Buffers& B, cudaStream_t s);
+int launch_sort_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s);
 void launch_count_raster_work(const StepParams* P, int num_tiles, const Buffers& B,
                               unsigned long long* d_out, cudaStream_t s);
 void launch_raster_forward(const StepParams* P, int num_tiles, int k_max, int W, int H,

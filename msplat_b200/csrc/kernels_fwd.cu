@@ -1,6 +1,5 @@
-// kernels_fwd.cu -- forward half of the step: projection + SH with tile
-// counting, the scan of the tile counts and the forward rasterizer (the
-// binning and per-tile depth order are in kernels_sort.cu).  Compiled with
+// kernels_fwd.cu -- forward half of the step: projection + SH, tile binning,
+// per-tile depth sort and the forward rasterizer.  Compiled with
 // --fmad=false (see msp_math.cuh): every value here is bit-identical to the
 // CPU oracle.
 #include "engine.h"
@@ -10,9 +9,27 @@
 namespace msp {
 
 constexpr int kProjThreads = 128;
+#ifndef MSP_SORT_THREADS
+#define MSP_SORT_THREADS 128
+#endif
+constexpr int kSortThreads = MSP_SORT_THREADS;
+#ifndef MSP_SORT_RADIX
+#define MSP_SORT_RADIX 1
+#endif
+#ifndef MSP_RADIX_SPLIT
+#define MSP_RADIX_SPLIT 1
+#endif
 #ifndef MSP_FWD_MIN_BLOCKS
 #define MSP_FWD_MIN_BLOCKS 6
 #endif
+#ifndef MSP_SCATTER_ROUNDS
+#define MSP_SCATTER_ROUNDS 1
+#endif
+#ifndef MSP_SORT_MIN_BLOCKS
+#define MSP_SORT_MIN_BLOCKS 8
+#endif
+constexpr int kSortRun = 2048;                   // keys sorted in registers in one pass
+constexpr int kSortKMax = kSortRun / kSortThreads;  // keys per thread at most
 
 // ---------------------------------------------------------------------------
 // Projection + SH colour + tile counting.
@@ -302,9 +319,9 @@ constexpr int kOrderBuckets = 1024;  // = the scan CTA's threads
 __device__ __forceinline__ int order_bucket(int count) { return min(count >> 1, kOrderBuckets - 1); }
 
 __global__ void __launch_bounds__(1024)
-scan_tiles_kernel(const StepParams* __restrict__ P, int T, int* __restrict__ count,
+scan_tiles_kernel(const StepParams* __restrict__ P, int T, const int* __restrict__ count,
                   int* __restrict__ offset, int* __restrict__ order, int* __restrict__ err,
-                  int* __restrict__ isect_total, unsigned* __restrict__ sort_ctrl)
+                  int* __restrict__ isect_total)
 {
     __shared__ int s_warp[32];
     __shared__ int s_bucket[kOrderBuckets];
@@ -377,18 +394,562 @@ scan_tiles_kernel(const StepParams* __restrict__ P, int T, int* __restrict__ cou
         s_bucket[b] = s_warp[warp] + x - c;
     }
     __syncthreads();
-    for (int i = beg; i < end; i++) {
+    for (int i = beg; i < end; i++)
         order[atomicAdd(&s_bucket[order_bucket(count[i * kCountPitch])], 1)] = i;
-        count[i * kCountPitch] = 0;   // read for the last time: ready for the next step
-    }
-    // the binning sort's tickets and histograms start from zero
-    for (int i = tid; i < kSortCtrlWords; i += 1024) sort_ctrl[i] = 0u;
 }
 
 void launch_scan_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s)
 {
     scan_tiles_kernel<<<1, 1024, 0, s>>>(P, num_tiles, B.tile_count, B.tile_offset, B.tile_order,
-                                         B.err, B.isect_total, B.sort.ctrl);
+                                         B.err, B.isect_total);
+}
+
+// ---------------------------------------------------------------------------
+// Key scatter: every visible Gaussian writes (depth bits << 32 | id) into
+// each tile of its rect.  The slot comes from counting the tile's counter
+// back down, which also leaves the counters at zero for the next step.
+// Reference key: scatter_to_prealloc_bins_kernel, msplat_metal.metal:2044-2056.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+scatter_kernel(const StepParams* __restrict__ P, int N, const int* __restrict__ radii,
+               const float* __restrict__ depth, const uint2* __restrict__ rect,
+               int* __restrict__ count, const int* __restrict__ offset,
+               unsigned long long* __restrict__ keys)
+{
+    // Warp-cooperative: the warp's 32 Gaussians' (Gaussian, tile) pairs are
+    // dealt out to all lanes, 32 at a time, so every lane has an atomic in
+    // flight each round however unevenly the rects are sized.
+    const int lane = threadIdx.x & 31;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    int x0 = 0, y0 = 0, w = 0, area = 0;
+    unsigned long long key = 0;
+    if (i < N && radii[i] > 0) {
+        const uint2 r = rect[i];
+        x0 = r.x & 0xffff;
+        y0 = r.x >> 16;
+        w = (r.y & 0xffff) - x0;
+        area = w * ((r.y >> 16) - y0);
+        key = ((unsigned long long)__float_as_uint(depth[i]) << 32) | (unsigned)i;
+    }
+    // inclusive prefix of the areas over the warp
+    int incl = area;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += u;
+    }
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
+    const long long cap = P->capacity;
+    const int tx_n = P->tiles_x;
+    // kRounds rounds of 32 pairs per iteration: their atomics are issued
+    // together, so a lane waits for one atomic latency per kRounds pairs.
+    // Measured at C1 (bin+sort): 1 round 0.195 ms, 2: 0.197, 3: 0.200,
+    // 4: 0.202, 8: 0.206 -- fewer registers and more warps beat more
+    // atomics in flight per warp.
+    constexpr int kRounds = MSP_SCATTER_ROUNDS;
+    for (int p0 = 0; p0 < total; p0 += 32 * kRounds) {
+        int tile[kRounds];
+        unsigned long long kv[kRounds];
+#pragma unroll
+        for (int u = 0; u < kRounds; u++) {
+            const int pidx = p0 + 32 * u + lane;
+            // owner = first lane whose inclusive prefix exceeds pidx
+            int owner = 0;
+#pragma unroll
+            for (int step = 16; step > 0; step >>= 1) {
+                const int probe = __shfl_sync(0xffffffffu, incl, owner + step - 1);
+                if (probe <= pidx) owner += step;
+            }
+            const int o_incl = __shfl_sync(0xffffffffu, incl, owner);
+            const int o_area = __shfl_sync(0xffffffffu, area, owner);
+            const int o_x0 = __shfl_sync(0xffffffffu, x0, owner);
+            const int o_y0 = __shfl_sync(0xffffffffu, y0, owner);
+            const int o_w = __shfl_sync(0xffffffffu, w, owner);
+            kv[u] = __shfl_sync(0xffffffffu, key, owner);
+            tile[u] = -1;
+            if (pidx < total) {
+                const int k = pidx - (o_incl - o_area);
+                tile[u] = (o_y0 + k / o_w) * tx_n + o_x0 + k % o_w;
+            }
+        }
+        int pos[kRounds];
+#pragma unroll
+        for (int u = 0; u < kRounds; u++)
+            if (tile[u] >= 0) pos[u] = atomicSub(&count[tile[u] * kCountPitch], 1) - 1;
+#pragma unroll
+        for (int u = 0; u < kRounds; u++) {
+            if (tile[u] < 0) continue;
+            const long long idx = (long long)offset[tile[u]] + pos[u];
+            if (idx < cap) keys[idx] = kv[u];
+        }
+    }
+}
+
+void launch_scatter(const StepParams* P, int N, const Buffers& B, cudaStream_t s)
+{
+    if (N <= 0) return;
+    scatter_kernel<<<(N + 255) / 256, 256, 0, s>>>(P, N, B.proj.radii, B.proj.depth, B.proj.rect,
+                                                   B.tile_count, B.tile_offset, B.keys);
+}
+
+// ---------------------------------------------------------------------------
+// Per-tile ascending sort of the 64-bit keys, then the Gaussian ids in that
+// order.  Reference: bitonic_sort_per_tile_kernel, msplat_metal.metal:2064-2138
+// (the fused pack is replaced by id gathers in the rasterizers).
+// A tile of n <= kSortRun keys is padded with ~0 to npow = max(256, 2^ceil(log2 n))
+// and sorted by a bitonic network whose element e = thread*K + r lives in
+// register r of `thread` (K = npow / 256): compare-exchange distances below K
+// stay in registers, distances below 32K use warp shuffles, larger ones go
+// through shared memory.  Larger tiles that the radix sorts below do not take
+// (more than kLargeRun keys, or refused) sort kSortRun runs that way and
+// merge them pairwise along merge paths.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cmpx(unsigned long long& lo, unsigned long long& hi, bool up)
+{
+    const unsigned long long a = lo, b = hi;
+    const bool swap = (a > b) == up;
+    lo = swap ? b : a;
+    hi = swap ? a : b;
+}
+
+template <int K>
+__device__ __forceinline__ void bitonic_regs(unsigned long long (&v)[K], unsigned long long* s,
+                                             int npow)
+{
+    const int t = threadIdx.x, lane = t & 31;
+    for (int k = 2; k <= npow; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            if (j < K) {
+                // compile-time distance jj == j keeps v[] in registers
+#pragma unroll
+                for (int jj = K >> 1; jj >= 1; jj >>= 1) {
+                    if (jj != j) continue;
+#pragma unroll
+                    for (int r = 0; r < K; r++) {
+                        if (r & jj) continue;
+                        const int e = t * K + r;
+                        cmpx(v[r], v[r | jj], (e & k) == 0);
+                    }
+                }
+            } else if (j < 32 * K) {
+                const int lm = j / K;                   // partner lane offset
+                const bool lower = (lane & lm) == 0;
+#pragma unroll
+                for (int r = 0; r < K; r++) {
+                    const int e = t * K + r;
+                    const bool up = (e & k) == 0;
+                    const unsigned long long o = __shfl_xor_sync(0xffffffffu, v[r], lm);
+                    const bool take_min = lower == up;
+                    v[r] = take_min ? (o < v[r] ? o : v[r]) : (o > v[r] ? o : v[r]);
+                }
+            } else {
+                // shared-memory exchange; index e is stored at e + e/16 so
+                // that a warp's 64-bit accesses hit distinct banks
+                __syncthreads();
+#pragma unroll
+                for (int r = 0; r < K; r++) {
+                    const int e = t * K + r;
+                    s[e + (e >> 4)] = v[r];
+                }
+                __syncthreads();
+#pragma unroll
+                for (int r = 0; r < K; r++) {
+                    const int e = t * K + r;
+                    const bool up = (e & k) == 0;
+                    const int f = e ^ j;
+                    const unsigned long long o = s[f + (f >> 4)];
+                    const bool take_min = ((e & j) == 0) == up;
+                    v[r] = take_min ? (o < v[r] ? o : v[r]) : (o > v[r] ? o : v[r]);
+                }
+            }
+        }
+    }
+}
+
+// Sort keys[0, n) (n <= kSortRun) in registers; write the sorted keys back to
+// `out_keys` and/or their ids to `out_ids` (either may be null).
+template <int K>
+__device__ __forceinline__ void sort_run(const unsigned long long* keys, int n,
+                                         unsigned long long* s, unsigned long long* out_keys,
+                                         int* out_ids)
+{
+    const int npow = K * kSortThreads;
+    unsigned long long v[K];
+#pragma unroll
+    for (int r = 0; r < K; r++) {
+        const int e = threadIdx.x * K + r;
+        v[r] = e < n ? keys[e] : ~0ull;
+    }
+    bitonic_regs<K>(v, s, npow);
+#pragma unroll
+    for (int r = 0; r < K; r++) {
+        const int e = threadIdx.x * K + r;
+        if (e < n) {
+            if (out_keys) out_keys[e] = v[r];
+            if (out_ids) out_ids[e] = (int)(unsigned)(v[r] & 0xffffffffull);
+        }
+    }
+}
+
+__device__ __forceinline__ void sort_small(const unsigned long long* keys, int n,
+                                           unsigned long long* s, unsigned long long* out_keys,
+                                           int* out_ids)
+{
+    if (n <= kSortThreads) sort_run<1>(keys, n, s, out_keys, out_ids);
+    else if (n <= 2 * kSortThreads) sort_run<2>(keys, n, s, out_keys, out_ids);
+    else if (n <= 4 * kSortThreads) sort_run<4>(keys, n, s, out_keys, out_ids);
+    else if (kSortKMax == 8 || n <= 8 * kSortThreads) sort_run<8>(keys, n, s, out_keys, out_ids);
+    else if constexpr (kSortKMax >= 16) sort_run<16>(keys, n, s, out_keys, out_ids);
+}
+
+__device__ __forceinline__ int merge_path(const unsigned long long* a, int la,
+                                          const unsigned long long* b, int lb, int d)
+{
+    int lo = max(0, d - lb), hi = min(d, la);
+    while (lo < hi) {
+        int mid = (lo + hi) >> 1;
+        if (a[mid] > b[d - 1 - mid]) hi = mid;
+        else lo = mid + 1;
+    }
+    return lo;
+}
+
+// Per-tile LSD radix sort of the 32-bit depths (the ids ride along) for
+// 2 <= n <= RUN keys with T threads: 8-bit digits, one pass per byte that
+// is not the same for every key of the tile.  Each pass is stable: warp w
+// ranks its contiguous share of the keys 32 at a time (__match_any_sync
+// groups the lanes with equal digits), and the per-(digit, warp) counts are
+// scanned digit-major, warp-minor.  Stability keeps equal depths in input
+// order, which the scatter's atomics leave arbitrary, so each run of equal
+// depths is then put in id order by one thread (insertion sort in shared
+// memory); the result is the order of the 64-bit keys (depth << 32 | id).
+// A tile whose depths are all equal, or that holds a run of more than
+// kMaxTieRun equal depths, is reported and sorted by the bitonic / merge
+// path on the full keys instead.
+constexpr int kRadixSplit = MSP_RADIX_SPLIT;
+constexpr int kMaxTieRun = 32;
+
+template <int T, int RUN>
+struct RadixSmemT {
+    static constexpr int kWarps = T / 32;
+    static constexpr int kChunks = RUN / T;  // 32-key chunks per warp at most
+    static constexpr int kCols = kWarps * kRadixSplit;
+    // Each warp's keys form kRadixSplit consecutive sub-ranges with their
+    // own digit counters, so its scatter runs kRadixSplit independent chains
+    // of counter reads and updates instead of one.
+    static_assert(kChunks % kRadixSplit == 0, "sub-ranges of whole chunks");
+    unsigned key[RUN];
+    int val[RUN];
+    // [column * 256 + digit], column = warp * split + sub-range: a warp's
+    // lanes with different digits touch different banks
+    int hist[256 * kCols];
+    int wsum[kWarps];
+    unsigned red[2 * kWarps];
+};
+using RadixSmem = RadixSmemT<kSortThreads, kSortRun>;
+
+// Exclusive prefix sum of S.hist in place, over the counters in
+// digit-major, column-minor order (256 * kCols counters).
+template <int T, int RUN>
+__device__ __forceinline__ int hist_at(int logical)
+{
+    constexpr int kCols = RadixSmemT<T, RUN>::kCols;
+    return (logical % kCols) * 256 + logical / kCols;
+}
+
+template <int T, int RUN>
+__device__ __forceinline__ void radix_scan(RadixSmemT<T, RUN>& S)
+{
+    using SM = RadixSmemT<T, RUN>;
+    constexpr int kPer = 256 * SM::kCols / T;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int c[kPer];
+    int sum = 0;
+#pragma unroll
+    for (int i = 0; i < kPer; i++) {
+        c[i] = S.hist[hist_at<T, RUN>(tid * kPer + i)];
+        sum += c[i];
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += u;
+    }
+    if (lane == 31) S.wsum[warp] = incl;
+    __syncthreads();
+    int base = incl - sum;
+#pragma unroll
+    for (int w = 0; w < SM::kWarps; w++) base += w < warp ? S.wsum[w] : 0;
+#pragma unroll
+    for (int i = 0; i < kPer; i++) {
+        S.hist[hist_at<T, RUN>(tid * kPer + i)] = base;
+        base += c[i];
+    }
+}
+
+// Returns false (and writes nothing) when the tile cannot be sorted here
+// (all depths equal, or a run of equal depths longer than kMaxTieRun);
+// otherwise writes the ids in ascending (depth, id) order.
+// Register r of a lane holds element w0 + ((r % split) * cv + r / split) * 32
+// + lane: sub-range r % split, its chunk r / split.
+template <int T, int RUN>
+__device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __restrict__ keys, int n,
+                                                RadixSmemT<T, RUN>& S, int* __restrict__ out_ids)
+{
+    using SM = RadixSmemT<T, RUN>;
+    constexpr int V = kRadixSplit;
+    constexpr int kChunks = SM::kChunks;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const unsigned lt = (1u << lane) - 1u;
+    const int C = (n + T - 1) / T;     // chunks per warp
+    const int cv = (C + V - 1) / V;    // chunks per sub-range
+    const int nr = cv * V;             // registers in use
+    const int w0 = warp * nr * 32;     // this warp's first element
+    auto elem = [&](int r) { return w0 + ((r % V) * cv + r / V) * 32 + lane; };
+    unsigned k[kChunks];
+    int v[kChunks];
+    unsigned ko = 0u, ka = ~0u;
+#pragma unroll
+    for (int r = 0; r < kChunks; r++) {
+        k[r] = ~0u;  // padding sorts last and stays behind equal real keys
+        v[r] = 0;
+        const int e = elem(r);
+        if (r < nr && e < n) {
+            const unsigned long long kv = keys[e];
+            k[r] = (unsigned)(kv >> 32);
+            v[r] = (int)(unsigned)(kv & 0xffffffffull);
+            ko |= k[r];
+            ka &= k[r];
+        }
+    }
+    ko = __reduce_or_sync(0xffffffffu, ko);
+    ka = __reduce_and_sync(0xffffffffu, ka);
+    if (lane == 0) {
+        S.red[warp] = ko;
+        S.red[SM::kWarps + warp] = ka;
+    }
+    __syncthreads();
+    unsigned all_or = 0u, all_and = ~0u;
+#pragma unroll
+    for (int w = 0; w < SM::kWarps; w++) {
+        all_or |= S.red[w];
+        all_and &= S.red[SM::kWarps + w];
+    }
+    const unsigned varying = all_or ^ all_and;
+    if (varying == 0u) return false;  // n >= 2 equal depths
+    for (int shift = 0; shift < 32; shift += 8) {
+        if (((varying >> shift) & 0xffu) == 0u) continue;
+        for (int i = lane; i < 256 * V; i += 32) S.hist[warp * V * 256 + i] = 0;
+        __syncwarp();
+        // counts need no order: shared-memory atomics, no chain between chunks
+#pragma unroll
+        for (int r = 0; r < kChunks; r++) {
+            if (r >= nr) break;
+            const unsigned d = (k[r] >> shift) & 0xffu;
+            atomicAdd(&S.hist[(warp * V + r % V) * 256 + d], 1);
+        }
+        __syncthreads();
+        radix_scan(S);
+        __syncthreads();
+        // V independent chains: chunk r0 / V of every sub-range at once
+#pragma unroll
+        for (int r0 = 0; r0 < kChunks; r0 += V) {
+            if (r0 >= nr) break;
+            unsigned peers[V];
+            int slot[V], base[V];
+#pragma unroll
+            for (int u = 0; u < V; u++) {
+                const unsigned d = (k[r0 + u] >> shift) & 0xffu;
+                peers[u] = __match_any_sync(0xffffffffu, d);
+                slot[u] = (warp * V + u) * 256 + d;
+                base[u] = S.hist[slot[u]];
+            }
+            __syncwarp();
+#pragma unroll
+            for (int u = 0; u < V; u++) {
+                if ((peers[u] & lt) == 0u) S.hist[slot[u]] = base[u] + __popc(peers[u]);
+                const int pos = base[u] + __popc(peers[u] & lt);
+                S.key[pos] = k[r0 + u];
+                S.val[pos] = v[r0 + u];
+            }
+            __syncwarp();
+        }
+        __syncthreads();
+#pragma unroll
+        for (int r = 0; r < kChunks; r++) {
+            if (r >= nr) break;
+            const int e = elem(r);
+            k[r] = S.key[e];
+            v[r] = S.val[e];
+        }
+    }
+    // S.key holds the sorted depths (at least one pass ran): any equal
+    // neighbours among the real keys?
+    bool tie = false;
+#pragma unroll
+    for (int r = 0; r < kChunks; r++) {
+        if (r >= nr) break;
+        const int e = elem(r);
+        if (e + 1 < n && k[r] == S.key[e + 1]) tie = true;
+    }
+    if (__syncthreads_or(tie)) {
+        // each run of equal depths, in id order: the thread holding the
+        // run's first element sorts its ids in place (runs are disjoint)
+        bool too_long = false;
+#pragma unroll
+        for (int r = 0; r < kChunks; r++) {
+            if (r >= nr) break;
+            const int e = elem(r);
+            if (e + 1 >= n || k[r] != S.key[e + 1] || (e > 0 && S.key[e - 1] == k[r])) continue;
+            int end = e + 2;
+            while (end < n && end - e <= kMaxTieRun && S.key[end] == k[r]) end++;
+            if (end - e > kMaxTieRun) {
+                too_long = true;
+                continue;
+            }
+            for (int a = e + 1; a < end; a++) {
+                const int x = S.val[a];
+                int b = a - 1;
+                while (b >= e && (unsigned)S.val[b] > (unsigned)x) {
+                    S.val[b + 1] = S.val[b];
+                    b--;
+                }
+                S.val[b + 1] = x;
+            }
+        }
+        if (__syncthreads_or(too_long)) return false;
+#pragma unroll
+        for (int r = 0; r < kChunks; r++) {
+            if (r >= nr) break;
+            v[r] = S.val[elem(r)];
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < kChunks; r++) {
+        if (r >= nr) break;
+        const int e = elem(r);
+        if (e < n) out_ids[e] = v[r];
+    }
+    return true;
+}
+
+// Tiles of kSortRun + 1 .. kLargeRun keys: the same radix sort with 512
+// threads and 80 KB of dynamic shared memory, two CTAs per SM, each CTA
+// walking the tile list (largest first) and taking every gridDim.x-th tile.
+// Slot 1 of a tile's counter line (slot 0 is the count) records whether the
+// tile is left to sort_tiles_kernel (1) or done (0); it is written for every
+// tile in this range and read only for those.
+constexpr int kLargeThreads = 512;
+constexpr int kLargeRun = 8192;
+using LargeSmem = RadixSmemT<kLargeThreads, kLargeRun>;
+
+__global__ void __launch_bounds__(kLargeThreads, 2)
+sort_large_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
+                        const int* __restrict__ order, int num_tiles,
+                        const unsigned long long* __restrict__ keys, int* __restrict__ ids,
+                        int* __restrict__ tile_line)
+{
+    extern __shared__ __align__(16) unsigned char s_large[];
+    LargeSmem& S = *reinterpret_cast<LargeSmem*>(s_large);
+    const long long cap = P->capacity;
+    for (int i = blockIdx.x; i < num_tiles; i += gridDim.x) {
+        const int t = order[i];
+        const long long start = min((long long)offset[t], cap);
+        const long long end = min((long long)offset[t + 1], cap);
+        const int n = (int)(end - start);
+        if (n <= kSortRun || n > kLargeRun) continue;
+        __syncthreads();  // the previous tile's last reads of S
+        const bool ok = radix_sort_tile(keys + start, n, S, ids + start);
+        if (threadIdx.x == 0) tile_line[t * kCountPitch + 1] = ok ? 0 : 1;
+    }
+}
+
+__global__ void __launch_bounds__(kSortThreads, MSP_SORT_MIN_BLOCKS)
+sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
+                  const int* __restrict__ order, unsigned long long* __restrict__ keys,
+                  unsigned long long* __restrict__ keys_alt, int* __restrict__ ids,
+                  const int* __restrict__ tile_line)
+{
+    __shared__ union {
+        unsigned long long bitonic[kSortRun + kSortRun / 16];
+        RadixSmem radix;
+    } sm;
+    unsigned long long* s = sm.bitonic;
+    const int t = order[blockIdx.x];
+    const long long cap = P->capacity;
+    const long long start = min((long long)offset[t], cap);
+    const long long end = min((long long)offset[t + 1], cap);
+    const int n = (int)(end - start);
+    if (n <= 0) return;
+    if (n <= kSortRun) {
+        if (MSP_SORT_RADIX && n > kSortThreads) {
+            if (radix_sort_tile(keys + start, n, sm.radix, ids + start)) return;
+            __syncthreads();
+        }
+        sort_small(keys + start, n, s, nullptr, ids + start);
+        return;
+    }
+    // kSortRun < n <= kLargeRun: sorted by sort_large_tiles_kernel unless
+    // it left the tile here
+    if (n <= kLargeRun && tile_line[t * kCountPitch + 1] == 0) return;
+    // Large tile: sorted runs of kSortRun, then pairwise merges.
+    unsigned long long* src = keys + start;
+    unsigned long long* dst = keys_alt + start;
+    for (int r0 = 0; r0 < n; r0 += kSortRun) {
+        __syncthreads();
+        sort_small(src + r0, min(kSortRun, n - r0), s, src + r0, nullptr);
+    }
+    __syncthreads();
+    for (long long L = kSortRun; L < n; L <<= 1) {
+        for (long long s0 = 0; s0 < n; s0 += 2 * L) {
+            const unsigned long long* a = src + s0;
+            const int la = (int)min(L, (long long)n - s0);
+            const unsigned long long* b = a + la;
+            const int lb = (int)max(0LL, min(L, (long long)n - s0 - la));
+            const int total = la + lb;
+            const int d0 = (int)((long long)total * threadIdx.x / kSortThreads);
+            const int d1 = (int)((long long)total * (threadIdx.x + 1) / kSortThreads);
+            int ia = merge_path(a, la, b, lb, d0);
+            int ib = d0 - ia;
+            unsigned long long* o = dst + s0 + d0;
+            for (int q = d0; q < d1; q++) {
+                bool take_a = ib >= lb || (ia < la && a[ia] < b[ib]);
+                *o++ = take_a ? a[ia++] : b[ib++];
+            }
+        }
+        __syncthreads();
+        unsigned long long* tmp = src;
+        src = dst;
+        dst = tmp;
+    }
+    for (int i = threadIdx.x; i < n; i += kSortThreads)
+        ids[start + i] = (int)(unsigned)(src[i] & 0xffffffffull);
+}
+
+// Two launches: the tiles of kSortRun + 1 .. kLargeRun keys first (a grid
+// of two CTAs per SM walking the tile list), then every other tile.
+int launch_sort_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s)
+{
+    if (num_tiles <= 0) return 0;
+    static std::once_flag once[kMaxDeviceSlots];
+    static int sms[kMaxDeviceSlots];
+    int dev = 0;
+    if (!once_per_device(once, [](int d) {
+            int n = 0;
+            cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
+            cudaFuncSetAttribute(sort_large_tiles_kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)sizeof(LargeSmem));
+            sms[d] = n > 0 ? n : 148;
+        }) || cudaGetDevice(&dev) != cudaSuccess)
+        return 0;
+    const int grid = std::min(num_tiles, 2 * sms[dev]);
+    sort_large_tiles_kernel<<<grid, kLargeThreads, sizeof(LargeSmem), s>>>(
+        P, B.tile_offset, B.tile_order, num_tiles, B.keys, B.sorted_ids, B.tile_count);
+    sort_tiles_kernel<<<num_tiles, kSortThreads, 0, s>>>(P, B.tile_offset, B.tile_order, B.keys, B.keys_alt,
+                                                        B.sorted_ids, B.tile_count);
+    return 2;
 }
 
 // ---------------------------------------------------------------------------

@@ -48,9 +48,7 @@ inline size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 // Byte offsets of every buffer inside the array; capacity = intersections.
 struct Layout {
     size_t params, err, xy, depth, radii, conic_op, rgb, rect, tile_count, tile_offset, tile_order;
-    size_t final_T, final_idx, chunk_T, chunk_C, chunk_idx, sorted_ids;
-    size_t dkey_a, dval_a, dkey_b, dval_b, ctrl, status, status_words;
-    size_t pkey_a, pkey_b, pval_a, pval_b;
+    size_t final_T, final_idx, chunk_T, chunk_C, chunk_idx, keys, keys_alt, sorted_ids;
     size_t end;
     long long capacity;
 };
@@ -84,17 +82,8 @@ Layout layout(long long N, long long P, long long T, int K, long long cap)
     L.chunk_T = take(kp * sizeof(float));
     L.chunk_C = take(kp * 3 * sizeof(float));
     L.chunk_idx = take(kp * sizeof(int));
-    L.dkey_a = take(n * sizeof(unsigned));
-    L.dval_a = take(n * sizeof(unsigned));
-    L.dkey_b = take(n * sizeof(unsigned));
-    L.dval_b = take(n * sizeof(unsigned));
-    L.ctrl = take(kSortCtrlWords * sizeof(unsigned));
-    L.status_words = (size_t)sort_status_words(N, cap);
-    L.status = take(L.status_words * sizeof(unsigned long long));
-    L.pkey_a = take((size_t)cap * sizeof(unsigned short));
-    L.pkey_b = take((size_t)cap * sizeof(unsigned short));
-    L.pval_a = take((size_t)cap * sizeof(unsigned));
-    L.pval_b = take((size_t)cap * sizeof(unsigned));
+    L.keys = take((size_t)cap * sizeof(unsigned long long));
+    L.keys_alt = take((size_t)cap * sizeof(unsigned long long));
     L.sorted_ids = take((size_t)cap * sizeof(int));
     L.end = o;
     L.capacity = cap;
@@ -172,7 +161,7 @@ extern "C" int msplat_render_noalloc(
     }
     // Whatever is left over becomes extra intersection slots.
     const size_t spare = kScratchBytes - need.end;
-    long long cap = std::min(min_cap + (long long)(spare / 17), (1LL << 30) - 1);
+    long long cap = min_cap + (long long)(spare / 20);
     Layout L = layout(N, P, p.num_tiles, p.k_max, cap);
     while (L.end > kScratchBytes) L = layout(N, P, p.num_tiles, p.k_max, --cap);
     p.capacity = cap;
@@ -199,16 +188,8 @@ extern "C" int msplat_render_noalloc(
         B.chunk_C = reinterpret_cast<float*>(base + L.chunk_C);
         B.chunk_idx = reinterpret_cast<int*>(base + L.chunk_idx);
     }
-    B.sort.dkey_a = reinterpret_cast<unsigned*>(base + L.dkey_a);
-    B.sort.dval_a = reinterpret_cast<unsigned*>(base + L.dval_a);
-    B.sort.dkey_b = reinterpret_cast<unsigned*>(base + L.dkey_b);
-    B.sort.dval_b = reinterpret_cast<unsigned*>(base + L.dval_b);
-    B.sort.ctrl = reinterpret_cast<unsigned*>(base + L.ctrl);
-    B.sort.status = reinterpret_cast<unsigned long long*>(base + L.status);
-    B.sort.pkey_a = reinterpret_cast<unsigned short*>(base + L.pkey_a);
-    B.sort.pkey_b = reinterpret_cast<unsigned short*>(base + L.pkey_b);
-    B.sort.pval_a = reinterpret_cast<unsigned*>(base + L.pval_a);
-    B.sort.pval_b = reinterpret_cast<unsigned*>(base + L.pval_b);
+    B.keys = reinterpret_cast<unsigned long long*>(base + L.keys);
+    B.keys_alt = reinterpret_cast<unsigned long long*>(base + L.keys_alt);
     B.sorted_ids = reinterpret_cast<int*>(base + L.sorted_ids);
     B.out_img = out_img;
 
@@ -217,14 +198,14 @@ extern "C" int msplat_render_noalloc(
     // memory has been staged by the time cudaMemcpyAsync returns.
     NA_CUDA(cudaMemcpyAsync(d_params, &p, sizeof(StepParams), cudaMemcpyHostToDevice, st));
     // Only the tile counters and the error word must start at zero; every
-    // other buffer is written before it is read (the scan of the tile
-    // counts clears the sort's histograms).
+    // other buffer is written before it is read.
     NA_CUDA(cudaMemsetAsync(B.err, 0, 4 * sizeof(int), st));
     NA_CUDA(cudaMemsetAsync(B.tile_count, 0, sizeof(int) * (size_t)p.num_tiles * kCountPitch, st));
     launch_project_forward(d_params, p.num_points, means3d, scales, quats, features_dc,
                            features_rest, opacities, B, false, p.degrees_to_use, p.rest_stride, st);
     launch_scan_tiles(d_params, p.num_tiles, B, st);
-    launch_bin_sort(d_params, p.num_points, p.num_tiles, cap, B, st);
+    launch_scatter(d_params, p.num_points, B, st);
+    launch_sort_tiles(d_params, p.num_tiles, B, st);
     launch_raster_forward(d_params, p.num_tiles, p.k_max, p.img_w, p.img_h, B, st);
     NA_CUDA(cudaGetLastError());
     int h_check[2] = {0, 0};

@@ -93,7 +93,7 @@ def test_noalloc_matches_render_twice(case):
 @pytest.mark.gpu
 def test_noalloc_reports_intersection_overflow():
     """4,000 large Gaussians in front of a 1280x720 camera each cover most
-    of its 3,600 tiles: 12.7M intersections, more than the ~3.5M slots left
+    of its 3,600 tiles: 12.7M intersections, more than the ~2.9M slots left
     in the static array once the per-pixel buffers are carved out.  The
     size check passes (it budgets 16 slots per Gaussian); the overflow is
     found on the device and reported, not returned as success."""
