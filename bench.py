@@ -96,6 +96,10 @@ def parse():
                     help="write the per-kernel counter summary from ncu --csv logs of "
                          "--profile-step runs (no GPU needed)")
     ap.add_argument("--hash-file", help="--summarize-ncu: the JSON line --profile-step printed")
+    ap.add_argument("--profile-config", choices=("C1", "C4q"), default="C1",
+                    help="--profile-step: C1, or C4q (C4's distributions at a quarter of the "
+                         "Gaussians and pixels: C4's ~4,000 intersections per tile, small enough "
+                         "for detailed captures)")
     return ap.parse_args()
 
 
@@ -1047,13 +1051,13 @@ def run_c4(args, rank: int, world: int) -> dict:
 
 
 def profile_step(args) -> dict:
-    """One C1 training step after W warm-up steps, alone between
+    """One training step (C1, or --profile-config) after W warm-up steps, alone between
     cudaProfilerStart and cudaProfilerStop (ncu --profile-from-start off)."""
     import torch
     from msplat_b200 import engine
     torch.cuda.set_device(0)
     engine.bind_stream()
-    g, setups, gts, model = build_workload(CONFIG)
+    g, setups, gts, model = build_workload(args.profile_config)
     ncam = len(setups)
     for s in range(args.warmup):
         engine.train_step(model, setups[s % ncam], gts[s % ncam])
@@ -1063,7 +1067,8 @@ def profile_step(args) -> dict:
     engine.train_step(model, setups[view], gts[view])
     torch.cuda.synchronize()
     torch.cuda.profiler.stop()
-    return {"build_hash": build_hash(), "view": view, "warmup": args.warmup, "config": CONFIG}
+    return {"build_hash": build_hash(), "view": view, "warmup": args.warmup,
+            "config": args.profile_config}
 
 
 def main():
