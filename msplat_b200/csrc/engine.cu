@@ -376,7 +376,7 @@ static int run_forward(const StepParams& p, const float* means, const float* sca
                            p.degrees_to_use, p.rest_stride, st);
     tm.mark(1, st);
     launch_scan_tiles(g.d_params, p.num_tiles, B, st);
-    launch_scatter(g.d_params, p.num_points, B, p.num_tiles, st);
+    launch_scatter(g.d_params, p.num_points, B, st);
     const int sort_launches = launch_sort_tiles(g.d_params, p.num_tiles, B, st);
     tm.mark(2, st);
     launch_raster_forward(g.d_params, p.num_tiles, p.k_max, p.img_w, p.img_h, B, st);

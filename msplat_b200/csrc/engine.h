@@ -186,7 +186,7 @@ void launch_project_forward(const StepParams* P, int N, const float* means, cons
                             const float* opac, const Buffers& B, bool zero_grads,
                             int degrees_to_use_host, int rest_stride_host, cudaStream_t s);
 void launch_scan_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s);
-void launch_scatter(const StepParams* P, int N, const Buffers& B, int num_tiles, cudaStream_t s);
+void launch_scatter(const StepParams* P, int N, const Buffers& B, cudaStream_t s);
 int launch_sort_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s);
 void launch_count_raster_work(const StepParams* P, int num_tiles, const Buffers& B,
                               unsigned long long* d_out, cudaStream_t s);

@@ -485,110 +485,9 @@ scatter_kernel(const StepParams* __restrict__ P, int N, const int* __restrict__ 
     }
 }
 
-// The same scatter with one global atomic per (block, tile) instead of per
-// pair: a block of kBinG Gaussians first counts its pairs per tile in
-// shared memory, then reserves each tile's range with one atomicSub on the
-// tile's counter (the block gets [old - c, old)), then walks its pairs again
-// and takes slots from the shared counters.  The L2 atomic units bound the
-// per-pair scatter (measured at C4: ~79G atomics/s); a block of 4,096
-// Gaussians touches most tiles once or more, so this cuts the global atomics
-// by the pairs per tile per block (about 4x at C4, 2x at C1).  The slot order
-// within a tile differs from the per-pair kernel's; nothing depends on it
-// (the per-tile sort orders the keys).
-constexpr int kBinG = 4096;                       // Gaussians per block
-constexpr int kBinMaxTiles = 48 * 1024;           // shared counters (192 KB) at most
-
-template <bool WRITE>
-__device__ __forceinline__ void bin_walk(const StepParams* __restrict__ P, int N, int g0,
-                                         const int* __restrict__ radii,
-                                         const float* __restrict__ depth,
-                                         const uint2* __restrict__ rect, int* s_tile,
-                                         const int* __restrict__ offset,
-                                         unsigned long long* __restrict__ keys)
-{
-    const int lane = threadIdx.x & 31;
-    const long long cap = P->capacity;
-    const int tx_n = P->tiles_x;
-    for (int c = 0; c < kBinG; c += blockDim.x) {
-        const int i = g0 + c + (int)threadIdx.x;
-        int x0 = 0, y0 = 0, w = 0, area = 0;
-        unsigned long long key = 0;
-        if (i < N && radii[i] > 0) {
-            const uint2 r = rect[i];
-            x0 = r.x & 0xffff;
-            y0 = r.x >> 16;
-            w = (r.y & 0xffff) - x0;
-            area = w * ((r.y >> 16) - y0);
-            if (WRITE) key = ((unsigned long long)__float_as_uint(depth[i]) << 32) | (unsigned)i;
-        }
-        int incl = area;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int u = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += u;
-        }
-        const int total = __shfl_sync(0xffffffffu, incl, 31);
-        for (int p0 = 0; p0 < total; p0 += 32) {
-            const int pidx = p0 + lane;
-            int owner = 0;
-#pragma unroll
-            for (int step = 16; step > 0; step >>= 1) {
-                const int probe = __shfl_sync(0xffffffffu, incl, owner + step - 1);
-                if (probe <= pidx) owner += step;
-            }
-            const int o_incl = __shfl_sync(0xffffffffu, incl, owner);
-            const int o_area = __shfl_sync(0xffffffffu, area, owner);
-            const int o_x0 = __shfl_sync(0xffffffffu, x0, owner);
-            const int o_y0 = __shfl_sync(0xffffffffu, y0, owner);
-            const int o_w = __shfl_sync(0xffffffffu, w, owner);
-            const unsigned long long kv = __shfl_sync(0xffffffffu, key, owner);
-            if (pidx >= total) continue;
-            const int k = pidx - (o_incl - o_area);
-            const int tile = (o_y0 + k / o_w) * tx_n + o_x0 + k % o_w;
-            if (!WRITE) {
-                atomicAdd(&s_tile[tile], 1);
-            } else {
-                const long long idx = (long long)offset[tile] + atomicAdd(&s_tile[tile], 1);
-                if (idx < cap) keys[idx] = kv;
-            }
-        }
-    }
-}
-
-__global__ void __launch_bounds__(256)
-scatter_binned_kernel(const StepParams* __restrict__ P, int N, int T,
-                      const int* __restrict__ radii, const float* __restrict__ depth,
-                      const uint2* __restrict__ rect, int* __restrict__ count,
-                      const int* __restrict__ offset, unsigned long long* __restrict__ keys)
-{
-    extern __shared__ int s_tile[];   // [T]
-    for (int t = threadIdx.x; t < T; t += blockDim.x) s_tile[t] = 0;
-    __syncthreads();
-    const int g0 = blockIdx.x * kBinG;
-    bin_walk<false>(P, N, g0, radii, depth, rect, s_tile, offset, keys);
-    __syncthreads();
-    for (int t = threadIdx.x; t < T; t += blockDim.x) {
-        const int c = s_tile[t];
-        if (c) s_tile[t] = atomicSub(&count[t * kCountPitch], c) - c;
-    }
-    __syncthreads();
-    bin_walk<true>(P, N, g0, radii, depth, rect, s_tile, offset, keys);
-}
-
-void launch_scatter(const StepParams* P, int N, const Buffers& B, int num_tiles, cudaStream_t s)
+void launch_scatter(const StepParams* P, int N, const Buffers& B, cudaStream_t s)
 {
     if (N <= 0) return;
-    if (num_tiles <= kBinMaxTiles) {
-        static std::once_flag once[kMaxDeviceSlots];
-        once_per_device(once, [](int) {
-            cudaFuncSetAttribute(scatter_binned_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 kBinMaxTiles * (int)sizeof(int));
-        });
-        scatter_binned_kernel<<<(N + kBinG - 1) / kBinG, 256, num_tiles * sizeof(int), s>>>(
-            P, N, num_tiles, B.proj.radii, B.proj.depth, B.proj.rect, B.tile_count, B.tile_offset,
-            B.keys);
-        return;
-    }
     scatter_kernel<<<(N + 255) / 256, 256, 0, s>>>(P, N, B.proj.radii, B.proj.depth, B.proj.rect,
                                                    B.tile_count, B.tile_offset, B.keys);
 }
@@ -960,24 +859,6 @@ sort_large_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict_
         const long long end = min((long long)offset[t + 1], cap);
         const int n = (int)(end - start);
         if (n <= kSortRun || n > kLargeRun) continue;
-        // the next tile this CTA takes: its keys into L2 while this one sorts
-        // (a hint; the 16-byte-aligned part of its key range only)
-        if (threadIdx.x == 0) {
-            for (int j = i + gridDim.x; j < num_tiles; j += gridDim.x) {
-                const int t2 = order[j];
-                const long long s2 = min((long long)offset[t2], cap);
-                const long long n2 = min((long long)offset[t2 + 1], cap) - s2;
-                if (n2 <= kSortRun) break;   // tiles come largest first: no more large ones
-                if (n2 > kLargeRun) continue;
-                const unsigned long long a0 = ((unsigned long long)(keys + s2) + 15) & ~15ull;
-                const unsigned long long a1 = (unsigned long long)(keys + s2 + n2) & ~15ull;
-                if (a1 > a0)
-                    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a0),
-                                 "r"((unsigned)(a1 - a0))
-                                 : "memory");
-                break;
-            }
-        }
         __syncthreads();  // the previous tile's last reads of S
         const bool ok = radix_sort_tile(keys + start, n, S, ids + start);
         if (threadIdx.x == 0) tile_line[t * kCountPitch + 1] = ok ? 0 : 1;
