@@ -113,11 +113,13 @@ CONFIGS = {
     "C4": dict(n=6_000_000, width=1920, height=1080, seed=0, mean_range=2.0,
                log_scale_mu=math.log(0.01), log_scale_sigma=0.4, camera="sphere", cameras=8,
                radius=4.0),
-    # C4 at a quarter of the Gaussians and a quarter of the pixels: the same
-    # intersections per tile (~4,000), a quarter of the tiles -- a case small
-    # enough for detailed profiler captures of C4's per-tile kernels
+    # C4 at a quarter of the Gaussians and a quarter of the pixels, with
+    # twice the scales (the same radii in pixels at half the focal length):
+    # the same intersections per tile (~4,000) on a quarter of the tiles --
+    # a case small enough for detailed profiler captures of C4's per-tile
+    # kernels
     "C4q": dict(n=1_500_000, width=960, height=540, seed=0, mean_range=2.0,
-                log_scale_mu=math.log(0.01), log_scale_sigma=0.4, camera="sphere", cameras=8,
+                log_scale_mu=math.log(0.02), log_scale_sigma=0.4, camera="sphere", cameras=8,
                 radius=4.0),
 }
 
