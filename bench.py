@@ -999,7 +999,7 @@ def run_c4(args, rank: int, world: int) -> dict:
     ms_max = dist.max_over_ranks(ms) if dist is not None else ms
     # second pass: the exchange (peer kernel or all-reduce) plus Adam, timed
     # per step between the rank's last backward and the step's end
-    ex_ms = None
+    ex_ms = ex_alone_ms = None
     if dist is not None:
         dist.barrier()
         torch.cuda.synchronize()
@@ -1014,6 +1014,22 @@ def run_c4(args, rank: int, world: int) -> dict:
             evs.append((a, b))
         torch.cuda.synchronize()
         ex_ms = dist.max_over_ranks(float(np.mean([a.elapsed_time(b) for a, b in evs])))
+        # third pass: the exchange alone, every rank starting it together
+        # (device idle and a barrier before each), so the time holds no wait
+        # for a slower rank's views
+        evs = []
+        for _ in range(steps):
+            model.step_count += 1
+            multigpu.accumulate_views(dist.ops, model, cams, tgts, dist.grad, dist.compact)
+            torch.cuda.synchronize()
+            dist.barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            dist.apply(cams[0])
+            b.record(stream)
+            evs.append((a, b))
+            torch.cuda.synchronize()
+        ex_alone_ms = dist.max_over_ranks(float(np.mean([a.elapsed_time(b) for a, b in evs])))
     n_isect = int(lib.msplat_num_intersections())
     xbytes = exchange_bytes(model.n, world, dist.compact if dist else False, args.dp_mode)
     result = {
@@ -1035,11 +1051,16 @@ def run_c4(args, rank: int, world: int) -> dict:
                            if args.dp_mode == "peer" else "NCCL all-reduce, Adam on every replica"))},
         "exchange": None if dist is None else {
             "mode": args.dp_mode, "ms_per_step": round(ex_ms, 3),
+            "ms_aligned": round(ex_alone_ms, 3),
+            "roofline_aligned": exchange_roofline(model.n, world, dist.compact, args.dp_mode,
+                                                  ex_alone_ms),
             "nvlink_bytes_per_rank": xbytes,
             "gbs_per_rank": round(xbytes / (ex_ms / 1000.0) / 1e9, 1) if ex_ms else None,
             "roofline": exchange_roofline(model.n, world, dist.compact, args.dp_mode, ex_ms),
             "timing": "CUDA events around the exchange + Adam of each step (includes waiting "
-                      "for the slowest rank's gradients), mean over steps, max over ranks"},
+                      "for the slowest rank's gradients), mean over steps, max over ranks; "
+                      "ms_aligned: the same with the device idle and a barrier before each "
+                      "exchange (no wait for a slower rank)"},
         "intersections_last_view": n_isect,
         "gpu_launches": launches, "clocks": clk,
     }
