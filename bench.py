@@ -941,6 +941,29 @@ def exchange_roofline(n: int, world: int, compact: bool, mode: str, ms: float):
             "frac": round(bound_ms / ms, 4)}
 
 
+def view_cost(model, cs) -> int:
+    """A view's work estimate: its intersections (one render)."""
+    from msplat_b200 import _lib, engine
+    engine.render(model, cs)
+    return int(_lib.load().msplat_num_intersections())
+
+
+def balanced_views(costs, world: int) -> list:
+    """The batch's views split into `world` groups of len(costs) / world,
+    balancing the summed cost: longest first, each to the least-loaded group
+    with room (ties to the lower index).  Every rank computes the same
+    split from the same costs; which rank trains which view does not change
+    the step (the exchange sums every view's gradients)."""
+    per = len(costs) // world
+    groups = [[] for _ in range(world)]
+    loads = [0] * world
+    for v in sorted(range(len(costs)), key=lambda v: (-costs[v], v)):
+        r = min((q for q in range(world) if len(groups[q]) < per), key=lambda q: (loads[q], q))
+        groups[r].append(v)
+        loads[r] += costs[v]
+    return [sorted(gr) for gr in groups]
+
+
 def run_c4(args, rank: int, world: int) -> dict:
     """BASELINE.json config 4, multi-GPU batched views: 6,000,000 Gaussians
     drawn as in config 1 (seed 0), 8 cameras on the radius-4 sphere at
@@ -961,7 +984,8 @@ def run_c4(args, rank: int, world: int) -> dict:
     torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
     engine.bind_stream()
     g, setups, gts, model = build_workload("C4")
-    mine = [rank + k * world for k in range(vpr)]
+    assign = balanced_views([view_cost(model, cs) for cs in setups], world)
+    mine = assign[rank]
     cams = [setups[v] for v in mine]
     tgts = [gts[v] for v in mine]
     dist = None
@@ -1043,6 +1067,8 @@ def run_c4(args, rank: int, world: int) -> dict:
                                "step on a radius-4 sphere",
                    "gaussians": model.n, "width": setups[0].width, "height": setups[0].height,
                    "views_per_step": batch, "views_per_gpu": vpr,
+                   "view_assignment": "views split over the ranks by intersection count "
+                                      "(longest first to the least-loaded rank)",
                    "l2": "inputs larger than L2 (parameters and moments ~4.2 GB)",
                    "parallelism": "single GPU" if world == 1 else (
                        f"dp{world}: replicated Gaussians, " + (

@@ -210,6 +210,58 @@ __device__ __forceinline__ void update_vec4(const DpArgs& a, int gi, int S,
     for (int q = 0; q < W; q++) st4(a.params[q][gi] + e0, p);
 }
 
+// kDpU vector elements per thread per round (elements v, v + nthreads, ...):
+// every load of the round -- each rank's gradient vector, most of them
+// remote, and the local parameter and moments -- is issued before any
+// store, so a thread keeps kDpU * world remote loads in flight.  (Two
+// update_vec4 calls in a row do not: the compiler cannot move the second's
+// loads above the first's stores into the replicas, which may alias.)
+constexpr int kDpU = 2;
+template <int W, int U>
+__device__ __forceinline__ void update_vec4_batch(const DpArgs& a, int gi, int S,
+                                                  const unsigned char* __restrict__ vis,
+                                                  long long e0s, long long v0, long long stride,
+                                                  long long nvec)
+{
+    float4 g[U], p[U], m[U], vv[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+        const long long vi = v0 + u * stride;
+        if (vi >= nvec) continue;
+        const long long e0 = e0s + 4 * vi;
+        float4 gq[W];
+#pragma unroll
+        for (int q = 0; q < W; q++) gq[q] = ld4(a.grads[q] + a.goff[gi] + e0);
+        p[u] = ld4(a.params[a.rank][gi] + e0);
+        m[u] = ld4(a.exp_avg[gi] + e0);
+        vv[u] = ld4(a.exp_avg_sq[gi] + e0);
+        g[u] = gq[0];
+#pragma unroll
+        for (int q = 1; q < W; q++) {
+            g[u].x += gq[q].x;
+            g[u].y += gq[q].y;
+            g[u].z += gq[q].z;
+            g[u].w += gq[q].w;
+        }
+    }
+#pragma unroll
+    for (int u = 0; u < U; u++) {
+        const long long vi = v0 + u * stride;
+        if (vi >= nvec) continue;
+        const long long rel = 4 * vi;
+        const long long e0 = e0s + rel;
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            if (updated(a, gi, S, vis, rel + k))
+                adam_math(comp(p[u], k), comp(m[u], k), comp(vv[u], k), comp(g[u], k) * a.scale,
+                          a.step[gi], a.b1, a.b2, a.inv_bc2[gi], a.eps);
+        st4(a.exp_avg[gi] + e0, m[u]);
+        st4(a.exp_avg_sq[gi] + e0, vv[u]);
+#pragma unroll
+        for (int q = 0; q < W; q++) st4(a.params[q][gi] + e0, p[u]);
+    }
+}
+
 // The update of the shard, group by group, as one flat vector stream per
 // group (no barriers); skipped when the phase-0 wait failed.
 template <int W>
@@ -229,10 +281,8 @@ dp_reduce_adam_kernel(DpArgs a, const unsigned char* __restrict__ vis)
             if (a.vec & (1 << gi)) {
                 body = total / 4 * 4;
                 const long long nvec = body / 4;
-                for (long long v = tid; v < nvec; v += 2 * nthreads) {
-                    update_vec4<W>(a, gi, S, vis, e0s, 4 * v);
-                    if (v + nthreads < nvec) update_vec4<W>(a, gi, S, vis, e0s, 4 * (v + nthreads));
-                }
+                for (long long v = tid; v < nvec; v += kDpU * nthreads)
+                    update_vec4_batch<W, kDpU>(a, gi, S, vis, e0s, v, nthreads, nvec);
             }
             for (long long rel = body + tid; rel < total; rel += nthreads)
                 update_scalar<W>(a, gi, S, vis, e0s, rel);

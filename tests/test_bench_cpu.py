@@ -98,3 +98,15 @@ def test_counter_summary_round_trip(tmp_path, monkeypatch):
                                  {"rast_fwd": 2.0})
     fwd = [r for r in roof if r["stage"] == "rast_fwd"][0]
     assert fwd["warp_instructions"] == 2 * 123456 and fwd["work_scale"] == 2.0
+
+
+def test_balanced_views_split_the_batch_evenly():
+    costs = [31, 34, 32, 33, 30, 35, 29, 36]
+    for world in (1, 2, 4, 8):
+        groups = bench.balanced_views(costs, world)
+        assert sorted(v for g in groups for v in g) == list(range(8))
+        assert all(len(g) == 8 // world for g in groups)
+    two = bench.balanced_views(costs, 2)
+    loads = [sum(costs[v] for v in g) for g in two]
+    assert abs(loads[0] - loads[1]) <= 2          # round-robin would give 8
+    assert bench.balanced_views(costs, 2) == two  # deterministic
