@@ -875,7 +875,7 @@ int rest_bases_updated(int degrees_to_use, int rest_stride)
 // ---------------------------------------------------------------------------
 constexpr int kRestThreads = 256;
 
-template <int RS, bool VEC>
+template <int RS>
 __global__ void __launch_bounds__(kRestThreads)
 rest_adam_kernel(const StepParams* __restrict__ P, int N, const int* __restrict__ radii,
                  const float* __restrict__ grad_acc, const float* __restrict__ sh_mean,
@@ -910,69 +910,18 @@ rest_adam_kernel(const StepParams* __restrict__ P, int N, const int* __restrict_
     const float b1 = P->beta1, b2 = P->beta2, eps = P->eps;
     const size_t e0 = (size_t)g0 * RS;
     const int total = cnt * RS;
-    // element e of the warp's slab: Gaussian e / RS, coefficient e % RS
-    auto live = [&](int e) {
-        const int gl = e / RS, kk = e - gl * RS;
-        return kk < used && s_vis[wbase + gl];
-    };
-    auto grad = [&](int e) {
-        const int gl = e / RS, kk = e - gl * RS;
-        const int b = kk / 3, c = kk - 3 * b;
-        return s_b[wbase + gl][b] * s_c[wbase + gl][c];
-    };
-    int body = 0;
-    if constexpr (VEC) {
-        // 16-byte vectors (the slab starts on a 16-byte boundary: g0 is a
-        // multiple of 32); a vector with no live element is neither read nor
-        // written, one with some is written back whole (its other elements
-        // unchanged: nothing else touches this group meanwhile)
-        constexpr int kU = 4;
-        const int nvec = total / 4;
-        body = 4 * nvec;
-        for (int vb = lane; vb < nvec; vb += 32 * kU) {
-            float4 pv[kU], mv[kU], vv[kU];
-            unsigned on[kU];
-#pragma unroll
-            for (int u = 0; u < kU; u++) {
-                const int vi = vb + 32 * u;
-                on[u] = 0;
-                if (vi >= nvec) continue;
-#pragma unroll
-                for (int k = 0; k < 4; k++) on[u] |= live(4 * vi + k) ? 1u << k : 0u;
-                if (!on[u]) continue;
-                const size_t e = e0 + 4 * (size_t)vi;
-                pv[u] = *reinterpret_cast<const float4*>(rest + e);
-                mv[u] = *reinterpret_cast<const float4*>(rest_m + e);
-                vv[u] = *reinterpret_cast<const float4*>(rest_v + e);
-            }
-#pragma unroll
-            for (int u = 0; u < kU; u++) {
-                if (!on[u]) continue;
-                const int vi = vb + 32 * u;
-                float* p4 = &pv[u].x;
-                float* m4 = &mv[u].x;
-                float* v4 = &vv[u].x;
-#pragma unroll
-                for (int k = 0; k < 4; k++)
-                    if (on[u] >> k & 1u)
-                        adam_math(p4[k], m4[k], v4[k], grad(4 * vi + k), step, b1, b2, inv_bc2, eps);
-                const size_t e = e0 + 4 * (size_t)vi;
-                *reinterpret_cast<float4*>(rest + e) = pv[u];
-                *reinterpret_cast<float4*>(rest_m + e) = mv[u];
-                *reinterpret_cast<float4*>(rest_v + e) = vv[u];
-            }
-        }
-    }
     constexpr int kU = 8;
-    for (int eb = body + lane; eb < total; eb += 32 * kU) {
+    for (int eb = lane; eb < total; eb += 32 * kU) {
         float g[kU], pv[kU], mv[kU], vv[kU];
         bool on[kU];
 #pragma unroll
         for (int u = 0; u < kU; u++) {
             const int e = eb + 32 * u;
-            on[u] = e < total && live(e);
+            const int gl = e / RS, kk = e - gl * RS;
+            on[u] = e < total && kk < used && s_vis[wbase + gl];
             if (on[u]) {
-                g[u] = grad(e);
+                const int b = kk / 3, c = kk - 3 * b;
+                g[u] = s_b[wbase + gl][b] * s_c[wbase + gl][c];
                 pv[u] = rest[e0 + e];
                 mv[u] = rest_m[e0 + e];
                 vv[u] = rest_v[e0 + e];
@@ -1070,18 +1019,10 @@ int launch_project_backward_adam(const StepParams* P, int N, int degrees_to_use_
         const bool forked = cudaEventRecord(side.fork, s) == cudaSuccess &&
                             cudaStreamWaitEvent(side.stream, side.fork, 0) == cudaSuccess;
         const cudaStream_t rs = forked ? side.stream : s;
-        // 16-byte vectors when all three arrays allow them
-        const bool vec = (((uintptr_t)A.param[4] | (uintptr_t)A.exp_avg[4] |
-                           (uintptr_t)A.exp_avg_sq[4]) & 15) == 0;
 #define MSP_REST(RS)                                                                            \
-    if (vec)                                                                                    \
-        rest_adam_kernel<RS, true><<<grid, kRestThreads, 0, rs>>>(                              \
-            P, N, B.proj.radii, B.grad_acc, B.proj.sh_mean, A.param[4], A.exp_avg[4],           \
-            A.exp_avg_sq[4], used);                                                             \
-    else                                                                                        \
-        rest_adam_kernel<RS, false><<<grid, kRestThreads, 0, rs>>>(                             \
-            P, N, B.proj.radii, B.grad_acc, B.proj.sh_mean, A.param[4], A.exp_avg[4],           \
-            A.exp_avg_sq[4], used)
+    rest_adam_kernel<RS><<<grid, kRestThreads, 0, rs>>>(P, N, B.proj.radii, B.grad_acc,       \
+                                                        B.proj.sh_mean, A.param[4], A.exp_avg[4], \
+                                                        A.exp_avg_sq[4], used)
         bool done = true;
         switch (rest_stride_host) {
             case 45: MSP_REST(45); break;
