@@ -537,9 +537,12 @@ long long msplat_num_intersections(void);
 /* Device error word of the last step (waits); bit 1 = intersection overflow. */
 int msplat_device_errors(void);
 /* Device pointer and element count of a named engine buffer: "xy", "depth",
- * "radii", "conic_op", "rgb", "tile_offset", "sorted_ids", "out_img",
- * "final_T", "final_idx", "v_rendered", "grad_acc", "chunk_idx".  Returns 0
- * or MSPLAT_ERR_ARG for an unknown name. */
+ * "radii", "conic_op", "rgb", "tile_offset", "tile_sorted", "sorted_ids",
+ * "out_img", "final_T", "final_idx", "v_rendered", "grad_acc", "chunk_idx".
+ * "tile_sorted" is the length of each tile's sorted prefix in "sorted_ids"
+ * (a tile of more than 8,192 keys may sort only its nearest keys; the
+ * positions past the prefix are never read).  Returns 0 or MSPLAT_ERR_ARG
+ * for an unknown name. */
 int msplat_debug_buffer(const char *name, void **dev_ptr, long long *count);
 /* Number of kernel launches the engine issued since the last reset. */
 long long msplat_kernel_launches(int reset);

@@ -51,12 +51,12 @@ static const char* kStageNames[kStages] = {"proj_sh_fwd", "bin_sort", "rast_fwd"
 
 // The step's parameters and, after them, the step's counters: one upload per
 // step sets the parameters and zeroes the counters, one readback returns
-// them (loss sum, error bits, intersections).
+// them (loss sum, error bits, intersections, the largest tile).
 struct alignas(64) ParamSlot {
     StepParams p;
     alignas(64) int counters[16];
 };
-constexpr int kCtrLoss = 0, kCtrErr = 4, kCtrIsect = 8, kCtrRead = 12;
+constexpr int kCtrLoss = 0, kCtrErr = 4, kCtrIsect = 8, kCtrMaxTile = 9, kCtrRead = 12;
 static_assert(offsetof(ParamSlot, p) == 0, "the parameters lead the slot");
 
 struct Engine {
@@ -83,6 +83,8 @@ struct Engine {
     double last_loss_scale = 1.0;
     long long growth_isect = 0;  // requested capacity after an overflow
     int last_k_max = 0;          // depth chunks of the last forward (0: none yet)
+    int last_max_tile = 0;       // largest tile count of the last view read back
+    bool last_prefix_sort = false;  // the last forward sorted long lists' fronts only
     int last_num_tiles = 0;
     unsigned long long* d_work = nullptr;  // msplat_count_raster_work's counters
     // timing
@@ -136,6 +138,7 @@ static int init_engine()
     g.B.loss_sum = reinterpret_cast<float*>(d_counters() + kCtrLoss);
     g.B.err = d_counters() + kCtrErr;
     g.B.isect_total = d_counters() + kCtrIsect;
+    g.B.max_tile = d_counters() + kCtrMaxTile;
     MSP_CUDA(cudaDeviceSynchronize());
     g.ready = true;
     return MSPLAT_OK;
@@ -162,7 +165,8 @@ static void free_buffers()
 {
     Buffers& B = g.B;
     void* ptrs[] = {B.proj.xy, B.proj.depth, B.proj.radii, B.proj.conic_op, B.proj.rgb, B.proj.rect,
-                    B.proj.sh_mean, B.tile_count, B.tile_offset, B.tile_order, B.keys, B.keys_alt, B.sorted_ids, B.out_img,
+                    B.proj.sh_mean, B.tile_count, B.tile_offset, B.tile_order, B.tile_sorted, B.tile_flag, B.keys, B.keys_alt,
+                    B.sorted_ids, B.out_img,
                     B.final_T, B.final_idx, B.v_rendered, B.grad_acc,
                     B.chunk_T, B.chunk_C, B.chunk_idx, B.prefix_T, B.after_C};
     for (void* p : ptrs)
@@ -170,10 +174,12 @@ static void free_buffers()
     float* ls = B.loss_sum;
     int* er = B.err;
     int* it = B.isect_total;
+    int* mt = B.max_tile;
     B = Buffers{};
     B.loss_sum = ls;
     B.err = er;
     B.isect_total = it;
+    B.max_tile = mt;
     g.cap_N = g.cap_grad_N = g.cap_pix = g.cap_T = g.cap_isect = g.cap_chunk = 0;
 }
 
@@ -217,6 +223,8 @@ static int ensure(long long N, long long W, long long H, long long T, int K, boo
         if ((rc = realloc_dev(B.tile_count, T * kCountPitch))) return rc;
         if ((rc = realloc_dev(B.tile_offset, T + 1))) return rc;
         if ((rc = realloc_dev(B.tile_order, T))) return rc;
+        if ((rc = realloc_dev(B.tile_sorted, T))) return rc;
+        if ((rc = realloc_dev(B.tile_flag, T + 1))) return rc;
         MSP_CUDA(cudaMemsetAsync(B.tile_count, 0, sizeof(int) * T * kCountPitch, g.stream()));
         g.cap_T = T;
     }
@@ -261,6 +269,7 @@ static void poll_readback(bool wait)
         memcpy(&loss_sum, &g.h_ctr[kCtrLoss], sizeof(float));
         g.last_loss = (float)((double)loss_sum * g.last_loss_scale);
     }
+    g.last_max_tile = g.h_ctr[kCtrMaxTile];
     const int err = g.h_ctr[kCtrErr];
     if (err & kErrStageTimeout)
         fprintf(stderr, "msplat: a shared-memory bulk copy timed out; the step is incomplete\n");
@@ -365,6 +374,13 @@ int fill_params(StepParams& p, const CamArgs& a)
     return MSPLAT_OK;
 }
 
+// Nearest-key sorting of long tile lists, when the last view read back had
+// a tile longer than the radix sorts take (single-pass raster only).
+static int prefix_sort_for(const StepParams& p)
+{
+    return (p.k_max == 1 && g.last_max_tile > kLargeRun) ? 1 : 0;
+}
+
 // Forward half shared by render and train (forward_pipeline, msplat_metal.mm:462-750).
 static int run_forward(const StepParams& p, const float* means, const float* scales,
                        const float* quats, const float* dc, const float* rest, const float* opac,
@@ -377,12 +393,14 @@ static int run_forward(const StepParams& p, const float* means, const float* sca
     tm.mark(1, st);
     launch_scan_tiles(g.d_params, p.num_tiles, B, st);
     launch_scatter(g.d_params, p.num_points, B, st);
-    const int sort_launches = launch_sort_tiles(g.d_params, p.num_tiles, B, st);
+    const int sort_launches = launch_sort_tiles(g.d_params, p.num_tiles, p.prefix_sort != 0, B, st);
     tm.mark(2, st);
-    launch_raster_forward(g.d_params, p.num_tiles, p.k_max, p.img_w, p.img_h, B, st);
+    launch_raster_forward(g.d_params, p.num_tiles, p.k_max, p.prefix_sort != 0, p.img_w, p.img_h, B,
+                          st);
     g.last_k_max = p.k_max;
     g.last_num_tiles = p.num_tiles;
-    g.launches += 3 + sort_launches + (p.k_max > 1 ? 2 : 1);
+    g.last_prefix_sort = p.prefix_sort != 0;
+    g.launches += 3 + sort_launches + (p.k_max > 1 ? 2 : p.prefix_sort ? 3 : 1);
     MSP_CUDA(cudaGetLastError());
     return MSPLAT_OK;
 }
@@ -512,11 +530,13 @@ void cleanup_msplat_cuda(void)
     std::lock_guard<std::mutex> lk(g_mu);
     if (!g.ready) return;
     cudaStreamSynchronize(g.stream());
+    poll_readback(true);  // consumed here, so no later call reads the old view's counters
     free_buffers();
     stage_release();
     if (g.d_work) cudaFree(g.d_work);
     g.d_work = nullptr;
     g.last_k_max = 0;
+    g.last_max_tile = 0;
     g.growth_isect = 0;
 }
 
@@ -593,6 +613,7 @@ static int train_common(const char* who, int num_points, float* means3d, float* 
               features_rest_bases * 3};
     const StepParams adam = p;
     if ((rc = fill_params(p, a))) return rc;
+    p.prefix_sort = prefix_sort_for(p);
     memcpy(p.adam_step, adam.adam_step, sizeof(p.adam_step));
     memcpy(p.adam_bc2, adam.adam_bc2, sizeof(p.adam_bc2));
     p.beta1 = adam.beta1;
@@ -866,6 +887,7 @@ int msplat_render(int num_points, const float* means3d, const float* scales, flo
               img_width, tile_bounds, degree, degrees_to_use, cam_pos, background, rest_stride};
     StepParams p;
     if ((rc = fill_params(p, a))) return rc;
+    p.prefix_sort = prefix_sort_for(p);
     const cudaStream_t st = g.stream();
     if ((rc = ensure(num_points, img_width, img_height, p.num_tiles, p.k_max, false))) return rc;
     p.capacity = g.cap_isect;
@@ -923,6 +945,7 @@ int msplat_debug_buffer(const char* name, void** dev_ptr, long long* count)
         {"xy", B.proj.xy, g.cap_N}, {"depth", B.proj.depth, g.cap_N},
         {"radii", B.proj.radii, g.cap_N}, {"conic_op", B.proj.conic_op, g.cap_N},
         {"rgb", B.proj.rgb, g.cap_N}, {"tile_offset", B.tile_offset, g.cap_T + 1},
+        {"tile_sorted", B.tile_sorted, g.cap_T},
         {"sorted_ids", B.sorted_ids, g.cap_isect}, {"out_img", B.out_img, g.cap_pix * 3},
         {"final_T", B.final_T, g.cap_pix}, {"final_idx", B.final_idx, g.cap_pix},
         {"v_rendered", B.v_rendered, g.cap_pix * 3},
@@ -930,6 +953,12 @@ int msplat_debug_buffer(const char* name, void** dev_ptr, long long* count)
         {"chunk_idx", B.chunk_idx, g.cap_chunk}};
     for (const Ent& e : ents) {
         if (strcmp(e.n, name) == 0) {
+            if (e.p == B.tile_sorted && e.p && !g.last_prefix_sort && g.last_num_tiles > 0) {
+                // a forward without prefix sorting leaves it unwritten: whole lists
+                launch_whole_lists(g.d_params, g.last_num_tiles, B, g.stream());
+                MSP_CUDA(cudaGetLastError());
+                MSP_CUDA(cudaStreamSynchronize(g.stream()));
+            }
             *dev_ptr = e.p;
             if (count) *count = e.c;
             return MSPLAT_OK;
@@ -955,7 +984,7 @@ int msplat_count_raster_work(unsigned long long* out)
     cudaStream_t st = g.stream();
     if (!g.d_work) MSP_CUDA(cudaMalloc(&g.d_work, 4 * sizeof(unsigned long long)));
     MSP_CUDA(cudaMemsetAsync(g.d_work, 0, 4 * sizeof(unsigned long long), st));
-    launch_count_raster_work(g.d_params, g.last_num_tiles, g.B, g.d_work, st);
+    launch_count_raster_work(g.d_params, g.last_num_tiles, g.last_prefix_sort, g.B, g.d_work, st);
     MSP_CUDA(cudaGetLastError());
     MSP_CUDA(cudaMemcpyAsync(out, g.d_work, 4 * sizeof(unsigned long long),
                              cudaMemcpyDeviceToHost, st));

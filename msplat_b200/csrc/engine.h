@@ -37,9 +37,17 @@ struct StepParams {
     int degree, degrees_to_use, rest_stride;
     int k_max;
     int num_adam_groups;
-    int pad0;
+    int prefix_sort;  // tiles of more than kLargeRun keys sort their nearest keys only
     long long capacity;
 };
+
+// Tiles of more than kLargeRun keys are past the shared-memory radix sorts.
+// With StepParams::prefix_sort set (single-pass raster only), such a tile
+// sorts only its nearest keys (at most kLargeRun of them), and the forward
+// raster sorts it whole only when one of its pixels runs past them.  The
+// host sets it when the previous view's largest tile was above kLargeRun,
+// so views without such tiles launch no fix-up kernels.
+constexpr int kLargeRun = 8192;
 
 // Per-Gaussian geometry written by the projection and read by binning and
 // both rasterizers.
@@ -62,6 +70,15 @@ struct Buffers {
     unsigned long long* keys;      // [capacity]
     unsigned long long* keys_alt;  // [capacity] merge scratch for tiles longer than one register-sorted run
     int* sorted_ids;       // [capacity]
+    // Tiles of more than kLargeRun keys (with StepParams::prefix_sort) get
+    // their nearest keys selected and sorted, not the whole list:
+    // tile_sorted[t] is the length of tile t's sorted prefix (its key count
+    // when the whole list is sorted).  The forward raster sets tile_flag[t] when a pixel
+    // of tile t runs past the prefix without terminating, and
+    // tile_flag[T] counts such tiles; those are then sorted whole and
+    // rasterized again.  Both reset by the scan of the tile counts.
+    int* tile_sorted;      // [T]
+    int* tile_flag;        // [T+1]
     float* out_img;        // [H*W*3]
     float* final_T;        // [H*W]
     int* final_idx;        // [H*W]
@@ -75,6 +92,7 @@ struct Buffers {
     float* loss_sum;       // [1]
     int* err;              // [1]
     int* isect_total;      // [1] intersections of the view (scan output), or null
+    int* max_tile;         // [1] the view's largest tile count (scan output), or null
 };
 
 // Device pointers of the optimiser, one entry per group.
@@ -187,10 +205,12 @@ void launch_project_forward(const StepParams* P, int N, const float* means, cons
                             int degrees_to_use_host, int rest_stride_host, cudaStream_t s);
 void launch_scan_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s);
 void launch_scatter(const StepParams* P, int N, const Buffers& B, cudaStream_t s);
-int launch_sort_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s);
-void launch_count_raster_work(const StepParams* P, int num_tiles, const Buffers& B,
+int launch_sort_tiles(const StepParams* P, int num_tiles, bool prefix_sort, const Buffers& B,
+                      cudaStream_t s);
+void launch_whole_lists(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s);
+void launch_count_raster_work(const StepParams* P, int num_tiles, bool prefix_sort, const Buffers& B,
                               unsigned long long* d_out, cudaStream_t s);
-void launch_raster_forward(const StepParams* P, int num_tiles, int k_max, int W, int H,
+void launch_raster_forward(const StepParams* P, int num_tiles, int k_max, bool prefix_sort, int W, int H,
                            const Buffers& B, cudaStream_t s);
 void launch_ssim(const StepParams* P, int W, int H, const float* gt, const Buffers& B,
                  cudaStream_t s);

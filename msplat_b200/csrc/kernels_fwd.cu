@@ -321,16 +321,26 @@ __device__ __forceinline__ int order_bucket(int count) { return min(count >> 1, 
 __global__ void __launch_bounds__(1024)
 scan_tiles_kernel(const StepParams* __restrict__ P, int T, const int* __restrict__ count,
                   int* __restrict__ offset, int* __restrict__ order, int* __restrict__ err,
-                  int* __restrict__ isect_total)
+                  int* __restrict__ isect_total, int* __restrict__ max_tile,
+                  int* __restrict__ tile_sorted, int* __restrict__ tile_flag)
 {
     __shared__ int s_warp[32];
     __shared__ int s_bucket[kOrderBuckets];
     const int tid = threadIdx.x;
     const int per = (T + 1023) / 1024;
     const int beg = min(tid * per, T), end = min(beg + per, T);
-    int local = 0;
-    for (int i = beg; i < end; i++) local += count[i * kCountPitch];
+    int local = 0, lmax = 0;
+    for (int i = beg; i < end; i++) {
+        const int c = count[i * kCountPitch];
+        local += c;
+        lmax = max(lmax, c);
+    }
     const int lane = tid & 31, warp = tid >> 5;
+    if (max_tile) {
+        // the largest tile, into a counter that starts the view at zero
+        lmax = __reduce_max_sync(0xffffffffu, lmax);
+        if (lane == 0 && lmax > 0) atomicMax(max_tile, lmax);
+    }
     int incl = local;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -351,10 +361,17 @@ scan_tiles_kernel(const StepParams* __restrict__ P, int T, const int* __restrict
     }
     __syncthreads();
     int run = s_warp[warp] + incl - local;
+    const bool prefix = P->prefix_sort != 0;
     for (int i = beg; i < end; i++) {
         offset[i] = run;
-        run += count[i * kCountPitch];
+        const int c = count[i * kCountPitch];
+        if (prefix) {
+            tile_sorted[i] = c;  // whole lists unless the prefix sort selects the front
+            tile_flag[i] = 0;
+        }
+        run += c;
     }
+    if (prefix && tid == 0) tile_flag[T] = 0;
     if (tid == 1023) {
         offset[T] = run;
         if (isect_total) *isect_total = run;
@@ -401,7 +418,8 @@ scan_tiles_kernel(const StepParams* __restrict__ P, int T, const int* __restrict
 void launch_scan_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s)
 {
     scan_tiles_kernel<<<1, 1024, 0, s>>>(P, num_tiles, B.tile_count, B.tile_offset, B.tile_order,
-                                         B.err, B.isect_total);
+                                         B.err, B.isect_total, B.max_tile, B.tile_sorted,
+                                         B.tile_flag);
 }
 
 // ---------------------------------------------------------------------------
@@ -693,7 +711,10 @@ __device__ __forceinline__ void radix_scan(RadixSmemT<T, RUN>& S)
 // otherwise writes the ids in ascending (depth, id) order.
 // Register r of a lane holds element w0 + ((r % split) * cv + r / split) * 32
 // + lane: sub-range r % split, its chunk r / split.
-template <int T, int RUN>
+// FROM_SMEM: the n keys are in S.key (depths) and S.val (ids) instead of
+// `keys` (which is then unused); every thread loads its share before the
+// first write to either.
+template <int T, int RUN, bool FROM_SMEM = false>
 __device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __restrict__ keys, int n,
                                                 RadixSmemT<T, RUN>& S, int* __restrict__ out_ids)
 {
@@ -716,9 +737,14 @@ __device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __rest
         v[r] = 0;
         const int e = elem(r);
         if (r < nr && e < n) {
-            const unsigned long long kv = keys[e];
-            k[r] = (unsigned)(kv >> 32);
-            v[r] = (int)(unsigned)(kv & 0xffffffffull);
+            if (FROM_SMEM) {
+                k[r] = S.key[e];
+                v[r] = S.val[e];
+            } else {
+                const unsigned long long kv = keys[e];
+                k[r] = (unsigned)(kv >> 32);
+                v[r] = (int)(unsigned)(kv & 0xffffffffull);
+            }
             ko |= k[r];
             ka &= k[r];
         }
@@ -839,10 +865,139 @@ __device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __rest
 // walking the tile list (largest first) and taking every gridDim.x-th tile.
 // Slot 1 of a tile's counter line (slot 0 is the count) records whether the
 // tile is left to sort_tiles_kernel (1) or done (0); it is written for every
-// tile in this range and read only for those.
+// tile of more than kSortRun keys and read only for those.
+//
+// Tiles of more than kLargeRun keys, when StepParams::prefix_sort is set
+// (single-pass raster only): a pixel stops at the first Gaussian that takes its
+// transmittance to 1e-4, and in a long list that is nearly always close to
+// the front.  So only the front of the list is sorted: the keys whose depth
+// is below a threshold chosen so that at most kLargeRun (and where the
+// depths allow, at least kLargeRun / 2) keys pass.  Every key with a
+// smaller depth passes too, so those keys are exactly the first m of the
+// whole list's (depth, id) order, and a raster that stays inside them
+// gives the result of the whole list bit for bit.  tile_sorted[t] = m; the
+// forward raster flags a tile whose pixels run past the prefix, and the
+// flagged tiles are then sorted whole and rasterized again.
+// The threshold: 2048 buckets over the tile's depth range (the depths as
+// unsigned bits, the order of the keys), a histogram, and the last bucket
+// that still fits; when that bucket leaves less than half the budget used,
+// the next bucket is split the same way (at most three levels: 11 bits a
+// level, down to single depth values).
 constexpr int kLargeThreads = 512;
-constexpr int kLargeRun = 8192;
 using LargeSmem = RadixSmemT<kLargeThreads, kLargeRun>;
+constexpr int kSelBuckets = 2048;
+constexpr int kSelCopies = 256 * LargeSmem::kCols / kSelBuckets;  // histograms in S.hist
+static_assert(kSelCopies >= 1 && kSelBuckets % kLargeThreads == 0, "selection histogram");
+
+// The nearest keys of a tile of n > kLargeRun keys, into S.key (depths) and
+// S.val (ids) in no particular order; returns their count m (0 when more
+// than kLargeRun keys share the smallest depth).
+__device__ int select_nearest(const unsigned long long* __restrict__ keys, int n, LargeSmem& S)
+{
+    constexpr int kWarps = kLargeThreads / 32;
+    constexpr int kPer = kSelBuckets / kLargeThreads;
+    __shared__ unsigned s_lo, s_hi;
+    __shared__ int s_cross[3];  // crossing bucket, keys before it, its count
+    __shared__ int s_m;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    unsigned dmin = ~0u, dmax = 0u;
+    for (int i = tid; i < n; i += kLargeThreads) {
+        const unsigned d = (unsigned)(keys[i] >> 32);
+        dmin = min(dmin, d);
+        dmax = max(dmax, d);
+    }
+    dmin = __reduce_min_sync(0xffffffffu, dmin);
+    dmax = __reduce_max_sync(0xffffffffu, dmax);
+    if (lane == 0) {
+        S.red[warp] = dmin;
+        S.red[kWarps + warp] = dmax;
+    }
+    __syncthreads();
+    unsigned lo = ~0u, hi = 0u;
+#pragma unroll
+    for (int w = 0; w < kWarps; w++) {
+        lo = min(lo, S.red[w]);
+        hi = max(hi, S.red[kWarps + w]);
+    }
+    // keys with depth < lo are selected (`base` of them); [lo, hi] is split
+    int base = 0;
+    unsigned long long thr = lo;
+    for (int level = 0; level < 3; level++) {
+        const unsigned span = hi - lo;
+        int shift = 0;
+        while ((span >> shift) >= (unsigned)kSelBuckets) shift++;
+        for (int i = tid; i < kSelBuckets * kSelCopies; i += kLargeThreads) S.hist[i] = 0;
+        __syncthreads();
+        int* h = S.hist + (warp % kSelCopies) * kSelBuckets;
+        for (int i = tid; i < n; i += kLargeThreads) {
+            const unsigned d = (unsigned)(keys[i] >> 32);
+            if (d >= lo && d <= hi) atomicAdd(&h[(d - lo) >> shift], 1);
+        }
+        __syncthreads();
+        int c[kPer], sum = 0;
+#pragma unroll
+        for (int r = 0; r < kPer; r++) {
+            c[r] = 0;
+#pragma unroll
+            for (int q = 0; q < kSelCopies; q++) c[r] += S.hist[q * kSelBuckets + tid * kPer + r];
+            sum += c[r];
+        }
+        int incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int u = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += u;
+        }
+        if (lane == 31) S.wsum[warp] = incl;
+        __syncthreads();
+        int run = base + incl - sum;
+#pragma unroll
+        for (int w = 0; w < kWarps; w++) run += w < warp ? S.wsum[w] : 0;
+        // The keys in [lo, hi] plus base exceed kLargeRun, so exactly one
+        // bucket crosses the budget: all before it fit, it does not.
+#pragma unroll
+        for (int r = 0; r < kPer; r++) {
+            if (run <= kLargeRun && run + c[r] > kLargeRun) {
+                s_cross[0] = tid * kPer + r;
+                s_cross[1] = run;
+                s_cross[2] = c[r];
+            }
+            run += c[r];
+        }
+        __syncthreads();
+        const int b = s_cross[0], before = s_cross[1];
+        const unsigned long long bucket_lo = (unsigned long long)lo + ((unsigned long long)b << shift);
+        thr = bucket_lo;  // selects everything before bucket b
+        base = before;
+        if (before >= kLargeRun / 2 || shift == 0) break;
+        // split bucket b at the next level
+        lo = (unsigned)bucket_lo;
+        hi = (unsigned)min((unsigned long long)hi, bucket_lo + ((1ull << shift) - 1ull));
+        __syncthreads();  // s_cross and S.wsum read by every thread
+    }
+    if (tid == 0) s_m = 0;
+    __syncthreads();
+    const unsigned lt = (1u << lane) - 1u;
+    for (int i0 = 0; i0 < n; i0 += kLargeThreads) {
+        const int i = i0 + tid;
+        unsigned long long kv = 0ull;
+        bool take = false;
+        if (i < n) {
+            kv = keys[i];
+            take = (kv >> 32) < thr;
+        }
+        const unsigned bal = __ballot_sync(0xffffffffu, take);
+        int at = 0;
+        if (lane == 0 && bal) at = atomicAdd(&s_m, __popc(bal));
+        at = __shfl_sync(0xffffffffu, at, 0) + __popc(bal & lt);
+        if (take && at < kLargeRun) {
+            S.key[at] = (unsigned)(kv >> 32);
+            S.val[at] = (int)(unsigned)(kv & 0xffffffffull);
+        }
+    }
+    __syncthreads();
+    return min(s_m, kLargeRun);
+}
 
 __global__ void __launch_bounds__(kLargeThreads, 2)
 sort_large_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
@@ -864,6 +1019,46 @@ sort_large_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict_
         if (threadIdx.x == 0) tile_line[t * kCountPitch + 1] = ok ? 0 : 1;
     }
 }
+
+// Tiles of more than kLargeRun keys with StepParams::prefix_sort set (the
+// only launches of this kernel): the nearest keys, selected and sorted.
+// Every CTA walks the whole tile list: its order is by count buckets that
+// put every tile of 2,046 keys or more together, so long and short tiles
+// interleave at its head.
+__global__ void __launch_bounds__(kLargeThreads, 2)
+sort_tile_prefixes_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
+                          const int* __restrict__ order, int num_tiles,
+                          const unsigned long long* __restrict__ keys, int* __restrict__ ids,
+                          int* __restrict__ tile_line, int* __restrict__ tile_sorted)
+{
+    extern __shared__ __align__(16) unsigned char s_large[];
+    LargeSmem& S = *reinterpret_cast<LargeSmem*>(s_large);
+    const long long cap = P->capacity;
+    for (int i = blockIdx.x; i < num_tiles; i += gridDim.x) {
+        const int t = order[i];
+        const long long start = min((long long)offset[t], cap);
+        const long long end = min((long long)offset[t + 1], cap);
+        const int n = (int)(end - start);
+        if (n <= kLargeRun) continue;
+        __syncthreads();  // the previous tile's last reads of S
+        bool ok = false;
+        const int m = select_nearest(keys + start, n, S);
+        if (m == 1) {
+            if (threadIdx.x == 0) ids[start] = S.val[0];
+            ok = true;
+        } else if (m > 1) {
+            ok = radix_sort_tile<kLargeThreads, kLargeRun, true>(nullptr, m, S, ids + start);
+        }
+        if (threadIdx.x == 0) {
+            if (ok) tile_sorted[t] = m;
+            tile_line[t * kCountPitch + 1] = ok ? 0 : 1;
+        }
+    }
+}
+
+__device__ void merge_sort_tile(unsigned long long* __restrict__ keys,
+                                unsigned long long* __restrict__ keys_alt, int n,
+                                unsigned long long* s, int* __restrict__ ids);
 
 __global__ void __launch_bounds__(kSortThreads, MSP_SORT_MIN_BLOCKS)
 sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
@@ -890,12 +1085,23 @@ sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offs
         sort_small(keys + start, n, s, nullptr, ids + start);
         return;
     }
-    // kSortRun < n <= kLargeRun: sorted by sort_large_tiles_kernel unless
-    // it left the tile here
-    if (n <= kLargeRun && tile_line[t * kCountPitch + 1] == 0) return;
-    // Large tile: sorted runs of kSortRun, then pairwise merges.
-    unsigned long long* src = keys + start;
-    unsigned long long* dst = keys_alt + start;
+    // n > kSortRun: sorted by sort_large_tiles_kernel (n <= kLargeRun) or
+    // its prefix by sort_tile_prefixes_kernel (with prefix_sort), unless
+    // the kernel left the tile here
+    if ((n <= kLargeRun || P->prefix_sort) && tile_line[t * kCountPitch + 1] == 0) return;
+    merge_sort_tile(keys + start, keys_alt + start, n, s, ids + start);
+}
+
+// The whole list of a large tile: sorted runs of kSortRun (in place in
+// `keys`), then pairwise merges along merge paths between `keys` and
+// `keys_alt`; the ids in (depth, id) order to `ids`.  One CTA of
+// kSortThreads threads.
+__device__ void merge_sort_tile(unsigned long long* __restrict__ keys,
+                                unsigned long long* __restrict__ keys_alt, int n,
+                                unsigned long long* s, int* __restrict__ ids)
+{
+    unsigned long long* src = keys;
+    unsigned long long* dst = keys_alt;
     for (int r0 = 0; r0 < n; r0 += kSortRun) {
         __syncthreads();
         sort_small(src + r0, min(kSortRun, n - r0), s, src + r0, nullptr);
@@ -924,32 +1130,76 @@ sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offs
         dst = tmp;
     }
     for (int i = threadIdx.x; i < n; i += kSortThreads)
-        ids[start + i] = (int)(unsigned)(src[i] & 0xffffffffull);
+        ids[i] = (int)(unsigned)(src[i] & 0xffffffffull);
 }
 
-// Two launches: the tiles of kSortRun + 1 .. kLargeRun keys first (a grid
-// of two CTAs per SM walking the tile list), then every other tile.
-int launch_sort_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s)
+// Tiles the forward raster flagged (a pixel ran past the selected prefix
+// without terminating): their whole list, sorted.  Launched after every
+// single-pass forward; exits at once when no tile was flagged.  Each CTA
+// takes every gridDim.x-th tile of the tile list.
+__global__ void __launch_bounds__(kSortThreads, MSP_SORT_MIN_BLOCKS)
+sort_flagged_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
+                          const int* __restrict__ order, int num_tiles,
+                          unsigned long long* __restrict__ keys,
+                          unsigned long long* __restrict__ keys_alt, int* __restrict__ ids,
+                          int* __restrict__ tile_sorted, const int* __restrict__ tile_flag)
 {
-    if (num_tiles <= 0) return 0;
+    __shared__ unsigned long long s[kSortRun + kSortRun / 16];
+    if (tile_flag[num_tiles] == 0) return;
+    const long long cap = P->capacity;
+    for (int i = blockIdx.x; i < num_tiles; i += gridDim.x) {
+        const int t = order[i];
+        if (!tile_flag[t]) continue;
+        const long long start = min((long long)offset[t], cap);
+        const int n = (int)(min((long long)offset[t + 1], cap) - start);
+        __syncthreads();  // the previous tile's last reads of s
+        merge_sort_tile(keys + start, keys_alt + start, n, s, ids + start);
+        if (threadIdx.x == 0) tile_sorted[t] = n;
+    }
+}
+
+// SM count of the current device (148, the B200's, if the query fails).
+static int device_sms()
+{
     static std::once_flag once[kMaxDeviceSlots];
     static int sms[kMaxDeviceSlots];
     int dev = 0;
     if (!once_per_device(once, [](int d) {
             int n = 0;
             cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
+            sms[d] = n > 0 ? n : 148;
+        }) || cudaGetDevice(&dev) != cudaSuccess)
+        return 148;
+    return sms[dev];
+}
+
+// Two launches: the tiles of kSortRun + 1 .. kLargeRun keys first (a grid
+// of two CTAs per SM walking the tile list), then every other tile; with
+// prefix_sort, a third before them for the tiles of more than kLargeRun keys.
+int launch_sort_tiles(const StepParams* P, int num_tiles, bool prefix_sort, const Buffers& B,
+                      cudaStream_t s)
+{
+    if (num_tiles <= 0) return 0;
+    static std::once_flag once[kMaxDeviceSlots];
+    if (!once_per_device(once, [](int) {
             cudaFuncSetAttribute(sort_large_tiles_kernel,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)sizeof(LargeSmem));
-            sms[d] = n > 0 ? n : 148;
-        }) || cudaGetDevice(&dev) != cudaSuccess)
+            cudaFuncSetAttribute(sort_tile_prefixes_kernel,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)sizeof(LargeSmem));
+        }))
         return 0;
-    const int grid = std::min(num_tiles, 2 * sms[dev]);
+    const int grid = std::min(num_tiles, 2 * device_sms());
+    if (prefix_sort)
+        sort_tile_prefixes_kernel<<<grid, kLargeThreads, sizeof(LargeSmem), s>>>(
+            P, B.tile_offset, B.tile_order, num_tiles, B.keys, B.sorted_ids, B.tile_count,
+            B.tile_sorted);
     sort_large_tiles_kernel<<<grid, kLargeThreads, sizeof(LargeSmem), s>>>(
         P, B.tile_offset, B.tile_order, num_tiles, B.keys, B.sorted_ids, B.tile_count);
     sort_tiles_kernel<<<num_tiles, kSortThreads, 0, s>>>(P, B.tile_offset, B.tile_order, B.keys, B.keys_alt,
                                                         B.sorted_ids, B.tile_count);
-    return 2;
+    return prefix_sort ? 3 : 2;
 }
 
 // ---------------------------------------------------------------------------
@@ -961,10 +1211,15 @@ int launch_sort_tiles(const StepParams* P, int num_tiles, const Buffers& B, cuda
 // staged batch drops the Gaussians that cannot reach any pixel of the tile
 // (tile_may_contribute), which changes no result: those never pass the
 // per-pixel tests.
+// Single pass, MODE: 0, every tile walks its whole list; 1, a tile walks
+// its sorted prefix (tile_sorted, the whole list unless the large-tile sort
+// selected the nearest keys), and when a pixel is still open at the end of
+// a prefix shorter than the list, the tile is flagged (tile_flag); 2, the
+// flagged tiles (by then sorted whole) only, their whole lists.
 // ---------------------------------------------------------------------------
 // Six resident CTAs per SM (40 registers): 0.377 ms at C1 against 0.385
 // with 47 registers (5 CTAs) and 0.379 with 32 (8 CTAs, spilling).
-template <bool CHUNKED>
+template <bool CHUNKED, int MODE>
 __global__ void __launch_bounds__(kTileThreads, MSP_FWD_MIN_BLOCKS)
 raster_forward_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
                       const int* __restrict__ order, const int* __restrict__ ids,
@@ -972,13 +1227,16 @@ raster_forward_kernel(const StepParams* __restrict__ P, const int* __restrict__ 
                       const float4* __restrict__ g_co, const float4* __restrict__ g_rgb,
                       float* __restrict__ out_img, float* __restrict__ final_T,
                       int* __restrict__ final_idx, float* __restrict__ chunk_T,
-                      float* __restrict__ chunk_C, int* __restrict__ chunk_idx)
+                      float* __restrict__ chunk_C, int* __restrict__ chunk_idx,
+                      const int* __restrict__ tile_sorted, int* __restrict__ tile_flag,
+                      int num_tiles)
 {
     __shared__ float2 s_xy[kTileThreads];
     __shared__ float4 s_co[kTileThreads];
     __shared__ float4 s_rgb[kTileThreads];
     __shared__ int s_idx[kTileThreads];
     __shared__ int s_wcnt[kTileThreads / 32];
+    if (!CHUNKED && MODE == 2 && tile_flag[num_tiles] == 0) return;  // nothing flagged
     const int tile = order[blockIdx.x];
     const int tx_n = P->tiles_x;
     const int W = P->img_w, H = P->img_h;
@@ -997,6 +1255,9 @@ raster_forward_kernel(const StepParams* __restrict__ P, const int* __restrict__ 
         beg = fbeg + k * kChunk;
         end = min(fbeg + (k + 1) * kChunk, fend);
         if (beg >= end) return;
+    } else {
+        if (MODE == 2 && tile_flag[tile] == 0) return;
+        if (MODE == 1) end = min(fend, fbeg + tile_sorted[tile]);
     }
     const float fpx = (float)px, fpy = (float)py;
     float T = 1.f, c0 = 0.f, c1 = 0.f, c2 = 0.f;
@@ -1058,6 +1319,13 @@ raster_forward_kernel(const StepParams* __restrict__ P, const int* __restrict__ 
             c2 = fmaf(rgb.z, vis, c2);
             T = next_T;
             last = s_idx[t];
+        }
+    }
+    if (!CHUNKED && MODE == 1 && end < fend) {
+        // a prefix: every pixel must have terminated inside it
+        if (__syncthreads_count(!done) != 0 && tid == 0) {
+            tile_flag[tile] = 1;
+            atomicAdd(&tile_flag[num_tiles], 1);
         }
     }
     if (!inside) return;
@@ -1140,8 +1408,9 @@ merge_chunks_kernel(const StepParams* __restrict__ P, const int* __restrict__ of
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kTileThreads)
 count_raster_work_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
-                         const int* __restrict__ ids, const float2* __restrict__ g_xy,
-                         const float4* __restrict__ g_co, unsigned long long* __restrict__ out)
+                         const int* __restrict__ tile_sorted, const int* __restrict__ ids,
+                         const float2* __restrict__ g_xy, const float4* __restrict__ g_co,
+                         unsigned long long* __restrict__ out)
 {
     const int tile = blockIdx.x;
     const int tx_n = P->tiles_x;
@@ -1149,7 +1418,10 @@ count_raster_work_kernel(const StepParams* __restrict__ P, const int* __restrict
     const int py = (tile / tx_n) * kBlockY + (threadIdx.x >> 4);
     const long long cap = P->capacity;
     const int beg = (int)min((long long)offset[tile], cap);
-    const int end = (int)min((long long)offset[tile + 1], cap);
+    // the sorted prefix (when the forward sorted prefixes): every pixel
+    // terminates inside it
+    int end = (int)min((long long)offset[tile + 1], cap);
+    if (tile_sorted) end = min(end, beg + tile_sorted[tile]);
     unsigned visited = 0, passed = 0, blended = 0, walk = 0;
     if (px < P->img_w && py < P->img_h) {
         const float fpx = (float)px, fpy = (float)py;
@@ -1182,27 +1454,58 @@ count_raster_work_kernel(const StepParams* __restrict__ P, const int* __restrict
     }
 }
 
-void launch_count_raster_work(const StepParams* P, int num_tiles, const Buffers& B,
+// tile_sorted for a forward without prefix_sort (which leaves it unwritten):
+// every list sorted whole.  Introspection only (msplat_debug_buffer).
+__global__ void whole_lists_kernel(const StepParams* __restrict__ P, int T,
+                                   const int* __restrict__ offset, int* __restrict__ tile_sorted)
+{
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= T) return;
+    const long long cap = P->capacity;
+    tile_sorted[t] = (int)(min((long long)offset[t + 1], cap) - min((long long)offset[t], cap));
+}
+
+void launch_whole_lists(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s)
+{
+    if (num_tiles <= 0) return;
+    whole_lists_kernel<<<(num_tiles + 255) / 256, 256, 0, s>>>(P, num_tiles, B.tile_offset,
+                                                               B.tile_sorted);
+}
+
+void launch_count_raster_work(const StepParams* P, int num_tiles, bool prefix_sort, const Buffers& B,
                               unsigned long long* d_out, cudaStream_t s)
 {
     if (num_tiles <= 0) return;
-    count_raster_work_kernel<<<num_tiles, kTileThreads, 0, s>>>(P, B.tile_offset, B.sorted_ids,
+    count_raster_work_kernel<<<num_tiles, kTileThreads, 0, s>>>(P, B.tile_offset,
+                                                               prefix_sort ? B.tile_sorted : nullptr,
+                                                               B.sorted_ids,
                                                                B.proj.xy, B.proj.conic_op, d_out);
 }
 
-void launch_raster_forward(const StepParams* P, int num_tiles, int k_max, int W, int H,
+void launch_raster_forward(const StepParams* P, int num_tiles, int k_max, bool prefix_sort, int W, int H,
                            const Buffers& B, cudaStream_t s)
 {
     if (num_tiles <= 0) return;
-    if (k_max <= 1) {
-        raster_forward_kernel<false><<<num_tiles, kTileThreads, 0, s>>>(
+    if (k_max <= 1 && !prefix_sort) {
+        raster_forward_kernel<false, 0><<<num_tiles, kTileThreads, 0, s>>>(
             P, B.tile_offset, B.tile_order, B.sorted_ids, B.proj.xy, B.proj.conic_op, B.proj.rgb, B.out_img,
-            B.final_T, B.final_idx, nullptr, nullptr, nullptr);
+            B.final_T, B.final_idx, nullptr, nullptr, nullptr, nullptr, nullptr, num_tiles);
+    } else if (k_max <= 1) {
+        // the prefixes, the whole sort of any flagged tile, the flagged tiles again
+        raster_forward_kernel<false, 1><<<num_tiles, kTileThreads, 0, s>>>(
+            P, B.tile_offset, B.tile_order, B.sorted_ids, B.proj.xy, B.proj.conic_op, B.proj.rgb, B.out_img,
+            B.final_T, B.final_idx, nullptr, nullptr, nullptr, B.tile_sorted, B.tile_flag, num_tiles);
+        sort_flagged_tiles_kernel<<<std::min(num_tiles, 2 * device_sms()), kSortThreads, 0, s>>>(
+            P, B.tile_offset, B.tile_order, num_tiles, B.keys, B.keys_alt, B.sorted_ids,
+            B.tile_sorted, B.tile_flag);
+        raster_forward_kernel<false, 2><<<num_tiles, kTileThreads, 0, s>>>(
+            P, B.tile_offset, B.tile_order, B.sorted_ids, B.proj.xy, B.proj.conic_op, B.proj.rgb, B.out_img,
+            B.final_T, B.final_idx, nullptr, nullptr, nullptr, B.tile_sorted, B.tile_flag, num_tiles);
     } else {
         dim3 grid(num_tiles, k_max);
-        raster_forward_kernel<true><<<grid, kTileThreads, 0, s>>>(
+        raster_forward_kernel<true, 0><<<grid, kTileThreads, 0, s>>>(
             P, B.tile_offset, B.tile_order, B.sorted_ids, B.proj.xy, B.proj.conic_op, B.proj.rgb, nullptr,
-            nullptr, nullptr, B.chunk_T, B.chunk_C, B.chunk_idx);
+            nullptr, nullptr, B.chunk_T, B.chunk_C, B.chunk_idx, nullptr, nullptr, num_tiles);
         dim3 mgrid((W + 15) / 16, (H + 15) / 16);
         merge_chunks_kernel<<<mgrid, 256, 0, s>>>(P, B.tile_offset, B.chunk_T, B.chunk_C,
                                                   B.chunk_idx, B.out_img, B.final_T,

@@ -48,6 +48,7 @@ inline size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 // Byte offsets of every buffer inside the array; capacity = intersections.
 struct Layout {
     size_t params, err, xy, depth, radii, conic_op, rgb, rect, tile_count, tile_offset, tile_order;
+    size_t tile_sorted, tile_flag;
     size_t final_T, final_idx, chunk_T, chunk_C, chunk_idx, keys, keys_alt, sorted_ids;
     size_t end;
     long long capacity;
@@ -76,6 +77,8 @@ Layout layout(long long N, long long P, long long T, int K, long long cap)
     L.tile_count = take((size_t)T * kCountPitch * sizeof(int));
     L.tile_offset = take((size_t)(T + 1) * sizeof(int));
     L.tile_order = take((size_t)T * sizeof(int));
+    L.tile_sorted = take((size_t)T * sizeof(int));
+    L.tile_flag = take((size_t)(T + 1) * sizeof(int));
     L.final_T = take(px * sizeof(float));
     L.final_idx = take(px * sizeof(int));
     const size_t kp = K > 1 ? (size_t)K * px : 0;
@@ -142,6 +145,9 @@ extern "C" int msplat_render_noalloc(
     StepParams p;
     int rc = fill_params(p, a);
     if (rc) return rc;
+    // one synchronous call with no earlier view to go by: long lists sort
+    // their nearest keys whenever the raster is single-pass
+    p.prefix_sort = p.k_max == 1 ? 1 : 0;
     if (!out_img || (num_points > 0 && (!means3d || !scales || !quats || !features_dc ||
                                         !opacities || (rest_stride > 0 && !features_rest)))) {
         set_error("msplat_render_noalloc: null device pointer");
@@ -181,6 +187,8 @@ extern "C" int msplat_render_noalloc(
     B.tile_count = reinterpret_cast<int*>(base + L.tile_count);
     B.tile_offset = reinterpret_cast<int*>(base + L.tile_offset);
     B.tile_order = reinterpret_cast<int*>(base + L.tile_order);
+    B.tile_sorted = reinterpret_cast<int*>(base + L.tile_sorted);
+    B.tile_flag = reinterpret_cast<int*>(base + L.tile_flag);
     B.final_T = reinterpret_cast<float*>(base + L.final_T);
     B.final_idx = reinterpret_cast<int*>(base + L.final_idx);
     if (p.k_max > 1) {
@@ -205,8 +213,8 @@ extern "C" int msplat_render_noalloc(
                            features_rest, opacities, B, false, p.degrees_to_use, p.rest_stride, st);
     launch_scan_tiles(d_params, p.num_tiles, B, st);
     launch_scatter(d_params, p.num_points, B, st);
-    launch_sort_tiles(d_params, p.num_tiles, B, st);
-    launch_raster_forward(d_params, p.num_tiles, p.k_max, p.img_w, p.img_h, B, st);
+    launch_sort_tiles(d_params, p.num_tiles, p.prefix_sort != 0, B, st);
+    launch_raster_forward(d_params, p.num_tiles, p.k_max, p.prefix_sort != 0, p.img_w, p.img_h, B, st);
     NA_CUDA(cudaGetLastError());
     int h_check[2] = {0, 0};
     NA_CUDA(cudaMemcpyAsync(&h_check[0], B.err, sizeof(int), cudaMemcpyDeviceToHost, st));

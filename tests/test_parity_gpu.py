@@ -44,8 +44,18 @@ def gpu():
     _lib.load().cleanup_msplat_cuda()
 
 
-def _render_pair(g, cam_setup):
+def _warm(model, cam_setup):
+    """One render whose read-back (the view's largest tile) the next call
+    sees: long tile lists then sort their nearest keys only."""
+    import torch
+    engine.render(model, cam_setup)
+    torch.cuda.synchronize()
+
+
+def _render_pair(g, cam_setup, warm=False):
     model = engine.GaussianModel(g.groups())
+    if warm:
+        _warm(model, cam_setup)
     engine.render(model, cam_setup)
     eng = harness.engine_forward_dump(g.n, cam_setup)
     run = oracle.Run(cam_setup, g.n)
@@ -152,15 +162,45 @@ def test_sort_sizes_and_depth_ties_bitexact(levels):
     harness.assert_forward_bitexact(run, eng, cs)
 
 
-def test_sort_tiles_beyond_large_radix_bitexact():
-    # Two dense clusters: tiles of more than 8,192 keys (merge path) beside
-    # tiles the two radix sorts take, single-pass raster.
-    g, cs = _scene(150_000, 640, 480, seed=12, log_mu=math.log(0.03), log_sigma=0.5, clusters=2)
-    run, eng = _render_pair(g, cs)
+def _clustered_scene():
+    return _scene(150_000, 640, 480, seed=12, log_mu=math.log(0.03), log_sigma=0.5, clusters=2)
+
+
+@pytest.mark.parametrize("prefix", [False, True])
+def test_sort_tiles_beyond_large_radix_bitexact(prefix):
+    # Two dense clusters: tiles of more than 8,192 keys beside tiles the two
+    # radix sorts take, single-pass raster.  With no earlier view (the
+    # engine just cleaned up) the long lists are sorted whole (merge path);
+    # after a view that had such tiles they sort only their nearest keys,
+    # and every pixel terminates inside those.
+    if not prefix:
+        _lib.load().cleanup_msplat_cuda()
+    g, cs = _clustered_scene()
+    run, eng = _render_pair(g, cs, warm=prefix)
     counts = np.diff(run.tile_bins.reshape(-1, 2), axis=1)[:, 0]
     assert run.P.k_max == 1 and (counts > 8192).sum() > 10
     assert ((counts > 2048) & (counts <= 8192)).sum() > 10
     harness.assert_forward_bitexact(run, eng, cs)
+    srt = engine.debug_buffer("tile_sorted", counts.size, np.int32)
+    if prefix:
+        assert (srt < counts).sum() > 10  # prefixes in use
+    else:
+        np.testing.assert_array_equal(srt, counts)
+
+
+def test_prefix_overrun_sorts_whole_tiles_bitexact():
+    # The same clusters, nearly transparent (alpha about 0.0045 at a
+    # Gaussian's centre): no pixel reaches T = 1e-4, every pixel of a long
+    # list runs past its sorted prefix, so the forward flags those tiles,
+    # sorts them whole and rasterizes them again.
+    g, cs = _clustered_scene()
+    g.opacities[:] = np.float32(math.log(0.0045 / (1 - 0.0045)))
+    run, eng = _render_pair(g, cs, warm=True)
+    counts = np.diff(run.tile_bins.reshape(-1, 2), axis=1)[:, 0]
+    assert (counts > 8192).sum() > 10
+    harness.assert_forward_bitexact(run, eng, cs)
+    srt = engine.debug_buffer("tile_sorted", counts.size, np.int32)
+    np.testing.assert_array_equal(srt, counts)  # every tile sorted whole in the end
 
 
 def test_render_all_culled():
@@ -182,11 +222,13 @@ def test_render_single_gaussian():
 # Training steps
 # ---------------------------------------------------------------------------
 
-def _train_pair(g, cs, gt, steps=1, dtu=None, ssim_weight=0.2):
+def _train_pair(g, cs, gt, steps=1, dtu=None, ssim_weight=0.2, warm=False):
     import torch
     if dtu is not None:
         cs.degrees_to_use = dtu
     model = engine.GaussianModel(g.groups())
+    if warm:
+        _warm(model, cs)
     gt_dev = torch.as_tensor(gt).cuda().contiguous()
     params = [x.copy() for x in g.groups()]
     m = [np.zeros_like(x) for x in params]
@@ -286,6 +328,19 @@ def test_train_three_steps():
     g, cs = _scene(20_000, 480, 320, seed=12)
     gt = synthetic.target_image(cs.width, cs.height, 4)
     _check_train(*_train_pair(g, cs, gt, steps=3), cs, check_grads=False, exact_forward=False)
+
+
+def test_train_step_prefix_sorted_tiles():
+    # Long lists that sort only their nearest keys: the backward walks the
+    # same prefixes.
+    g, cs = _clustered_scene()
+    gt = synthetic.target_image(cs.width, cs.height, 6)
+    out = _train_pair(g, cs, gt, warm=True)
+    counts = np.diff(out[1].tile_bins.reshape(-1, 2), axis=1)[:, 0]
+    srt = engine.debug_buffer("tile_sorted", counts.size, np.int32)
+    assert (srt < counts).sum() > 10
+    _check_train(*out, cs)
+    _check_geometry_grads(g, cs, gt, out[1])
 
 
 def test_train_step_l1_only():
