@@ -374,11 +374,13 @@ int fill_params(StepParams& p, const CamArgs& a)
     return MSPLAT_OK;
 }
 
-// Nearest-key sorting of long tile lists, when the last view read back had
-// a tile longer than the radix sorts take (single-pass raster only).
+// Nearest-key sorting of long tile lists, when the last view whose counters
+// were read back had a tile longer than kSortRun keys (single-pass raster
+// only).  The readback is consumed only once complete, so a host running
+// ahead of the device keeps an older view's answer: any answer is correct.
 static int prefix_sort_for(const StepParams& p)
 {
-    return (p.k_max == 1 && g.last_max_tile > kLargeRun) ? 1 : 0;
+    return (p.k_max == 1 && g.last_max_tile > kSortRun) ? 1 : 0;
 }
 
 // Forward half shared by render and train (forward_pipeline, msplat_metal.mm:462-750).

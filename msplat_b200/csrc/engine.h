@@ -37,17 +37,22 @@ struct StepParams {
     int degree, degrees_to_use, rest_stride;
     int k_max;
     int num_adam_groups;
-    int prefix_sort;  // tiles of more than kLargeRun keys sort their nearest keys only
+    int prefix_sort;  // tiles of more than kSortRun keys sort their nearest keys only
     long long capacity;
 };
 
-// Tiles of more than kLargeRun keys are past the shared-memory radix sorts.
-// With StepParams::prefix_sort set (single-pass raster only), such a tile
-// sorts only its nearest keys (at most kLargeRun of them), and the forward
-// raster sorts it whole only when one of its pixels runs past them.  The
-// host sets it when the previous view's largest tile was above kLargeRun,
-// so views without such tiles launch no fix-up kernels.
+// Per-tile sorts: up to kSortRun keys in one CTA's registers or the
+// 128-thread radix sort, up to kLargeRun in the 512-thread radix sort.
+// With StepParams::prefix_sort set (single-pass raster only), a tile of
+// more than kSortRun keys sorts only its nearest keys (about
+// kPrefixTarget, at most kLargeRun of them), and the forward raster sorts
+// it whole only when one of its pixels runs past them.  The host sets it
+// when the largest tile of the last view whose counters it read back was
+// above kSortRun, so scenes without such tiles launch exactly what they
+// did without it.
+constexpr int kSortRun = 2048;
 constexpr int kLargeRun = 8192;
+constexpr int kPrefixTarget = 1024;
 
 // Per-Gaussian geometry written by the projection and read by binning and
 // both rasterizers.
@@ -70,7 +75,7 @@ struct Buffers {
     unsigned long long* keys;      // [capacity]
     unsigned long long* keys_alt;  // [capacity] merge scratch for tiles longer than one register-sorted run
     int* sorted_ids;       // [capacity]
-    // Tiles of more than kLargeRun keys (with StepParams::prefix_sort) get
+    // Tiles of more than kSortRun keys (with StepParams::prefix_sort) get
     // their nearest keys selected and sorted, not the whole list:
     // tile_sorted[t] is the length of tile t's sorted prefix (its key count
     // when the whole list is sorted).  The forward raster sets tile_flag[t] when a pixel

@@ -28,7 +28,6 @@ constexpr int kSortThreads = MSP_SORT_THREADS;
 #ifndef MSP_SORT_MIN_BLOCKS
 #define MSP_SORT_MIN_BLOCKS 8
 #endif
-constexpr int kSortRun = 2048;                   // keys sorted in registers in one pass
 constexpr int kSortKMax = kSortRun / kSortThreads;  // keys per thread at most
 
 // ---------------------------------------------------------------------------
@@ -867,114 +866,118 @@ __device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __rest
 // tile is left to sort_tiles_kernel (1) or done (0); it is written for every
 // tile of more than kSortRun keys and read only for those.
 //
-// Tiles of more than kLargeRun keys, when StepParams::prefix_sort is set
-// (single-pass raster only): a pixel stops at the first Gaussian that takes its
-// transmittance to 1e-4, and in a long list that is nearly always close to
-// the front.  So only the front of the list is sorted: the keys whose depth
-// is below a threshold chosen so that at most kLargeRun (and where the
-// depths allow, at least kLargeRun / 2) keys pass.  Every key with a
-// smaller depth passes too, so those keys are exactly the first m of the
-// whole list's (depth, id) order, and a raster that stays inside them
-// gives the result of the whole list bit for bit.  tile_sorted[t] = m; the
-// forward raster flags a tile whose pixels run past the prefix, and the
-// flagged tiles are then sorted whole and rasterized again.
-// The threshold: 2048 buckets over the tile's depth range (the depths as
-// unsigned bits, the order of the keys), a histogram, and the last bucket
-// that still fits; when that bucket leaves less than half the budget used,
-// the next bucket is split the same way (at most three levels: 11 bits a
-// level, down to single depth values).
+// Tiles of more than kSortRun keys, when StepParams::prefix_sort is set
+// (single-pass raster only; sort_tile_prefixes_kernel takes them all and
+// sort_large_tiles_kernel is not launched): a pixel stops at the first
+// Gaussian that takes its transmittance to 1e-4, and in a long list that
+// is nearly always close to the front.  So only the front of the list is
+// sorted: the keys whose depth is below a threshold that about
+// kPrefixTarget (at most kLargeRun) keys pass.  Every key with a smaller
+// depth passes too, so those keys are exactly the first m of the whole
+// list's (depth, id) order, and a raster that stays inside them gives the
+// result of the whole list bit for bit.  tile_sorted[t] = m; the forward
+// raster flags a tile whose pixels run past the prefix, and the flagged
+// tiles are then sorted whole and rasterized again.  The depths are
+// compared as unsigned bits, the order of the keys.
 constexpr int kLargeThreads = 512;
 using LargeSmem = RadixSmemT<kLargeThreads, kLargeRun>;
 constexpr int kSelBuckets = 2048;
 constexpr int kSelCopies = 256 * LargeSmem::kCols / kSelBuckets;  // histograms in S.hist
 static_assert(kSelCopies >= 1 && kSelBuckets % kLargeThreads == 0, "selection histogram");
 
-// The nearest keys of a tile of n > kLargeRun keys, into S.key (depths) and
-// S.val (ids) in no particular order; returns their count m (0 when more
-// than kLargeRun keys share the smallest depth).
-__device__ int select_nearest(const unsigned long long* __restrict__ keys, int n, LargeSmem& S)
+// Histogram of the depths depth(0 .. count-1) that lie in [lo, hi], in
+// kSelBuckets buckets of 2^shift values, then the bucket b at which
+// base + the running count first exceeds `budget` (one must).  Returns b
+// and, in *before, base + the count of the buckets before b.
+template <typename DepthAt>
+__device__ int crossing_bucket(DepthAt depth, int count, unsigned lo, unsigned hi, int shift,
+                               int base, int budget, LargeSmem& S, int* before)
 {
     constexpr int kWarps = kLargeThreads / 32;
     constexpr int kPer = kSelBuckets / kLargeThreads;
-    __shared__ unsigned s_lo, s_hi;
-    __shared__ int s_cross[3];  // crossing bucket, keys before it, its count
-    __shared__ int s_m;
+    __shared__ int s_cross[2];  // crossing bucket, keys before it
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    unsigned dmin = ~0u, dmax = 0u;
-    for (int i = tid; i < n; i += kLargeThreads) {
-        const unsigned d = (unsigned)(keys[i] >> 32);
-        dmin = min(dmin, d);
-        dmax = max(dmax, d);
-    }
-    dmin = __reduce_min_sync(0xffffffffu, dmin);
-    dmax = __reduce_max_sync(0xffffffffu, dmax);
-    if (lane == 0) {
-        S.red[warp] = dmin;
-        S.red[kWarps + warp] = dmax;
+    __syncthreads();  // earlier reads of S.hist, S.wsum and s_cross are done
+    for (int i = tid; i < kSelBuckets * kSelCopies; i += kLargeThreads) S.hist[i] = 0;
+    __syncthreads();
+    int* h = S.hist + (warp % kSelCopies) * kSelBuckets;
+    for (int i = tid; i < count; i += kLargeThreads) {
+        const unsigned d = depth(i);
+        if (d >= lo && d <= hi) atomicAdd(&h[(d - lo) >> shift], 1);
     }
     __syncthreads();
-    unsigned lo = ~0u, hi = 0u;
+    int c[kPer], sum = 0;
+#pragma unroll
+    for (int r = 0; r < kPer; r++) {
+        c[r] = 0;
+#pragma unroll
+        for (int q = 0; q < kSelCopies; q++) c[r] += S.hist[q * kSelBuckets + tid * kPer + r];
+        sum += c[r];
+    }
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += u;
+    }
+    if (lane == 31) S.wsum[warp] = incl;
+    __syncthreads();
+    int run = base + incl - sum;
+#pragma unroll
+    for (int w = 0; w < kWarps; w++) run += w < warp ? S.wsum[w] : 0;
+#pragma unroll
+    for (int r = 0; r < kPer; r++) {
+        if (run <= budget && run + c[r] > budget) {
+            s_cross[0] = tid * kPer + r;
+            s_cross[1] = run;
+        }
+        run += c[r];
+    }
+    __syncthreads();
+    *before = s_cross[1];
+    return s_cross[0];
+}
+
+// Smallest shift with span >> shift < kSelBuckets.
+__device__ __forceinline__ int bucket_shift(unsigned span)
+{
+    int shift = 0;
+    while ((span >> shift) >= (unsigned)kSelBuckets) shift++;
+    return shift;
+}
+
+// Block-wide min and max of one value per thread.
+__device__ __forceinline__ void block_min_max(unsigned vmin, unsigned vmax, LargeSmem& S,
+                                              unsigned* lo, unsigned* hi)
+{
+    constexpr int kWarps = kLargeThreads / 32;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    vmin = __reduce_min_sync(0xffffffffu, vmin);
+    vmax = __reduce_max_sync(0xffffffffu, vmax);
+    __syncthreads();  // earlier reads of S.red are done
+    if (lane == 0) {
+        S.red[warp] = vmin;
+        S.red[kWarps + warp] = vmax;
+    }
+    __syncthreads();
+    unsigned a = ~0u, b = 0u;
 #pragma unroll
     for (int w = 0; w < kWarps; w++) {
-        lo = min(lo, S.red[w]);
-        hi = max(hi, S.red[kWarps + w]);
+        a = min(a, S.red[w]);
+        b = max(b, S.red[kWarps + w]);
     }
-    // keys with depth < lo are selected (`base` of them); [lo, hi] is split
-    int base = 0;
-    unsigned long long thr = lo;
-    for (int level = 0; level < 3; level++) {
-        const unsigned span = hi - lo;
-        int shift = 0;
-        while ((span >> shift) >= (unsigned)kSelBuckets) shift++;
-        for (int i = tid; i < kSelBuckets * kSelCopies; i += kLargeThreads) S.hist[i] = 0;
-        __syncthreads();
-        int* h = S.hist + (warp % kSelCopies) * kSelBuckets;
-        for (int i = tid; i < n; i += kLargeThreads) {
-            const unsigned d = (unsigned)(keys[i] >> 32);
-            if (d >= lo && d <= hi) atomicAdd(&h[(d - lo) >> shift], 1);
-        }
-        __syncthreads();
-        int c[kPer], sum = 0;
-#pragma unroll
-        for (int r = 0; r < kPer; r++) {
-            c[r] = 0;
-#pragma unroll
-            for (int q = 0; q < kSelCopies; q++) c[r] += S.hist[q * kSelBuckets + tid * kPer + r];
-            sum += c[r];
-        }
-        int incl = sum;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int u = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += u;
-        }
-        if (lane == 31) S.wsum[warp] = incl;
-        __syncthreads();
-        int run = base + incl - sum;
-#pragma unroll
-        for (int w = 0; w < kWarps; w++) run += w < warp ? S.wsum[w] : 0;
-        // The keys in [lo, hi] plus base exceed kLargeRun, so exactly one
-        // bucket crosses the budget: all before it fit, it does not.
-#pragma unroll
-        for (int r = 0; r < kPer; r++) {
-            if (run <= kLargeRun && run + c[r] > kLargeRun) {
-                s_cross[0] = tid * kPer + r;
-                s_cross[1] = run;
-                s_cross[2] = c[r];
-            }
-            run += c[r];
-        }
-        __syncthreads();
-        const int b = s_cross[0], before = s_cross[1];
-        const unsigned long long bucket_lo = (unsigned long long)lo + ((unsigned long long)b << shift);
-        thr = bucket_lo;  // selects everything before bucket b
-        base = before;
-        if (before >= kLargeRun / 2 || shift == 0) break;
-        // split bucket b at the next level
-        lo = (unsigned)bucket_lo;
-        hi = (unsigned)min((unsigned long long)hi, bucket_lo + ((1ull << shift) - 1ull));
-        __syncthreads();  // s_cross and S.wsum read by every thread
-    }
+    *lo = a;
+    *hi = b;
+}
+
+// The keys of depth < thr into S.key (depths) and S.val (ids), the first
+// kLargeRun of them; returns how many there are (possibly more).
+__device__ int compact_below(const unsigned long long* __restrict__ keys, int n,
+                             unsigned long long thr, LargeSmem& S)
+{
+    __shared__ int s_m;
+    const int tid = threadIdx.x, lane = tid & 31;
+    __syncthreads();  // every thread has read what it needs of S.key
     if (tid == 0) s_m = 0;
     __syncthreads();
     const unsigned lt = (1u << lane) - 1u;
@@ -996,7 +999,78 @@ __device__ int select_nearest(const unsigned long long* __restrict__ keys, int n
         }
     }
     __syncthreads();
-    return min(s_m, kLargeRun);
+    return s_m;
+}
+
+// The nearest keys of a tile of n > kSortRun keys, into S.key (depths) and
+// S.val (ids) in no particular order; returns their count m, 1 <= m <=
+// kLargeRun, or 0 when none was found.
+// First from a sample: kSelSample depths at even strides through the list
+// give a threshold expected to pass about kPrefixTarget keys; one pass
+// counts and gathers them.  When that passes none or more than kLargeRun
+// keys and n > kLargeRun, the exact levels: 2048-bucket histograms of all
+// n depths, the last bucket that still fits kLargeRun, and where that
+// leaves less than half of it used, the next bucket split the same way (at
+// most three levels: 11 bits a level, down to single depth values; 0 when
+// more than kLargeRun keys share the smallest depth).
+constexpr int kSelSample = 2048;
+static_assert(kSelSample <= kSortRun && kSelSample % kLargeThreads == 0, "sample in S.key");
+static_assert(kPrefixTarget < kSortRun, "the sample rank is below the sample size");
+
+__device__ int select_nearest(const unsigned long long* __restrict__ keys, int n, LargeSmem& S)
+{
+    const int tid = threadIdx.x;
+    {
+        constexpr int kPer = kSelSample / kLargeThreads;
+        unsigned smin = ~0u, smax = 0u;
+#pragma unroll
+        for (int r = 0; r < kPer; r++) {
+            const int j = tid + r * kLargeThreads;
+            const unsigned d = (unsigned)(keys[(long long)j * n / kSelSample] >> 32);
+            S.key[j] = d;
+            smin = min(smin, d);
+            smax = max(smax, d);
+        }
+        unsigned lo, hi;
+        block_min_max(smin, smax, S, &lo, &hi);  // its barriers also publish S.key
+        const int shift = bucket_shift(hi - lo);
+        // sample rank of the target: q of kSelSample samples ~ kPrefixTarget of n keys
+        const int q = max(1, (int)((long long)kPrefixTarget * kSelSample / n));
+        int before = 0;
+        const int b = crossing_bucket([&](int i) { return S.key[i]; }, kSelSample, lo, hi, shift, 0,
+                                      q, S, &before);
+        const unsigned long long thr = (unsigned long long)lo + ((unsigned long long)b << shift);
+        const int m = compact_below(keys, n, thr, S);
+        if (m >= 1 && m <= kLargeRun) return m;
+    }
+    if (n <= kLargeRun) return 0;  // no budget to cross: the caller sorts it whole
+    unsigned dmin = ~0u, dmax = 0u;
+    for (int i = tid; i < n; i += kLargeThreads) {
+        const unsigned d = (unsigned)(keys[i] >> 32);
+        dmin = min(dmin, d);
+        dmax = max(dmax, d);
+    }
+    unsigned lo, hi;
+    block_min_max(dmin, dmax, S, &lo, &hi);
+    // keys with depth < lo are selected (`base` of them); [lo, hi] is split
+    int base = 0;
+    unsigned long long thr = lo;
+    for (int level = 0; level < 3; level++) {
+        const int shift = bucket_shift(hi - lo);
+        // The keys in [lo, hi] plus base exceed kLargeRun, so exactly one
+        // bucket crosses the budget: all before it fit, it does not.
+        int before = 0;
+        const int b = crossing_bucket([&](int i) { return (unsigned)(keys[i] >> 32); }, n, lo, hi,
+                                      shift, base, kLargeRun, S, &before);
+        const unsigned long long bucket_lo = (unsigned long long)lo + ((unsigned long long)b << shift);
+        thr = bucket_lo;  // selects everything before bucket b
+        base = before;
+        if (before >= kLargeRun / 2 || shift == 0) break;
+        // split bucket b at the next level
+        lo = (unsigned)bucket_lo;
+        hi = (unsigned)min((unsigned long long)hi, bucket_lo + ((1ull << shift) - 1ull));
+    }
+    return min(compact_below(keys, n, thr, S), kLargeRun);
 }
 
 __global__ void __launch_bounds__(kLargeThreads, 2)
@@ -1020,11 +1094,11 @@ sort_large_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict_
     }
 }
 
-// Tiles of more than kLargeRun keys with StepParams::prefix_sort set (the
-// only launches of this kernel): the nearest keys, selected and sorted.
-// Every CTA walks the whole tile list: its order is by count buckets that
-// put every tile of 2,046 keys or more together, so long and short tiles
-// interleave at its head.
+// Tiles of more than kSortRun keys with StepParams::prefix_sort set (the
+// only launches of this kernel): the nearest keys, selected and sorted; a
+// tile of at most kLargeRun keys whose selection fails is sorted whole.
+// Two CTAs per SM, each walking the tile list and taking every
+// gridDim.x-th tile.
 __global__ void __launch_bounds__(kLargeThreads, 2)
 sort_tile_prefixes_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
                           const int* __restrict__ order, int num_tiles,
@@ -1039,15 +1113,20 @@ sort_tile_prefixes_kernel(const StepParams* __restrict__ P, const int* __restric
         const long long start = min((long long)offset[t], cap);
         const long long end = min((long long)offset[t + 1], cap);
         const int n = (int)(end - start);
-        if (n <= kLargeRun) continue;
+        if (n <= kSortRun) continue;
         __syncthreads();  // the previous tile's last reads of S
         bool ok = false;
-        const int m = select_nearest(keys + start, n, S);
+        int m = select_nearest(keys + start, n, S);
         if (m == 1) {
             if (threadIdx.x == 0) ids[start] = S.val[0];
             ok = true;
         } else if (m > 1) {
             ok = radix_sort_tile<kLargeThreads, kLargeRun, true>(nullptr, m, S, ids + start);
+        }
+        if (!ok && n <= kLargeRun) {
+            __syncthreads();
+            m = n;
+            ok = radix_sort_tile(keys + start, n, S, ids + start);
         }
         if (threadIdx.x == 0) {
             if (ok) tile_sorted[t] = m;
@@ -1086,8 +1165,8 @@ sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offs
         return;
     }
     // n > kSortRun: sorted by sort_large_tiles_kernel (n <= kLargeRun) or
-    // its prefix by sort_tile_prefixes_kernel (with prefix_sort), unless
-    // the kernel left the tile here
+    // its prefix (or whole) by sort_tile_prefixes_kernel (with
+    // prefix_sort), unless the kernel left the tile here
     if ((n <= kLargeRun || P->prefix_sort) && tile_line[t * kCountPitch + 1] == 0) return;
     merge_sort_tile(keys + start, keys_alt + start, n, s, ids + start);
 }
@@ -1173,9 +1252,9 @@ static int device_sms()
     return sms[dev];
 }
 
-// Two launches: the tiles of kSortRun + 1 .. kLargeRun keys first (a grid
-// of two CTAs per SM walking the tile list), then every other tile; with
-// prefix_sort, a third before them for the tiles of more than kLargeRun keys.
+// Two launches: the tiles of more than kSortRun keys first (a grid of two
+// CTAs per SM walking the tile list: sort_large_tiles_kernel, or with
+// prefix_sort sort_tile_prefixes_kernel), then every other tile.
 int launch_sort_tiles(const StepParams* P, int num_tiles, bool prefix_sort, const Buffers& B,
                       cudaStream_t s)
 {
@@ -1195,11 +1274,12 @@ int launch_sort_tiles(const StepParams* P, int num_tiles, bool prefix_sort, cons
         sort_tile_prefixes_kernel<<<grid, kLargeThreads, sizeof(LargeSmem), s>>>(
             P, B.tile_offset, B.tile_order, num_tiles, B.keys, B.sorted_ids, B.tile_count,
             B.tile_sorted);
-    sort_large_tiles_kernel<<<grid, kLargeThreads, sizeof(LargeSmem), s>>>(
-        P, B.tile_offset, B.tile_order, num_tiles, B.keys, B.sorted_ids, B.tile_count);
+    else
+        sort_large_tiles_kernel<<<grid, kLargeThreads, sizeof(LargeSmem), s>>>(
+            P, B.tile_offset, B.tile_order, num_tiles, B.keys, B.sorted_ids, B.tile_count);
     sort_tiles_kernel<<<num_tiles, kSortThreads, 0, s>>>(P, B.tile_offset, B.tile_order, B.keys, B.keys_alt,
                                                         B.sorted_ids, B.tile_count);
-    return prefix_sort ? 3 : 2;
+    return 2;
 }
 
 // ---------------------------------------------------------------------------

@@ -15,10 +15,11 @@ def setup_cam(cam, step=10**9, sh_degree=3, interval=1000, rest_bases=15):
                                  rest_bases=rest_bases)
 
 
-# Tiles of more than LARGE_RUN keys sort only the front of their list when
-# the raster is single-pass (the engine's nearest-key selection); the
-# positions past that prefix are never read.
-LARGE_RUN = 8192
+# Tiles of more than SORT_RUN keys may sort only the front of their list
+# when the raster is single-pass (the engine's nearest-key selection, on
+# after a view with such a tile); the positions past that prefix are never
+# read.
+SORT_RUN = 2048
 
 
 def tile_ids_engine(cs, n_isect):
@@ -69,7 +70,7 @@ def assert_forward_bitexact(run, eng, cs):
     np.testing.assert_array_equal(off[:-1], tb[:, 0])
     np.testing.assert_array_equal(off[1:], tb[:, 1])
     counts = np.diff(off)
-    whole = (counts <= LARGE_RUN) | (run.P.k_max > 1)
+    whole = (counts <= SORT_RUN) | (run.P.k_max > 1)
     np.testing.assert_array_equal(srt[whole], counts[whole])
     assert ((srt >= 1) & (srt <= counts))[counts > 0].all()
     mask = sorted_prefix_mask(off, srt)

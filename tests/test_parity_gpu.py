@@ -44,18 +44,22 @@ def gpu():
     _lib.load().cleanup_msplat_cuda()
 
 
-def _warm(model, cam_setup):
-    """One render whose read-back (the view's largest tile) the next call
-    sees: long tile lists then sort their nearest keys only."""
+def _warm(model, cam_setup, warm):
+    """warm: one render whose read-back (the view's largest tile) the next
+    call sees, so tiles of more than 2,048 keys sort their nearest keys
+    only.  Otherwise the engine is cleaned up first: no earlier view, every
+    list sorted whole."""
     import torch
-    engine.render(model, cam_setup)
-    torch.cuda.synchronize()
+    if warm:
+        engine.render(model, cam_setup)
+        torch.cuda.synchronize()
+    else:
+        _lib.load().cleanup_msplat_cuda()
 
 
 def _render_pair(g, cam_setup, warm=False):
     model = engine.GaussianModel(g.groups())
-    if warm:
-        _warm(model, cam_setup)
+    _warm(model, cam_setup, warm)
     engine.render(model, cam_setup)
     eng = harness.engine_forward_dump(g.n, cam_setup)
     run = oracle.Run(cam_setup, g.n)
@@ -141,20 +145,23 @@ def test_distinct_depths_radix_sizes_bitexact():
     harness.assert_forward_bitexact(run, eng, cs)
 
 
+@pytest.mark.parametrize("warm", [False, True])
 @pytest.mark.parametrize("levels", [0, 20_000, 60])
-def test_sort_sizes_and_depth_ties_bitexact(levels):
+def test_sort_sizes_and_depth_ties_bitexact(levels, warm):
     # Tiles of 129-2,048 keys (128-thread radix sort) and 2,049-6,400 keys
     # (512-thread radix sort).  levels = 0: distinct means, yet most large
     # tiles hold a few equal depths (a tile of 4,000 float depths usually
     # does); 20,000 depth planes: runs of up to ~6 equal depths, put in id
     # order inside the radix sorts; 60 planes: runs of ~100, longer than the
     # radix sorts order, so those tiles fall back to the bitonic (small) and
-    # merge (large) sorts of the full (depth, id) keys.
+    # merge (large) sorts of the full (depth, id) keys.  warm: the tiles of
+    # more than 2,048 keys sort their nearest keys instead (prefixes with the
+    # same ties), falling back to whole sorts where the ties refuse them.
     g, cs = _scene(250_000, 640, 480, seed=12, log_mu=math.log(0.03), log_sigma=0.5)
     if levels:
         planes = np.linspace(-0.5, 0.5, levels).astype(np.float32)
         g.means[:, 2] = planes[np.arange(g.n) % levels]
-    run, eng = _render_pair(g, cs)
+    run, eng = _render_pair(g, cs, warm=warm)
     counts = np.diff(run.tile_bins.reshape(-1, 2), axis=1)[:, 0]
     assert run.P.k_max == 1
     assert ((counts > 128) & (counts <= 2048)).sum() > 100
@@ -173,8 +180,6 @@ def test_sort_tiles_beyond_large_radix_bitexact(prefix):
     # engine just cleaned up) the long lists are sorted whole (merge path);
     # after a view that had such tiles they sort only their nearest keys,
     # and every pixel terminates inside those.
-    if not prefix:
-        _lib.load().cleanup_msplat_cuda()
     g, cs = _clustered_scene()
     run, eng = _render_pair(g, cs, warm=prefix)
     counts = np.diff(run.tile_bins.reshape(-1, 2), axis=1)[:, 0]
@@ -227,8 +232,7 @@ def _train_pair(g, cs, gt, steps=1, dtu=None, ssim_weight=0.2, warm=False):
     if dtu is not None:
         cs.degrees_to_use = dtu
     model = engine.GaussianModel(g.groups())
-    if warm:
-        _warm(model, cs)
+    _warm(model, cs, warm)
     gt_dev = torch.as_tensor(gt).cuda().contiguous()
     params = [x.copy() for x in g.groups()]
     m = [np.zeros_like(x) for x in params]
