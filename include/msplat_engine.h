@@ -546,6 +546,11 @@ int msplat_device_errors(void);
 int msplat_debug_buffer(const char *name, void **dev_ptr, long long *count);
 /* Number of kernel launches the engine issued since the last reset. */
 long long msplat_kernel_launches(int reset);
+/* Binning modes of the last forward, for tests and benchmarks: bit 0, long
+ * tile lists sorted their nearest keys only; bit 1, dense binning (large
+ * rects counted by the corners of a 2D difference array).  Neither changes
+ * any result. */
+int msplat_last_binning(void);
 /* Raster work of the last forward (render or training step), for
  * benchmarks; no counterpart in the reference.  Replays the reference's
  * per-pixel loop (nd_rasterize_forward_kernel, msplat_metal.metal:472-585)

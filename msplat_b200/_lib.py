@@ -184,6 +184,7 @@ SIGNATURES = {
     "msplat_device_errors": (_i, []),
     "msplat_debug_buffer": (_i, [C.c_char_p, C.POINTER(_p), C.POINTER(C.c_longlong)]),
     "msplat_kernel_launches": (C.c_longlong, [_i]),
+    "msplat_last_binning": (_i, []),
     "msplat_count_raster_work": (_i, [C.POINTER(C.c_ulonglong)]),
     "msplat_shared_alloc": (_p, [C.c_size_t, _i]),
     "msplat_shared_free": (None, [_p]),

@@ -84,7 +84,11 @@ struct Engine {
     long long growth_isect = 0;  // requested capacity after an overflow
     int last_k_max = 0;          // depth chunks of the last forward (0: none yet)
     int last_max_tile = 0;       // largest tile count of the last view read back
+    long long last_isect = 0;    // its intersections
+    long long last_isect_n = 0;  // and its Gaussians
+    long long readback_n = 0;    // Gaussians of the view whose readback is queued
     bool last_prefix_sort = false;  // the last forward sorted long lists' fronts only
+    bool last_dense_bins = false;   // the last forward used dense binning
     int last_num_tiles = 0;
     unsigned long long* d_work = nullptr;  // msplat_count_raster_work's counters
     // timing
@@ -270,6 +274,8 @@ static void poll_readback(bool wait)
         g.last_loss = (float)((double)loss_sum * g.last_loss_scale);
     }
     g.last_max_tile = g.h_ctr[kCtrMaxTile];
+    g.last_isect = g.h_ctr[kCtrIsect];
+    g.last_isect_n = g.readback_n;
     const int err = g.h_ctr[kCtrErr];
     if (err & kErrStageTimeout)
         fprintf(stderr, "msplat: a shared-memory bulk copy timed out; the step is incomplete\n");
@@ -383,6 +389,15 @@ static int prefix_sort_for(const StepParams& p)
     return (p.k_max == 1 && g.last_max_tile > kSortRun) ? 1 : 0;
 }
 
+// Dense binning, when the last view whose counters were read back averaged
+// more than kDenseRatio intersections per Gaussian (same rule as above for
+// a host running ahead).
+static int dense_bins_for(const StepParams& p)
+{
+    (void)p;
+    return (g.last_isect_n > 0 && g.last_isect > (long long)kDenseRatio * g.last_isect_n) ? 1 : 0;
+}
+
 // Forward half shared by render and train (forward_pipeline, msplat_metal.mm:462-750).
 static int run_forward(const StepParams& p, const float* means, const float* scales,
                        const float* quats, const float* dc, const float* rest, const float* opac,
@@ -393,7 +408,7 @@ static int run_forward(const StepParams& p, const float* means, const float* sca
     launch_project_forward(g.d_params, p.num_points, means, scales, quats, dc, rest, opac, B, train,
                            p.degrees_to_use, p.rest_stride, st);
     tm.mark(1, st);
-    launch_scan_tiles(g.d_params, p.num_tiles, B, st);
+    launch_scan_tiles(g.d_params, p.num_tiles, p.dense_bins != 0, B, st);
     launch_scatter(g.d_params, p.num_points, B, st);
     const int sort_launches = launch_sort_tiles(g.d_params, p.num_tiles, p.prefix_sort != 0, B, st);
     tm.mark(2, st);
@@ -402,6 +417,7 @@ static int run_forward(const StepParams& p, const float* means, const float* sca
     g.last_k_max = p.k_max;
     g.last_num_tiles = p.num_tiles;
     g.last_prefix_sort = p.prefix_sort != 0;
+    g.last_dense_bins = p.dense_bins != 0;
     g.launches += 3 + sort_launches + (p.k_max > 1 ? 2 : p.prefix_sort ? 3 : 1);
     MSP_CUDA(cudaGetLastError());
     return MSPLAT_OK;
@@ -414,6 +430,7 @@ static int queue_readback(cudaStream_t st, const StepParams& p)
     MSP_CUDA(cudaEventRecord(g.readback_ev, st));
     g.readback_pending = true;
     g.readback_has_loss = true;
+    g.readback_n = p.num_points;
     g.last_loss_scale = 1.0 / (3.0 * (double)p.img_w * (double)p.img_h);
     return MSPLAT_OK;
 }
@@ -539,6 +556,7 @@ void cleanup_msplat_cuda(void)
     g.d_work = nullptr;
     g.last_k_max = 0;
     g.last_max_tile = 0;
+    g.last_isect = g.last_isect_n = 0;
     g.growth_isect = 0;
 }
 
@@ -616,6 +634,7 @@ static int train_common(const char* who, int num_points, float* means3d, float* 
     const StepParams adam = p;
     if ((rc = fill_params(p, a))) return rc;
     p.prefix_sort = prefix_sort_for(p);
+    p.dense_bins = dense_bins_for(p);
     memcpy(p.adam_step, adam.adam_step, sizeof(p.adam_step));
     memcpy(p.adam_bc2, adam.adam_bc2, sizeof(p.adam_bc2));
     p.beta1 = adam.beta1;
@@ -890,6 +909,7 @@ int msplat_render(int num_points, const float* means3d, const float* scales, flo
     StepParams p;
     if ((rc = fill_params(p, a))) return rc;
     p.prefix_sort = prefix_sort_for(p);
+    p.dense_bins = dense_bins_for(p);
     const cudaStream_t st = g.stream();
     if ((rc = ensure(num_points, img_width, img_height, p.num_tiles, p.k_max, false))) return rc;
     p.capacity = g.cap_isect;
@@ -904,6 +924,7 @@ int msplat_render(int num_points, const float* means3d, const float* scales, flo
     MSP_CUDA(cudaEventRecord(g.readback_ev, st));
     g.readback_pending = true;
     g.readback_has_loss = false;
+    g.readback_n = p.num_points;
     if (out_img) *out_img = g.B.out_img;
     return MSPLAT_OK;
 }
@@ -1000,6 +1021,12 @@ long long msplat_kernel_launches(int reset)
     long long n = g.launches;
     if (reset) g.launches = 0;
     return n;
+}
+
+int msplat_last_binning(void)
+{
+    std::lock_guard<std::mutex> lk(g_mu);
+    return (g.last_prefix_sort ? 1 : 0) | (g.last_dense_bins ? 2 : 0);
 }
 
 }  // extern "C"

@@ -38,8 +38,19 @@ struct StepParams {
     int k_max;
     int num_adam_groups;
     int prefix_sort;  // tiles of more than kSortRun keys sort their nearest keys only
+    int dense_bins;   // binning for views of many tiles per Gaussian (kDenseArea)
+    int pad0;
     long long capacity;
 };
+
+// Dense binning (StepParams::dense_bins, set by the host when the last view
+// read back held more than kDenseRatio intersections per Gaussian).  The
+// projection counts a rect of more than kDenseArea tiles as the four
+// corners of a 2D difference array (slot 2 of the tiles' counter lines)
+// instead of one atomic per tile, and the scan sums the corners back into
+// counts.  The counts, and so every result, are the same.
+constexpr int kDenseArea = 8;
+constexpr int kDenseRatio = 16;
 
 // Per-tile sorts: up to kSortRun keys in one CTA's registers or the
 // 128-thread radix sort, up to kLargeRun in the 512-thread radix sort.
@@ -208,7 +219,8 @@ void launch_project_forward(const StepParams* P, int N, const float* means, cons
                             const float* quats, const float* dc, const float* rest,
                             const float* opac, const Buffers& B, bool zero_grads,
                             int degrees_to_use_host, int rest_stride_host, cudaStream_t s);
-void launch_scan_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s);
+void launch_scan_tiles(const StepParams* P, int num_tiles, bool dense_bins, const Buffers& B,
+                       cudaStream_t s);
 void launch_scatter(const StepParams* P, int N, const Buffers& B, cudaStream_t s);
 int launch_sort_tiles(const StepParams* P, int num_tiles, bool prefix_sort, const Buffers& B,
                       cudaStream_t s);

@@ -278,8 +278,18 @@ project_forward_kernel(const StepParams* __restrict__ P, int N, const float* __r
         out.sh_mean[3 * (size_t)i + 2] = p[2];
     }
     const int tx_n = P->tiles_x;
-    for (int ty = y0; ty < y1; ty++)
-        for (int tx = x0; tx < x1; tx++) atomicAdd(&tile_count[(ty * tx_n + tx) * kCountPitch], 1);
+    if (P->dense_bins && (x1 - x0) * (y1 - y0) > kDenseArea) {
+        // corners of the rect in a 2D difference array; a corner past the
+        // grid's last row or column changes no tile of the grid
+        const int ty_n = P->tiles_y;
+        atomicAdd(&tile_count[(y0 * tx_n + x0) * kCountPitch + 2], 1);
+        if (x1 < tx_n) atomicAdd(&tile_count[(y0 * tx_n + x1) * kCountPitch + 2], -1);
+        if (y1 < ty_n) atomicAdd(&tile_count[(y1 * tx_n + x0) * kCountPitch + 2], -1);
+        if (x1 < tx_n && y1 < ty_n) atomicAdd(&tile_count[(y1 * tx_n + x1) * kCountPitch + 2], 1);
+    } else {
+        for (int ty = y0; ty < y1; ty++)
+            for (int tx = x0; tx < x1; tx++) atomicAdd(&tile_count[(ty * tx_n + tx) * kCountPitch], 1);
+    }
     if (ZERO_GRADS) {
         float* g = grad_acc + (size_t)i * kGradStride;
 #pragma unroll
@@ -317,8 +327,45 @@ void launch_project_forward(const StepParams* P, int N, const float* means, cons
 constexpr int kOrderBuckets = 1024;  // = the scan CTA's threads
 __device__ __forceinline__ int order_bucket(int count) { return min(count >> 1, kOrderBuckets - 1); }
 
+// Dense binning: the rows, then the columns, of the 2D difference array in
+// slot 2 of the counter lines, summed in place (a warp per row or column,
+// 32 entries a step); slot 0 then gets the whole count and slot 2 is zeroed
+// for the next view.
+__device__ void sum_difference_corners(int* count, int tx_n, int ty_n, int T)
+{
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int kWarps = 1024 / 32;
+    for (int pass = 0; pass < 2; pass++) {
+        const int lines = pass == 0 ? ty_n : tx_n;    // rows, then columns
+        const int len = pass == 0 ? tx_n : ty_n;
+        for (int l = warp; l < lines; l += kWarps) {
+            int carry = 0;
+            for (int k0 = 0; k0 < len; k0 += 32) {
+                const int k = k0 + lane;
+                const int t = pass == 0 ? l * tx_n + k : k * tx_n + l;
+                int v = k < len ? count[t * kCountPitch + 2] : 0;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int u = __shfl_up_sync(0xffffffffu, v, o);
+                    if (lane >= o) v += u;
+                }
+                v += carry;
+                if (k < len) count[t * kCountPitch + 2] = v;
+                carry = __shfl_sync(0xffffffffu, v, 31);
+            }
+        }
+        __syncthreads();
+    }
+    for (int t = threadIdx.x; t < T; t += 1024) {
+        count[t * kCountPitch] += count[t * kCountPitch + 2];
+        count[t * kCountPitch + 2] = 0;
+    }
+    __syncthreads();
+}
+
+template <bool DENSE>
 __global__ void __launch_bounds__(1024)
-scan_tiles_kernel(const StepParams* __restrict__ P, int T, const int* __restrict__ count,
+scan_tiles_kernel(const StepParams* __restrict__ P, int T, int* __restrict__ count,
                   int* __restrict__ offset, int* __restrict__ order, int* __restrict__ err,
                   int* __restrict__ isect_total, int* __restrict__ max_tile,
                   int* __restrict__ tile_sorted, int* __restrict__ tile_flag)
@@ -326,6 +373,7 @@ scan_tiles_kernel(const StepParams* __restrict__ P, int T, const int* __restrict
     __shared__ int s_warp[32];
     __shared__ int s_bucket[kOrderBuckets];
     const int tid = threadIdx.x;
+    if (DENSE) sum_difference_corners(count, P->tiles_x, P->tiles_y, T);
     const int per = (T + 1023) / 1024;
     const int beg = min(tid * per, T), end = min(beg + per, T);
     int local = 0, lmax = 0;
@@ -414,11 +462,17 @@ scan_tiles_kernel(const StepParams* __restrict__ P, int T, const int* __restrict
         order[atomicAdd(&s_bucket[order_bucket(count[i * kCountPitch])], 1)] = i;
 }
 
-void launch_scan_tiles(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s)
+void launch_scan_tiles(const StepParams* P, int num_tiles, bool dense_bins, const Buffers& B,
+                       cudaStream_t s)
 {
-    scan_tiles_kernel<<<1, 1024, 0, s>>>(P, num_tiles, B.tile_count, B.tile_offset, B.tile_order,
-                                         B.err, B.isect_total, B.max_tile, B.tile_sorted,
-                                         B.tile_flag);
+    if (dense_bins)
+        scan_tiles_kernel<true><<<1, 1024, 0, s>>>(P, num_tiles, B.tile_count, B.tile_offset,
+                                                   B.tile_order, B.err, B.isect_total, B.max_tile,
+                                                   B.tile_sorted, B.tile_flag);
+    else
+        scan_tiles_kernel<false><<<1, 1024, 0, s>>>(P, num_tiles, B.tile_count, B.tile_offset,
+                                                    B.tile_order, B.err, B.isect_total, B.max_tile,
+                                                    B.tile_sorted, B.tile_flag);
 }
 
 // ---------------------------------------------------------------------------

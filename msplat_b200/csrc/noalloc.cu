@@ -211,7 +211,7 @@ extern "C" int msplat_render_noalloc(
     NA_CUDA(cudaMemsetAsync(B.tile_count, 0, sizeof(int) * (size_t)p.num_tiles * kCountPitch, st));
     launch_project_forward(d_params, p.num_points, means3d, scales, quats, features_dc,
                            features_rest, opacities, B, false, p.degrees_to_use, p.rest_stride, st);
-    launch_scan_tiles(d_params, p.num_tiles, B, st);
+    launch_scan_tiles(d_params, p.num_tiles, false, B, st);
     launch_scatter(d_params, p.num_points, B, st);
     launch_sort_tiles(d_params, p.num_tiles, p.prefix_sort != 0, B, st);
     launch_raster_forward(d_params, p.num_tiles, p.k_max, p.prefix_sort != 0, p.img_w, p.img_h, B, st);

@@ -62,7 +62,9 @@ def _render_pair(g, cam_setup, warm=False):
     _warm(model, cam_setup, warm)
     engine.render(model, cam_setup)
     eng = harness.engine_forward_dump(g.n, cam_setup)
-    run = oracle.Run(cam_setup, g.n)
+    # room for scenes of many intersections per Gaussian (the oracle does
+    # not grow its buffer)
+    run = oracle.Run(cam_setup, g.n, isect_capacity=64 * max(g.n, 1))
     run.render(g.groups())
     return run, eng
 
@@ -187,6 +189,7 @@ def test_sort_tiles_beyond_large_radix_bitexact(prefix):
     assert ((counts > 2048) & (counts <= 8192)).sum() > 10
     harness.assert_forward_bitexact(run, eng, cs)
     srt = engine.debug_buffer("tile_sorted", counts.size, np.int32)
+    assert bool(_lib.load().msplat_last_binning() & 1) == prefix
     if prefix:
         assert (srt < counts).sum() > 10  # prefixes in use
     else:
@@ -206,6 +209,22 @@ def test_prefix_overrun_sorts_whole_tiles_bitexact():
     harness.assert_forward_bitexact(run, eng, cs)
     srt = engine.debug_buffer("tile_sorted", counts.size, np.int32)
     np.testing.assert_array_equal(srt, counts)  # every tile sorted whole in the end
+
+
+@pytest.mark.parametrize("mean_range", [1.0, 2.0])
+def test_dense_binning_bitexact(mean_range):
+    # Large Gaussians, 34-41 intersections each (rects of up to ~100 tiles):
+    # after a warm view the projection counts the large rects by the corners
+    # of a 2D difference array, which the scan sums back into counts.
+    # mean_range 2: rects reach the image's last tile row and column, whose
+    # outer corners are dropped.  Tile ranges, sorted lists and image
+    # bit-exact.
+    log_mu = math.log(0.06) if mean_range == 1.0 else math.log(0.08)
+    g, cs = _scene(40_000, 640, 480, seed=3, mean_range=mean_range, log_mu=log_mu, log_sigma=0.5)
+    run, eng = _render_pair(g, cs, warm=True)
+    assert run.num_isects > 16 * g.n
+    assert _lib.load().msplat_last_binning() & 2
+    harness.assert_forward_bitexact(run, eng, cs)
 
 
 def test_render_all_culled():
@@ -241,7 +260,8 @@ def _train_pair(g, cs, gt, steps=1, dtu=None, ssim_weight=0.2, warm=False):
     for _ in range(steps):
         engine.train_step(model, cs, gt_dev, ssim_weight=ssim_weight)
         steps_sz, bc2 = model.adam_scalars()
-        run = oracle.Run(cs, g.n, ssim_weight=ssim_weight, adam_steps=steps_sz, adam_bc2=bc2)
+        run = oracle.Run(cs, g.n, ssim_weight=ssim_weight, adam_steps=steps_sz, adam_bc2=bc2,
+                         isect_capacity=64 * max(g.n, 1))
         run.train_step(params, m, v, gt, *st)
     torch.cuda.synchronize()
     return model, run, params, m, v, st
@@ -343,6 +363,16 @@ def test_train_step_prefix_sorted_tiles():
     counts = np.diff(out[1].tile_bins.reshape(-1, 2), axis=1)[:, 0]
     srt = engine.debug_buffer("tile_sorted", counts.size, np.int32)
     assert (srt < counts).sum() > 10
+    _check_train(*out, cs)
+    _check_geometry_grads(g, cs, gt, out[1])
+
+
+def test_train_step_dense_binning():
+    # ~24 intersections per Gaussian, rects reaching the image borders
+    g, cs = _scene(20_000, 480, 320, seed=5, mean_range=2.0, log_mu=math.log(0.1), log_sigma=0.4)
+    gt = synthetic.target_image(cs.width, cs.height, 7)
+    out = _train_pair(g, cs, gt, warm=True)
+    assert _lib.load().msplat_last_binning() & 2
     _check_train(*out, cs)
     _check_geometry_grads(g, cs, gt, out[1])
 
