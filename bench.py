@@ -1152,11 +1152,40 @@ def main():
             return
         res = run_reference(args, rank, world)
     else:
+        # one process group for the whole run: the headline leg and the C4
+        # leg share it (a group destroyed and created again between them
+        # could meet ranks still drawing the C4 scene with the old group's
+        # NCCL bootstrap address)
+        group = shared_group(rank, world)
         res = run_ours(args, rank, world, args.config)
         if args.config == "C1" and not args.no_c4:
             res["c4"] = c4_leg(args, rank, world)
+        if group:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
     if rank == 0 and res is not None:
         print(json.dumps(res), flush=True)
+
+
+def shared_group(rank: int, world: int) -> bool:
+    """The default NCCL process group for world > 1 (127.0.0.1 rendezvous
+    from torchrun's environment), created once here so that every leg's
+    DataParallel uses it instead of creating and destroying its own; a
+    10-minute timeout bounds the wait for a rank still drawing a scene."""
+    if world <= 1:
+        return False
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    if dist.is_initialized():
+        return False
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    dist.init_process_group(backend="nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=600),
+                            device_id=torch.device("cuda", torch.cuda.current_device()))
+    return True
 
 
 def c4_leg(args, rank: int, world: int) -> dict:

@@ -1035,21 +1035,27 @@ __device__ int compact_below(const unsigned long long* __restrict__ keys, int n,
     if (tid == 0) s_m = 0;
     __syncthreads();
     const unsigned lt = (1u << lane) - 1u;
-    for (int i0 = 0; i0 < n; i0 += kLargeThreads) {
-        const int i = i0 + tid;
-        unsigned long long kv = 0ull;
-        bool take = false;
-        if (i < n) {
-            kv = keys[i];
-            take = (kv >> 32) < thr;
+    // kU keys per thread loaded before any is placed: a long list is one
+    // CTA's work, so its loads must overlap
+    constexpr int kU = 8;
+    for (int i0 = 0; i0 < n; i0 += kLargeThreads * kU) {
+        unsigned long long kv[kU];
+#pragma unroll
+        for (int u = 0; u < kU; u++) {
+            const int i = i0 + u * kLargeThreads + tid;
+            kv[u] = i < n ? keys[i] : 0ull;
         }
-        const unsigned bal = __ballot_sync(0xffffffffu, take);
-        int at = 0;
-        if (lane == 0 && bal) at = atomicAdd(&s_m, __popc(bal));
-        at = __shfl_sync(0xffffffffu, at, 0) + __popc(bal & lt);
-        if (take && at < kLargeRun) {
-            S.key[at] = (unsigned)(kv >> 32);
-            S.val[at] = (int)(unsigned)(kv & 0xffffffffull);
+#pragma unroll
+        for (int u = 0; u < kU; u++) {
+            const bool take = i0 + u * kLargeThreads + tid < n && (kv[u] >> 32) < thr;
+            const unsigned bal = __ballot_sync(0xffffffffu, take);
+            int at = 0;
+            if (lane == 0 && bal) at = atomicAdd(&s_m, __popc(bal));
+            at = __shfl_sync(0xffffffffu, at, 0) + __popc(bal & lt);
+            if (take && at < kLargeRun) {
+                S.key[at] = (unsigned)(kv[u] >> 32);
+                S.val[at] = (int)(unsigned)(kv[u] & 0xffffffffull);
+            }
         }
     }
     __syncthreads();
