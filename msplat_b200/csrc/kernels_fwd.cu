@@ -1203,7 +1203,7 @@ __global__ void __launch_bounds__(kSortThreads, MSP_SORT_MIN_BLOCKS)
 sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
                   const int* __restrict__ order, unsigned long long* __restrict__ keys,
                   unsigned long long* __restrict__ keys_alt, int* __restrict__ ids,
-                  const int* __restrict__ tile_line)
+                  const int* __restrict__ tile_line, int large_done)
 {
     __shared__ union {
         unsigned long long bitonic[kSortRun + kSortRun / 16];
@@ -1226,8 +1226,10 @@ sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offs
     }
     // n > kSortRun: sorted by sort_large_tiles_kernel (n <= kLargeRun) or
     // its prefix (or whole) by sort_tile_prefixes_kernel (with
-    // prefix_sort), unless the kernel left the tile here
-    if ((n <= kLargeRun || P->prefix_sort) && tile_line[t * kCountPitch + 1] == 0) return;
+    // prefix_sort), unless the kernel left the tile here or was not
+    // launched (large_done = 0: the merge path takes every such tile)
+    if (large_done && (n <= kLargeRun || P->prefix_sort) && tile_line[t * kCountPitch + 1] == 0)
+        return;
     merge_sort_tile(keys + start, keys_alt + start, n, s, ids + start);
 }
 
@@ -1312,11 +1314,13 @@ static int device_sms()
     return sms[dev];
 }
 
-// Two launches: the tiles of more than kSortRun keys first (a grid of two
-// CTAs per SM walking the tile list: sort_large_tiles_kernel, or with
-// prefix_sort sort_tile_prefixes_kernel), then every other tile.
-int launch_sort_tiles(const StepParams* P, int num_tiles, bool prefix_sort, const Buffers& B,
-                      cudaStream_t s)
+// The tiles of more than kSortRun keys first (a grid of two CTAs per SM
+// walking the tile list: sort_large_tiles_kernel, or with prefix_sort
+// sort_tile_prefixes_kernel), then every other tile.  large_sort = false
+// (a view after one whose largest tile held at most kSortRun keys) skips
+// the first launch; the merge path then takes any longer tile.
+int launch_sort_tiles(const StepParams* P, int num_tiles, bool prefix_sort, bool large_sort,
+                      const Buffers& B, cudaStream_t s)
 {
     if (num_tiles <= 0) return 0;
     static std::once_flag once[kMaxDeviceSlots];
@@ -1330,16 +1334,17 @@ int launch_sort_tiles(const StepParams* P, int num_tiles, bool prefix_sort, cons
         }))
         return 0;
     const int grid = std::min(num_tiles, 2 * device_sms());
+    const bool large_done = prefix_sort || large_sort;
     if (prefix_sort)
         sort_tile_prefixes_kernel<<<grid, kLargeThreads, sizeof(LargeSmem), s>>>(
             P, B.tile_offset, B.tile_order, num_tiles, B.keys, B.sorted_ids, B.tile_count,
             B.tile_sorted);
-    else
+    else if (large_sort)
         sort_large_tiles_kernel<<<grid, kLargeThreads, sizeof(LargeSmem), s>>>(
             P, B.tile_offset, B.tile_order, num_tiles, B.keys, B.sorted_ids, B.tile_count);
     sort_tiles_kernel<<<num_tiles, kSortThreads, 0, s>>>(P, B.tile_offset, B.tile_order, B.keys, B.keys_alt,
-                                                        B.sorted_ids, B.tile_count);
-    return 2;
+                                                        B.sorted_ids, B.tile_count, large_done ? 1 : 0);
+    return large_done ? 2 : 1;
 }
 
 // ---------------------------------------------------------------------------

@@ -196,6 +196,28 @@ def test_sort_tiles_beyond_large_radix_bitexact(prefix):
         np.testing.assert_array_equal(srt, counts)
 
 
+def test_long_tiles_after_a_light_view_bitexact():
+    # A view whose tiles all hold at most 2,048 keys, then the two-cluster
+    # scene: the engine launches neither the 512-thread radix sort nor the
+    # nearest-key sort for it, so every tile of more than 2,048 keys takes
+    # the merge path whole.
+    import torch
+    _lib.load().cleanup_msplat_cuda()
+    lg, lcs = _scene(6_000, 100, 75, seed=4)
+    engine.render(engine.GaussianModel(lg.groups()), lcs)
+    torch.cuda.synchronize()
+    g, cs = _clustered_scene()
+    model = engine.GaussianModel(g.groups())
+    engine.render(model, cs)
+    assert _lib.load().msplat_last_binning() == 0
+    eng = harness.engine_forward_dump(g.n, cs)
+    run = oracle.Run(cs, g.n, isect_capacity=64 * g.n)
+    run.render(g.groups())
+    counts = np.diff(run.tile_bins.reshape(-1, 2), axis=1)[:, 0]
+    assert ((counts > 2048) & (counts <= 8192)).sum() > 10 and (counts > 8192).sum() > 10
+    harness.assert_forward_bitexact(run, eng, cs)
+
+
 def test_prefix_overrun_sorts_whole_tiles_bitexact():
     # The same clusters, nearly transparent (alpha about 0.0045 at a
     # Gaussian's centre): no pixel reaches T = 1e-4, every pixel of a long
