@@ -177,13 +177,13 @@ def peaks() -> dict:
 #
 # Capture (one GPU, one kernel per ncu command, one launch each; the step is
 # bracketed by cudaProfilerStart/Stop in --profile-step mode):
-#   python bench.py --profile-step > gpurun_out/profile_step.json &&
+#   python bench.py --profile-step > ncu_out/profile_step.json &&
 #   ncu --profile-from-start off --clock-control none --kernel-name-base function \
 #       -k regex:<KERNEL> -c 1 --metrics <COUNTER_METRICS> --csv --print-units base \
-#       --log-file gpurun_out/ctr_<KERNEL>.csv python bench.py --profile-step
+#       --log-file ncu_out/ctr_<KERNEL>.csv python bench.py --profile-step
 # Summary:
-#   python bench.py --summarize-ncu gpurun_out/ctr_*.csv \
-#       --hash-file gpurun_out/profile_step.json
+#   python bench.py --summarize-ncu ncu_out/ctr_*.csv \
+#       --hash-file ncu_out/profile_step.json
 # ---------------------------------------------------------------------------
 COUNTERS_FILE = os.path.join(ROOT, "profiles", "counters_c1_train_step.txt")
 COUNTER_METRICS = ("dram__bytes_read.sum", "dram__bytes_write.sum", "smsp__inst_executed.sum",
@@ -277,13 +277,13 @@ def summarize_ncu(csv_paths, hash_file: str, out_path: str = COUNTERS_FILE) -> s
              f"# build {info['build_hash']}",
              f"# view {info['view']}",
              "# command, per kernel K (repository root, one GPU):",
-             "#   python bench.py --profile-step > gpurun_out/profile_step.json &&",
+             "#   python bench.py --profile-step > ncu_out/profile_step.json &&",
              "#   ncu --profile-from-start off --clock-control none --kernel-name-base function \\",
              f"#       -k regex:K -c 1 --metrics {','.join(COUNTER_METRICS)} \\",
              "#       --csv --print-units base \\",
-             "#       --log-file gpurun_out/ctr_K.csv python bench.py --profile-step",
-             "# summary: python bench.py --summarize-ncu gpurun_out/ctr_*.csv "
-             "--hash-file gpurun_out/profile_step.json",
+             "#       --log-file ncu_out/ctr_K.csv python bench.py --profile-step",
+             "# summary: python bench.py --summarize-ncu ncu_out/ctr_*.csv "
+             "--hash-file ncu_out/profile_step.json",
              "\t".join(cols)]
     for k in PROFILED_KERNELS:
         if k in rows and all(m in rows[k] for m in COUNTER_METRICS):
