@@ -410,11 +410,12 @@ static int run_forward(const StepParams& p, const float* means, const float* sca
     tm.mark(1, st);
     launch_scan_tiles(g.d_params, p.num_tiles, p.dense_bins != 0, B, st);
     launch_scatter(g.d_params, p.num_points, B, st);
-    // the 2,049-8,192-key sort only when the last view read back (or none
-    // yet) had such a tile
+    // the sorts of tiles above kSortRun / kLargeRun keys only when the last
+    // view read back (or none yet) had such a tile
     const bool large_sort = g.last_max_tile == 0 || g.last_max_tile > kSortRun;
-    const int sort_launches =
-        launch_sort_tiles(g.d_params, p.num_tiles, p.prefix_sort != 0, large_sort, B, st);
+    const bool huge_sort = g.last_max_tile > kLargeRun;
+    const int sort_launches = launch_sort_tiles(g.d_params, p.num_tiles, p.prefix_sort != 0,
+                                                large_sort, huge_sort, B, st);
     tm.mark(2, st);
     launch_raster_forward(g.d_params, p.num_tiles, p.k_max, p.prefix_sort != 0, p.img_w, p.img_h, B,
                           st);

@@ -223,7 +223,7 @@ void launch_scan_tiles(const StepParams* P, int num_tiles, bool dense_bins, cons
                        cudaStream_t s);
 void launch_scatter(const StepParams* P, int N, const Buffers& B, cudaStream_t s);
 int launch_sort_tiles(const StepParams* P, int num_tiles, bool prefix_sort, bool large_sort,
-                      const Buffers& B, cudaStream_t s);
+                      bool huge_sort, const Buffers& B, cudaStream_t s);
 void launch_whole_lists(const StepParams* P, int num_tiles, const Buffers& B, cudaStream_t s);
 void launch_count_raster_work(const StepParams* P, int num_tiles, bool prefix_sort, const Buffers& B,
                               unsigned long long* d_out, cudaStream_t s);

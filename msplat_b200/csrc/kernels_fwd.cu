@@ -935,27 +935,35 @@ __device__ __forceinline__ bool radix_sort_tile(const unsigned long long* __rest
 // compared as unsigned bits, the order of the keys.
 constexpr int kLargeThreads = 512;
 using LargeSmem = RadixSmemT<kLargeThreads, kLargeRun>;
-constexpr int kSelBuckets = 2048;
-constexpr int kSelCopies = 256 * LargeSmem::kCols / kSelBuckets;  // histograms in S.hist
-static_assert(kSelCopies >= 1 && kSelBuckets % kLargeThreads == 0, "selection histogram");
+// The selection histogram of a CTA of T threads over RadixSmemT<T, RUN>:
+// as many buckets (at most 2048) as S.hist holds, in kCopies copies.
+template <int T, int RUN>
+struct SelShape {
+    using Smem = RadixSmemT<T, RUN>;
+    static constexpr int kHist = 256 * Smem::kCols;
+    static constexpr int kBuckets = kHist >= 2048 ? 2048 : kHist;
+    static constexpr int kCopies = kHist / kBuckets;
+    static_assert(kBuckets % T == 0, "whole buckets per thread");
+};
 
 // Histogram of the depths depth(0 .. count-1) that lie in [lo, hi], in
-// kSelBuckets buckets of 2^shift values, then the bucket b at which
+// SelShape::kBuckets buckets of 2^shift values, then the bucket b at which
 // base + the running count first exceeds `budget` (one must).  Returns b
 // and, in *before, base + the count of the buckets before b.
-template <typename DepthAt>
+template <int T, int RUN, typename DepthAt>
 __device__ int crossing_bucket(DepthAt depth, int count, unsigned lo, unsigned hi, int shift,
-                               int base, int budget, LargeSmem& S, int* before)
+                               int base, int budget, RadixSmemT<T, RUN>& S, int* before)
 {
-    constexpr int kWarps = kLargeThreads / 32;
-    constexpr int kPer = kSelBuckets / kLargeThreads;
+    using Sh = SelShape<T, RUN>;
+    constexpr int kWarps = T / 32;
+    constexpr int kPer = Sh::kBuckets / T;
     __shared__ int s_cross[2];  // crossing bucket, keys before it
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     __syncthreads();  // earlier reads of S.hist, S.wsum and s_cross are done
-    for (int i = tid; i < kSelBuckets * kSelCopies; i += kLargeThreads) S.hist[i] = 0;
+    for (int i = tid; i < Sh::kBuckets * Sh::kCopies; i += T) S.hist[i] = 0;
     __syncthreads();
-    int* h = S.hist + (warp % kSelCopies) * kSelBuckets;
-    for (int i = tid; i < count; i += kLargeThreads) {
+    int* h = S.hist + (warp % Sh::kCopies) * Sh::kBuckets;
+    for (int i = tid; i < count; i += T) {
         const unsigned d = depth(i);
         if (d >= lo && d <= hi) atomicAdd(&h[(d - lo) >> shift], 1);
     }
@@ -965,7 +973,7 @@ __device__ int crossing_bucket(DepthAt depth, int count, unsigned lo, unsigned h
     for (int r = 0; r < kPer; r++) {
         c[r] = 0;
 #pragma unroll
-        for (int q = 0; q < kSelCopies; q++) c[r] += S.hist[q * kSelBuckets + tid * kPer + r];
+        for (int q = 0; q < Sh::kCopies; q++) c[r] += S.hist[q * Sh::kBuckets + tid * kPer + r];
         sum += c[r];
     }
     int incl = sum;
@@ -992,19 +1000,21 @@ __device__ int crossing_bucket(DepthAt depth, int count, unsigned lo, unsigned h
     return s_cross[0];
 }
 
-// Smallest shift with span >> shift < kSelBuckets.
+// Smallest shift with span >> shift < B.
+template <int B>
 __device__ __forceinline__ int bucket_shift(unsigned span)
 {
     int shift = 0;
-    while ((span >> shift) >= (unsigned)kSelBuckets) shift++;
+    while ((span >> shift) >= (unsigned)B) shift++;
     return shift;
 }
 
 // Block-wide min and max of one value per thread.
-__device__ __forceinline__ void block_min_max(unsigned vmin, unsigned vmax, LargeSmem& S,
+template <int T, int RUN>
+__device__ __forceinline__ void block_min_max(unsigned vmin, unsigned vmax, RadixSmemT<T, RUN>& S,
                                               unsigned* lo, unsigned* hi)
 {
-    constexpr int kWarps = kLargeThreads / 32;
+    constexpr int kWarps = T / 32;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     vmin = __reduce_min_sync(0xffffffffu, vmin);
     vmax = __reduce_max_sync(0xffffffffu, vmax);
@@ -1025,9 +1035,10 @@ __device__ __forceinline__ void block_min_max(unsigned vmin, unsigned vmax, Larg
 }
 
 // The keys of depth < thr into S.key (depths) and S.val (ids), the first
-// kLargeRun of them; returns how many there are (possibly more).
+// RUN of them; returns how many there are (possibly more).
+template <int T, int RUN>
 __device__ int compact_below(const unsigned long long* __restrict__ keys, int n,
-                             unsigned long long thr, LargeSmem& S)
+                             unsigned long long thr, RadixSmemT<T, RUN>& S)
 {
     __shared__ int s_m;
     const int tid = threadIdx.x, lane = tid & 31;
@@ -1038,21 +1049,21 @@ __device__ int compact_below(const unsigned long long* __restrict__ keys, int n,
     // kU keys per thread loaded before any is placed: a long list is one
     // CTA's work, so its loads must overlap
     constexpr int kU = 8;
-    for (int i0 = 0; i0 < n; i0 += kLargeThreads * kU) {
+    for (int i0 = 0; i0 < n; i0 += T * kU) {
         unsigned long long kv[kU];
 #pragma unroll
         for (int u = 0; u < kU; u++) {
-            const int i = i0 + u * kLargeThreads + tid;
+            const int i = i0 + u * T + tid;
             kv[u] = i < n ? keys[i] : 0ull;
         }
 #pragma unroll
         for (int u = 0; u < kU; u++) {
-            const bool take = i0 + u * kLargeThreads + tid < n && (kv[u] >> 32) < thr;
+            const bool take = i0 + u * T + tid < n && (kv[u] >> 32) < thr;
             const unsigned bal = __ballot_sync(0xffffffffu, take);
             int at = 0;
             if (lane == 0 && bal) at = atomicAdd(&s_m, __popc(bal));
             at = __shfl_sync(0xffffffffu, at, 0) + __popc(bal & lt);
-            if (take && at < kLargeRun) {
+            if (take && at < RUN) {
                 S.key[at] = (unsigned)(kv[u] >> 32);
                 S.val[at] = (int)(unsigned)(kv[u] & 0xffffffffull);
             }
@@ -1063,29 +1074,32 @@ __device__ int compact_below(const unsigned long long* __restrict__ keys, int n,
 }
 
 // The nearest keys of a tile of n > kSortRun keys, into S.key (depths) and
-// S.val (ids) in no particular order; returns their count m, 1 <= m <=
-// kLargeRun, or 0 when none was found.
+// S.val (ids) in no particular order, for a CTA of T threads; returns their
+// count m, 1 <= m <= RUN, or 0 when none was found.
 // First from a sample: kSelSample depths at even strides through the list
 // give a threshold expected to pass about kPrefixTarget keys; one pass
-// counts and gathers them.  When that passes none or more than kLargeRun
-// keys and n > kLargeRun, the exact levels: 2048-bucket histograms of all
-// n depths, the last bucket that still fits kLargeRun, and where that
-// leaves less than half of it used, the next bucket split the same way (at
-// most three levels: 11 bits a level, down to single depth values; 0 when
-// more than kLargeRun keys share the smallest depth).
+// counts and gathers them.  When that passes none or more than RUN keys,
+// the exact levels: histograms of all n depths, the last bucket that still
+// fits RUN, and where that leaves less than half of it used, the next
+// bucket split the same way (10 or 11 bits a level, down to single depth
+// values; 0 when more than RUN keys share the smallest depth).
 constexpr int kSelSample = 2048;
-static_assert(kSelSample <= kSortRun && kSelSample % kLargeThreads == 0, "sample in S.key");
+static_assert(kSelSample <= kSortRun, "the sample fits S.key of the smaller sort");
 static_assert(kPrefixTarget < kSortRun, "the sample rank is below the sample size");
 
-__device__ int select_nearest(const unsigned long long* __restrict__ keys, int n, LargeSmem& S)
+template <int T, int RUN>
+__device__ int select_nearest(const unsigned long long* __restrict__ keys, int n,
+                              RadixSmemT<T, RUN>& S)
 {
+    constexpr int kB = SelShape<T, RUN>::kBuckets;
+    static_assert(kSelSample <= RUN && kSelSample % T == 0, "sample in S.key");
     const int tid = threadIdx.x;
     {
-        constexpr int kPer = kSelSample / kLargeThreads;
+        constexpr int kPer = kSelSample / T;
         unsigned smin = ~0u, smax = 0u;
 #pragma unroll
         for (int r = 0; r < kPer; r++) {
-            const int j = tid + r * kLargeThreads;
+            const int j = tid + r * T;
             const unsigned d = (unsigned)(keys[(long long)j * n / kSelSample] >> 32);
             S.key[j] = d;
             smin = min(smin, d);
@@ -1093,7 +1107,7 @@ __device__ int select_nearest(const unsigned long long* __restrict__ keys, int n
         }
         unsigned lo, hi;
         block_min_max(smin, smax, S, &lo, &hi);  // its barriers also publish S.key
-        const int shift = bucket_shift(hi - lo);
+        const int shift = bucket_shift<kB>(hi - lo);
         // sample rank of the target: q of kSelSample samples ~ kPrefixTarget of n keys
         const int q = max(1, (int)((long long)kPrefixTarget * kSelSample / n));
         int before = 0;
@@ -1101,11 +1115,11 @@ __device__ int select_nearest(const unsigned long long* __restrict__ keys, int n
                                       q, S, &before);
         const unsigned long long thr = (unsigned long long)lo + ((unsigned long long)b << shift);
         const int m = compact_below(keys, n, thr, S);
-        if (m >= 1 && m <= kLargeRun) return m;
+        if (m >= 1 && m <= RUN) return m;
     }
-    if (n <= kLargeRun) return 0;  // no budget to cross: the caller sorts it whole
+    if (n <= RUN) return 0;  // no budget to cross: the caller sorts it whole
     unsigned dmin = ~0u, dmax = 0u;
-    for (int i = tid; i < n; i += kLargeThreads) {
+    for (int i = tid; i < n; i += T) {
         const unsigned d = (unsigned)(keys[i] >> 32);
         dmin = min(dmin, d);
         dmax = max(dmax, d);
@@ -1115,22 +1129,22 @@ __device__ int select_nearest(const unsigned long long* __restrict__ keys, int n
     // keys with depth < lo are selected (`base` of them); [lo, hi] is split
     int base = 0;
     unsigned long long thr = lo;
-    for (int level = 0; level < 3; level++) {
-        const int shift = bucket_shift(hi - lo);
-        // The keys in [lo, hi] plus base exceed kLargeRun, so exactly one
-        // bucket crosses the budget: all before it fit, it does not.
+    for (int level = 0; level < 4; level++) {
+        const int shift = bucket_shift<kB>(hi - lo);
+        // The keys in [lo, hi] plus base exceed RUN, so exactly one bucket
+        // crosses the budget: all before it fit, it does not.
         int before = 0;
         const int b = crossing_bucket([&](int i) { return (unsigned)(keys[i] >> 32); }, n, lo, hi,
-                                      shift, base, kLargeRun, S, &before);
+                                      shift, base, RUN, S, &before);
         const unsigned long long bucket_lo = (unsigned long long)lo + ((unsigned long long)b << shift);
         thr = bucket_lo;  // selects everything before bucket b
         base = before;
-        if (before >= kLargeRun / 2 || shift == 0) break;
+        if (before >= RUN / 2 || shift == 0) break;
         // split bucket b at the next level
         lo = (unsigned)bucket_lo;
         hi = (unsigned)min((unsigned long long)hi, bucket_lo + ((1ull << shift) - 1ull));
     }
-    return min(compact_below(keys, n, thr, S), kLargeRun);
+    return min(compact_below(keys, n, thr, S), RUN);
 }
 
 __global__ void __launch_bounds__(kLargeThreads, 2)
@@ -1154,11 +1168,17 @@ sort_large_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict_
     }
 }
 
-// Tiles of more than kSortRun keys with StepParams::prefix_sort set (the
-// only launches of this kernel): the nearest keys, selected and sorted; a
-// tile of at most kLargeRun keys whose selection fails is sorted whole.
-// Two CTAs per SM, each walking the tile list and taking every
-// gridDim.x-th tile.
+// With StepParams::prefix_sort set (the only launches of these two
+// kernels) the tiles of more than kSortRun keys sort their nearest keys,
+// selected as in select_nearest, and record the prefix in tile_sorted and
+// their flag in slot 1 of the counter line; a tile whose selection or
+// sort fails is left to sort_tiles_kernel's merge path (flag 1).
+//   sort_tile_prefixes_kernel: more than kLargeRun keys (long lists are
+//     one CTA's work: 512 threads, two CTAs per SM walking the tile list),
+//     prefixes of up to kLargeRun keys;
+//   sort_mid_prefixes_kernel: kSortRun + 1 .. kLargeRun keys, one CTA of
+//     kSortThreads per tile on the shared memory of the 2,048-key radix
+//     sort (eight CTAs per SM), prefixes of up to kSortRun keys.
 __global__ void __launch_bounds__(kLargeThreads, 2)
 sort_tile_prefixes_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
                           const int* __restrict__ order, int num_tiles,
@@ -1173,25 +1193,46 @@ sort_tile_prefixes_kernel(const StepParams* __restrict__ P, const int* __restric
         const long long start = min((long long)offset[t], cap);
         const long long end = min((long long)offset[t + 1], cap);
         const int n = (int)(end - start);
-        if (n <= kSortRun) continue;
+        if (n <= kLargeRun) continue;
         __syncthreads();  // the previous tile's last reads of S
         bool ok = false;
-        int m = select_nearest(keys + start, n, S);
+        const int m = select_nearest(keys + start, n, S);
         if (m == 1) {
             if (threadIdx.x == 0) ids[start] = S.val[0];
             ok = true;
         } else if (m > 1) {
             ok = radix_sort_tile<kLargeThreads, kLargeRun, true>(nullptr, m, S, ids + start);
         }
-        if (!ok && n <= kLargeRun) {
-            __syncthreads();
-            m = n;
-            ok = radix_sort_tile(keys + start, n, S, ids + start);
-        }
         if (threadIdx.x == 0) {
             if (ok) tile_sorted[t] = m;
             tile_line[t * kCountPitch + 1] = ok ? 0 : 1;
         }
+    }
+}
+
+__global__ void __launch_bounds__(kSortThreads, MSP_SORT_MIN_BLOCKS)
+sort_mid_prefixes_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
+                         const int* __restrict__ order, const unsigned long long* __restrict__ keys,
+                         int* __restrict__ ids, int* __restrict__ tile_line,
+                         int* __restrict__ tile_sorted)
+{
+    __shared__ RadixSmem S;
+    const int t = order[blockIdx.x];
+    const long long cap = P->capacity;
+    const long long start = min((long long)offset[t], cap);
+    const int n = (int)(min((long long)offset[t + 1], cap) - start);
+    if (n <= kSortRun || n > kLargeRun) return;
+    bool ok = false;
+    const int m = select_nearest(keys + start, n, S);
+    if (m == 1) {
+        if (threadIdx.x == 0) ids[start] = S.val[0];
+        ok = true;
+    } else if (m > 1) {
+        ok = radix_sort_tile<kSortThreads, kSortRun, true>(nullptr, m, S, ids + start);
+    }
+    if (threadIdx.x == 0) {
+        if (ok) tile_sorted[t] = m;
+        tile_line[t * kCountPitch + 1] = ok ? 0 : 1;
     }
 }
 
@@ -1203,7 +1244,7 @@ __global__ void __launch_bounds__(kSortThreads, MSP_SORT_MIN_BLOCKS)
 sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offset,
                   const int* __restrict__ order, unsigned long long* __restrict__ keys,
                   unsigned long long* __restrict__ keys_alt, int* __restrict__ ids,
-                  const int* __restrict__ tile_line, int large_done)
+                  const int* __restrict__ tile_line, int mid_done, int huge_done)
 {
     __shared__ union {
         unsigned long long bitonic[kSortRun + kSortRun / 16];
@@ -1224,12 +1265,12 @@ sort_tiles_kernel(const StepParams* __restrict__ P, const int* __restrict__ offs
         sort_small(keys + start, n, s, nullptr, ids + start);
         return;
     }
-    // n > kSortRun: sorted by sort_large_tiles_kernel (n <= kLargeRun) or
-    // its prefix (or whole) by sort_tile_prefixes_kernel (with
-    // prefix_sort), unless the kernel left the tile here or was not
-    // launched (large_done = 0: the merge path takes every such tile)
-    if (large_done && (n <= kLargeRun || P->prefix_sort) && tile_line[t * kCountPitch + 1] == 0)
-        return;
+    // n > kSortRun: already sorted (n <= kLargeRun: by sort_large_tiles_kernel
+    // or, with prefix_sort, its prefix by sort_mid_prefixes_kernel; longer:
+    // its prefix by sort_tile_prefixes_kernel) unless that kernel left the
+    // tile here or was not launched (mid_done / huge_done = 0): then the
+    // merge path sorts it whole
+    if ((n <= kLargeRun ? mid_done : huge_done) && tile_line[t * kCountPitch + 1] == 0) return;
     merge_sort_tile(keys + start, keys_alt + start, n, s, ids + start);
 }
 
@@ -1314,13 +1355,14 @@ static int device_sms()
     return sms[dev];
 }
 
-// The tiles of more than kSortRun keys first (a grid of two CTAs per SM
-// walking the tile list: sort_large_tiles_kernel, or with prefix_sort
-// sort_tile_prefixes_kernel), then every other tile.  large_sort = false
-// (a view after one whose largest tile held at most kSortRun keys) skips
-// the first launch; the merge path then takes any longer tile.
+// The tiles of more than kSortRun keys first, then every other tile.
+// Without prefix_sort: sort_large_tiles_kernel (2,049-8,192 keys), unless
+// large_sort is false (the last view read back had no tile above kSortRun
+// keys).  With prefix_sort: sort_tile_prefixes_kernel when huge_sort (the
+// last view had a tile above kLargeRun keys), and sort_mid_prefixes_kernel.
+// A tile of a range whose kernel was not launched takes the merge path.
 int launch_sort_tiles(const StepParams* P, int num_tiles, bool prefix_sort, bool large_sort,
-                      const Buffers& B, cudaStream_t s)
+                      bool huge_sort, const Buffers& B, cudaStream_t s)
 {
     if (num_tiles <= 0) return 0;
     static std::once_flag once[kMaxDeviceSlots];
@@ -1334,17 +1376,26 @@ int launch_sort_tiles(const StepParams* P, int num_tiles, bool prefix_sort, bool
         }))
         return 0;
     const int grid = std::min(num_tiles, 2 * device_sms());
-    const bool large_done = prefix_sort || large_sort;
-    if (prefix_sort)
+    int launches = 1;
+    const bool mid_done = prefix_sort || large_sort;
+    const bool huge_done = prefix_sort && huge_sort;
+    if (huge_done) {
         sort_tile_prefixes_kernel<<<grid, kLargeThreads, sizeof(LargeSmem), s>>>(
             P, B.tile_offset, B.tile_order, num_tiles, B.keys, B.sorted_ids, B.tile_count,
             B.tile_sorted);
+        launches++;
+    }
+    if (prefix_sort)
+        sort_mid_prefixes_kernel<<<num_tiles, kSortThreads, 0, s>>>(
+            P, B.tile_offset, B.tile_order, B.keys, B.sorted_ids, B.tile_count, B.tile_sorted);
     else if (large_sort)
         sort_large_tiles_kernel<<<grid, kLargeThreads, sizeof(LargeSmem), s>>>(
             P, B.tile_offset, B.tile_order, num_tiles, B.keys, B.sorted_ids, B.tile_count);
+    if (mid_done) launches++;
     sort_tiles_kernel<<<num_tiles, kSortThreads, 0, s>>>(P, B.tile_offset, B.tile_order, B.keys, B.keys_alt,
-                                                        B.sorted_ids, B.tile_count, large_done ? 1 : 0);
-    return large_done ? 2 : 1;
+                                                        B.sorted_ids, B.tile_count, mid_done ? 1 : 0,
+                                                        huge_done ? 1 : 0);
+    return launches;
 }
 
 // ---------------------------------------------------------------------------

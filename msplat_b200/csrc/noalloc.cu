@@ -213,7 +213,7 @@ extern "C" int msplat_render_noalloc(
                            features_rest, opacities, B, false, p.degrees_to_use, p.rest_stride, st);
     launch_scan_tiles(d_params, p.num_tiles, false, B, st);
     launch_scatter(d_params, p.num_points, B, st);
-    launch_sort_tiles(d_params, p.num_tiles, p.prefix_sort != 0, true, B, st);
+    launch_sort_tiles(d_params, p.num_tiles, p.prefix_sort != 0, true, true, B, st);
     launch_raster_forward(d_params, p.num_tiles, p.k_max, p.prefix_sort != 0, p.img_w, p.img_h, B, st);
     NA_CUDA(cudaGetLastError());
     int h_check[2] = {0, 0};

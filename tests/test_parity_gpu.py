@@ -218,6 +218,35 @@ def test_long_tiles_after_a_light_view_bitexact():
     harness.assert_forward_bitexact(run, eng, cs)
 
 
+def test_long_tiles_after_a_mid_view_bitexact():
+    # A view whose largest tile holds 2,049-8,192 keys, then the two-cluster
+    # scene: the mid-size tiles sort their nearest keys, but the kernel for
+    # tiles above 8,192 keys is not launched, so those take the merge path
+    # whole.
+    import torch
+    _lib.load().cleanup_msplat_cuda()
+    mg, mcs = _scene(250_000, 640, 480, seed=12, log_mu=math.log(0.03), log_sigma=0.5)
+    engine.render(engine.GaussianModel(mg.groups()), mcs)
+    torch.cuda.synchronize()
+    g, cs = _clustered_scene()
+    model = engine.GaussianModel(g.groups())
+    engine.render(model, cs)
+    assert _lib.load().msplat_last_binning() & 1
+    eng = harness.engine_forward_dump(g.n, cs)
+    run = oracle.Run(cs, g.n, isect_capacity=64 * g.n)
+    run.render(g.groups())
+    harness.assert_forward_bitexact(run, eng, cs)
+    counts = np.diff(run.tile_bins.reshape(-1, 2), axis=1)[:, 0]
+    srt = engine.debug_buffer("tile_sorted", counts.size, np.int32)
+    huge = counts > 8192
+    assert huge.sum() > 10
+    np.testing.assert_array_equal(srt[huge], counts[huge])
+    mid = (counts > 2048) & (counts <= 8192)
+    # prefixes in use (a mid tile whose pixels walk past ~1,024 keys is
+    # flagged by the raster and sorted whole)
+    assert (srt[mid] < counts[mid]).sum() > 0
+
+
 def test_prefix_overrun_sorts_whole_tiles_bitexact():
     # The same clusters, nearly transparent (alpha about 0.0045 at a
     # Gaussian's centre): no pixel reaches T = 1e-4, every pixel of a long
